@@ -1,0 +1,125 @@
+"""Generate golden fixtures by running the REFERENCE scalar path (oracle/_ref).
+
+Each case writes tests/golden/<case>.json (hashes, sizes, settings) and, for
+small streams, tests/golden/<case>.tsac.  Weights come from the seeded package
+(tsac_cuda.seeded_package(0): seeded libnc originals packed into the 20-file
+package); PCM comes from synthetic.music_like.  Run here, where the reference
+sources exist; the fixtures then travel with the repository.
+
+    python tests/golden/make_golden.py --cases short
+    python tests/golden/make_golden.py --cases cfg0_stereo_30s
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import hashlib
+import json
+import pathlib
+import sys
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT / "tsac-metal_b200"))
+import synthetic  # noqa: E402
+import tsac_cuda  # noqa: E402
+
+HERE = pathlib.Path(__file__).resolve().parent
+REF = ROOT / "oracle" / "_ref" / "libtsac_ref.so"
+
+# name: (pcm seed, seconds, channels, method, codebooks, separate, batch)
+CASES = {
+    "stereo_q12_auto_0p1s": (1, 0.1, 2, 1, 0, 0, 0),
+    "stereo_q12_b3_1s": (2, 1.0, 2, 1, 12, 0, 3),
+    "mono_q9_b2_0p5s": (3, 0.5, 1, 1, 0, 0, 2),
+    "separate_q5_b2_0p5s": (4, 0.5, 2, 1, 5, 1, 2),
+    "stereo_fast_q3_0p5s": (5, 0.5, 2, 0, 3, 0, 0),
+    "stereo_q1_b7_0p3s": (6, 0.3, 2, 1, 1, 0, 7),
+    "stereo_q4_b8_0p05s": (7, 0.05, 2, 1, 4, 0, 8),
+    "mono_q2_one_sample": (8, 1.0 / 44100.0, 1, 1, 2, 0, 0),
+    "cfg0_stereo_30s": (0, 30.0, 2, 1, 12, 0, 3),
+}
+SHORT = [k for k in CASES if k != "cfg0_stereo_30s"]
+
+
+def ref_library() -> ctypes.CDLL:
+    lib = ctypes.CDLL(str(REF))
+    lib.ref_last_error.restype = ctypes.c_char_p
+    return lib
+
+
+def ref_check(lib, rc):
+    if rc != 0:
+        raise RuntimeError(lib.ref_last_error().decode())
+
+
+def sha(data: bytes) -> str:
+    return hashlib.sha256(data).hexdigest()
+
+
+def run_case(name: str, package: pathlib.Path) -> dict:
+    seed, seconds, channels, method, codebooks, separate, batch = CASES[name]
+    lib = ref_library()
+    pcm = synthetic.music_like(seed, seconds, channels)
+    samples = pcm.shape[0]
+    out = ctypes.POINTER(ctypes.c_uint8)()
+    nbytes, bits = ctypes.c_size_t(), ctypes.c_size_t()
+    t0 = time.time()
+    ref_check(lib, lib.ref_encode(str(package).encode(), pcm.ctypes.data_as(ctypes.c_void_p),
+                                  ctypes.c_size_t(channels), ctypes.c_size_t(samples), method,
+                                  codebooks, separate, batch, ctypes.byref(out),
+                                  ctypes.byref(nbytes), ctypes.byref(bits)))
+    encode_s = time.time() - t0
+    stream = bytes(out[: nbytes.value])
+    lib.ref_free(out)
+    tok = ctypes.POINTER(ctypes.c_uint16)()
+    count = ctypes.c_size_t()
+    ref_check(lib, lib.ref_stream_tokens(str(package).encode(), stream, ctypes.c_size_t(len(stream)),
+                                         ctypes.byref(tok), ctypes.byref(count)))
+    tokens = np.ctypeslib.as_array(tok, shape=(count.value,)).copy()
+    lib.ref_free(tok)
+    pcm_out = ctypes.POINTER(ctypes.c_float)()
+    ns, nc = ctypes.c_size_t(), ctypes.c_uint()
+    t0 = time.time()
+    ref_check(lib, lib.ref_decode(str(package).encode(), stream, ctypes.c_size_t(len(stream)),
+                                  ctypes.byref(pcm_out), ctypes.byref(ns), ctypes.byref(nc)))
+    decode_s = time.time() - t0
+    decoded = np.ctypeslib.as_array(pcm_out, shape=(ns.value,)).copy()
+    lib.ref_free(pcm_out)
+    record = {
+        "case": name, "pcm_seed": seed, "seconds": seconds, "channels": channels,
+        "method": method, "codebooks": codebooks, "separate": separate, "batch": batch,
+        "weights_seed": 0, "pack_id": tsac_cuda.SEEDED_PACK_ID,
+        "stream_bytes": len(stream), "stream_sha256": sha(stream),
+        "symbol_bits": bits.value if method == 1 else None,
+        "tokens": int(tokens.size), "tokens_sha256": sha(tokens.astype("<u2").tobytes()),
+        "pcm_samples": int(decoded.size), "pcm_channels": nc.value,
+        "pcm_sha256": sha(decoded.astype("<f4").tobytes()),
+        "pcm_head": decoded[: 4096].astype(float).tolist(),
+        "reference_encode_seconds": round(encode_s, 3),
+        "reference_decode_seconds": round(decode_s, 3),
+    }
+    if len(stream) <= 65536:
+        (HERE / f"{name}.tsac").write_bytes(stream)
+    (HERE / f"{name}.json").write_text(json.dumps(record, indent=1) + "\n")
+    return record
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--cases", default="short",
+                        help="'short', 'all' or a comma-separated list of case names")
+    args = parser.parse_args()
+    names = SHORT if args.cases == "short" else list(CASES) if args.cases == "all" \
+        else args.cases.split(",")
+    package = tsac_cuda.seeded_package(0)
+    for name in names:
+        r = run_case(name, package)
+        print(name, r["stream_bytes"], r["stream_sha256"][:16],
+              r["reference_encode_seconds"], r["reference_decode_seconds"], flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,31 @@
+// Host-side launch interface of the BF8L quantized linear kernels.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace tsacb::dev
+{
+struct QLinearArgs
+{
+    const std::int8_t* weights = nullptr;     // [n][k] int8
+    const float* weight_scales = nullptr;     // [k/256][n]
+    const float* bias = nullptr;              // [n]
+    const std::int8_t* xq = nullptr;          // [m][k] quantized activations
+    const float* xscale = nullptr;            // [m][k/256]
+    const std::uint16_t* residual = nullptr;  // [m][n] bf16, added after rounding
+    const std::uint16_t* lut = nullptr;       // bf16 -> bf16 map applied last (GELU)
+    std::uint16_t* y = nullptr;               // [m][n] bf16
+    int m = 0, n = 0, k = 0;
+};
+
+// Bytes of scratch holding the quantized activations of m columns of k inputs.
+size_t qlinear_scratch_bytes(size_t m, size_t k);
+// BF8L quantization of bf16 activations [m][k] into int8 + per-block scales.
+void qlinear_quantize(const std::uint16_t* x, int m, int k, std::int8_t* xq, float* xscale,
+                      unsigned* error_word, cudaStream_t stream);
+// Exact int8 block dots + ordered FP32 epilogue (GEMV for m <= 16, tiled GEMM above).
+void qlinear_matmul(const QLinearArgs& args, cudaStream_t stream);
+// One-time kernel attribute setup (dynamic shared memory limits).
+void qlinear_init();
+} // namespace tsacb::dev
