@@ -58,6 +58,122 @@ int tsac_cuda_write_seeded_sources(const char* directory, uint64_t seed);
 int tsac_cuda_pack_models(const char* input_directory, const char* output_directory,
                           const char* pack_id, int include_transformer);
 
+/* ---- analyzer context (one per AudioAnalyzer instance and device) ------ */
+
+typedef struct tsac_cuda_context tsac_cuda_context;
+
+/* EncodeOptions (include/tsac/audio_analyzer.hpp:16-22). */
+typedef struct tsac_cuda_encode_options
+{
+    int method;             /* 0 = fast (10-bit fields), 1 = normal (Transformer + range coder) */
+    unsigned codebooks;     /* 0 = model maximum (12 joint stereo, 9 otherwise) */
+    int separate_channels;  /* nonzero: code a stereo input as two mono groups */
+    int entropy_batch;      /* 0 = automatic (select_entropy_batch), else 1..65535 */
+} tsac_cuda_encode_options;
+
+/* Binds a model package directory (the reference's ModelDirectory: 20
+ * `.weights` files + adapter_offsets.hpp, include/tsac/model_directory.hpp:15-25)
+ * to CUDA device `device`.  Prepared device weights are created on first use
+ * and kept for later calls.  A context is used by one thread at a time;
+ * separate contexts are independent (AUDIO_API.md:81-118). */
+int tsac_cuda_context_create(const char* package_directory, int device, tsac_cuda_context** out);
+void tsac_cuda_context_destroy(tsac_cuda_context* context);
+
+/* AudioAnalyzer::encode (include/tsac/audio_analyzer.hpp:33-34) for a host
+ * PCM view [channel, sample] with the given strides (in floats, as
+ * tsac::PcmView's layout_stride).  *out (free with tsac_cuda_free) receives the
+ * .tsac stream; *symbol_bits (nullable) the payload bit position before
+ * termination (the sum an EntropyObserver's after_symbol would report). */
+int tsac_cuda_encode(tsac_cuda_context* context, const float* pcm, size_t channels,
+                     size_t samples, ptrdiff_t channel_stride, ptrdiff_t sample_stride,
+                     const tsac_cuda_encode_options* options, uint8_t** out, size_t* out_bytes,
+                     size_t* symbol_bits);
+
+/* AudioAnalyzer::decode (include/tsac/audio_analyzer.hpp:35): stream ->
+ * interleaved float PCM [sample][channel], padding retained. */
+int tsac_cuda_decode(tsac_cuda_context* context, const uint8_t* stream, size_t bytes,
+                     float** out, size_t* samples, unsigned* channels);
+
+/* Batched forms: `count` independent interleaved recordings per call (the
+ * throughput path: all recordings share each GPU launch). */
+int tsac_cuda_encode_batch(tsac_cuda_context* context, size_t count, const float* const* pcm,
+                           const size_t* channels, const size_t* samples,
+                           const tsac_cuda_encode_options* options, uint8_t** out,
+                           size_t* out_bytes);
+int tsac_cuda_decode_batch(tsac_cuda_context* context, size_t count,
+                           const uint8_t* const* streams, const size_t* bytes, float** out,
+                           size_t* samples, unsigned* channels);
+
+/* ---- pipeline stages (host buffers; synchronous) ----------------------- */
+
+/* Encoder front end: padding, 400-frame chunks with 8/9 context, DAC analysis
+ * and RVQ (detail::analyze_audio, src/common/audio_pipeline.hpp:36-61) ->
+ * tokens [frame][group][book]. */
+int tsac_cuda_analyze_tokens(tsac_cuda_context* context, const float* interleaved_pcm,
+                             size_t channels, size_t samples,
+                             const tsac_cuda_encode_options* options, uint16_t** tokens,
+                             size_t* count);
+
+/* DacAnalysis::apply (src/common/analysis.tpp:169-214) of one window:
+ * pcm [pcm_frames][channels] (pcm_frames a multiple of 512) -> latent [pcm_frames/512][1024]. */
+int tsac_cuda_dac_analysis(tsac_cuda_context* context, unsigned channels, const float* pcm,
+                           size_t pcm_frames, float* latent);
+
+/* DacSynthesis::apply (src/common/synthesis.tpp:168-213) of one window:
+ * latent [frames][1024] -> pcm [frames*512][channels]. */
+int tsac_cuda_dac_synthesis(tsac_cuda_context* context, unsigned channels, const float* latent,
+                            size_t frames, float* pcm);
+
+/* RvqEncoder::encode (src/common/rvq.tpp:59-95) of one group: latent
+ * [frames][1024] -> tokens [frames][books]; RvqDecoder::decode
+ * (src/common/rvq.cpp:76-120) the inverse reconstruction. */
+int tsac_cuda_rvq_encode(tsac_cuda_context* context, unsigned channels, unsigned books,
+                         const float* latent, size_t frames, uint16_t* tokens);
+int tsac_cuda_rvq_decode(tsac_cuda_context* context, unsigned channels, unsigned books,
+                         const uint16_t* tokens, size_t frames, float* latent);
+
+/* TokenPredictor over known tokens (TransformerPredictor + CpuTransformer,
+ * src/common/transformer.cpp:59-166, src/common/cpu_transformer.tpp:317-385):
+ * for tokens [frame][group][book], writes per symbol (token-offset order) the
+ * float probabilities [1024] (nullable) and the Q15 zero-probabilities of the
+ * 10 bisection nodes on the path to the symbol's token (nullable,
+ * encode_categorical, src/format/categorical.cpp:91-117). */
+int tsac_cuda_transformer_probabilities(tsac_cuda_context* context, unsigned channels,
+                                        unsigned groups, unsigned books, size_t frames,
+                                        unsigned batch, const uint16_t* tokens,
+                                        float* probabilities, uint16_t* q15);
+
+/* pack_normal (src/format/entropy.cpp:57-123) for known tokens [frame][group][book]
+ * with the GPU predictor and the host range coder: the normal-mode stream. */
+int tsac_cuda_pack_normal(tsac_cuda_context* context, unsigned channels, unsigned groups,
+                          unsigned books, size_t frames, unsigned batch, const uint16_t* tokens,
+                          uint8_t** out, size_t* out_bytes);
+
+/* ---- kernel-level entry points (device pointers, enqueue on `stream`) -- */
+
+/* Scratch bytes tsac_cuda_qlinear needs for m columns of k inputs (the BF8L
+ * quantized activations: int8 [m][k] then f32 scales [m][k/256]). */
+size_t tsac_cuda_qlinear_scratch_bytes(size_t m, size_t k);
+
+/* Quantized linear projection, y = bf16(W x + bias) [+ residual]:
+ * PackedLinear::apply_into (src/common/packed_linear.tpp:85-123) = scalar::bf8l
+ * (src/scalar/probability.cpp:16-40) + Kernels::linear_column per column
+ * (src/scalar/packed_linear.cpp:8-30).
+ *   weights       device int8 [n][k] canonical row-major (the package's
+ *                 transformer-source plane; no R4 re-tiling)
+ *   weight_scales device f32 [k/256][n];  bias device f32 [n]
+ *   x             device bf16 [m][k];     y device bf16 [m][n]
+ *   residual      device bf16 [m][n] or NULL: y = bf16(residual + y)
+ *                 (probability_add_bf16, src/common/probability.cpp:7-12)
+ *   scratch       device, >= tsac_cuda_qlinear_scratch_bytes(m, k)
+ *   error_word    device unsigned or NULL; bit 1 set on nonfinite input
+ *                 (the reference throws "BF8L activations must be finite").
+ * k: multiple of 256 up to 8192; n: multiple of 64; buffers 16-byte aligned. */
+int tsac_cuda_qlinear(const int8_t* weights, const float* weight_scales, const float* bias,
+                      size_t k, size_t n, const uint16_t* x, size_t m, const uint16_t* residual,
+                      uint16_t* y, void* scratch, size_t scratch_bytes, unsigned* error_word,
+                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -440,3 +440,63 @@ int ref_snake(const float* input, std::size_t channels, std::size_t frames, cons
         });
 }
 }
+
+extern "C"
+{
+// pack_normal with the reference CpuTransformer predictor for known tokens
+// [frame][group][book] (src/format/entropy.cpp:57-123).  Also returns, when
+// `row_crc` is non-null, one CRC-32 per symbol (token-offset order) of the
+// 4096 bytes of that symbol's float probabilities.
+int ref_pack_normal(const char* package, unsigned channels, unsigned groups, unsigned books,
+                    std::size_t frames, unsigned batch, const std::uint16_t* tokens,
+                    std::uint8_t** out, std::size_t* out_bytes, std::uint32_t* row_crc)
+{
+    return guarded(
+        [&]
+        {
+            tsac::Header header;
+            header.method = 1;
+            header.model_channels = static_cast<std::uint8_t>(channels);
+            header.groups = static_cast<std::uint8_t>(groups);
+            header.codebooks = static_cast<std::uint8_t>(books);
+            header.frames = frames;
+            header.batch = static_cast<std::uint16_t>(batch);
+            auto transformer = tsac::scalar::CpuTransformer::from_model(tsac::TransformerModel(
+                tsac::ModelDirectory(package),
+                channels == 1 ? tsac::ModelVariant::mono : tsac::ModelVariant::stereo, books));
+            tsac::TransformerPredictor inner(transformer);
+            struct Recording final : tsac::TokenPredictor
+            {
+                tsac::TokenPredictor& base;
+                std::uint32_t* crc;
+                explicit Recording(tsac::TokenPredictor& b, std::uint32_t* c) : base(b), crc(c) {}
+                void reset(const tsac::Header& h) override { base.reset(h); }
+                std::span<const float> predict(const tsac::EntropyPosition& p) override
+                {
+                    const auto probs = base.predict(p);
+                    if (crc)
+                    {
+                        std::uint32_t c = 0xffffffffu;
+                        const auto* bytes = reinterpret_cast<const std::uint8_t*>(probs.data());
+                        for (std::size_t i = 0; i < probs.size() * 4; ++i)
+                        {
+                            c ^= bytes[i];
+                            for (int k = 0; k < 8; ++k)
+                                c = (c >> 1) ^ (0xedb88320u & (0u - (c & 1u)));
+                        }
+                        crc[p.token_offset] = ~c;
+                    }
+                    return probs;
+                }
+                void commit(const tsac::EntropyPosition& p, std::uint16_t t) override
+                {
+                    base.commit(p, t);
+                }
+            } predictor(inner, row_crc);
+            const auto bytes = tsac::pack_normal(
+                header, std::span<const std::uint16_t>(tokens, header.symbol_count()), predictor);
+            *out = copy_out(bytes);
+            *out_bytes = bytes.size();
+        });
+}
+}

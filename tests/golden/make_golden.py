@@ -8,6 +8,7 @@ sources exist; the fixtures then travel with the repository.
 
     python tests/golden/make_golden.py --cases short
     python tests/golden/make_golden.py --cases cfg0_stereo_30s
+    python tests/golden/make_golden.py --cases known
 """
 from __future__ import annotations
 
@@ -42,6 +43,48 @@ CASES = {
     "cfg0_stereo_30s": (0, 30.0, 2, 1, 12, 0, 3),
 }
 SHORT = [k for k in CASES if k != "cfg0_stereo_30s"]
+# Known-token Transformer + range coder cases, the header shapes of the
+# reference's Metal known-token test (tests/metal_optimized.cpp:252-270):
+# name: (frames, batch, groups, channels, books); tokens (i*73 + 19) % 1024.
+KNOWN = {
+    "known_17_8_16": (17, 8, 16, 2, 12),
+    "known_101_3_1": (101, 3, 1, 2, 12),
+    "known_51_3_1": (51, 3, 1, 2, 12),
+    "known_35_3_2": (35, 3, 2, 2, 12),
+    "known_17_1_1": (17, 1, 1, 2, 12),
+    "known_3_8_2": (3, 8, 2, 2, 12),
+    "known_1026_1_1": (1026, 1, 1, 2, 1),
+    "known_mono_40_2_1": (40, 2, 1, 1, 9),
+}
+
+
+def known_tokens(frames, groups, books):
+    i = np.arange(frames * groups * books, dtype=np.int64)
+    return ((i * 73 + 19) % 1024).astype(np.uint16)
+
+
+def run_known(name: str, package: pathlib.Path) -> dict:
+    frames, batch, groups, channels, books = KNOWN[name]
+    lib = ref_library()
+    tokens = known_tokens(frames, groups, books)
+    crc = np.zeros(tokens.size, np.uint32)
+    out = ctypes.POINTER(ctypes.c_uint8)()
+    nbytes = ctypes.c_size_t()
+    t0 = time.time()
+    ref_check(lib, lib.ref_pack_normal(str(package).encode(), channels, groups, books,
+                                       ctypes.c_size_t(frames), batch,
+                                       tokens.ctypes.data_as(ctypes.c_void_p), ctypes.byref(out),
+                                       ctypes.byref(nbytes), crc.ctypes.data_as(ctypes.c_void_p)))
+    stream = bytes(out[: nbytes.value])
+    lib.ref_free(out)
+    record = {"case": name, "frames": frames, "batch": batch, "groups": groups,
+              "channels": channels, "books": books, "tokens": "(i*73+19)%1024",
+              "weights_seed": 0, "stream_bytes": len(stream), "stream_sha256": sha(stream),
+              "probability_row_crc32": [int(c) for c in crc],
+              "reference_seconds": round(time.time() - t0, 3)}
+    (HERE / f"{name}.tsac").write_bytes(stream)
+    (HERE / f"{name}.json").write_text(json.dumps(record) + "\n")
+    return record
 
 
 def ref_library() -> ctypes.CDLL:
@@ -112,10 +155,15 @@ def main() -> None:
     parser.add_argument("--cases", default="short",
                         help="'short', 'all' or a comma-separated list of case names")
     args = parser.parse_args()
-    names = SHORT if args.cases == "short" else list(CASES) if args.cases == "all" \
-        else args.cases.split(",")
+    names = SHORT if args.cases == "short" else list(KNOWN) if args.cases == "known" \
+        else list(CASES) + list(KNOWN) if args.cases == "all" else args.cases.split(",")
     package = tsac_cuda.seeded_package(0)
     for name in names:
+        if name in KNOWN:
+            r = run_known(name, package)
+            print(name, r["stream_bytes"], r["stream_sha256"][:16], r["reference_seconds"],
+                  flush=True)
+            continue
         r = run_case(name, package)
         print(name, r["stream_bytes"], r["stream_sha256"][:16],
               r["reference_encode_seconds"], r["reference_decode_seconds"], flush=True)

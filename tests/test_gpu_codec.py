@@ -1,0 +1,103 @@
+"""Whole-codec parity: CudaAnalyzer vs the reference ScalarAnalyzer.
+
+Golden streams/PCM hashes come from the reference scalar path on the seeded
+package (tests/golden/make_golden.py).  Streams must be byte-identical; decoded
+PCM is compared bit-exactly (the synthesis kernels keep the reference's
+operation order), and every stream must decode on either side.  The failure
+cases follow tests/audio_analyzer.cpp:307-425 of the reference.
+"""
+import hashlib
+import json
+
+import numpy as np
+import pytest
+
+from support import GOLDEN
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import synthetic  # noqa: E402
+import tsac_cuda  # noqa: E402
+
+CASES = sorted(p.stem for p in GOLDEN.glob("*.json")
+               if not p.stem.startswith("known_") and p.stem != "cfg0_stereo_30s")
+
+
+@pytest.fixture(scope="module")
+def analyzer():
+    a = tsac_cuda.CudaAnalyzer(tsac_cuda.seeded_package(0), 0)
+    yield a
+    a.close()
+
+
+def _golden(case):
+    return json.loads((GOLDEN / f"{case}.json").read_text())
+
+
+def _options(g):
+    return tsac_cuda.EncodeOptions(method="normal" if g["method"] == 1 else "fast",
+                                   codebooks=g["codebooks"], separate_channels=bool(g["separate"]),
+                                   entropy_batch=g["batch"] or None)
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_encode_stream_byte_identical(analyzer, case):
+    g = _golden(case)
+    pcm = synthetic.music_like(g["pcm_seed"], g["seconds"], g["channels"])
+    stream = analyzer.encode(pcm, _options(g))
+    assert len(stream) == g["stream_bytes"]
+    assert hashlib.sha256(stream).hexdigest() == g["stream_sha256"]
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_decode_reference_stream_bit_exact(analyzer, case):
+    g = _golden(case)
+    stream = (GOLDEN / f"{case}.tsac").read_bytes()
+    audio = analyzer.decode(stream)
+    assert audio.channels == g["pcm_channels"] and audio.samples.size == g["pcm_samples"]
+    head = np.array(g["pcm_head"], np.float32)
+    flat = audio.samples.ravel()
+    assert np.array_equal(flat[: head.size].view(np.uint32), head.view(np.uint32)), \
+        f"max |d| {np.abs(flat[:head.size] - head).max()}"
+    assert hashlib.sha256(flat.astype("<f4").tobytes()).hexdigest() == g["pcm_sha256"]
+
+
+def test_batch_equals_single(analyzer):
+    cases = [c for c in CASES if _golden(c)["seconds"] >= 0.05][:4]
+    pcms = [synthetic.music_like(_golden(c)["pcm_seed"], _golden(c)["seconds"], _golden(c)["channels"])
+            for c in cases]
+    opts = tsac_cuda.EncodeOptions()
+    single = [analyzer.encode(p, opts) for p in pcms]
+    assert analyzer.encode_batch(pcms, opts) == single
+    decoded = analyzer.decode_batch(single)
+    for s, d in zip(single, decoded):
+        one = analyzer.decode(s)
+        assert np.array_equal(one.samples, d.samples)
+
+
+def test_strided_views_give_identical_streams(analyzer):
+    pcm = synthetic.music_like(31, 0.2, 2)
+    planar = np.ascontiguousarray(pcm.T).T  # channel-major memory, same values
+    assert analyzer.encode(pcm) == analyzer.encode(planar)
+
+
+def test_failures_are_errors_and_analyzer_is_reusable(analyzer):
+    pcm = synthetic.music_like(32, 0.05, 2)
+    bad = pcm.copy()
+    bad[10, 1] = np.nan
+    with pytest.raises(tsac_cuda.TsacError, match="nonfinite PCM"):
+        analyzer.encode(bad)
+    with pytest.raises(tsac_cuda.TsacError, match="codebooks"):
+        analyzer.encode(pcm, tsac_cuda.EncodeOptions(codebooks=13))
+    with pytest.raises(tsac_cuda.TsacError, match="normal coding"):
+        analyzer.encode(pcm, tsac_cuda.EncodeOptions(method="fast", entropy_batch=2))
+    with pytest.raises(tsac_cuda.TsacError):
+        analyzer.decode(b"")
+    stream = bytearray(analyzer.encode(pcm))
+    stream[-1] ^= 1  # corrupt the token CRC
+    with pytest.raises(tsac_cuda.TsacError, match="CRC"):
+        analyzer.decode(bytes(stream))
+    # Reuse after failures.
+    good = analyzer.encode(pcm)
+    assert analyzer.decode(good).samples.shape == (512 * 5, 2)

@@ -1,0 +1,500 @@
+#include "codec.hpp"
+
+#include "dac_engine.hpp"
+
+#include <algorithm>
+#include <future>
+#include <thread>
+
+namespace tsacb
+{
+namespace
+{
+struct Chunk // detail::AudioChunk (src/common/audio_analyzer.cpp:154-162)
+{
+    std::size_t begin, count, left, right;
+};
+
+Chunk audio_chunk(std::size_t begin, std::size_t frames, std::size_t size, std::size_t lc,
+                  std::size_t rc)
+{
+    require(size > 0 && begin < frames, "invalid audio chunk");
+    const auto count = std::min(size, frames - begin);
+    const auto end = begin + count;
+    return {begin, count, begin > lc ? begin - lc : 0, end + std::min(rc, frames - end)};
+}
+
+std::size_t audio_chunk_frames(std::size_t target, const Limits& limits)
+{
+    const auto available = limits.tensor_elements / (std::size_t{96} * 512);
+    return std::min(target, available > 22 ? available - 22 : std::size_t{1});
+}
+
+// Windows per DAC launch group (bounds device memory; ~250 MB per window).
+constexpr std::size_t window_group = 48;
+
+template <class F> void parallel_for(std::size_t n, F&& f)
+{
+    const std::size_t workers = std::max<std::size_t>(1, std::min<std::size_t>(n, std::thread::hardware_concurrency()));
+    if (workers <= 1)
+    {
+        for (std::size_t i = 0; i < n; ++i)
+            f(i);
+        return;
+    }
+    std::vector<std::future<void>> jobs;
+    std::atomic<std::size_t> next{0};
+    for (std::size_t w = 0; w < workers; ++w)
+    {
+        jobs.push_back(std::async(std::launch::async,
+                                  [&]
+                                  {
+                                      for (std::size_t i; (i = next++) < n;)
+                                          f(i);
+                                  }));
+    }
+    for (auto& j : jobs)
+        j.get();
+}
+} // namespace
+
+Header audio_header(const PcmInput& pcm, const EncodeOptions& options, const Limits& limits)
+{
+    const auto channels = pcm.channels, samples = pcm.samples;
+    require(channels > 0 && channels <= 127, "invalid PCM channel count");
+    require(pcm.channel_stride > 0 && pcm.sample_stride > 0, "invalid PCM strides");
+    require(samples == 0 || pcm.data != nullptr, "null PCM data");
+    require(checked_mul(samples, channels) <= limits.tensor_elements, "PCM exceeds element limit");
+    require(options.method == 0 || options.method == 1, "invalid coding method");
+    Header header;
+    header.method = static_cast<std::uint8_t>(options.method);
+    header.model_channels = channels == 2 && !options.separate_channels ? 2 : 1;
+    header.groups = static_cast<std::uint8_t>(channels / header.model_channels);
+    const unsigned maximum = header.model_channels == 2 ? 12 : 9;
+    require(options.codebooks <= maximum, "invalid number of codebooks for audio model");
+    header.codebooks = static_cast<std::uint8_t>(options.codebooks ? options.codebooks : maximum);
+    header.frames = checked_add(samples, 511) / 512;
+    require(options.entropy_batch >= 0, "zero entropy batch size");
+    require(header.method == 1 || options.entropy_batch == 0, "entropy batch requires normal coding");
+    if (header.method == 1)
+    {
+        header.batch = select_entropy_batch(header.frames, options.entropy_batch);
+    }
+    validate_header(header, limits);
+    require(checked_mul(header.samples_per_channel(), channels) <= limits.tensor_elements,
+            "padded PCM exceeds element limit");
+    return header;
+}
+
+namespace
+{
+// detail::padded_audio: [group][sample][model channel], zero padded.
+std::vector<float> padded_audio(const PcmInput& pcm, const Header& header)
+{
+    const std::size_t mc = header.model_channels, spc = header.samples_per_channel();
+    std::vector<float> out(header.groups * spc * mc, 0.0f);
+    for (std::size_t g = 0; g < header.groups; ++g)
+        for (std::size_t f = 0; f < pcm.samples; ++f)
+            for (std::size_t c = 0; c < mc; ++c)
+            {
+                const float v = pcm.data[static_cast<std::ptrdiff_t>(g * mc + c) * pcm.channel_stride +
+                                         static_cast<std::ptrdiff_t>(f) * pcm.sample_stride];
+                require(std::isfinite(v), "nonfinite PCM sample");
+                out[(g * spc + f) * mc + c] = v;
+            }
+    return out;
+}
+
+struct AnalysisWindow
+{
+    std::size_t recording, group;
+    Chunk chunk;
+};
+
+// DAC analysis + RVQ for every recording of one model variant.
+void analyze_recordings(Context& ctx, const std::vector<const std::vector<float>*>& padded,
+                        const std::vector<Header>& headers,
+                        std::vector<std::vector<std::uint16_t>>& tokens)
+{
+    if (headers.empty())
+        return;
+    const unsigned mc = headers[0].model_channels;
+    auto& dac = ctx.analysis(mc);
+    auto& rvq = ctx.rvq(mc);
+    const auto chunk_frames = audio_chunk_frames(400, ctx.limits());
+    std::vector<AnalysisWindow> windows;
+    for (std::size_t r = 0; r < headers.size(); ++r)
+    {
+        tokens[r].assign(headers[r].symbol_count(), 0);
+        for (std::size_t g = 0; g < headers[r].groups; ++g)
+            for (std::size_t b = 0; b < headers[r].frames;)
+            {
+                const auto c = audio_chunk(b, headers[r].frames, chunk_frames, 8, 9);
+                windows.push_back({r, g, c});
+                b += c.count;
+            }
+    }
+    auto s = ctx.stream();
+    for (std::size_t w0 = 0; w0 < windows.size(); w0 += window_group)
+    {
+        const auto wn = std::min(window_group, windows.size() - w0);
+        std::vector<int> frames;
+        std::size_t samples = 0, latent_frames = 0, central = 0;
+        for (std::size_t i = 0; i < wn; ++i)
+        {
+            const auto& c = windows[w0 + i].chunk;
+            frames.push_back(static_cast<int>(c.right - c.left));
+            samples += (c.right - c.left) * 512;
+            latent_frames += c.right - c.left;
+            central += c.count;
+        }
+        std::vector<float> host_pcm(samples * mc);
+        std::size_t at = 0;
+        for (std::size_t i = 0; i < wn; ++i)
+        {
+            const auto& w = windows[w0 + i];
+            const auto& h = headers[w.recording];
+            const auto spc = h.samples_per_channel();
+            const auto n = (w.chunk.right - w.chunk.left) * 512 * mc;
+            std::copy_n(padded[w.recording]->data() + (w.group * spc + w.chunk.left * 512) * mc, n,
+                        host_pcm.data() + at);
+            at += n;
+        }
+        DeviceBuffer d_pcm(host_pcm.size() * 4), d_latent(latent_frames * 1024 * 4),
+            d_central(central * 1024 * 4);
+        cuda_ok(cudaMemcpyAsync(d_pcm.as<void>(), host_pcm.data(), host_pcm.size() * 4,
+                                cudaMemcpyHostToDevice, s),
+                "H2D");
+        dac.analyze(d_pcm.as<float>(), frames, d_latent.as<float>());
+        // Keep each window's central latents (src/common/audio_pipeline.hpp:49-56).
+        std::size_t lat = 0, cen = 0;
+        for (std::size_t i = 0; i < wn; ++i)
+        {
+            const auto& c = windows[w0 + i].chunk;
+            cuda_ok(cudaMemcpyAsync(d_central.as<float>() + cen * 1024,
+                                    d_latent.as<float>() + (lat + c.begin - c.left) * 1024,
+                                    c.count * 1024 * 4, cudaMemcpyDeviceToDevice, s),
+                    "D2D");
+            lat += c.right - c.left;
+            cen += c.count;
+        }
+        const int books = headers[0].codebooks;
+        DeviceBuffer d_tok(central * static_cast<std::size_t>(books) * 2);
+        rvq.encode(d_central.as<float>(), static_cast<int>(central), books,
+                   d_tok.as<std::uint16_t>(), books);
+        std::vector<std::uint16_t> host_tok(central * static_cast<std::size_t>(books));
+        cuda_ok(cudaMemcpyAsync(host_tok.data(), d_tok.as<void>(), host_tok.size() * 2,
+                                cudaMemcpyDeviceToHost, s),
+                "D2H");
+        unsigned words[2] = {0, 0};
+        cuda_ok(cudaMemcpyAsync(&words[0], dac.error_word(), 4, cudaMemcpyDeviceToHost, s), "D2H");
+        cuda_ok(cudaMemcpyAsync(&words[1], rvq.error_word(), 4, cudaMemcpyDeviceToHost, s), "D2H");
+        cuda_ok(cudaStreamSynchronize(s), "analysis");
+        if (words[0] || words[1])
+        {
+            cuda_ok(cudaMemsetAsync(dac.error_word(), 0, 4, s), "memset");
+            cuda_ok(cudaMemsetAsync(rvq.error_word(), 0, 4, s), "memset");
+            throw NumericError(words[0] ? "nonfinite DSP value" : "nonfinite RVQ residual");
+        }
+        // store_tokens (src/common/audio_analyzer.cpp:164-172).
+        cen = 0;
+        for (std::size_t i = 0; i < wn; ++i)
+        {
+            const auto& w = windows[w0 + i];
+            const auto& h = headers[w.recording];
+            for (std::size_t f = 0; f < w.chunk.count; ++f)
+                std::copy_n(host_tok.data() + (cen + f) * books, books,
+                            tokens[w.recording].data() +
+                                ((w.chunk.begin + f) * h.groups + w.group) * h.codebooks);
+            cen += w.chunk.count;
+        }
+    }
+}
+} // namespace
+
+std::vector<std::uint16_t> analyze_tokens(Context& ctx, const PcmInput& pcm,
+                                          const EncodeOptions& options, Header* header_out)
+{
+    ctx.bind();
+    const auto header = audio_header(pcm, options, ctx.limits());
+    const auto padded = padded_audio(pcm, header);
+    std::vector<std::vector<std::uint16_t>> tokens(1);
+    analyze_recordings(ctx, {&padded}, {header}, tokens);
+    if (header_out)
+        *header_out = header;
+    return std::move(tokens[0]);
+}
+
+namespace
+{
+Bytes range_code(const Header& h, std::span<const std::uint16_t> tok, const std::uint16_t* q,
+                 const Limits& limits, std::size_t* bits)
+{
+    require(limits.file_bytes >= 19, "normal framing exceeds file limit");
+    RangeEncoder encoder(limits.file_bytes - 18);
+    visit_entropy_positions(h,
+                            [&](const EntropyPosition& p)
+                            {
+                                const unsigned token = tok[p.token_offset];
+                                const auto* path = q + p.token_offset * 10;
+                                for (int d = 0; d < 10; ++d)
+                                    encoder.put(path[d], (token >> (9 - d)) & 1u);
+                            });
+    if (bits)
+        *bits = encoder.bit_position();
+    const auto payload = encoder.finish();
+    return frame_normal(h, payload);
+}
+} // namespace
+
+Bytes pack_normal(Context& ctx, Header header, std::span<const std::uint16_t> tokens,
+                  std::size_t* bits)
+{
+    ctx.bind();
+    header.method = 1;
+    validate_header(header, ctx.limits());
+    require(header.frames <= 0xffffffffu, "normal frame count exceeds uint32");
+    require(tokens.size() == header.symbol_count(), "normal token count does not match header");
+    header.token_crc = token_crc32(tokens);
+    std::vector<std::uint16_t> q(header.symbol_count() * 10);
+    ctx.transformer(header.model_channels).predict_known(header, tokens, q.data(), nullptr);
+    return range_code(header, tokens, q.data(), ctx.limits(), bits);
+}
+
+std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
+                                const EncodeOptions& options, std::vector<std::size_t>* bits)
+{
+    ctx.bind();
+    const auto n = pcm.size();
+    std::vector<Header> headers(n);
+    std::vector<std::vector<float>> padded(n);
+    for (std::size_t i = 0; i < n; ++i)
+    {
+        headers[i] = audio_header(pcm[i], options, ctx.limits());
+        padded[i] = padded_audio(pcm[i], headers[i]);
+    }
+    std::vector<std::vector<std::uint16_t>> tokens(n);
+    for (unsigned mc : {1u, 2u})
+    {
+        std::vector<std::size_t> ids;
+        std::vector<const std::vector<float>*> p;
+        std::vector<Header> h;
+        for (std::size_t i = 0; i < n; ++i)
+            if (headers[i].model_channels == mc)
+            {
+                ids.push_back(i);
+                p.push_back(&padded[i]);
+                h.push_back(headers[i]);
+            }
+        std::vector<std::vector<std::uint16_t>> t(ids.size());
+        analyze_recordings(ctx, p, h, t);
+        for (std::size_t j = 0; j < ids.size(); ++j)
+            tokens[ids[j]] = std::move(t[j]);
+    }
+    std::vector<Bytes> out(n);
+    if (bits)
+        bits->assign(n, 0);
+    std::vector<std::vector<std::uint16_t>> q15(n);
+    for (std::size_t i = 0; i < n; ++i)
+    {
+        if (headers[i].method == 0)
+        {
+            out[i] = pack_fast(headers[i], tokens[i], ctx.limits());
+            continue;
+        }
+        headers[i].token_crc = token_crc32(tokens[i]);
+        q15[i].resize(headers[i].symbol_count() * 10);
+        ctx.transformer(headers[i].model_channels)
+            .predict_known(headers[i], tokens[i], q15[i].data(), nullptr);
+    }
+    // Sequential range coding per recording on host cores (pack_normal,
+    // src/format/entropy.cpp:57-123), recordings in parallel.
+    parallel_for(n,
+                 [&](std::size_t i)
+                 {
+                     if (headers[i].method == 0)
+                         return;
+                     out[i] = range_code(headers[i], tokens[i], q15[i].data(), ctx.limits(),
+                                         bits ? &(*bits)[i] : nullptr);
+                 });
+    return out;
+}
+
+std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>& streams)
+{
+    ctx.bind();
+    const auto n = streams.size();
+    std::vector<Header> headers(n);
+    std::vector<std::vector<std::uint16_t>> tokens(n);
+    for (std::size_t i = 0; i < n; ++i)
+    {
+        headers[i] = parse_header(streams[i], ctx.limits());
+        if (headers[i].method == 0)
+            tokens[i] = unpack_fast(streams[i], ctx.limits());
+        else
+            tokens[i].assign(headers[i].symbol_count(), 0);
+    }
+    // Normal streams: GPU predictor + host range decoders, one variant at a time.
+    for (unsigned mc : {1u, 2u})
+    {
+        std::vector<std::size_t> ids;
+        std::vector<Header> hs;
+        for (std::size_t i = 0; i < n; ++i)
+            if (headers[i].method == 1 && headers[i].model_channels == mc)
+            {
+                ids.push_back(i);
+                hs.push_back(headers[i]);
+            }
+        if (ids.empty())
+            continue;
+        auto& engine = ctx.transformer(mc);
+        engine.decode_begin(hs);
+        std::vector<RangeDecoder> decoders;
+        std::size_t steps = 0, books = 0, lanes = 0;
+        for (auto i : ids)
+        {
+            const auto& h = headers[i];
+            decoders.emplace_back(streams[i].subspan(h.payload_offset, h.payload_bytes));
+            steps = std::max(steps, h.frames / h.batch + (h.frames % h.batch != 0));
+            books = std::max<std::size_t>(books, h.codebooks);
+            lanes += h.lanes();
+        }
+        std::vector<float> masses(lanes * 1023);
+        for (std::size_t step = 0; step < steps; ++step)
+            for (std::size_t book = 0; book < books; ++book)
+            {
+                const auto rows = engine.decode_predict(step, book, masses.data());
+                std::vector<std::uint16_t> decoded(rows.size());
+                // Rows are ordered recording, lane, group = stream order per recording.
+                std::vector<std::size_t> first(ids.size() + 1, rows.size());
+                for (std::size_t j = rows.size(); j-- > 0;)
+                    first[static_cast<std::size_t>(rows[j].recording)] = j;
+                parallel_for(ids.size(),
+                             [&](std::size_t r)
+                             {
+                                 for (std::size_t j = first[r];
+                                      j < rows.size() && static_cast<std::size_t>(rows[j].recording) == r; ++j)
+                                 {
+                                     decoded[j] = decode_categorical_tree(decoders[r], masses.data() + j * 1023);
+                                 }
+                             });
+                for (std::size_t j = 0; j < rows.size(); ++j)
+                {
+                    const auto r = static_cast<std::size_t>(rows[j].recording);
+                    const auto& h = headers[ids[r]];
+                    const std::size_t lane_b = static_cast<std::size_t>(rows[j].lane) / h.groups;
+                    const std::size_t g = static_cast<std::size_t>(rows[j].lane) % h.groups;
+                    const std::size_t base = h.frames / h.batch, extra = h.frames % h.batch;
+                    const std::size_t frame = lane_b * base + std::min(lane_b, extra) + step;
+                    tokens[ids[r]][(frame * h.groups + g) * h.codebooks + book] = decoded[j];
+                }
+                engine.decode_commit(decoded);
+            }
+        for (auto i : ids)
+            verify_token_crc(headers[i], tokens[i]);
+    }
+    // RVQ reconstruction + DAC synthesis over chunk windows
+    // (src/common/audio_pipeline.hpp:63-83, context 11/11).
+    std::vector<DecodedAudio> out(n);
+    for (std::size_t i = 0; i < n; ++i)
+    {
+        out[i].channels = static_cast<unsigned>(headers[i].channels());
+        out[i].samples.assign(headers[i].channels() * headers[i].samples_per_channel(), 0.0f);
+    }
+    auto s = ctx.stream();
+    const auto chunk_frames = audio_chunk_frames(400, ctx.limits());
+    for (unsigned mc : {1u, 2u})
+    {
+        std::vector<AnalysisWindow> windows;
+        for (std::size_t i = 0; i < n; ++i)
+        {
+            if (headers[i].model_channels != mc)
+                continue;
+            for (std::size_t g = 0; g < headers[i].groups; ++g)
+                for (std::size_t b = 0; b < headers[i].frames;)
+                {
+                    const auto c = audio_chunk(b, headers[i].frames, chunk_frames, 11, 11);
+                    windows.push_back({i, g, c});
+                    b += c.count;
+                }
+        }
+        if (windows.empty())
+            continue;
+        auto& rvq = ctx.rvq(mc);
+        auto& dac = ctx.synthesis(mc);
+        for (std::size_t w0 = 0; w0 < windows.size(); w0 += window_group)
+        {
+            const auto wn = std::min(window_group, windows.size() - w0);
+            std::vector<int> frames;
+            std::size_t total = 0;
+            int books = 0;
+            for (std::size_t i = 0; i < wn; ++i)
+            {
+                const auto& c = windows[w0 + i].chunk;
+                frames.push_back(static_cast<int>(c.right - c.left));
+                total += c.right - c.left;
+                books = std::max<int>(books, headers[windows[w0 + i].recording].codebooks);
+            }
+            // Window tokens [frame][books] (chunk_tokens, src/common/audio_analyzer.cpp:174-183).
+            std::vector<std::uint16_t> wt(total * static_cast<std::size_t>(books), 0);
+            std::vector<int> wbooks;
+            std::size_t at = 0;
+            for (std::size_t i = 0; i < wn; ++i)
+            {
+                const auto& w = windows[w0 + i];
+                const auto& h = headers[w.recording];
+                for (std::size_t f = w.chunk.left; f < w.chunk.right; ++f, ++at)
+                    std::copy_n(tokens[w.recording].data() + (f * h.groups + w.group) * h.codebooks,
+                                h.codebooks, wt.data() + at * books);
+            }
+            DeviceBuffer d_tok(wt.size() * 2), d_latent(total * 1024 * 4),
+                d_pcm(total * 512 * mc * 4);
+            cuda_ok(cudaMemcpyAsync(d_tok.as<void>(), wt.data(), wt.size() * 2,
+                                    cudaMemcpyHostToDevice, s),
+                    "H2D");
+            // Windows of one group share the recording's book count (one variant per launch).
+            bool uniform = true;
+            for (std::size_t i = 1; i < wn; ++i)
+                uniform = uniform && headers[windows[w0 + i].recording].codebooks == books;
+            if (uniform)
+            {
+                rvq.decode(d_tok.as<std::uint16_t>(), books, static_cast<int>(total), books,
+                           d_latent.as<float>());
+            }
+            else
+            {
+                std::size_t off = 0;
+                for (std::size_t i = 0; i < wn; ++i)
+                {
+                    const auto& w = windows[w0 + i];
+                    const auto len = w.chunk.right - w.chunk.left;
+                    rvq.decode(d_tok.as<std::uint16_t>() + off * books, books, static_cast<int>(len),
+                               headers[w.recording].codebooks, d_latent.as<float>() + off * 1024);
+                    off += len;
+                }
+            }
+            dac.synthesize(d_latent.as<float>(), frames, d_pcm.as<float>());
+            std::vector<float> host_pcm(total * 512 * mc);
+            cuda_ok(cudaMemcpyAsync(host_pcm.data(), d_pcm.as<void>(), host_pcm.size() * 4,
+                                    cudaMemcpyDeviceToHost, s),
+                    "D2H");
+            dac.check_errors("synthesis");
+            // store_pcm (src/common/audio_analyzer.cpp:185-199).
+            std::size_t off = 0;
+            for (std::size_t i = 0; i < wn; ++i)
+            {
+                const auto& w = windows[w0 + i];
+                const auto& h = headers[w.recording];
+                auto& o = out[w.recording];
+                for (std::size_t sample = 0; sample < w.chunk.count * 512; ++sample)
+                    for (std::size_t c = 0; c < mc; ++c)
+                        o.samples[(w.chunk.begin * 512 + sample) * o.channels + w.group * mc + c] =
+                            host_pcm[(off + (w.chunk.begin - w.chunk.left) * 512 + sample) * mc + c];
+                off += (w.chunk.right - w.chunk.left) * 512;
+                (void)h;
+            }
+        }
+    }
+    return out;
+}
+} // namespace tsacb

@@ -1,0 +1,96 @@
+#include "context.hpp"
+
+#include "dac_engine.hpp"
+#include "kernels/qlinear.cuh"
+
+namespace tsacb
+{
+namespace
+{
+void ensure_device(int device)
+{
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0)
+    {
+        throw DeviceError("no CUDA device available (this library has no CPU fallback)");
+    }
+    require(device >= 0 && device < count, "CUDA device index out of range");
+}
+} // namespace
+
+Context::Context(const std::string& package, int device, const Limits& limits)
+    : package_(package, limits), device_(device), limits_(limits)
+{
+    ensure_device(device);
+    cuda_ok(cudaSetDevice(device), "cudaSetDevice");
+    cuda_ok(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+    dev::qlinear_init();
+}
+
+Context::~Context()
+{
+    cudaSetDevice(device_);
+    for (auto& e : engines_)
+        e.reset();
+    for (auto& a : analysis_)
+        a.reset();
+    for (auto& s : synthesis_)
+        s.reset();
+    for (auto& r : rvq_)
+        r.reset();
+    for (auto& t : transformers_)
+        t.reset();
+    if (stream_)
+    {
+        cudaStreamSynchronize(stream_);
+        cudaStreamDestroy(stream_);
+    }
+}
+
+void Context::bind() const
+{
+    cuda_ok(cudaSetDevice(device_), "cudaSetDevice");
+}
+
+TransformerEngine& Context::transformer(unsigned channels)
+{
+    require(channels == 1 || channels == 2, "invalid model variant");
+    auto& e = engines_[channels - 1];
+    if (!e)
+    {
+        const unsigned books = channels == 1 ? 9 : 12;
+        transformers_[channels - 1] = std::make_shared<DeviceTransformer>(
+            prepare_transformer(package_, channels, books), stream_);
+        e = std::make_unique<TransformerEngine>(transformers_[channels - 1], stream_);
+    }
+    return *e;
+}
+
+DacEngine& Context::analysis(unsigned channels)
+{
+    require(channels == 1 || channels == 2, "invalid model variant");
+    auto& e = analysis_[channels - 1];
+    if (!e)
+        e = std::make_unique<DacEngine>(prepare_dac(package_, channels, false, limits_), stream_);
+    return *e;
+}
+
+DacEngine& Context::synthesis(unsigned channels)
+{
+    require(channels == 1 || channels == 2, "invalid model variant");
+    auto& e = synthesis_[channels - 1];
+    if (!e)
+        e = std::make_unique<DacEngine>(prepare_dac(package_, channels, true, limits_), stream_);
+    return *e;
+}
+
+RvqEngine& Context::rvq(unsigned channels)
+{
+    require(channels == 1 || channels == 2, "invalid model variant");
+    auto& e = rvq_[channels - 1];
+    if (!e)
+        e = std::make_unique<RvqEngine>(prepare_rvq(package_, channels, channels == 1 ? 9 : 12),
+                                        stream_);
+    return *e;
+}
+} // namespace tsacb

@@ -1,0 +1,53 @@
+// One analyzer instance: a model package bound to one CUDA device and stream.
+// Mirrors the reference analyzers' ownership (ModelDirectory + Limits,
+// include/tsac/scalar_analyzer.hpp:8-19): prepared device models are created
+// on first use per variant and reused by later calls on the same context.
+#pragma once
+#include "models.hpp"
+#include "transformer_engine.hpp"
+
+#include <memory>
+#include <mutex>
+
+namespace tsacb
+{
+class DacEngine;
+class RvqEngine;
+
+class Context
+{
+public:
+    Context(const std::string& package, int device, const Limits& limits);
+    ~Context();
+    Context(const Context&) = delete;
+    Context& operator=(const Context&) = delete;
+
+    const Limits& limits() const
+    {
+        return limits_;
+    }
+    cudaStream_t stream() const
+    {
+        return stream_;
+    }
+    void bind() const; // makes the context's device current on this thread
+    TransformerEngine& transformer(unsigned channels);
+    DacEngine& analysis(unsigned channels);
+    DacEngine& synthesis(unsigned channels);
+    RvqEngine& rvq(unsigned channels);
+    const Package& package() const
+    {
+        return package_;
+    }
+
+private:
+    Package package_;
+    int device_;
+    Limits limits_;
+    cudaStream_t stream_ = nullptr;
+    std::shared_ptr<DeviceTransformer> transformers_[2];
+    std::unique_ptr<TransformerEngine> engines_[2];
+    std::unique_ptr<DacEngine> analysis_[2], synthesis_[2];
+    std::unique_ptr<RvqEngine> rvq_[2];
+};
+} // namespace tsacb

@@ -1,0 +1,267 @@
+#include "dac_engine.hpp"
+
+#include <algorithm>
+#include <array>
+
+namespace tsacb
+{
+namespace
+{
+// Reference folded weights -> device [tap][in][out] (layout only).
+std::vector<float> device_layout(const PreparedConv& c)
+{
+    const auto& s = c.spec;
+    const std::size_t cin = s.input_channels, cout = s.output_channels, k = s.kernel;
+    std::vector<float> out(c.weights.size());
+    for (std::size_t tap = 0; tap < k; ++tap)
+        for (std::size_t in = 0; in < cin; ++in)
+            for (std::size_t o = 0; o < cout; ++o)
+                out[(tap * cin + in) * cout + o] =
+                    s.transposed ? c.weights[o + tap * cout + in * cout * k]
+                                 : c.weights[in + tap * cin + o * cin * k];
+    return out;
+}
+
+// Output length of a convolution (src/common/dsp.tpp:141-156).
+int output_frames(const Conv1dSpec& s, int frames)
+{
+    const int span = (static_cast<int>(s.kernel) - 1) * static_cast<int>(s.dilation) + 1;
+    const int padding = 2 * static_cast<int>(s.padding);
+    if (!s.transposed)
+    {
+        require(frames + padding >= span, "convolution has no output frames");
+        return (frames + padding - span) / static_cast<int>(s.stride) + 1;
+    }
+    const int full = (frames - 1) * static_cast<int>(s.stride) + span;
+    require(full > padding, "transposed convolution has no output frames");
+    return full - padding;
+}
+} // namespace
+
+DacEngine::DacEngine(const PreparedDac& dac, cudaStream_t stream)
+    : synthesis_(dac.synthesis), channels_(dac.channels), stream_(stream), error_(sizeof(unsigned))
+{
+    for (const auto& c : dac.convs)
+    {
+        require(!c.spec.transposed || c.spec.dilation == 1, "transposed dilation unsupported");
+        DeviceConv d;
+        d.spec = c.spec;
+        d.weights = upload(device_layout(c), stream);
+        d.bias = upload(c.bias, stream);
+        convs_.push_back(std::move(d));
+    }
+    for (const auto& a : dac.alphas)
+    {
+        alphas_.push_back(upload(a, stream));
+        alpha_width_.push_back(static_cast<int>(a.size()));
+    }
+    cuda_ok(cudaMemsetAsync(error_.as<void>(), 0, sizeof(unsigned), stream), "memset");
+    cuda_ok(cudaStreamSynchronize(stream), "DAC weight upload");
+}
+
+void DacEngine::check_errors(const char* what)
+{
+    unsigned word = 0;
+    cuda_ok(cudaMemcpyAsync(&word, error_.as<void>(), 4, cudaMemcpyDeviceToHost, stream_), "D2H");
+    cuda_ok(cudaStreamSynchronize(stream_), what);
+    if (word)
+    {
+        cuda_ok(cudaMemsetAsync(error_.as<void>(), 0, 4, stream_), "memset");
+        throw NumericError(std::string("nonfinite DSP value (") + what + ")");
+    }
+}
+
+void DacEngine::snake(int index, const float* x, float* y, long long frames)
+{
+    dev::snake(x, alphas_[static_cast<std::size_t>(index)].as<float>(),
+               alpha_width_[static_cast<std::size_t>(index)], frames, y, error_word(), stream_);
+}
+
+void DacEngine::conv(int index, const float* x, float* y, const float* residual,
+                     const std::vector<int>& in_frames, std::vector<int>& out_frames)
+{
+    const auto& c = convs_[static_cast<std::size_t>(index)];
+    const auto& sp = c.spec;
+    dev::ConvShape shape{static_cast<int>(sp.input_channels), static_cast<int>(sp.output_channels),
+                         static_cast<int>(sp.kernel), static_cast<int>(sp.stride),
+                         static_cast<int>(sp.padding), static_cast<int>(sp.dilation),
+                         sp.transposed};
+    std::vector<dev::Sequence> seqs;
+    std::vector<int4> tiles;
+    out_frames.clear();
+    int in_off = 0, out_off = 0;
+    const int tf = dev::conv_tile_frames(shape);
+    for (std::size_t q = 0; q < in_frames.size(); ++q)
+    {
+        const int of = output_frames(sp, in_frames[q]);
+        seqs.push_back({in_off, in_frames[q], out_off, of});
+        out_frames.push_back(of);
+        if (sp.transposed)
+        {
+            for (int phase = 0; phase < shape.stride; ++phase)
+            {
+                const int count = of > phase ? (of - phase + shape.stride - 1) / shape.stride : 0;
+                for (int i0 = 0; i0 < count; i0 += tf)
+                    tiles.push_back({static_cast<int>(q), i0, phase, 0});
+            }
+        }
+        else
+        {
+            for (int f0 = 0; f0 < of; f0 += tf)
+                tiles.push_back({static_cast<int>(q), f0, 0, 0});
+        }
+        in_off += in_frames[q];
+        out_off += of;
+    }
+    const std::string key = "conv" + std::to_string(index);
+    auto* d_seq = ws_.get<dev::Sequence>(key + "s", seqs.size());
+    cuda_ok(cudaMemcpyAsync(d_seq, seqs.data(), seqs.size() * sizeof(dev::Sequence),
+                            cudaMemcpyHostToDevice, stream_),
+            "H2D");
+    if (shape.cout < 16)
+    {
+        dev::conv1d_narrow(x, c.weights.as<float>(), c.bias.as<float>(), y, d_seq,
+                           static_cast<int>(seqs.size()), shape,
+                           static_cast<long long>(out_off) * shape.cout, error_word(), stream_);
+        require(residual == nullptr, "narrow convolution has no residual input");
+        return;
+    }
+    auto* d_tiles = ws_.get<int4>(key + "t", tiles.size());
+    cuda_ok(cudaMemcpyAsync(d_tiles, tiles.data(), tiles.size() * sizeof(int4),
+                            cudaMemcpyHostToDevice, stream_),
+            "H2D");
+    dev::ConvLaunch l{error_word(), x, c.weights.as<float>(), c.bias.as<float>(), residual, y,
+                      d_seq, d_tiles, static_cast<int>(tiles.size()), shape};
+    dev::conv1d(l, stream_);
+}
+
+void DacEngine::analyze(const float* pcm, const std::vector<int>& frames, float* latent)
+{
+    require(!synthesis_, "analysis on a synthesis model");
+    std::vector<int> f0(frames.size()), f1;
+    long long total = 0;
+    for (std::size_t i = 0; i < frames.size(); ++i)
+    {
+        f0[i] = frames[i] * 512;
+        total += f0[i];
+    }
+    // Widest activation: 64 channels at full rate (= 512*64 per frame ... all
+    // stages hold frames*512*64/... floats; stage sizes shrink as width grows).
+    const std::size_t biggest = static_cast<std::size_t>(total) * 64;
+    auto* a = ws_.get<float>("a", biggest);
+    auto* t1 = ws_.get<float>("t1", biggest);
+    auto* t2 = ws_.get<float>("t2", biggest);
+    std::vector<int> cur = f0;
+    conv(0, pcm, a, nullptr, cur, f1);
+    cur = f1;
+    int width = 64;
+    for (int stage = 0; stage < 4; ++stage)
+    {
+        long long n = 0;
+        for (int v : cur)
+            n += v;
+        for (int unit = 0; unit < 3; ++unit)
+        {
+            const int base = 1 + stage * 7 + unit * 2; // convolution index
+            const int alpha = stage * 7 + unit * 2;    // activation index
+            snake(alpha, a, t1, n);
+            conv(base, t1, t2, nullptr, cur, f1);
+            snake(alpha + 1, t2, t1, n);
+            conv(base + 1, t1, a, a, cur, f1);
+        }
+        snake(stage * 7 + 6, a, t1, n);
+        conv(1 + stage * 7 + 6, t1, a, nullptr, cur, f1);
+        cur = f1;
+        width *= 2;
+    }
+    long long n = 0;
+    for (int v : cur)
+        n += v;
+    snake(28, a, t1, n);
+    conv(29, t1, latent, nullptr, cur, f1);
+    cuda_ok(cudaGetLastError(), "analysis launch");
+}
+
+void DacEngine::synthesize(const float* latent, const std::vector<int>& frames, float* pcm)
+{
+    require(synthesis_, "synthesis on an analysis model");
+    long long total = 0;
+    for (int v : frames)
+        total += v;
+    // Widest activation: 1536 x n at entry, 768 x 8n after stage 0 ... = 6144n;
+    // the last stage holds 96 x 512n = 49152n floats.
+    const std::size_t biggest = static_cast<std::size_t>(total) * 49152;
+    auto* a = ws_.get<float>("a", biggest);
+    auto* t1 = ws_.get<float>("t1", biggest);
+    auto* t2 = ws_.get<float>("t2", biggest);
+    std::vector<int> cur = frames, f1;
+    conv(0, latent, a, nullptr, cur, f1);
+    cur = f1;
+    for (int stage = 0; stage < 4; ++stage)
+    {
+        long long n = 0;
+        for (int v : cur)
+            n += v;
+        snake(stage * 7, a, t1, n);
+        conv(1 + stage * 7, t1, a, nullptr, cur, f1);
+        cur = f1;
+        n = 0;
+        for (int v : cur)
+            n += v;
+        for (int unit = 0; unit < 3; ++unit)
+        {
+            const int base = 1 + stage * 7 + 1 + unit * 2;
+            const int alpha = stage * 7 + 1 + unit * 2;
+            snake(alpha, a, t1, n);
+            conv(base, t1, t2, nullptr, cur, f1);
+            snake(alpha + 1, t2, t1, n);
+            conv(base + 1, t1, a, a, cur, f1);
+        }
+    }
+    long long n = 0;
+    for (int v : cur)
+        n += v;
+    snake(28, a, t1, n);
+    conv(29, t1, pcm, nullptr, cur, f1);
+    cuda_ok(cudaGetLastError(), "synthesis launch");
+}
+
+// ----------------------------------------------------------------- RVQ ----
+RvqEngine::RvqEngine(const std::vector<PreparedRvqBook>& books, cudaStream_t stream)
+    : books_(static_cast<int>(books.size())), stream_(stream), error_(sizeof(unsigned))
+{
+    std::vector<dev::RvqBookDevice> table;
+    for (const auto& b : books)
+    {
+        const auto up = [&](const std::vector<float>& v)
+        {
+            storage_.push_back(upload(v, stream));
+            return storage_.back().as<float>();
+        };
+        dev::RvqBookDevice d;
+        d.input_weights = up(b.input_weights);
+        d.input_bias = up(b.input_bias);
+        d.search = up(b.search);
+        d.codebook = up(b.codebook);
+        d.output_weights = up(b.output_weights);
+        d.output_bias = up(b.output_bias);
+        table.push_back(d);
+    }
+    table_ = upload(table, stream);
+    cuda_ok(cudaMemsetAsync(error_.as<void>(), 0, 4, stream), "memset");
+    cuda_ok(cudaStreamSynchronize(stream), "RVQ upload");
+}
+
+void RvqEngine::encode(const float* latent, int frames, int books, std::uint16_t* tokens, int stride)
+{
+    require(books > 0 && books <= books_, "stream and prepared RVQ codebooks do not match");
+    dev::rvq_encode(latent, frames, table_.as<dev::RvqBookDevice>(), books, tokens, stride,
+                    error_word(), stream_);
+}
+
+void RvqEngine::decode(const std::uint16_t* tokens, int stride, int frames, int books, float* latent)
+{
+    require(books > 0 && books <= books_, "stream and prepared RVQ codebooks do not match");
+    dev::rvq_decode(tokens, stride, frames, table_.as<dev::RvqBookDevice>(), books, latent, stream_);
+}
+} // namespace tsacb

@@ -1,0 +1,76 @@
+// DAC analysis (encoder) / synthesis (decoder) and the residual VQ on the
+// device, over batches of independent windows.
+//
+// DacAnalysis::apply / DacSynthesis::apply (src/common/analysis.tpp:169-214,
+// src/common/synthesis.tpp:168-213) evaluate one window at a time with zero
+// padding at the window edges; here every window of a call (all chunks of all
+// recordings) is one "sequence" of a single launch per layer.
+#pragma once
+#include "device.hpp"
+#include "models.hpp"
+#include "kernels/dac.cuh"
+
+namespace tsacb
+{
+struct DeviceConv
+{
+    Conv1dSpec spec;
+    DeviceBuffer weights; // [tap][in][out]
+    DeviceBuffer bias;
+};
+
+class DacEngine
+{
+public:
+    DacEngine(const PreparedDac& dac, cudaStream_t stream);
+    unsigned channels() const
+    {
+        return channels_;
+    }
+    // Analysis: pcm windows [sum of window samples][C] (window w has
+    // frames[w]*512 samples) -> latent [sum of frames][1024].
+    void analyze(const float* pcm, const std::vector<int>& frames, float* latent);
+    // Synthesis: latent windows [sum of frames][1024] -> pcm [sum frames*512][C].
+    void synthesize(const float* latent, const std::vector<int>& frames, float* pcm);
+    unsigned* error_word() const
+    {
+        return error_.as<unsigned>();
+    }
+    void check_errors(const char* what);
+
+private:
+    struct Layout; // per-layer sequence tables for one window set
+    void conv(int index, const float* x, float* y, const float* residual,
+              const std::vector<int>& in_frames, std::vector<int>& out_frames);
+    void snake(int index, const float* x, float* y, long long frames);
+
+    bool synthesis_;
+    unsigned channels_;
+    std::vector<DeviceConv> convs_;
+    std::vector<DeviceBuffer> alphas_;
+    std::vector<int> alpha_width_;
+    cudaStream_t stream_;
+    Workspace ws_;
+    DeviceBuffer error_;
+};
+
+class RvqEngine
+{
+public:
+    RvqEngine(const std::vector<PreparedRvqBook>& books, cudaStream_t stream);
+    // latent [frames][1024] (consumed as residual) -> tokens [frames][stride], books 0..count-1.
+    void encode(const float* latent, int frames, int books, std::uint16_t* tokens, int stride);
+    void decode(const std::uint16_t* tokens, int stride, int frames, int books, float* latent);
+    unsigned* error_word() const
+    {
+        return error_.as<unsigned>();
+    }
+
+private:
+    std::vector<DeviceBuffer> storage_;
+    DeviceBuffer table_; // RvqBookDevice[books]
+    int books_ = 0;
+    cudaStream_t stream_;
+    DeviceBuffer error_;
+};
+} // namespace tsacb

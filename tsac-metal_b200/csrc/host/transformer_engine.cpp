@@ -1,0 +1,597 @@
+#include "transformer_engine.hpp"
+
+#include "kernels/qlinear.cuh"
+#include "kernels/transformer_ops.cuh"
+
+#include <algorithm>
+#include <deque>
+
+namespace tsacb
+{
+namespace
+{
+using dev::RowMeta;
+
+constexpr int context = 1024, replay_frames = 256;
+
+int norm_index(bool temporal, int layer, bool mlp) // src/models/contract.cpp:191-196
+{
+    return (temporal ? 0 : 25) + layer * 2 + (mlp ? 1 : 0);
+}
+
+int final_norm(bool temporal)
+{
+    return temporal ? 24 : 31;
+}
+
+int projection_index(bool temporal, int layer, int op) // src/models/contract.cpp:185-189
+{
+    return (temporal ? 0 : 48) + layer * 4 + op;
+}
+} // namespace
+
+DeviceTransformer::DeviceTransformer(const PreparedTransformer& t, cudaStream_t stream)
+    : channels(t.channels), books(t.books)
+{
+    for (const auto& p : t.projections)
+    {
+        DeviceLinear l;
+        l.input = static_cast<int>(p.input);
+        l.output = static_cast<int>(p.output);
+        l.weights = upload(p.weights, stream);
+        l.scales = upload(p.scales, stream);
+        l.bias = upload(p.bias, stream);
+        projections.push_back(std::move(l));
+    }
+    for (const auto& n : t.norms)
+    {
+        norm_gain.push_back(upload(n.gain, stream));
+        norm_bias.push_back(upload(n.bias, stream));
+    }
+    positions = upload(t.positions, stream);
+    rotations = upload(t.rotations, stream);
+    embeddings = upload(t.embeddings, stream);
+    gelu.resize(65536 * 2);
+    dev::build_gelu_table(gelu.as<std::uint16_t>(), stream);
+    cuda_ok(cudaGetLastError(), "transformer weight upload");
+    cuda_ok(cudaStreamSynchronize(stream), "transformer weight upload");
+}
+
+TransformerEngine::TransformerEngine(std::shared_ptr<const DeviceTransformer> model,
+                                     cudaStream_t stream)
+    : model_(std::move(model)), stream_(stream), error_(sizeof(unsigned))
+{
+    cuda_ok(cudaMemsetAsync(error_.as<void>(), 0, sizeof(unsigned), stream_), "memset");
+}
+
+void TransformerEngine::check_errors()
+{
+    unsigned word = 0;
+    cuda_ok(cudaMemcpyAsync(&word, error_.as<void>(), sizeof(word), cudaMemcpyDeviceToHost, stream_),
+            "error word");
+    cuda_ok(cudaStreamSynchronize(stream_), "transformer");
+    if (word)
+    {
+        cuda_ok(cudaMemsetAsync(error_.as<void>(), 0, sizeof(unsigned), stream_), "memset");
+        throw NumericError("Transformer activations must be finite");
+    }
+}
+
+void TransformerEngine::quantize(const std::uint16_t* x, int rows, int k, std::int8_t* xq, float* xs)
+{
+    dev::qlinear_quantize(x, rows, k, xq, xs, error_word(), stream_);
+}
+
+void TransformerEngine::run_linear(int projection, const std::int8_t* xq, const float* xs,
+                                   int rows, std::uint16_t* y, const std::uint16_t* residual,
+                                   bool gelu)
+{
+    const auto& l = model_->projections.at(static_cast<std::size_t>(projection));
+    dev::QLinearArgs a;
+    a.weights = l.weights.as<std::int8_t>();
+    a.weight_scales = l.scales.as<float>();
+    a.bias = l.bias.as<float>();
+    a.xq = xq;
+    a.xscale = xs;
+    a.residual = residual;
+    a.lut = gelu ? model_->gelu.as<std::uint16_t>() : nullptr;
+    a.y = y;
+    a.m = rows;
+    a.n = l.output;
+    a.k = l.input;
+    dev::qlinear_matmul(a, stream_);
+}
+
+// evaluate_stack (src/common/cpu_transformer.tpp:99-141) over a set of rows.
+void TransformerEngine::run_stack(bool temporal, int rows, std::uint16_t* h, const void* meta_device,
+                                  int max_time, std::uint16_t* cache_k, std::uint16_t* cache_v,
+                                  std::size_t cache_layer_stride, std::uint16_t* final_out,
+                                  std::int8_t* final_q, float* final_s)
+{
+    const auto* meta = static_cast<const RowMeta*>(meta_device);
+    const int layers = temporal ? 12 : 3;
+    auto* xq = ws_.get<std::int8_t>("xq", static_cast<std::size_t>(rows) * 2048);
+    auto* xs = ws_.get<float>("xs", static_cast<std::size_t>(rows) * 8);
+    auto* qkv = ws_.get<std::uint16_t>("qkv", static_cast<std::size_t>(rows) * 1536);
+    auto* query = ws_.get<std::uint16_t>("query", static_cast<std::size_t>(rows) * 512);
+    auto* att = ws_.get<std::uint16_t>("att", static_cast<std::size_t>(rows) * 512);
+    auto* mlp = ws_.get<std::uint16_t>("mlp", static_cast<std::size_t>(rows) * 2048);
+    auto* partials = ws_.get<float>("partials", dev::attention_partials_bytes(rows, max_time) / 4);
+    const auto* rotations = model_->rotations.as<std::uint16_t>();
+    for (int l = 0; l < layers; ++l)
+    {
+        const int n1 = norm_index(temporal, l, false), n2 = norm_index(temporal, l, true);
+        auto* ck = cache_k + cache_layer_stride * static_cast<std::size_t>(l);
+        auto* cv = cache_v + cache_layer_stride * static_cast<std::size_t>(l);
+        dev::layer_norm(h, model_->norm_gain[n1].as<std::uint16_t>(),
+                        model_->norm_bias[n1].as<std::uint16_t>(), rows, nullptr, xq, xs,
+                        error_word(), stream_);
+        run_linear(projection_index(temporal, l, 0), xq, xs, rows, qkv, nullptr, false);
+        dev::rotary_scatter(qkv, meta, rotations, rows, query, ck, cv, stream_);
+        dev::attention(query, meta, ck, cv, rows, max_time, partials, att, stream_);
+        quantize(att, rows, 512, xq, xs);
+        run_linear(projection_index(temporal, l, 1), xq, xs, rows, h, h, false);
+        dev::layer_norm(h, model_->norm_gain[n2].as<std::uint16_t>(),
+                        model_->norm_bias[n2].as<std::uint16_t>(), rows, nullptr, xq, xs,
+                        error_word(), stream_);
+        run_linear(projection_index(temporal, l, 2), xq, xs, rows, mlp, nullptr, true);
+        quantize(mlp, rows, 2048, xq, xs);
+        run_linear(projection_index(temporal, l, 3), xq, xs, rows, h, h, false);
+    }
+    const int f = final_norm(temporal);
+    dev::layer_norm(h, model_->norm_gain[f].as<std::uint16_t>(),
+                    model_->norm_bias[f].as<std::uint16_t>(), rows, final_out, final_q, final_s,
+                    error_word(), stream_);
+}
+
+void TransformerEngine::predict_known(const Header& header, std::span<const std::uint16_t> tokens,
+                                      std::uint16_t* q15, float* probabilities)
+{
+    validate_header(header);
+    require(header.method == 1, "Transformer predictor requires normal framing");
+    require(header.model_channels == model_->channels && header.codebooks <= model_->books,
+            "Transformer stream/model mismatch");
+    require(tokens.size() == header.symbol_count(), "normal token count does not match header");
+    for (auto t : tokens)
+    {
+        require(t < 1024, "Transformer feedback token exceeds alphabet");
+    }
+    const int F = static_cast<int>(header.frames), G = header.groups, Q = header.codebooks;
+    const int B = header.batch;
+    const int lanes_b = std::min(B, F);
+    const int base = F / B, extra = F % B;
+
+    // ---- temporal rows: the per-step schedule of TransformerPredictor::prepare
+    // (src/common/transformer.cpp:106-142) flattened into sequences.
+    std::vector<RowMeta> tmeta;
+    std::vector<int> toffsets, tcounts;
+    std::vector<int> cond_row(static_cast<std::size_t>(F) * G, -1);
+    // Token pool: the recording's tokens followed by one all-zero frame.
+    std::vector<std::uint16_t> pool(tokens.begin(), tokens.end());
+    const int zero_frame = static_cast<int>(pool.size());
+    pool.resize(pool.size() + static_cast<std::size_t>(Q), 0);
+    int next_slot = 0, max_time = 1;
+    for (int lane = 0; lane < lanes_b; ++lane)
+    {
+        const int length = base + (lane < extra);
+        const int start = lane * base + std::min(lane, extra);
+        for (int g = 0; g < G; ++g)
+        {
+            int used = 0, segment = next_slot;
+            std::deque<int> history;
+            const auto add = [&](int feedback_offset, bool replay)
+            {
+                const int position = used++;
+                const int slot = segment + position;
+                tmeta.push_back({slot, segment, position + 1, position,
+                                 (position + 1 > 64 || replay) ? 1 : 0});
+                toffsets.push_back(feedback_offset);
+                tcounts.push_back(Q);
+                next_slot = std::max(next_slot, slot + 1);
+                max_time = std::max(max_time, position + 1);
+            };
+            for (int s = 0; s < length; ++s)
+            {
+                const int f = start + s;
+                if (used == context)
+                {
+                    segment = next_slot;
+                    used = 0;
+                    for (int h : history)
+                    {
+                        add((h * G + g) * Q, true);
+                    }
+                }
+                else
+                {
+                    add(s == 0 ? zero_frame : ((f - 1) * G + g) * Q, false);
+                }
+                cond_row[static_cast<std::size_t>(f) * G + g] = static_cast<int>(tmeta.size()) - 1;
+                history.push_back(f);
+                if (static_cast<int>(history.size()) > replay_frames)
+                {
+                    history.pop_front();
+                }
+            }
+        }
+    }
+    const int trows = static_cast<int>(tmeta.size());
+    auto s = stream_;
+    auto* d_pool = ws_.get<std::uint16_t>("pool", pool.size());
+    cuda_ok(cudaMemcpyAsync(d_pool, pool.data(), pool.size() * 2, cudaMemcpyHostToDevice, s), "H2D");
+    auto* d_tmeta = ws_.get<RowMeta>("tmeta", tmeta.size());
+    cuda_ok(cudaMemcpyAsync(d_tmeta, tmeta.data(), tmeta.size() * sizeof(RowMeta), cudaMemcpyHostToDevice, s), "H2D");
+    auto* d_toff = ws_.get<int>("toff", toffsets.size());
+    cuda_ok(cudaMemcpyAsync(d_toff, toffsets.data(), toffsets.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+    auto* d_tcnt = ws_.get<int>("tcnt", tcounts.size());
+    cuda_ok(cudaMemcpyAsync(d_tcnt, tcounts.data(), tcounts.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+
+    // Temporal stack: feedback embedding -> cb_proj -> 12 layers -> ln_f.
+    auto* emb = ws_.get<std::uint16_t>("emb", static_cast<std::size_t>(trows) * 1024);
+    dev::embed_sum(model_->embeddings.as<std::uint16_t>(), d_pool, d_toff, d_tcnt, trows, emb, s);
+    auto* eq = ws_.get<std::int8_t>("eq", static_cast<std::size_t>(trows) * 1024);
+    auto* es = ws_.get<float>("es", static_cast<std::size_t>(trows) * 4);
+    quantize(emb, trows, 1024, eq, es);
+    auto* th = ws_.get<std::uint16_t>("th", static_cast<std::size_t>(trows) * 512);
+    run_linear(60, eq, es, trows, th, nullptr, false);
+    const std::size_t tstride = static_cast<std::size_t>(next_slot) * 512;
+    auto* tck = ws_.get<std::uint16_t>("tck", tstride * 12);
+    auto* tcv = ws_.get<std::uint16_t>("tcv", tstride * 12);
+    auto* cond = ws_.get<std::uint16_t>("cond", static_cast<std::size_t>(trows) * 512);
+    run_stack(true, trows, th, d_tmeta, max_time, tck, tcv, tstride, cond, nullptr, nullptr);
+
+    // ---- codebook stack, chunked by (frame, group) sequences of Q rows.
+    const int sequences = F * G;
+    const int chunk = std::max(1, 2048 / 1);
+    for (int first = 0; first < sequences; first += chunk)
+    {
+        const int count = std::min(chunk, sequences - first);
+        const int rows = count * Q;
+        std::vector<RowMeta> cmeta(static_cast<std::size_t>(rows));
+        std::vector<int> src0(static_cast<std::size_t>(count)), zero_books(static_cast<std::size_t>(count), 0);
+        std::vector<int> poff, pcnt, pbook, pid;
+        std::vector<int> token_index(static_cast<std::size_t>(rows));
+        // Row order: all book-0 rows, then books >= 1 sequence by sequence.
+        for (int i = 0; i < count; ++i)
+        {
+            const int fg = first + i;
+            src0[static_cast<std::size_t>(i)] = cond_row[static_cast<std::size_t>(fg)];
+            cmeta[static_cast<std::size_t>(i)] = {i * Q, i * Q, 1, -1, 0};
+            token_index[static_cast<std::size_t>(i)] = fg * Q;
+        }
+        int r = count;
+        for (int i = 0; i < count; ++i)
+        {
+            const int fg = first + i;
+            for (int b = 1; b < Q; ++b, ++r)
+            {
+                cmeta[static_cast<std::size_t>(r)] = {i * Q + b, i * Q, b + 1, -1, 0};
+                poff.push_back(fg * Q);
+                pcnt.push_back(b);
+                pbook.push_back(b);
+                pid.push_back(static_cast<int>(pid.size()));
+                token_index[static_cast<std::size_t>(r)] = fg * Q + b;
+            }
+        }
+        const int prows = rows - count;
+        auto* d_cmeta = ws_.get<RowMeta>("cmeta", cmeta.size());
+        cuda_ok(cudaMemcpyAsync(d_cmeta, cmeta.data(), cmeta.size() * sizeof(RowMeta), cudaMemcpyHostToDevice, s), "H2D");
+        auto* d_src0 = ws_.get<int>("src0", src0.size());
+        cuda_ok(cudaMemcpyAsync(d_src0, src0.data(), src0.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+        auto* d_zero = ws_.get<int>("zbook", zero_books.size());
+        cuda_ok(cudaMemcpyAsync(d_zero, zero_books.data(), zero_books.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+        auto* d_tidx = ws_.get<int>("tidx", token_index.size());
+        cuda_ok(cudaMemcpyAsync(d_tidx, token_index.data(), token_index.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+        auto* ch = ws_.get<std::uint16_t>("ch", static_cast<std::size_t>(rows) * 512);
+        dev::add_positions(cond, d_src0, d_zero, model_->positions.as<std::uint16_t>(), count, ch, s);
+        if (prows > 0)
+        {
+            auto* d_poff = ws_.get<int>("poff", poff.size());
+            cuda_ok(cudaMemcpyAsync(d_poff, poff.data(), poff.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+            auto* d_pcnt = ws_.get<int>("pcnt", pcnt.size());
+            cuda_ok(cudaMemcpyAsync(d_pcnt, pcnt.data(), pcnt.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+            auto* d_pbook = ws_.get<int>("pbook", pbook.size());
+            cuda_ok(cudaMemcpyAsync(d_pbook, pbook.data(), pbook.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+            auto* d_pid = ws_.get<int>("pid", pid.size());
+            cuda_ok(cudaMemcpyAsync(d_pid, pid.data(), pid.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+            auto* pemb = ws_.get<std::uint16_t>("pemb", static_cast<std::size_t>(prows) * 1024);
+            dev::embed_sum(model_->embeddings.as<std::uint16_t>(), d_pool, d_poff, d_pcnt, prows, pemb, s);
+            auto* pq = ws_.get<std::int8_t>("pq", static_cast<std::size_t>(prows) * 1024);
+            auto* ps = ws_.get<float>("ps", static_cast<std::size_t>(prows) * 4);
+            quantize(pemb, prows, 1024, pq, ps);
+            auto* pproj = ws_.get<std::uint16_t>("pproj", static_cast<std::size_t>(prows) * 512);
+            run_linear(61, pq, ps, prows, pproj, nullptr, false);
+            dev::add_positions(pproj, d_pid, d_pbook, model_->positions.as<std::uint16_t>(), prows,
+                               ch + static_cast<std::size_t>(count) * 512, s);
+        }
+        const std::size_t cstride = static_cast<std::size_t>(rows) * 512;
+        auto* cck = ws_.get<std::uint16_t>("cck", cstride * 3);
+        auto* ccv = ws_.get<std::uint16_t>("ccv", cstride * 3);
+        auto* fq = ws_.get<std::int8_t>("fq", static_cast<std::size_t>(rows) * 512);
+        auto* fs = ws_.get<float>("fs", static_cast<std::size_t>(rows) * 2);
+        run_stack(false, rows, ch, d_cmeta, Q, cck, ccv, cstride, nullptr, fq, fs);
+        auto* logits = ws_.get<std::uint16_t>("logits", static_cast<std::size_t>(rows) * 1024);
+        run_linear(62, fq, fs, rows, logits, nullptr, false);
+        auto* tree = ws_.get<float>("tree", static_cast<std::size_t>(rows) * 1023);
+        float* probs = probabilities ? ws_.get<float>("probs", static_cast<std::size_t>(rows) * 1024) : nullptr;
+        dev::softmax_tree(logits, rows, nullptr, probs, tree, error_word(), s);
+        auto* dq = ws_.get<std::uint16_t>("q15", static_cast<std::size_t>(rows) * 10);
+        dev::categorical_path_q15(tree, d_pool, d_tidx, rows, dq, s);
+        cuda_ok(cudaGetLastError(), "transformer launch");
+        std::vector<std::uint16_t> hq(static_cast<std::size_t>(rows) * 10);
+        cuda_ok(cudaMemcpyAsync(hq.data(), dq, hq.size() * 2, cudaMemcpyDeviceToHost, s), "D2H");
+        std::vector<float> hp;
+        if (probabilities)
+        {
+            hp.resize(static_cast<std::size_t>(rows) * 1024);
+            cuda_ok(cudaMemcpyAsync(hp.data(), probs, hp.size() * 4, cudaMemcpyDeviceToHost, s), "D2H");
+        }
+        check_errors();
+        for (int i = 0; i < rows; ++i)
+        {
+            const auto t = static_cast<std::size_t>(token_index[static_cast<std::size_t>(i)]);
+            std::copy_n(hq.data() + static_cast<std::size_t>(i) * 10, 10, q15 + t * 10);
+            if (probabilities)
+            {
+                std::copy_n(hp.data() + static_cast<std::size_t>(i) * 1024, 1024, probabilities + t * 1024);
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ decode --
+struct TransformerEngine::DecodeState
+{
+    struct Lane
+    {
+        int recording = 0, lane_b = 0, group = 0;
+        int start = 0, length = 0, used = 0;
+        std::vector<std::uint16_t> current;
+        std::deque<std::vector<std::uint16_t>> history;
+        int tslot = 0; // first temporal cache slot (1024 per lane)
+        int cslot = 0; // first codebook cache slot (Q per lane)
+    };
+    std::vector<Header> headers;
+    std::vector<Lane> lanes;
+    int max_books = 0;
+    std::vector<LaneRef> last;
+    std::vector<int> last_lanes;
+    std::size_t last_book = 0;
+};
+
+void TransformerEngine::decode_begin(const std::vector<Header>& headers)
+{
+    auto state = std::make_shared<DecodeState>();
+    state->headers = headers;
+    int tslots = 0, cslots = 0;
+    for (std::size_t r = 0; r < headers.size(); ++r)
+    {
+        const auto& h = headers[r];
+        validate_header(h);
+        require(h.method == 1 && h.model_channels == model_->channels &&
+                    h.codebooks <= model_->books,
+                "Transformer stream/model mismatch");
+        const int F = static_cast<int>(h.frames), B = h.batch, G = h.groups;
+        const int lanes_b = std::min(B, F), base = F / B, extra = F % B;
+        state->max_books = std::max<int>(state->max_books, h.codebooks);
+        for (int lane = 0; lane < lanes_b; ++lane)
+        {
+            for (int g = 0; g < G; ++g)
+            {
+                DecodeState::Lane l;
+                l.recording = static_cast<int>(r);
+                l.lane_b = lane;
+                l.group = g;
+                l.length = base + (lane < extra);
+                l.start = lane * base + std::min(lane, extra);
+                l.current.assign(h.codebooks, 0);
+                l.tslot = tslots;
+                l.cslot = cslots;
+                tslots += context;
+                cslots += h.codebooks;
+                state->lanes.push_back(std::move(l));
+            }
+        }
+    }
+    const std::size_t tstride = static_cast<std::size_t>(tslots) * 512;
+    ws_.get<std::uint16_t>("dtck", tstride * 12);
+    ws_.get<std::uint16_t>("dtcv", tstride * 12);
+    const std::size_t cstride = static_cast<std::size_t>(cslots) * 512;
+    ws_.get<std::uint16_t>("dcck", cstride * 3);
+    ws_.get<std::uint16_t>("dccv", cstride * 3);
+    ws_.get<std::uint16_t>("dcond", state->lanes.size() * 512);
+    decode_ = std::move(state);
+}
+
+std::vector<TransformerEngine::LaneRef>
+TransformerEngine::decode_predict(std::size_t step, std::size_t book, float* masses_host)
+{
+    require(decode_ != nullptr, "decode session not started");
+    auto& st = *decode_;
+    auto s = stream_;
+    const int total_lanes = static_cast<int>(st.lanes.size());
+    int tslots = 0, cslots = 0;
+    for (const auto& l : st.lanes)
+    {
+        tslots += context;
+        cslots += static_cast<int>(l.current.size());
+    }
+    const std::size_t tstride = static_cast<std::size_t>(tslots) * 512;
+    const std::size_t cstride = static_cast<std::size_t>(cslots) * 512;
+    auto* tck = ws_.get<std::uint16_t>("dtck", tstride * 12);
+    auto* tcv = ws_.get<std::uint16_t>("dtcv", tstride * 12);
+    auto* cck = ws_.get<std::uint16_t>("dcck", cstride * 3);
+    auto* ccv = ws_.get<std::uint16_t>("dccv", cstride * 3);
+    auto* cond = ws_.get<std::uint16_t>("dcond", static_cast<std::size_t>(total_lanes) * 512);
+
+    std::vector<int> active;
+    for (int i = 0; i < total_lanes; ++i)
+    {
+        const auto& l = st.lanes[static_cast<std::size_t>(i)];
+        if (static_cast<int>(step) < l.length && book < l.current.size())
+        {
+            active.push_back(i);
+        }
+    }
+    st.last.clear();
+    st.last_lanes = active;
+    st.last_book = book;
+    if (active.empty())
+    {
+        return {};
+    }
+    const int n = static_cast<int>(active.size());
+    const int Qmax = st.max_books;
+    if (book == 0)
+    {
+        // Temporal step (or context reset + replay) for every active lane.
+        std::vector<RowMeta> meta;
+        std::vector<std::uint16_t> tok;
+        std::vector<int> off, cnt, out_row;
+        int max_time = 1;
+        for (int i : active)
+        {
+            auto& l = st.lanes[static_cast<std::size_t>(i)];
+            const int Q = static_cast<int>(l.current.size());
+            const auto add = [&](const std::vector<std::uint16_t>& fb, bool replay)
+            {
+                const int position = l.used++;
+                meta.push_back({l.tslot + position, l.tslot, position + 1, position,
+                                (position + 1 > 64 || replay) ? 1 : 0});
+                off.push_back(static_cast<int>(tok.size()));
+                cnt.push_back(Q);
+                tok.insert(tok.end(), fb.begin(), fb.end());
+                max_time = std::max(max_time, position + 1);
+            };
+            std::fill(l.current.begin(), l.current.end(), 0);
+            if (l.used == context)
+            {
+                require(static_cast<int>(l.history.size()) == replay_frames,
+                        "incomplete Transformer replay history");
+                l.used = 0;
+                for (const auto& fb : l.history)
+                {
+                    add(fb, true);
+                }
+            }
+            else
+            {
+                add(l.history.empty() ? l.current : l.history.back(), false);
+            }
+            out_row.push_back(static_cast<int>(meta.size()) - 1);
+        }
+        const int rows = static_cast<int>(meta.size());
+        auto* d_tok = ws_.get<std::uint16_t>("dtok", tok.size());
+        cuda_ok(cudaMemcpyAsync(d_tok, tok.data(), tok.size() * 2, cudaMemcpyHostToDevice, s), "H2D");
+        auto* d_meta = ws_.get<RowMeta>("dtmeta", meta.size());
+        cuda_ok(cudaMemcpyAsync(d_meta, meta.data(), meta.size() * sizeof(RowMeta), cudaMemcpyHostToDevice, s), "H2D");
+        auto* d_off = ws_.get<int>("dtoff", off.size());
+        cuda_ok(cudaMemcpyAsync(d_off, off.data(), off.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+        auto* d_cnt = ws_.get<int>("dtcnt", cnt.size());
+        cuda_ok(cudaMemcpyAsync(d_cnt, cnt.data(), cnt.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+        auto* emb = ws_.get<std::uint16_t>("demb", static_cast<std::size_t>(rows) * 1024);
+        dev::embed_sum(model_->embeddings.as<std::uint16_t>(), d_tok, d_off, d_cnt, rows, emb, s);
+        auto* eq = ws_.get<std::int8_t>("deq", static_cast<std::size_t>(rows) * 1024);
+        auto* es = ws_.get<float>("des", static_cast<std::size_t>(rows) * 4);
+        quantize(emb, rows, 1024, eq, es);
+        auto* th = ws_.get<std::uint16_t>("dth", static_cast<std::size_t>(rows) * 512);
+        run_linear(60, eq, es, rows, th, nullptr, false);
+        auto* tout = ws_.get<std::uint16_t>("dtout", static_cast<std::size_t>(rows) * 512);
+        run_stack(true, rows, th, d_meta, max_time, tck, tcv, tstride, tout, nullptr, nullptr);
+        // Keep each lane's conditioning (the last row it produced).
+        for (std::size_t j = 0; j < active.size(); ++j)
+        {
+            cuda_ok(cudaMemcpyAsync(cond + static_cast<std::size_t>(active[j]) * 512,
+                                    tout + static_cast<std::size_t>(out_row[j]) * 512, 1024,
+                                    cudaMemcpyDeviceToDevice, s),
+                    "D2D");
+        }
+    }
+    // Codebook step for book `book` of every active lane.
+    std::vector<RowMeta> meta(static_cast<std::size_t>(n));
+    std::vector<int> lane_rows(static_cast<std::size_t>(n)), books(static_cast<std::size_t>(n), static_cast<int>(book));
+    std::vector<std::uint16_t> tok;
+    std::vector<int> off, cnt;
+    for (int j = 0; j < n; ++j)
+    {
+        const auto& l = st.lanes[static_cast<std::size_t>(active[static_cast<std::size_t>(j)])];
+        meta[static_cast<std::size_t>(j)] = {l.cslot + static_cast<int>(book), l.cslot,
+                                             static_cast<int>(book) + 1, -1, 0};
+        lane_rows[static_cast<std::size_t>(j)] = active[static_cast<std::size_t>(j)];
+        off.push_back(static_cast<int>(tok.size()));
+        cnt.push_back(static_cast<int>(book));
+        tok.insert(tok.end(), l.current.begin(), l.current.begin() + static_cast<std::ptrdiff_t>(book));
+        st.last.push_back({l.recording, l.lane_b * st.headers[static_cast<std::size_t>(l.recording)].groups + l.group});
+    }
+    auto* d_meta = ws_.get<RowMeta>("dcmeta", meta.size());
+    cuda_ok(cudaMemcpyAsync(d_meta, meta.data(), meta.size() * sizeof(RowMeta), cudaMemcpyHostToDevice, s), "H2D");
+    auto* d_books = ws_.get<int>("dcbook", books.size());
+    cuda_ok(cudaMemcpyAsync(d_books, books.data(), books.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+    auto* ch = ws_.get<std::uint16_t>("dch", static_cast<std::size_t>(n) * 512);
+    if (book == 0)
+    {
+        auto* d_rows = ws_.get<int>("dcrows", lane_rows.size());
+        cuda_ok(cudaMemcpyAsync(d_rows, lane_rows.data(), lane_rows.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+        dev::add_positions(cond, d_rows, d_books, model_->positions.as<std::uint16_t>(), n, ch, s);
+    }
+    else
+    {
+        std::vector<int> ident(static_cast<std::size_t>(n));
+        for (int j = 0; j < n; ++j)
+            ident[static_cast<std::size_t>(j)] = j;
+        if (tok.empty())
+            tok.push_back(0);
+        auto* d_tok = ws_.get<std::uint16_t>("dctok", tok.size());
+        cuda_ok(cudaMemcpyAsync(d_tok, tok.data(), tok.size() * 2, cudaMemcpyHostToDevice, s), "H2D");
+        auto* d_off = ws_.get<int>("dcoff", off.size());
+        cuda_ok(cudaMemcpyAsync(d_off, off.data(), off.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+        auto* d_cnt = ws_.get<int>("dccnt", cnt.size());
+        cuda_ok(cudaMemcpyAsync(d_cnt, cnt.data(), cnt.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+        auto* d_id = ws_.get<int>("dcid", ident.size());
+        cuda_ok(cudaMemcpyAsync(d_id, ident.data(), ident.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
+        auto* pemb = ws_.get<std::uint16_t>("dpemb", static_cast<std::size_t>(n) * 1024);
+        dev::embed_sum(model_->embeddings.as<std::uint16_t>(), d_tok, d_off, d_cnt, n, pemb, s);
+        auto* pq = ws_.get<std::int8_t>("dpq", static_cast<std::size_t>(n) * 1024);
+        auto* ps = ws_.get<float>("dps", static_cast<std::size_t>(n) * 4);
+        quantize(pemb, n, 1024, pq, ps);
+        auto* pproj = ws_.get<std::uint16_t>("dpproj", static_cast<std::size_t>(n) * 512);
+        run_linear(61, pq, ps, n, pproj, nullptr, false);
+        dev::add_positions(pproj, d_id, d_books, model_->positions.as<std::uint16_t>(), n, ch, s);
+    }
+    auto* fq = ws_.get<std::int8_t>("dfq", static_cast<std::size_t>(n) * 512);
+    auto* fs = ws_.get<float>("dfs", static_cast<std::size_t>(n) * 2);
+    run_stack(false, n, ch, d_meta, static_cast<int>(book) + 1, cck, ccv, cstride, nullptr, fq, fs);
+    auto* logits = ws_.get<std::uint16_t>("dlogits", static_cast<std::size_t>(n) * 1024);
+    run_linear(62, fq, fs, n, logits, nullptr, false);
+    auto* tree = ws_.get<float>("dtree", static_cast<std::size_t>(n) * 1023);
+    dev::softmax_tree(logits, n, nullptr, nullptr, tree, error_word(), s);
+    cuda_ok(cudaGetLastError(), "transformer launch");
+    cuda_ok(cudaMemcpyAsync(masses_host, tree, static_cast<std::size_t>(n) * 1023 * 4,
+                            cudaMemcpyDeviceToHost, s),
+            "D2H");
+    (void)Qmax;
+    check_errors();
+    return st.last;
+}
+
+void TransformerEngine::decode_commit(std::span<const std::uint16_t> tokens)
+{
+    require(decode_ != nullptr, "decode session not started");
+    auto& st = *decode_;
+    require(tokens.size() == st.last_lanes.size(), "decode commit does not match prediction");
+    for (std::size_t j = 0; j < tokens.size(); ++j)
+    {
+        require(tokens[j] < 1024, "Transformer feedback token exceeds alphabet");
+        auto& l = st.lanes[static_cast<std::size_t>(st.last_lanes[j])];
+        l.current[st.last_book] = tokens[j];
+        if (st.last_book + 1 == l.current.size())
+        {
+            l.history.push_back(l.current);
+            if (static_cast<int>(l.history.size()) > replay_frames)
+            {
+                l.history.pop_front();
+            }
+        }
+    }
+}
+} // namespace tsacb

@@ -1,0 +1,98 @@
+// GPU TokenPredictor: the two-stack probability model on the device.
+//
+// Replaces CpuTransformer + TransformerPredictor (src/common/cpu_transformer.tpp,
+// src/common/transformer.cpp) behind the TokenPredictor seam
+// (src/format/entropy.hpp:12-26).  Work is organised in rows (see
+// kernels/transformer_ops.cuh); a row's K/V lives in a cache slot and its
+// attention reads the slots of its own sequence.
+//
+// Encode (known tokens): the whole recording is evaluated as one layer-wise
+// causal prefill per lane, exactly reproducing the per-step schedule of
+// TransformerPredictor::prepare (1024-position context, reset and replay of
+// the last 256 frames with replay rounding), and emits for every symbol the
+// Q15 probabilities of the bisection nodes on the path to its token.
+//
+// Decode: one (step, book) at a time for all lanes of all recordings in the
+// batch; emits the left-child subtree masses the host range decoder walks.
+#pragma once
+#include "device.hpp"
+#include "format.hpp"
+#include "models.hpp"
+
+#include <memory>
+
+namespace tsacb
+{
+struct DeviceLinear
+{
+    DeviceBuffer weights, scales, bias;
+    int input = 0, output = 0;
+};
+
+struct DeviceTransformer
+{
+    unsigned channels = 0, books = 0;
+    std::vector<DeviceLinear> projections; // 63, contract order
+    std::vector<DeviceBuffer> norm_gain, norm_bias; // 32
+    DeviceBuffer positions, rotations, embeddings, gelu;
+
+    DeviceTransformer(const PreparedTransformer& t, cudaStream_t stream);
+};
+
+// Rows of one stack evaluation with their cache metadata (host side).
+struct RowPlan;
+
+class TransformerEngine
+{
+public:
+    TransformerEngine(std::shared_ptr<const DeviceTransformer> model, cudaStream_t stream);
+
+    // Known-token evaluation of whole recordings (encode).
+    // tokens: [frames][groups][books] of each recording; outputs per recording
+    // q15[symbol][10] indexed by token offset, and optionally the float
+    // probabilities [symbol][1024] (token-offset order).
+    void predict_known(const Header& header, std::span<const std::uint16_t> tokens,
+                       std::uint16_t* q15, float* probabilities);
+
+    // --- decode stepping for a batch of recordings (same model) -------------
+    struct Stream
+    {
+        Header header;
+    };
+    void decode_begin(const std::vector<Header>& headers);
+    // Computes the distributions of book `book` at `step` for every lane of
+    // every recording that has that step; writes left-child masses
+    // [row][1023] (host pinned) and returns the lane ids (recording, lane) of
+    // the rows in order.
+    struct LaneRef
+    {
+        int recording, lane;
+    };
+    std::vector<LaneRef> decode_predict(std::size_t step, std::size_t book, float* masses_host);
+    // Commits the decoded tokens of the rows returned by the last decode_predict.
+    void decode_commit(std::span<const std::uint16_t> tokens);
+
+    unsigned* error_word() const
+    {
+        return error_.as<unsigned>();
+    }
+    void check_errors();
+
+private:
+    void run_linear(int projection, const std::int8_t* xq, const float* xs, int rows,
+                    std::uint16_t* y, const std::uint16_t* residual, bool gelu);
+    void quantize(const std::uint16_t* x, int rows, int k, std::int8_t* xq, float* xs);
+    void run_stack(bool temporal, int rows, std::uint16_t* h, const void* meta_device,
+                   int max_time, std::uint16_t* cache_k, std::uint16_t* cache_v,
+                   std::size_t cache_layer_stride, std::uint16_t* final_out,
+                   std::int8_t* final_q, float* final_s);
+
+    std::shared_ptr<const DeviceTransformer> model_;
+    cudaStream_t stream_;
+    Workspace ws_;
+    DeviceBuffer error_;
+
+    struct DecodeState;
+    std::shared_ptr<DecodeState> decode_;
+};
+} // namespace tsacb

@@ -1,0 +1,179 @@
+// Causal attention of the TSAC probability model (4 heads x 128) over a bf16
+// K/V cache, restating scalar::Attention (src/scalar/attention.cpp:12-131):
+//   per head, keys in 64-key blocks; score = (serial fma over the 128
+//   coordinates) * 0.0883883461356163; block max; e = original_exp(s - max);
+//   value sums serial over the block's keys (bf16-rounded when the history is
+//   longer than 64 keys or the row is a replay prefill); blocks merged in
+//   order with old/new scales original_exp(-|dmax|); out = bf16(num / total).
+//
+// B200 mapping (flash-decoding with an order-exact combine):
+//   kernel 1, one CTA per (row, head, 64-key block): stage the block's K and V
+//   in shared memory (rows padded to 65 words, conflict-free), 64 threads run
+//   the serial score chains, 128 threads the serial value chains; it writes
+//   (block max, block sum, 128 value sums).
+//   kernel 2, one CTA per (row, head): the sequential merge over blocks, which
+//   is cheap (16 steps at 1024 keys) and keeps the reference's order.
+#include "kernels/numeric.cuh"
+#include "kernels/transformer_ops.cuh"
+
+namespace tsacb::dev
+{
+namespace
+{
+constexpr int HEADS = 4, HW = 128, WIDTH = 512, BLOCK = 64, PSTRIDE = HW + 2;
+constexpr float SCALE = 0.0883883461356163f;
+
+struct ArgMax
+{
+    float value;
+    int index;
+};
+
+__device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b)
+{
+    return (a.value < b.value || (a.value == b.value && b.index < a.index)) ? b : a;
+}
+
+__global__ void __launch_bounds__(128)
+    attention_block_kernel(const std::uint16_t* __restrict__ query,
+                           const RowMeta* __restrict__ meta,
+                           const std::uint16_t* __restrict__ cache_k,
+                           const std::uint16_t* __restrict__ cache_v, int max_blocks,
+                           float* __restrict__ partials)
+{
+    __shared__ unsigned ks[BLOCK][65];
+    __shared__ unsigned vs[BLOCK][65];
+    __shared__ float q[HW];
+    __shared__ float scores[BLOCK];
+    __shared__ ArgMax warp_best[2];
+    __shared__ float block_sum;
+    const int block = blockIdx.y;
+    const int task = blockIdx.x; // row * HEADS + head
+    const int row = task / HEADS, head = task % HEADS;
+    const RowMeta m = meta[row];
+    const int start = block * BLOCK;
+    if (start >= m.time)
+        return;
+    const int count = m.time - start < BLOCK ? m.time - start : BLOCK;
+    const int t = threadIdx.x;
+    q[t] = from_bf16(query[static_cast<size_t>(row) * WIDTH + head * HW + t]);
+    // Stage K and V rows [start, start+count) of this head: 64 words per row.
+    for (int i = t; i < count * 64; i += 128)
+    {
+        const int r = i >> 6, w = i & 63;
+        const size_t slot = static_cast<size_t>(m.base + start + r) * WIDTH + head * HW;
+        ks[r][w] = reinterpret_cast<const unsigned*>(cache_k + slot)[w];
+        vs[r][w] = reinterpret_cast<const unsigned*>(cache_v + slot)[w];
+    }
+    __syncthreads();
+    ArgMax best{-INFINITY, BLOCK};
+    if (t < count)
+    {
+        float dot = 0.0f;
+#pragma unroll 8
+        for (int w = 0; w < 64; ++w)
+        {
+            const unsigned pair = ks[t][w];
+            dot = __fmaf_rn(q[2 * w], from_bf16(pair & 0xffffu), dot);
+            dot = __fmaf_rn(q[2 * w + 1], from_bf16(pair >> 16), dot);
+        }
+        const float s = __fmul_rn(dot, SCALE);
+        scores[t] = s;
+        best = ArgMax{s, t};
+    }
+    if (t < 64)
+    {
+#pragma unroll
+        for (int offset = 16; offset > 0; offset >>= 1)
+        {
+            ArgMax other{__shfl_xor_sync(0xffffffffu, best.value, offset),
+                         __shfl_xor_sync(0xffffffffu, best.index, offset)};
+            best = better(best, other);
+        }
+        if ((t & 31) == 0)
+            warp_best[t >> 5] = best;
+    }
+    __syncthreads();
+    const float maximum = better(warp_best[0], warp_best[1]).value;
+    if (t < count)
+        scores[t] = original_exp(__fsub_rn(scores[t], maximum));
+    __syncthreads();
+    if (t < 32)
+    {
+        float s;
+        if (count <= 8)
+            s = t == 0 ? pair_sum_serial(scores, count, 8) : 0.0f;
+        else
+            s = warp_pair_sum64(2 * t < count ? scores[2 * t] : 0.0f,
+                                2 * t + 1 < count ? scores[2 * t + 1] : 0.0f);
+        if (t == 0)
+            block_sum = s;
+    }
+    // Value sums: thread t owns coordinate t, serial over the block's keys.
+    float sum = 0.0f;
+    const int w = t >> 1;
+    const bool high = t & 1;
+#pragma unroll 4
+    for (int r = 0; r < count; ++r)
+    {
+        const unsigned pair = vs[r][w];
+        sum = __fmaf_rn(from_bf16(high ? (pair >> 16) : (pair & 0xffffu)), scores[r], sum);
+    }
+    if (m.round)
+        sum = from_bf16(to_bf16(sum));
+    __syncthreads();
+    float* out = partials + (static_cast<size_t>(task) * max_blocks + block) * PSTRIDE;
+    out[2 + t] = sum;
+    if (t == 0)
+    {
+        out[0] = maximum;
+        out[1] = block_sum;
+    }
+}
+
+__global__ void __launch_bounds__(128)
+    attention_combine_kernel(const RowMeta* __restrict__ meta, const float* __restrict__ partials,
+                             int max_blocks, std::uint16_t* __restrict__ out)
+{
+    const int task = blockIdx.x;
+    const int row = task / HEADS, head = task % HEADS;
+    const int t = threadIdx.x;
+    const int blocks = (meta[row].time + BLOCK - 1) / BLOCK;
+    float running = -INFINITY, total = 0.0f, numerator = 0.0f;
+    for (int b = 0; b < blocks; ++b)
+    {
+        const float* p = partials + (static_cast<size_t>(task) * max_blocks + b) * PSTRIDE;
+        const float maximum = p[0];
+        const float difference = __fsub_rn(maximum, running);
+        const float factor = original_exp(-fabsf(difference));
+        const float old_scale = running > maximum ? 1.0f : factor;
+        const float new_scale = running > maximum ? factor : 1.0f;
+        const float old_total = __fmul_rn(total, old_scale);
+        total = __fmaf_rn(p[1], new_scale, old_total);
+        const float old = __fmul_rn(numerator, old_scale);
+        numerator = __fmaf_rn(p[2 + t], new_scale, old);
+        running = running < maximum ? maximum : running;
+    }
+    const float reciprocal = __fdiv_rn(1.0f, total);
+    out[static_cast<size_t>(row) * WIDTH + head * HW + t] = to_bf16(__fmul_rn(numerator, reciprocal));
+}
+} // namespace
+
+size_t attention_partials_bytes(int rows, int max_time)
+{
+    const int blocks = (max_time + BLOCK - 1) / BLOCK;
+    return static_cast<size_t>(rows) * HEADS * blocks * PSTRIDE * sizeof(float);
+}
+
+void attention(const std::uint16_t* query, const RowMeta* meta, const std::uint16_t* cache_k,
+               const std::uint16_t* cache_v, int rows, int max_time, float* partials,
+               std::uint16_t* out, cudaStream_t stream)
+{
+    if (rows <= 0)
+        return;
+    const int blocks = (max_time + BLOCK - 1) / BLOCK;
+    attention_block_kernel<<<dim3(rows * HEADS, blocks), 128, 0, stream>>>(query, meta, cache_k,
+                                                                          cache_v, blocks, partials);
+    attention_combine_kernel<<<rows * HEADS, 128, 0, stream>>>(meta, partials, blocks, out);
+}
+} // namespace tsacb::dev

@@ -1,0 +1,469 @@
+// DAC analysis/synthesis kernels and the residual vector quantizer.
+//
+// Reference arithmetic restated (reference project paths):
+//   scalar::Conv1d::sample   src/scalar/dsp.cpp:11-35 (serial unfused mul+add over
+//                            (tap, input channel), invalid taps skipped, + bias)
+//   source_frame geometry    src/common/dsp.tpp:141-178
+//   Snake / dac_sine_squared src/scalar/dsp.cpp:55-119, epsilon 0x3089705f
+//                            (src/weights/normalization.hpp:9)
+//   residual unit add        src/common/analysis.tpp:59-66, synthesis.tpp:59-66
+//   RVQ encode               src/common/rvq.tpp:37-57, src/common/rvq.cpp:126-146,
+//                            src/weights/preparation.cpp:69-114
+//   RVQ decode               src/common/rvq.cpp:76-120
+//
+// B200 mapping of the exact-order convolution: the reference's per-output
+// serial chain is kept (products and sums rounded separately, taps outer,
+// input channels inner), and parallelism comes from outputs.  A CTA owns a
+// 128-frame x 64-channel output tile, 256 threads each accumulating 8 frames x
+// 4 channels in registers; per (tap, 32-channel chunk) it stages the needed
+// input rows and the weight slice in shared memory, so every staged value is
+// reused 4x (inputs) or 8x (weights) from registers.  Device weights are laid
+// out [tap][in][out] so the weight slice loads are contiguous.
+#include "kernels/dac.cuh"
+#include "kernels/numeric.cuh"
+
+namespace tsacb::dev
+{
+namespace
+{
+__device__ __forceinline__ float sine_squared(float phase)
+{
+    const float reduced = __fmul_rn(phase, __uint_as_float(0x3f22f983u));
+    const float quadrant = rintf(reduced); // ties to even
+    const int q = (quadrant >= -2147483648.0f && quadrant < 2147483648.0f)
+                      ? static_cast<int>(quadrant)
+                      : INT_MIN;
+    float x = __fmaf_rn(quadrant, __uint_as_float(0xbfc90000u), phase);
+    x = __fmaf_rn(quadrant, __uint_as_float(0xb9fdaa22u), x);
+    const float x2 = __fmul_rn(x, x);
+    float value;
+    if ((q & 1) == 0)
+    {
+        float p = __fmaf_rn(__uint_as_float(0xb94ca1f9u), x2, __uint_as_float(0x3c08839eu));
+        p = __fmaf_rn(p, x2, __uint_as_float(0xbe2aaaa3u));
+        const float cube = __fmul_rn(x, x2);
+        value = __fmaf_rn(cube, p, x);
+    }
+    else
+    {
+        float p = __fmaf_rn(__uint_as_float(0x37ccf5ceu), x2, __uint_as_float(0xbab6061au));
+        p = __fmaf_rn(p, x2, __uint_as_float(0x3d2aaaa5u));
+        p = __fmaf_rn(p, x2, __uint_as_float(0xbf000000u));
+        value = __fmaf_rn(p, x2, 1.0f);
+    }
+    return __fmul_rn(value, value);
+}
+
+__global__ void snake_kernel(const float* __restrict__ x, const float* __restrict__ alpha,
+                             int channels, long long count, float* __restrict__ y,
+                             unsigned* error_word)
+{
+    const float eps = __uint_as_float(0x3089705fu);
+    bool ok = true;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+    {
+        const float a = alpha[i % channels];
+        const float v = x[i];
+        const float phase = __fmul_rn(a, v);
+        ok = ok && isfinite(v) && isfinite(phase);
+        const float out = __fadd_rn(v, __fdiv_rn(sine_squared(phase), __fadd_rn(a, eps)));
+        ok = ok && isfinite(out);
+        y[i] = out;
+    }
+    if (!ok && error_word)
+        atomicOr(error_word, error_nonfinite);
+}
+
+constexpr int TF = 128, TO = 64, CK = 32;
+
+// Output frame of tile row r and the input frame feeding it through `tap`.
+struct TileGeometry
+{
+    int f_first; // ordinary: first output frame; transposed: first phase index i0
+    int phase;
+    __device__ __forceinline__ int out_frame(const ConvShape& s, int r) const
+    {
+        return s.transposed ? phase + s.stride * (f_first + r) : f_first + r;
+    }
+    __device__ __forceinline__ int in_frame(const ConvShape& s, int r, int tap) const
+    {
+        if (s.transposed)
+        {
+            return f_first + r + (phase + s.padding - tap) / s.stride;
+        }
+        return (f_first + r) * s.stride + tap * s.dilation - s.padding;
+    }
+};
+
+__global__ void __launch_bounds__(256)
+    conv1d_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                  const float* __restrict__ bias, const float* __restrict__ residual,
+                  float* __restrict__ y, const Sequence* __restrict__ sequences,
+                  const int4* __restrict__ tiles, ConvShape s, unsigned* error_word)
+{
+    __shared__ float xs[TF][CK + 1];
+    __shared__ __align__(16) float ws[CK][TO];
+    const int4 tile = tiles[blockIdx.x];
+    const Sequence seq = sequences[tile.x];
+    const TileGeometry g{tile.y, tile.z};
+    const int o0 = blockIdx.y * TO;
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    float sum[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            sum[i][j] = 0.0f;
+    // Taps in ascending order; a transposed tile uses its phase's two taps.
+    const int tap_count = s.transposed ? 2 : s.kernel;
+    const int tap_first = s.transposed ? (g.phase + s.padding) % s.stride : 0;
+    for (int ti = 0; ti < tap_count; ++ti)
+    {
+        const int tap = s.transposed ? tap_first + ti * s.stride : ti;
+        unsigned valid = 0; // bit i: this thread's frame row ty*8+i takes this tap
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+        {
+            const int r = ty * 8 + i;
+            const int src = g.in_frame(s, r, tap);
+            const int f = g.out_frame(s, r);
+            if (f < seq.out_frames && src >= 0 && src < seq.in_frames &&
+                (!s.transposed || f + s.padding >= tap))
+                valid |= 1u << i;
+        }
+        const bool any = __syncthreads_or(valid != 0);
+        if (!any)
+            continue;
+        const bool all = __syncthreads_and(valid == 0xffu);
+        for (int c0 = 0; c0 < s.cin; c0 += CK)
+        {
+            const int cn = s.cin - c0 < CK ? s.cin - c0 : CK;
+            // Stage input rows (zeros where the tap is invalid; never added).
+            for (int e = tid; e < TF * CK; e += 256)
+            {
+                const int c = e & (CK - 1), r = e >> 5;
+                const int src = g.in_frame(s, r, tap);
+                float v = 0.0f;
+                if (c < cn && src >= 0 && src < seq.in_frames)
+                    v = x[static_cast<size_t>(seq.in_offset + src) * s.cin + c0 + c];
+                xs[r][c] = v;
+            }
+            for (int e = tid; e < CK * TO; e += 256)
+            {
+                const int o = e & (TO - 1), c = e >> 6;
+                float v = 0.0f;
+                if (c < cn && o0 + o < s.cout)
+                    v = w[(static_cast<size_t>(tap) * s.cin + c0 + c) * s.cout + o0 + o];
+                ws[c][o] = v;
+            }
+            __syncthreads();
+            if (all)
+            {
+#pragma unroll 4
+                for (int c = 0; c < cn; ++c)
+                {
+                    const float4 wv = *reinterpret_cast<const float4*>(&ws[c][tx * 4]);
+                    const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                    {
+                        const float xv = xs[ty * 8 + i][c];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            sum[i][j] = __fadd_rn(sum[i][j], __fmul_rn(xv, wa[j]));
+                    }
+                }
+            }
+            else
+            {
+#pragma unroll 2
+                for (int c = 0; c < cn; ++c)
+                {
+                    const float4 wv = *reinterpret_cast<const float4*>(&ws[c][tx * 4]);
+                    const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                    {
+                        const float xv = xs[ty * 8 + i][c];
+                        const bool take = (valid >> i) & 1u;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                        {
+                            const float n = __fadd_rn(sum[i][j], __fmul_rn(xv, wa[j]));
+                            sum[i][j] = take ? n : sum[i][j];
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+    {
+        const int f = g.out_frame(s, ty * 8 + i);
+        if (f >= seq.out_frames)
+            continue;
+        const size_t row = static_cast<size_t>(seq.out_offset + f) * s.cout;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+        {
+            const int o = o0 + tx * 4 + j;
+            if (o >= s.cout)
+                continue;
+            float v = __fadd_rn(sum[i][j], bias[o]);
+            if (residual)
+                v = __fadd_rn(residual[row + o], v);
+            ok = ok && isfinite(v);
+            y[row + o] = v;
+        }
+    }
+    if (!ok && error_word)
+        atomicOr(error_word, error_nonfinite);
+}
+
+// Narrow outputs (DAC exit convolution to 1-2 PCM channels): one thread per
+// output, the whole serial chain in registers.
+__global__ void conv1d_narrow_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                     const float* __restrict__ bias, float* __restrict__ y,
+                                     const Sequence* __restrict__ sequences, int sequence_count,
+                                     ConvShape s, long long total, unsigned* error_word)
+{
+    const long long id = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+    if (id >= total)
+        return;
+    // Locate the sequence by scanning (sequence counts are small).
+    long long rest = id;
+    int q = 0;
+    for (; q < sequence_count; ++q)
+    {
+        const long long n = static_cast<long long>(sequences[q].out_frames) * s.cout;
+        if (rest < n)
+            break;
+        rest -= n;
+    }
+    const Sequence seq = sequences[q];
+    const int f = static_cast<int>(rest / s.cout), o = static_cast<int>(rest % s.cout);
+    float sum = 0.0f;
+    for (int tap = 0; tap < s.kernel; ++tap)
+    {
+        const int src = f * s.stride + tap * s.dilation - s.padding;
+        if (src < 0 || src >= seq.in_frames)
+            continue;
+        const float* xr = x + static_cast<size_t>(seq.in_offset + src) * s.cin;
+        const float* wr = w + static_cast<size_t>(tap) * s.cin * s.cout + o;
+        for (int c = 0; c < s.cin; ++c)
+            sum = __fadd_rn(sum, __fmul_rn(xr[c], wr[static_cast<size_t>(c) * s.cout]));
+    }
+    const float v = __fadd_rn(sum, bias[o]);
+    if (!isfinite(v) && error_word)
+        atomicOr(error_word, error_nonfinite);
+    y[static_cast<size_t>(seq.out_offset + f) * s.cout + o] = v;
+}
+
+// ---------------------------------------------------------------- RVQ ----
+struct ArgMax
+{
+    float value;
+    int index;
+};
+
+// Strict `>` over ascending indices keeps the lowest index among equal maxima.
+__device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b)
+{
+    return (a.value < b.value || (a.value == b.value && b.index < a.index)) ? b : a;
+}
+
+__global__ void __launch_bounds__(256)
+    rvq_encode_kernel(const float* __restrict__ latent, const RvqBookDevice* __restrict__ books,
+                      int book_count, std::uint16_t* __restrict__ tokens, int token_stride,
+                      unsigned* error_word)
+{
+    __shared__ float residual[1024];
+    __shared__ float projected[8];
+    __shared__ float query[8];
+    __shared__ ArgMax warp_best[8];
+    __shared__ int selected;
+    const int frame = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    for (int i = t; i < 1024; i += 256)
+        residual[i] = latent[static_cast<size_t>(frame) * 1024 + i];
+    __syncthreads();
+    bool ok = true;
+    for (int b = 0; b < book_count; ++b)
+    {
+        const RvqBookDevice book = books[b];
+        // In-projection 1024 -> 8: eight serial chains (one per output, lane 0 of warps 0-7).
+        if (lane == 0)
+        {
+            const float* wr = book.input_weights + warp * 1024;
+            float sum = 0.0f;
+            for (int i = 0; i < 1024; ++i)
+                sum = __fadd_rn(sum, __fmul_rn(residual[i], wr[i]));
+            projected[warp] = __fadd_rn(sum, book.input_bias[warp]);
+        }
+        __syncthreads();
+        if (t == 0)
+        {
+            // normalize_search: pair tree of squares, RMS with epsilon 0x2b8cbccc.
+            float sq[8];
+            for (int i = 0; i < 8; ++i)
+                sq[i] = __fmul_rn(projected[i], projected[i]);
+            for (int width = 8; width > 1; width /= 2)
+                for (int i = 0; i < width / 2; ++i)
+                    sq[i] = __fadd_rn(sq[2 * i], sq[2 * i + 1]);
+            ok = ok && isfinite(sq[0]);
+            const float mean = __fmul_rn(sq[0], 0.125f);
+            const float inverse_rms =
+                __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, __uint_as_float(0x2b8cbcccu))));
+            const float inverse_width = __fdiv_rn(1.0f, __fsqrt_rn(8.0f));
+            for (int i = 0; i < 8; ++i)
+                query[i] = __fmul_rn(__fmul_rn(projected[i], inverse_rms), inverse_width);
+        }
+        __syncthreads();
+        ArgMax best{-INFINITY, 1 << 20};
+        for (int index = t; index < 1024; index += 256)
+        {
+            const float* v = book.search + index * 8;
+            float similarity = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                similarity = __fmaf_rn(v[i], query[i], similarity);
+            // Candidates that never exceed -inf (NaN) are never selected, as in the reference.
+            if (similarity > -INFINITY || index == 0)
+                best = better(best, ArgMax{similarity > -INFINITY ? similarity : -INFINITY, index});
+        }
+#pragma unroll
+        for (int offset = 16; offset > 0; offset >>= 1)
+        {
+            ArgMax other{__shfl_xor_sync(0xffffffffu, best.value, offset),
+                         __shfl_xor_sync(0xffffffffu, best.index, offset)};
+            best = better(best, other);
+        }
+        if (lane == 0)
+            warp_best[warp] = best;
+        __syncthreads();
+        if (t == 0)
+        {
+            ArgMax all = warp_best[0];
+            for (int i = 1; i < 8; ++i)
+                all = better(all, warp_best[i]);
+            // A reference search that never passes -inf keeps index 0.
+            selected = all.value > -INFINITY ? all.index : 0;
+            tokens[static_cast<size_t>(frame) * token_stride + b] =
+                static_cast<std::uint16_t>(selected);
+        }
+        __syncthreads();
+        const float* cb = book.codebook + selected * 8;
+        for (int j = t; j < 1024; j += 256)
+        {
+            const float* wr = book.output_weights + j * 8;
+            float sum = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                sum = __fmaf_rn(wr[i], cb[i], sum);
+            const float contribution = __fadd_rn(sum, book.output_bias[j]);
+            residual[j] = __fsub_rn(residual[j], contribution);
+            ok = ok && isfinite(residual[j]);
+        }
+        __syncthreads();
+    }
+    if (!__syncthreads_and(ok) && t == 0 && error_word)
+        atomicOr(error_word, error_nonfinite);
+}
+
+__global__ void rvq_decode_kernel(const std::uint16_t* __restrict__ tokens, int token_stride,
+                                  const RvqBookDevice* __restrict__ books, int book_count,
+                                  float* __restrict__ latent)
+{
+    const int frame = blockIdx.x;
+    for (int j = threadIdx.x; j < 1024; j += blockDim.x)
+    {
+        float acc = 0.0f;
+        for (int b = 0; b < book_count; ++b)
+        {
+            const RvqBookDevice book = books[b];
+            const int token = tokens[static_cast<size_t>(frame) * token_stride + b] & 1023;
+            const float* wr = book.output_weights + j * 8;
+            const float* cb = book.codebook + token * 8;
+            float sum = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                sum = __fmaf_rn(wr[i], cb[i], sum);
+            acc = __fadd_rn(acc, __fadd_rn(sum, book.output_bias[j]));
+        }
+        latent[static_cast<size_t>(frame) * 1024 + j] = acc;
+    }
+}
+
+__global__ void check_finite_kernel(const float* __restrict__ x, long long count,
+                                    unsigned* error_word)
+{
+    bool ok = true;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        ok = ok && isfinite(x[i]);
+    if (!ok)
+        atomicOr(error_word, error_nonfinite);
+}
+} // namespace
+
+void snake(const float* x, const float* alpha, int channels, long long frames, float* y,
+           unsigned* error_word, cudaStream_t stream)
+{
+    const long long count = frames * channels;
+    if (count <= 0)
+        return;
+    long long blocks = (count + 255) / 256;
+    blocks = blocks > 148 * 16 ? 148 * 16 : blocks;
+    snake_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(x, alpha, channels, count, y,
+                                                               error_word);
+}
+
+int conv_tile_frames(const ConvShape&)
+{
+    return TF;
+}
+
+void conv1d(const ConvLaunch& l, cudaStream_t stream)
+{
+    if (l.tile_count <= 0)
+        return;
+    const dim3 grid(l.tile_count, (l.shape.cout + TO - 1) / TO);
+    conv1d_kernel<<<grid, 256, 0, stream>>>(l.x, l.weights, l.bias, l.residual, l.y, l.sequences,
+                                            l.tiles, l.shape, l.error_word);
+}
+
+void conv1d_narrow(const float* x, const float* w, const float* bias, float* y,
+                   const Sequence* sequences, int sequence_count, const ConvShape& s,
+                   long long total_outputs, unsigned* error_word, cudaStream_t stream)
+{
+    if (total_outputs <= 0)
+        return;
+    conv1d_narrow_kernel<<<static_cast<int>((total_outputs + 127) / 128), 128, 0, stream>>>(
+        x, w, bias, y, sequences, sequence_count, s, total_outputs, error_word);
+}
+
+void rvq_encode(const float* latent, int frames, const RvqBookDevice* books, int book_count,
+                std::uint16_t* tokens, int token_stride, unsigned* error_word, cudaStream_t stream)
+{
+    if (frames > 0)
+        rvq_encode_kernel<<<frames, 256, 0, stream>>>(latent, books, book_count, tokens,
+                                                      token_stride, error_word);
+}
+
+void rvq_decode(const std::uint16_t* tokens, int token_stride, int frames,
+                const RvqBookDevice* books, int book_count, float* latent, cudaStream_t stream)
+{
+    if (frames > 0)
+        rvq_decode_kernel<<<frames, 256, 0, stream>>>(tokens, token_stride, books, book_count,
+                                                      latent);
+}
+
+void check_finite(const float* x, long long count, unsigned* error_word, cudaStream_t stream)
+{
+    if (count > 0)
+        check_finite_kernel<<<148 * 4, 256, 0, stream>>>(x, count, error_word);
+}
+} // namespace tsacb::dev

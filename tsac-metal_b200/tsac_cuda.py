@@ -88,3 +88,224 @@ def seeded_package(seed: int = 0) -> pathlib.Path:
     if not marker.exists():
         tmp.rename(package)
     return package
+
+
+# ------------------------------------------------------------ kernel calls --
+# Thin wrappers over the per-kernel C-ABI entry points.  Arguments are torch
+# CUDA tensors (torch supplies device memory and streams; the arithmetic is
+# entirely in this library's kernels).
+def _dev(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _stream():
+    import torch
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def qlinear_scratch_bytes(m: int, k: int) -> int:
+    lib = library()
+    lib.tsac_cuda_qlinear_scratch_bytes.restype = ctypes.c_size_t
+    return lib.tsac_cuda_qlinear_scratch_bytes(ctypes.c_size_t(m), ctypes.c_size_t(k))
+
+
+def qlinear(weights, scales, bias, x, y, scratch, residual=None, error_word=None):
+    """y[m][n] = bf16(W x + b) (+residual), all tensors on the device."""
+    n, k = weights.shape
+    m = x.shape[0]
+    check(library().tsac_cuda_qlinear(
+        _dev(weights), _dev(scales), _dev(bias), ctypes.c_size_t(k), ctypes.c_size_t(n), _dev(x),
+        ctypes.c_size_t(m), _dev(residual), _dev(y), _dev(scratch),
+        ctypes.c_size_t(scratch.numel() * scratch.element_size()), _dev(error_word), _stream()))
+
+
+# --------------------------------------------------------------- analyzer --
+@dataclasses.dataclass
+class EncodeOptions:
+    """tsac::EncodeOptions (include/tsac/audio_analyzer.hpp:16-22)."""
+    method: str = "normal"          # "normal" or "fast"
+    codebooks: int = 0              # 0: model maximum
+    separate_channels: bool = False
+    entropy_batch: int | None = None  # None: automatic
+
+
+class _Options(ctypes.Structure):
+    _fields_ = [("method", ctypes.c_int), ("codebooks", ctypes.c_uint),
+                ("separate_channels", ctypes.c_int), ("entropy_batch", ctypes.c_int)]
+
+
+def _options(o: EncodeOptions | None) -> _Options:
+    o = o or EncodeOptions()
+    if o.method not in ("normal", "fast"):
+        raise TsacError("invalid coding method")
+    return _Options(1 if o.method == "normal" else 0, o.codebooks,
+                    1 if o.separate_channels else 0, o.entropy_batch or 0)
+
+
+@dataclasses.dataclass
+class PcmAudio:
+    """tsac::PcmAudio: interleaved float32 samples [frames][channels]."""
+    samples: np.ndarray
+    channels: int
+
+
+def _take(ptr, count, dtype):
+    """Copy a library-allocated buffer into numpy and free it."""
+    lib = library()
+    if count:
+        arr = np.ctypeslib.as_array(ctypes.cast(ptr, ctypes.POINTER(np.ctypeslib.as_ctypes_type(dtype))),
+                                    shape=(count,)).copy()
+    else:
+        arr = np.zeros(0, dtype)
+    lib.tsac_cuda_free(ptr)
+    return arr
+
+
+class CudaAnalyzer:
+    """B200 implementation of tsac::AudioAnalyzer (include/tsac/audio_analyzer.hpp:30-37).
+
+    Calls are synchronous; one instance is used by one thread at a time.
+    """
+
+    def __init__(self, package: os.PathLike, device: int = 0):
+        lib = library()
+        self._ctx = ctypes.c_void_p()
+        check(lib.tsac_cuda_context_create(str(package).encode(), device, ctypes.byref(self._ctx)))
+
+    def close(self):
+        if self._ctx:
+            library().tsac_cuda_context_destroy(self._ctx)
+            self._ctx = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def encode(self, pcm: np.ndarray, options: EncodeOptions | None = None,
+               with_bits: bool = False):
+        """pcm: float32 [samples][channels] (interleaved) or any 2-D strided view."""
+        pcm = np.asarray(pcm, dtype=np.float32)
+        if pcm.ndim == 1:
+            pcm = pcm[:, None]
+        samples, channels = pcm.shape
+        out = ctypes.c_void_p()
+        nbytes, bits = ctypes.c_size_t(), ctypes.c_size_t()
+        opts = _options(options)
+        check(library().tsac_cuda_encode(
+            self._ctx, pcm.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(channels),
+            ctypes.c_size_t(samples), ctypes.c_ssize_t(pcm.strides[1] // 4),
+            ctypes.c_ssize_t(pcm.strides[0] // 4), ctypes.byref(opts), ctypes.byref(out),
+            ctypes.byref(nbytes), ctypes.byref(bits)))
+        data = _take(out, nbytes.value, np.uint8).tobytes()
+        return (data, bits.value) if with_bits else data
+
+    def decode(self, stream: bytes) -> PcmAudio:
+        out = ctypes.c_void_p()
+        samples, channels = ctypes.c_size_t(), ctypes.c_uint()
+        check(library().tsac_cuda_decode(self._ctx, stream, ctypes.c_size_t(len(stream)),
+                                         ctypes.byref(out), ctypes.byref(samples),
+                                         ctypes.byref(channels)))
+        data = _take(out, samples.value, np.float32)
+        return PcmAudio(data.reshape(-1, channels.value), channels.value)
+
+    def encode_batch(self, pcms, options: EncodeOptions | None = None):
+        pcms = [np.ascontiguousarray(p, dtype=np.float32).reshape(p.shape[0], -1) for p in pcms]
+        n = len(pcms)
+        ptrs = (ctypes.c_void_p * n)(*[p.ctypes.data for p in pcms])
+        chans = (ctypes.c_size_t * n)(*[p.shape[1] for p in pcms])
+        sams = (ctypes.c_size_t * n)(*[p.shape[0] for p in pcms])
+        outs = (ctypes.c_void_p * n)()
+        sizes = (ctypes.c_size_t * n)()
+        opts = _options(options)
+        check(library().tsac_cuda_encode_batch(self._ctx, ctypes.c_size_t(n), ptrs, chans, sams,
+                                               ctypes.byref(opts), outs, sizes))
+        return [_take(ctypes.c_void_p(outs[i]), sizes[i], np.uint8).tobytes() for i in range(n)]
+
+    def decode_batch(self, streams):
+        n = len(streams)
+        bufs = [ctypes.create_string_buffer(s, len(s)) for s in streams]
+        ptrs = (ctypes.c_void_p * n)(*[ctypes.addressof(b) for b in bufs])
+        sizes = (ctypes.c_size_t * n)(*[len(s) for s in streams])
+        outs = (ctypes.c_void_p * n)()
+        samples = (ctypes.c_size_t * n)()
+        chans = (ctypes.c_uint * n)()
+        check(library().tsac_cuda_decode_batch(self._ctx, ctypes.c_size_t(n), ptrs, sizes, outs,
+                                               samples, chans))
+        return [PcmAudio(_take(ctypes.c_void_p(outs[i]), samples[i], np.float32)
+                         .reshape(-1, chans[i]), chans[i]) for i in range(n)]
+
+    # ---- pipeline stages (parity tests) ---------------------------------
+    def analyze_tokens(self, pcm: np.ndarray, options: EncodeOptions | None = None):
+        pcm = np.ascontiguousarray(pcm, dtype=np.float32).reshape(pcm.shape[0], -1)
+        out = ctypes.c_void_p()
+        count = ctypes.c_size_t()
+        opts = _options(options)
+        check(library().tsac_cuda_analyze_tokens(
+            self._ctx, pcm.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(pcm.shape[1]),
+            ctypes.c_size_t(pcm.shape[0]), ctypes.byref(opts), ctypes.byref(out),
+            ctypes.byref(count)))
+        return _take(out, count.value, np.uint16)
+
+    def dac_analysis(self, channels: int, pcm: np.ndarray) -> np.ndarray:
+        pcm = np.ascontiguousarray(pcm, dtype=np.float32)
+        frames = pcm.size // channels
+        latent = np.zeros((frames // 512, 1024), np.float32)
+        check(library().tsac_cuda_dac_analysis(self._ctx, channels, pcm.ctypes.data_as(ctypes.c_void_p),
+                                                ctypes.c_size_t(frames),
+                                                latent.ctypes.data_as(ctypes.c_void_p)))
+        return latent
+
+    def dac_synthesis(self, channels: int, latent: np.ndarray) -> np.ndarray:
+        latent = np.ascontiguousarray(latent, dtype=np.float32)
+        frames = latent.size // 1024
+        pcm = np.zeros((frames * 512, channels), np.float32)
+        check(library().tsac_cuda_dac_synthesis(self._ctx, channels,
+                                                 latent.ctypes.data_as(ctypes.c_void_p),
+                                                 ctypes.c_size_t(frames),
+                                                 pcm.ctypes.data_as(ctypes.c_void_p)))
+        return pcm
+
+    def rvq_encode(self, channels: int, books: int, latent: np.ndarray) -> np.ndarray:
+        latent = np.ascontiguousarray(latent, dtype=np.float32)
+        frames = latent.size // 1024
+        tokens = np.zeros((frames, books), np.uint16)
+        check(library().tsac_cuda_rvq_encode(self._ctx, channels, books,
+                                             latent.ctypes.data_as(ctypes.c_void_p),
+                                             ctypes.c_size_t(frames),
+                                             tokens.ctypes.data_as(ctypes.c_void_p)))
+        return tokens
+
+    def rvq_decode(self, channels: int, books: int, tokens: np.ndarray) -> np.ndarray:
+        tokens = np.ascontiguousarray(tokens, dtype=np.uint16)
+        frames = tokens.size // books
+        latent = np.zeros((frames, 1024), np.float32)
+        check(library().tsac_cuda_rvq_decode(self._ctx, channels, books,
+                                             tokens.ctypes.data_as(ctypes.c_void_p),
+                                             ctypes.c_size_t(frames),
+                                             latent.ctypes.data_as(ctypes.c_void_p)))
+        return latent
+
+    def transformer_probabilities(self, channels, groups, books, frames, batch, tokens,
+                                  probabilities=True):
+        tokens = np.ascontiguousarray(tokens, dtype=np.uint16)
+        symbols = frames * groups * books
+        probs = np.zeros((symbols, 1024), np.float32) if probabilities else None
+        q15 = np.zeros((symbols, 10), np.uint16)
+        check(library().tsac_cuda_transformer_probabilities(
+            self._ctx, channels, groups, books, ctypes.c_size_t(frames), batch,
+            tokens.ctypes.data_as(ctypes.c_void_p),
+            probs.ctypes.data_as(ctypes.c_void_p) if probs is not None else None,
+            q15.ctypes.data_as(ctypes.c_void_p)))
+        return probs, q15
+
+    def pack_normal(self, channels, groups, books, frames, batch, tokens) -> bytes:
+        tokens = np.ascontiguousarray(tokens, dtype=np.uint16)
+        out = ctypes.c_void_p()
+        nbytes = ctypes.c_size_t()
+        check(library().tsac_cuda_pack_normal(self._ctx, channels, groups, books,
+                                              ctypes.c_size_t(frames), batch,
+                                              tokens.ctypes.data_as(ctypes.c_void_p),
+                                              ctypes.byref(out), ctypes.byref(nbytes)))
+        return _take(out, nbytes.value, np.uint8).tobytes()
