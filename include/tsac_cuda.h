@@ -104,6 +104,23 @@ int tsac_cuda_decode_batch(tsac_cuda_context* context, size_t count,
                            const uint8_t* const* streams, const size_t* bytes, float** out,
                            size_t* samples, unsigned* channels);
 
+/* HBM-resident forms of the batched calls: PCM inputs are device pointers
+ * (interleaved [sample][channel] floats); decoded PCM is written to
+ * caller-allocated device buffers of channels x samples_per_channel floats
+ * (sizes from tsac_cuda_stream_info).  Streams stay host byte buffers. */
+int tsac_cuda_encode_batch_device(tsac_cuda_context* context, size_t count,
+                                  const float* const* pcm_device, const size_t* channels,
+                                  const size_t* samples, const tsac_cuda_encode_options* options,
+                                  uint8_t** out, size_t* out_bytes);
+int tsac_cuda_decode_batch_device(tsac_cuda_context* context, size_t count,
+                                  const uint8_t* const* streams, const size_t* bytes,
+                                  float* const* pcm_device);
+
+/* parse_header (src/format/container.cpp:43-80): channels, padded samples per
+ * channel and symbol count of a stream, without decoding it. */
+int tsac_cuda_stream_info(const uint8_t* stream, size_t bytes, unsigned* channels,
+                          size_t* samples_per_channel, size_t* symbols);
+
 /* ---- pipeline stages (host buffers; synchronous) ----------------------- */
 
 /* Encoder front end: padding, 400-frame chunks with 8/9 context, DAC analysis
@@ -148,6 +165,16 @@ int tsac_cuda_transformer_probabilities(tsac_cuda_context* context, unsigned cha
 int tsac_cuda_pack_normal(tsac_cuda_context* context, unsigned channels, unsigned groups,
                           unsigned books, size_t frames, unsigned batch, const uint16_t* tokens,
                           uint8_t** out, size_t* out_bytes);
+
+/* ---- instrumentation --------------------------------------------------- */
+
+/* Enables (nonzero) or disables per-kernel-family timing: each launch family
+ * (conv_exact, conv_transposed, snake, qlinear_gemv, qlinear_gemm, attention,
+ * rvq_encode, ...) is bracketed by CUDA events on its stream; resets totals. */
+int tsac_cuda_kernel_timing(int enable);
+/* JSON {family: {"launches": n, "ms": total, "work": algorithmic FLOPs or bytes}}
+ * accumulated since the last tsac_cuda_kernel_timing call (free with tsac_cuda_free). */
+int tsac_cuda_kernel_stats(char** json);
 
 /* ---- kernel-level entry points (device pointers, enqueue on `stream`) -- */
 

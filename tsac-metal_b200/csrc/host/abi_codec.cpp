@@ -142,6 +142,63 @@ int tsac_cuda_decode_batch(tsac_cuda_context* ctx, size_t count, const uint8_t* 
         });
 }
 
+int tsac_cuda_stream_info(const uint8_t* stream, size_t bytes, unsigned* channels,
+                          size_t* samples_per_channel, size_t* symbols)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            tsacb::require(stream && channels && samples_per_channel, "null argument");
+            const auto h = tsacb::parse_header(tsacb::ByteView(stream, bytes));
+            *channels = static_cast<unsigned>(h.channels());
+            *samples_per_channel = h.samples_per_channel();
+            if (symbols)
+                *symbols = h.symbol_count();
+        });
+}
+
+int tsac_cuda_encode_batch_device(tsac_cuda_context* ctx, size_t count,
+                                  const float* const* pcm_device, const size_t* channels,
+                                  const size_t* samples, const tsac_cuda_encode_options* opts,
+                                  uint8_t** out, size_t* out_bytes)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            tsacb::require(ctx && pcm_device && channels && samples && out && out_bytes,
+                           "null argument");
+            std::vector<tsacb::PcmInput> inputs;
+            for (size_t i = 0; i < count; ++i)
+            {
+                auto p = pcm_input(pcm_device[i], channels[i], samples[i], 1,
+                                   static_cast<ptrdiff_t>(channels[i]));
+                p.device = true;
+                inputs.push_back(p);
+            }
+            auto r = tsacb::encode_batch(ctx->impl, inputs, options(opts), nullptr);
+            for (size_t i = 0; i < count; ++i)
+            {
+                out[i] = tsacb::malloc_copy(r[i].data(), r[i].size());
+                out_bytes[i] = r[i].size();
+            }
+        });
+}
+
+int tsac_cuda_decode_batch_device(tsac_cuda_context* ctx, size_t count,
+                                  const uint8_t* const* streams, const size_t* bytes,
+                                  float* const* pcm_device)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            tsacb::require(ctx && streams && bytes && pcm_device, "null argument");
+            std::vector<tsacb::ByteView> views;
+            for (size_t i = 0; i < count; ++i)
+                views.emplace_back(streams[i], bytes[i]);
+            tsacb::decode_batch(ctx->impl, views, pcm_device);
+        });
+}
+
 int tsac_cuda_analyze_tokens(tsac_cuda_context* ctx, const float* pcm, size_t channels,
                              size_t samples, const tsac_cuda_encode_options* opts,
                              uint16_t** tokens, size_t* count)
@@ -223,7 +280,7 @@ int tsac_cuda_dac_analysis(tsac_cuda_context* ctx, unsigned channels, const floa
             auto d_pcm = to_device(pcm, pcm_frames * channels, s);
             const auto frames = pcm_frames / 512;
             tsacb::DeviceBuffer d_lat(frames * 1024 * 4);
-            dac.analyze(d_pcm.as<float>(), {static_cast<int>(frames)}, d_lat.as<float>());
+            dac.analyze(d_pcm.as<float>(), {0}, {static_cast<int>(frames)}, d_lat.as<float>());
             tsacb::cuda_ok(cudaMemcpyAsync(latent, d_lat.as<void>(), frames * 1024 * 4,
                                            cudaMemcpyDeviceToHost, s),
                            "D2H");

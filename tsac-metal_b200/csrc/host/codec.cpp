@@ -1,8 +1,13 @@
 #include "codec.hpp"
 
 #include "dac_engine.hpp"
+#include "kernels/dac.cuh"
 
 #include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
 #include <future>
 #include <thread>
 
@@ -30,12 +35,13 @@ std::size_t audio_chunk_frames(std::size_t target, const Limits& limits)
     return std::min(target, available > 22 ? available - 22 : std::size_t{1});
 }
 
-// Windows per DAC launch group (bounds device memory; ~250 MB per window).
+// Windows per DAC launch group: bounds device scratch (~250 MB per window).
 constexpr std::size_t window_group = 48;
 
 template <class F> void parallel_for(std::size_t n, F&& f)
 {
-    const std::size_t workers = std::max<std::size_t>(1, std::min<std::size_t>(n, std::thread::hardware_concurrency()));
+    const std::size_t workers =
+        std::max<std::size_t>(1, std::min<std::size_t>(n, std::thread::hardware_concurrency()));
     if (workers <= 1)
     {
         for (std::size_t i = 0; i < n; ++i)
@@ -56,73 +62,128 @@ template <class F> void parallel_for(std::size_t n, F&& f)
     for (auto& j : jobs)
         j.get();
 }
-} // namespace
 
-Header audio_header(const PcmInput& pcm, const EncodeOptions& options, const Limits& limits)
+// Stage timing (TSAC_CUDA_PROFILE=1): synchronises the stream at each mark.
+class Profile
 {
-    const auto channels = pcm.channels, samples = pcm.samples;
-    require(channels > 0 && channels <= 127, "invalid PCM channel count");
-    require(pcm.channel_stride > 0 && pcm.sample_stride > 0, "invalid PCM strides");
-    require(samples == 0 || pcm.data != nullptr, "null PCM data");
-    require(checked_mul(samples, channels) <= limits.tensor_elements, "PCM exceeds element limit");
-    require(options.method == 0 || options.method == 1, "invalid coding method");
-    Header header;
-    header.method = static_cast<std::uint8_t>(options.method);
-    header.model_channels = channels == 2 && !options.separate_channels ? 2 : 1;
-    header.groups = static_cast<std::uint8_t>(channels / header.model_channels);
-    const unsigned maximum = header.model_channels == 2 ? 12 : 9;
-    require(options.codebooks <= maximum, "invalid number of codebooks for audio model");
-    header.codebooks = static_cast<std::uint8_t>(options.codebooks ? options.codebooks : maximum);
-    header.frames = checked_add(samples, 511) / 512;
-    require(options.entropy_batch >= 0, "zero entropy batch size");
-    require(header.method == 1 || options.entropy_batch == 0, "entropy batch requires normal coding");
-    if (header.method == 1)
+public:
+    Profile(cudaStream_t s, const char* name) : stream_(s), name_(name)
     {
-        header.batch = select_entropy_batch(header.frames, options.entropy_batch);
+        const char* e = std::getenv("TSAC_CUDA_PROFILE");
+        enabled_ = e && *e && *e != '0';
+        last_ = std::chrono::steady_clock::now();
     }
-    validate_header(header, limits);
-    require(checked_mul(header.samples_per_channel(), channels) <= limits.tensor_elements,
-            "padded PCM exceeds element limit");
-    return header;
-}
+    void mark(const char* stage)
+    {
+        if (!enabled_)
+            return;
+        cudaStreamSynchronize(stream_);
+        const auto now = std::chrono::steady_clock::now();
+        std::fprintf(stderr, "tsac_cuda %s %-22s %9.3f ms\n", name_, stage,
+                     std::chrono::duration<double, std::milli>(now - last_).count());
+        last_ = now;
+    }
 
-namespace
-{
-// detail::padded_audio: [group][sample][model channel], zero padded.
-std::vector<float> padded_audio(const PcmInput& pcm, const Header& header)
-{
-    const std::size_t mc = header.model_channels, spc = header.samples_per_channel();
-    std::vector<float> out(header.groups * spc * mc, 0.0f);
-    for (std::size_t g = 0; g < header.groups; ++g)
-        for (std::size_t f = 0; f < pcm.samples; ++f)
-            for (std::size_t c = 0; c < mc; ++c)
-            {
-                const float v = pcm.data[static_cast<std::ptrdiff_t>(g * mc + c) * pcm.channel_stride +
-                                         static_cast<std::ptrdiff_t>(f) * pcm.sample_stride];
-                require(std::isfinite(v), "nonfinite PCM sample");
-                out[(g * spc + f) * mc + c] = v;
-            }
-    return out;
-}
+private:
+    cudaStream_t stream_;
+    const char* name_;
+    bool enabled_ = false;
+    std::chrono::steady_clock::time_point last_;
+};
 
-struct AnalysisWindow
+struct Window
 {
     std::size_t recording, group;
     Chunk chunk;
 };
 
+void check_word(cudaStream_t s, unsigned* word, const char* message)
+{
+    unsigned host = 0;
+    cuda_ok(cudaMemcpyAsync(&host, word, 4, cudaMemcpyDeviceToHost, s), "D2H");
+    cuda_ok(cudaStreamSynchronize(s), message);
+    if (host)
+    {
+        cuda_ok(cudaMemsetAsync(word, 0, 4, s), "memset");
+        throw NumericError(message);
+    }
+}
+
+// padded_audio on the device for every recording of one variant, laid end to
+// end: recording r, group g starts at PCM row base[r] + g * padded_samples.
+DeviceBuffer padded_device(Context& ctx, const std::vector<PcmInput>& pcm,
+                           const std::vector<Header>& headers, std::vector<long long>& base,
+                           unsigned* error_word)
+{
+    auto s = ctx.stream();
+    long long rows = 0;
+    base.clear();
+    for (const auto& h : headers)
+    {
+        base.push_back(rows);
+        rows += static_cast<long long>(h.groups) * static_cast<long long>(h.samples_per_channel());
+    }
+    const unsigned mc = headers.empty() ? 1 : headers[0].model_channels;
+    DeviceBuffer out(static_cast<std::size_t>(rows) * mc * 4 + 4);
+    for (std::size_t r = 0; r < pcm.size(); ++r)
+    {
+        const auto& p = pcm[r];
+        const auto& h = headers[r];
+        const float* src = p.data;
+        long long cs = p.channel_stride, ss = p.sample_stride;
+        DeviceBuffer staged;
+        if (!p.device && p.samples)
+        {
+            // Host view -> contiguous interleaved device copy, then regroup there.
+            std::vector<float> packed;
+            const float* host = p.data;
+            if (!(cs == 1 && ss == static_cast<long long>(p.channels)))
+            {
+                packed.resize(p.samples * p.channels);
+                for (std::size_t f = 0; f < p.samples; ++f)
+                    for (std::size_t c = 0; c < p.channels; ++c)
+                        packed[f * p.channels + c] =
+                            p.data[static_cast<std::ptrdiff_t>(c) * p.channel_stride +
+                                   static_cast<std::ptrdiff_t>(f) * p.sample_stride];
+                host = packed.data();
+            }
+            staged.resize(p.samples * p.channels * 4);
+            cuda_ok(cudaMemcpyAsync(staged.as<void>(), host, p.samples * p.channels * 4,
+                                    cudaMemcpyHostToDevice, s),
+                    "H2D");
+            src = staged.as<float>();
+            cs = 1;
+            ss = static_cast<long long>(p.channels);
+        }
+        dev::pcm_regroup(src, static_cast<long long>(p.samples), cs, ss, h.groups, mc,
+                         static_cast<long long>(h.samples_per_channel()),
+                         out.as<float>() + base[r] * mc, error_word, s);
+        if (staged.bytes())
+        {
+            // The staging copy must finish before `staged` is released.
+            cuda_ok(cudaStreamSynchronize(s), "PCM upload");
+        }
+    }
+    return out;
+}
+
 // DAC analysis + RVQ for every recording of one model variant.
-void analyze_recordings(Context& ctx, const std::vector<const std::vector<float>*>& padded,
+void analyze_recordings(Context& ctx, const std::vector<PcmInput>& pcm,
                         const std::vector<Header>& headers,
-                        std::vector<std::vector<std::uint16_t>>& tokens)
+                        std::vector<std::vector<std::uint16_t>>& tokens, Profile& profile)
 {
     if (headers.empty())
         return;
     const unsigned mc = headers[0].model_channels;
     auto& dac = ctx.analysis(mc);
     auto& rvq = ctx.rvq(mc);
+    auto s = ctx.stream();
+    std::vector<long long> base;
+    auto padded = padded_device(ctx, pcm, headers, base, dac.error_word());
+    check_word(s, dac.error_word(), "nonfinite PCM sample");
+    profile.mark("pcm upload/pad");
     const auto chunk_frames = audio_chunk_frames(400, ctx.limits());
-    std::vector<AnalysisWindow> windows;
+    std::vector<Window> windows;
     for (std::size_t r = 0; r < headers.size(); ++r)
     {
         tokens[r].assign(headers[r].symbol_count(), 0);
@@ -134,38 +195,25 @@ void analyze_recordings(Context& ctx, const std::vector<const std::vector<float>
                 b += c.count;
             }
     }
-    auto s = ctx.stream();
     for (std::size_t w0 = 0; w0 < windows.size(); w0 += window_group)
     {
         const auto wn = std::min(window_group, windows.size() - w0);
         std::vector<int> frames;
-        std::size_t samples = 0, latent_frames = 0, central = 0;
-        for (std::size_t i = 0; i < wn; ++i)
-        {
-            const auto& c = windows[w0 + i].chunk;
-            frames.push_back(static_cast<int>(c.right - c.left));
-            samples += (c.right - c.left) * 512;
-            latent_frames += c.right - c.left;
-            central += c.count;
-        }
-        std::vector<float> host_pcm(samples * mc);
-        std::size_t at = 0;
+        std::vector<long long> offsets;
+        std::size_t latent_frames = 0, central = 0;
         for (std::size_t i = 0; i < wn; ++i)
         {
             const auto& w = windows[w0 + i];
             const auto& h = headers[w.recording];
-            const auto spc = h.samples_per_channel();
-            const auto n = (w.chunk.right - w.chunk.left) * 512 * mc;
-            std::copy_n(padded[w.recording]->data() + (w.group * spc + w.chunk.left * 512) * mc, n,
-                        host_pcm.data() + at);
-            at += n;
+            frames.push_back(static_cast<int>(w.chunk.right - w.chunk.left));
+            offsets.push_back(base[w.recording] +
+                              static_cast<long long>(w.group * h.samples_per_channel() +
+                                                     w.chunk.left * 512));
+            latent_frames += w.chunk.right - w.chunk.left;
+            central += w.chunk.count;
         }
-        DeviceBuffer d_pcm(host_pcm.size() * 4), d_latent(latent_frames * 1024 * 4),
-            d_central(central * 1024 * 4);
-        cuda_ok(cudaMemcpyAsync(d_pcm.as<void>(), host_pcm.data(), host_pcm.size() * 4,
-                                cudaMemcpyHostToDevice, s),
-                "H2D");
-        dac.analyze(d_pcm.as<float>(), frames, d_latent.as<float>());
+        DeviceBuffer d_latent(latent_frames * 1024 * 4), d_central(central * 1024 * 4);
+        dac.analyze(padded.as<float>(), offsets, frames, d_latent.as<float>());
         // Keep each window's central latents (src/common/audio_pipeline.hpp:49-56).
         std::size_t lat = 0, cen = 0;
         for (std::size_t i = 0; i < wn; ++i)
@@ -178,6 +226,7 @@ void analyze_recordings(Context& ctx, const std::vector<const std::vector<float>
             lat += c.right - c.left;
             cen += c.count;
         }
+        profile.mark("dac analysis");
         const int books = headers[0].codebooks;
         DeviceBuffer d_tok(central * static_cast<std::size_t>(books) * 2);
         rvq.encode(d_central.as<float>(), static_cast<int>(central), books,
@@ -186,16 +235,9 @@ void analyze_recordings(Context& ctx, const std::vector<const std::vector<float>
         cuda_ok(cudaMemcpyAsync(host_tok.data(), d_tok.as<void>(), host_tok.size() * 2,
                                 cudaMemcpyDeviceToHost, s),
                 "D2H");
-        unsigned words[2] = {0, 0};
-        cuda_ok(cudaMemcpyAsync(&words[0], dac.error_word(), 4, cudaMemcpyDeviceToHost, s), "D2H");
-        cuda_ok(cudaMemcpyAsync(&words[1], rvq.error_word(), 4, cudaMemcpyDeviceToHost, s), "D2H");
-        cuda_ok(cudaStreamSynchronize(s), "analysis");
-        if (words[0] || words[1])
-        {
-            cuda_ok(cudaMemsetAsync(dac.error_word(), 0, 4, s), "memset");
-            cuda_ok(cudaMemsetAsync(rvq.error_word(), 0, 4, s), "memset");
-            throw NumericError(words[0] ? "nonfinite DSP value" : "nonfinite RVQ residual");
-        }
+        check_word(s, dac.error_word(), "nonfinite DSP value");
+        check_word(s, rvq.error_word(), "nonfinite RVQ residual");
+        profile.mark("rvq encode");
         // store_tokens (src/common/audio_analyzer.cpp:164-172).
         cen = 0;
         for (std::size_t i = 0; i < wn; ++i)
@@ -210,23 +252,7 @@ void analyze_recordings(Context& ctx, const std::vector<const std::vector<float>
         }
     }
 }
-} // namespace
 
-std::vector<std::uint16_t> analyze_tokens(Context& ctx, const PcmInput& pcm,
-                                          const EncodeOptions& options, Header* header_out)
-{
-    ctx.bind();
-    const auto header = audio_header(pcm, options, ctx.limits());
-    const auto padded = padded_audio(pcm, header);
-    std::vector<std::vector<std::uint16_t>> tokens(1);
-    analyze_recordings(ctx, {&padded}, {header}, tokens);
-    if (header_out)
-        *header_out = header;
-    return std::move(tokens[0]);
-}
-
-namespace
-{
 Bytes range_code(const Header& h, std::span<const std::uint16_t> tok, const std::uint16_t* q,
                  const Limits& limits, std::size_t* bits)
 {
@@ -247,6 +273,47 @@ Bytes range_code(const Header& h, std::span<const std::uint16_t> tok, const std:
 }
 } // namespace
 
+Header audio_header(const PcmInput& pcm, const EncodeOptions& options, const Limits& limits)
+{
+    const auto channels = pcm.channels, samples = pcm.samples;
+    require(channels > 0 && channels <= 127, "invalid PCM channel count");
+    require(pcm.channel_stride > 0 && pcm.sample_stride > 0, "invalid PCM strides");
+    require(samples == 0 || pcm.data != nullptr, "null PCM data");
+    require(checked_mul(samples, channels) <= limits.tensor_elements, "PCM exceeds element limit");
+    require(options.method == 0 || options.method == 1, "invalid coding method");
+    Header header;
+    header.method = static_cast<std::uint8_t>(options.method);
+    header.model_channels = channels == 2 && !options.separate_channels ? 2 : 1;
+    header.groups = static_cast<std::uint8_t>(channels / header.model_channels);
+    const unsigned maximum = header.model_channels == 2 ? 12 : 9;
+    require(options.codebooks <= maximum, "invalid number of codebooks for audio model");
+    header.codebooks = static_cast<std::uint8_t>(options.codebooks ? options.codebooks : maximum);
+    header.frames = checked_add(samples, 511) / 512;
+    require(options.entropy_batch >= 0 && options.entropy_batch <= 65535, "invalid entropy batch size");
+    require(header.method == 1 || options.entropy_batch == 0, "entropy batch requires normal coding");
+    if (header.method == 1)
+    {
+        header.batch = select_entropy_batch(header.frames, options.entropy_batch);
+    }
+    validate_header(header, limits);
+    require(checked_mul(header.samples_per_channel(), channels) <= limits.tensor_elements,
+            "padded PCM exceeds element limit");
+    return header;
+}
+
+std::vector<std::uint16_t> analyze_tokens(Context& ctx, const PcmInput& pcm,
+                                          const EncodeOptions& options, Header* header_out)
+{
+    ctx.bind();
+    Profile profile(ctx.stream(), "analyze");
+    const auto header = audio_header(pcm, options, ctx.limits());
+    std::vector<std::vector<std::uint16_t>> tokens(1);
+    analyze_recordings(ctx, {pcm}, {header}, tokens, profile);
+    if (header_out)
+        *header_out = header;
+    return std::move(tokens[0]);
+}
+
 Bytes pack_normal(Context& ctx, Header header, std::span<const std::uint16_t> tokens,
                   std::size_t* bits)
 {
@@ -265,29 +332,26 @@ std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
                                 const EncodeOptions& options, std::vector<std::size_t>* bits)
 {
     ctx.bind();
+    Profile profile(ctx.stream(), "encode");
     const auto n = pcm.size();
     std::vector<Header> headers(n);
-    std::vector<std::vector<float>> padded(n);
     for (std::size_t i = 0; i < n; ++i)
-    {
         headers[i] = audio_header(pcm[i], options, ctx.limits());
-        padded[i] = padded_audio(pcm[i], headers[i]);
-    }
     std::vector<std::vector<std::uint16_t>> tokens(n);
     for (unsigned mc : {1u, 2u})
     {
         std::vector<std::size_t> ids;
-        std::vector<const std::vector<float>*> p;
+        std::vector<PcmInput> p;
         std::vector<Header> h;
         for (std::size_t i = 0; i < n; ++i)
             if (headers[i].model_channels == mc)
             {
                 ids.push_back(i);
-                p.push_back(&padded[i]);
+                p.push_back(pcm[i]);
                 h.push_back(headers[i]);
             }
         std::vector<std::vector<std::uint16_t>> t(ids.size());
-        analyze_recordings(ctx, p, h, t);
+        analyze_recordings(ctx, p, h, t, profile);
         for (std::size_t j = 0; j < ids.size(); ++j)
             tokens[ids[j]] = std::move(t[j]);
     }
@@ -307,22 +371,25 @@ std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
         ctx.transformer(headers[i].model_channels)
             .predict_known(headers[i], tokens[i], q15[i].data(), nullptr);
     }
+    profile.mark("transformer (known)");
     // Sequential range coding per recording on host cores (pack_normal,
     // src/format/entropy.cpp:57-123), recordings in parallel.
     parallel_for(n,
                  [&](std::size_t i)
                  {
-                     if (headers[i].method == 0)
-                         return;
-                     out[i] = range_code(headers[i], tokens[i], q15[i].data(), ctx.limits(),
-                                         bits ? &(*bits)[i] : nullptr);
+                     if (headers[i].method == 1)
+                         out[i] = range_code(headers[i], tokens[i], q15[i].data(), ctx.limits(),
+                                             bits ? &(*bits)[i] : nullptr);
                  });
+    profile.mark("range encode");
     return out;
 }
 
-std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>& streams)
+std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>& streams,
+                                       float* const* device_out)
 {
     ctx.bind();
+    Profile profile(ctx.stream(), "decode");
     const auto n = streams.size();
     std::vector<Header> headers(n);
     std::vector<std::vector<std::uint16_t>> tokens(n);
@@ -369,15 +436,17 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
                 std::vector<std::size_t> first(ids.size() + 1, rows.size());
                 for (std::size_t j = rows.size(); j-- > 0;)
                     first[static_cast<std::size_t>(rows[j].recording)] = j;
-                parallel_for(ids.size(),
-                             [&](std::size_t r)
-                             {
-                                 for (std::size_t j = first[r];
-                                      j < rows.size() && static_cast<std::size_t>(rows[j].recording) == r; ++j)
-                                 {
-                                     decoded[j] = decode_categorical_tree(decoders[r], masses.data() + j * 1023);
-                                 }
-                             });
+                const auto decode_one = [&](std::size_t r)
+                {
+                    for (std::size_t j = first[r];
+                         j < rows.size() && static_cast<std::size_t>(rows[j].recording) == r; ++j)
+                        decoded[j] = decode_categorical_tree(decoders[r], masses.data() + j * 1023);
+                };
+                if (ids.size() > 2)
+                    parallel_for(ids.size(), decode_one);
+                else
+                    for (std::size_t r = 0; r < ids.size(); ++r)
+                        decode_one(r);
                 for (std::size_t j = 0; j < rows.size(); ++j)
                 {
                     const auto r = static_cast<std::size_t>(rows[j].recording);
@@ -393,19 +462,33 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
         for (auto i : ids)
             verify_token_crc(headers[i], tokens[i]);
     }
+    profile.mark("transformer + range");
     // RVQ reconstruction + DAC synthesis over chunk windows
     // (src/common/audio_pipeline.hpp:63-83, context 11/11).
     std::vector<DecodedAudio> out(n);
+    std::vector<DeviceBuffer> owned(n);
+    std::vector<float*> dst(n);
     for (std::size_t i = 0; i < n; ++i)
     {
         out[i].channels = static_cast<unsigned>(headers[i].channels());
-        out[i].samples.assign(headers[i].channels() * headers[i].samples_per_channel(), 0.0f);
+        out[i].frames = headers[i].samples_per_channel();
+        const auto count = headers[i].channels() * headers[i].samples_per_channel();
+        require(count <= ctx.limits().tensor_elements, "output audio exceeds element limit");
+        if (device_out)
+        {
+            dst[i] = device_out[i];
+        }
+        else
+        {
+            owned[i].resize(count * 4 + 4);
+            dst[i] = owned[i].as<float>();
+        }
     }
     auto s = ctx.stream();
     const auto chunk_frames = audio_chunk_frames(400, ctx.limits());
     for (unsigned mc : {1u, 2u})
     {
-        std::vector<AnalysisWindow> windows;
+        std::vector<Window> windows;
         for (std::size_t i = 0; i < n; ++i)
         {
             if (headers[i].model_channels != mc)
@@ -437,7 +520,6 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
             }
             // Window tokens [frame][books] (chunk_tokens, src/common/audio_analyzer.cpp:174-183).
             std::vector<std::uint16_t> wt(total * static_cast<std::size_t>(books), 0);
-            std::vector<int> wbooks;
             std::size_t at = 0;
             for (std::size_t i = 0; i < wn; ++i)
             {
@@ -452,48 +534,54 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
             cuda_ok(cudaMemcpyAsync(d_tok.as<void>(), wt.data(), wt.size() * 2,
                                     cudaMemcpyHostToDevice, s),
                     "H2D");
-            // Windows of one group share the recording's book count (one variant per launch).
-            bool uniform = true;
-            for (std::size_t i = 1; i < wn; ++i)
-                uniform = uniform && headers[windows[w0 + i].recording].codebooks == books;
-            if (uniform)
-            {
-                rvq.decode(d_tok.as<std::uint16_t>(), books, static_cast<int>(total), books,
-                           d_latent.as<float>());
-            }
-            else
-            {
-                std::size_t off = 0;
-                for (std::size_t i = 0; i < wn; ++i)
-                {
-                    const auto& w = windows[w0 + i];
-                    const auto len = w.chunk.right - w.chunk.left;
-                    rvq.decode(d_tok.as<std::uint16_t>() + off * books, books, static_cast<int>(len),
-                               headers[w.recording].codebooks, d_latent.as<float>() + off * 1024);
-                    off += len;
-                }
-            }
-            dac.synthesize(d_latent.as<float>(), frames, d_pcm.as<float>());
-            std::vector<float> host_pcm(total * 512 * mc);
-            cuda_ok(cudaMemcpyAsync(host_pcm.data(), d_pcm.as<void>(), host_pcm.size() * 4,
-                                    cudaMemcpyDeviceToHost, s),
-                    "D2H");
-            dac.check_errors("synthesis");
-            // store_pcm (src/common/audio_analyzer.cpp:185-199).
             std::size_t off = 0;
+            for (std::size_t i = 0; i < wn;)
+            {
+                // Runs of windows with the same book count decode in one launch.
+                std::size_t j = i, len = 0;
+                const int q = headers[windows[w0 + i].recording].codebooks;
+                while (j < wn && headers[windows[w0 + j].recording].codebooks == q)
+                {
+                    len += windows[w0 + j].chunk.right - windows[w0 + j].chunk.left;
+                    ++j;
+                }
+                rvq.decode(d_tok.as<std::uint16_t>() + off * books, books, static_cast<int>(len), q,
+                           d_latent.as<float>() + off * 1024);
+                off += len;
+                i = j;
+            }
+            profile.mark("rvq decode");
+            dac.synthesize(d_latent.as<float>(), frames, d_pcm.as<float>());
+            // store_pcm (src/common/audio_analyzer.cpp:185-199): central samples
+            // of each window into the interleaved output, channel g*mc + c.
+            off = 0;
             for (std::size_t i = 0; i < wn; ++i)
             {
                 const auto& w = windows[w0 + i];
-                const auto& h = headers[w.recording];
-                auto& o = out[w.recording];
-                for (std::size_t sample = 0; sample < w.chunk.count * 512; ++sample)
-                    for (std::size_t c = 0; c < mc; ++c)
-                        o.samples[(w.chunk.begin * 512 + sample) * o.channels + w.group * mc + c] =
-                            host_pcm[(off + (w.chunk.begin - w.chunk.left) * 512 + sample) * mc + c];
+                const auto channels = headers[w.recording].channels();
+                cuda_ok(cudaMemcpy2DAsync(dst[w.recording] + w.chunk.begin * 512 * channels + w.group * mc,
+                                          channels * 4,
+                                          d_pcm.as<float>() + (off + (w.chunk.begin - w.chunk.left) * 512) * mc,
+                                          mc * 4, mc * 4, w.chunk.count * 512,
+                                          cudaMemcpyDeviceToDevice, s),
+                        "D2D");
                 off += (w.chunk.right - w.chunk.left) * 512;
-                (void)h;
             }
+            dac.check_errors("synthesis");
+            profile.mark("dac synthesis");
         }
+    }
+    if (!device_out)
+    {
+        for (std::size_t i = 0; i < n; ++i)
+        {
+            out[i].samples.resize(headers[i].channels() * headers[i].samples_per_channel());
+            cuda_ok(cudaMemcpyAsync(out[i].samples.data(), dst[i], out[i].samples.size() * 4,
+                                    cudaMemcpyDeviceToHost, s),
+                    "D2H");
+        }
+        cuda_ok(cudaStreamSynchronize(s), "decode");
+        profile.mark("pcm download");
     }
     return out;
 }

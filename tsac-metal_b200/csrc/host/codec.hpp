@@ -2,6 +2,11 @@
 // tsac::AudioAnalyzer (include/tsac/audio_analyzer.hpp:30-37), restating the
 // shared pipeline glue of the reference (src/common/audio_analyzer.cpp:79-209,
 // src/common/audio_pipeline.hpp:36-83, src/scalar/audio_analyzer.cpp:14-63).
+//
+// Data stay in HBM from PCM to latents to tokens: padded PCM is built by a
+// device kernel, analysis windows are addressed in place, decoded windows are
+// scattered straight into the output PCM.  Only tokens (encode) and the
+// range coder's per-symbol inputs cross to the host.
 #pragma once
 #include "context.hpp"
 #include "format.hpp"
@@ -16,18 +21,21 @@ struct EncodeOptions
     int entropy_batch = 0;     // 0: automatic
 };
 
-// Borrowed PCM view [channel, frame] with positive strides (in floats).
+// Borrowed PCM view [channel, frame] with positive strides (in floats), in
+// host memory or (device = true) in this context's GPU memory.
 struct PcmInput
 {
     const float* data = nullptr;
     std::size_t channels = 0, samples = 0;
     std::ptrdiff_t channel_stride = 1, sample_stride = 1;
+    bool device = false;
 };
 
 struct DecodedAudio
 {
-    std::vector<float> samples; // interleaved [sample][channel]
+    std::vector<float> samples; // interleaved [sample][channel] (host results only)
     unsigned channels = 1;
+    std::size_t frames = 0;     // samples per channel
 };
 
 Header audio_header(const PcmInput& pcm, const EncodeOptions& options, const Limits& limits);
@@ -35,7 +43,10 @@ Header audio_header(const PcmInput& pcm, const EncodeOptions& options, const Lim
 // Batched entry points (one call = many independent recordings).
 std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
                                 const EncodeOptions& options, std::vector<std::size_t>* bits);
-std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>& streams);
+// With device_out, recording i is written to device_out[i] (interleaved,
+// channels x padded samples floats) and DecodedAudio::samples stays empty.
+std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>& streams,
+                                       float* const* device_out = nullptr);
 
 // pack_normal (src/format/entropy.cpp:57-123) for known tokens with the GPU
 // predictor: header.method must be 1; returns the framed normal stream.

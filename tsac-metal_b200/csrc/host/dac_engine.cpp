@@ -1,5 +1,7 @@
 #include "dac_engine.hpp"
 
+#include "kernel_timer.hpp"
+
 #include <algorithm>
 #include <array>
 
@@ -73,12 +75,15 @@ void DacEngine::check_errors(const char* what)
 
 void DacEngine::snake(int index, const float* x, float* y, long long frames)
 {
+    KernelTimer::Scope timing("snake", stream_,
+                              8.0 * static_cast<double>(frames) * alpha_width_[static_cast<std::size_t>(index)]);
     dev::snake(x, alphas_[static_cast<std::size_t>(index)].as<float>(),
                alpha_width_[static_cast<std::size_t>(index)], frames, y, error_word(), stream_);
 }
 
 void DacEngine::conv(int index, const float* x, float* y, const float* residual,
-                     const std::vector<int>& in_frames, std::vector<int>& out_frames)
+                     const std::vector<int>& in_frames, std::vector<int>& out_frames,
+                     const std::vector<long long>* in_offsets)
 {
     const auto& c = convs_[static_cast<std::size_t>(index)];
     const auto& sp = c.spec;
@@ -94,7 +99,9 @@ void DacEngine::conv(int index, const float* x, float* y, const float* residual,
     for (std::size_t q = 0; q < in_frames.size(); ++q)
     {
         const int of = output_frames(sp, in_frames[q]);
-        seqs.push_back({in_off, in_frames[q], out_off, of});
+        const long long start = in_offsets ? (*in_offsets)[q] : in_off;
+        require(start + in_frames[q] < (1ll << 31), "convolution input exceeds 2^31 rows");
+        seqs.push_back({static_cast<int>(start), in_frames[q], out_off, of});
         out_frames.push_back(of);
         if (sp.transposed)
         {
@@ -118,6 +125,11 @@ void DacEngine::conv(int index, const float* x, float* y, const float* residual,
     cuda_ok(cudaMemcpyAsync(d_seq, seqs.data(), seqs.size() * sizeof(dev::Sequence),
                             cudaMemcpyHostToDevice, stream_),
             "H2D");
+    double macs = 0;
+    for (int of : out_frames)
+        macs += static_cast<double>(of) * shape.cout * shape.cin * (sp.transposed ? 2 : shape.kernel);
+    KernelTimer::Scope timing(shape.cout < 16 ? "conv_narrow" : sp.transposed ? "conv_transposed" : "conv_exact",
+                              stream_, 2.0 * macs);
     if (shape.cout < 16)
     {
         dev::conv1d_narrow(x, c.weights.as<float>(), c.bias.as<float>(), y, d_seq,
@@ -135,9 +147,11 @@ void DacEngine::conv(int index, const float* x, float* y, const float* residual,
     dev::conv1d(l, stream_);
 }
 
-void DacEngine::analyze(const float* pcm, const std::vector<int>& frames, float* latent)
+void DacEngine::analyze(const float* pcm, const std::vector<long long>& offsets,
+                        const std::vector<int>& frames, float* latent)
 {
     require(!synthesis_, "analysis on a synthesis model");
+    require(offsets.size() == frames.size(), "analysis window table mismatch");
     std::vector<int> f0(frames.size()), f1;
     long long total = 0;
     for (std::size_t i = 0; i < frames.size(); ++i)
@@ -152,7 +166,7 @@ void DacEngine::analyze(const float* pcm, const std::vector<int>& frames, float*
     auto* t1 = ws_.get<float>("t1", biggest);
     auto* t2 = ws_.get<float>("t2", biggest);
     std::vector<int> cur = f0;
-    conv(0, pcm, a, nullptr, cur, f1);
+    conv(0, pcm, a, nullptr, cur, f1, &offsets);
     cur = f1;
     int width = 64;
     for (int stage = 0; stage < 4; ++stage)
@@ -254,6 +268,7 @@ RvqEngine::RvqEngine(const std::vector<PreparedRvqBook>& books, cudaStream_t str
 
 void RvqEngine::encode(const float* latent, int frames, int books, std::uint16_t* tokens, int stride)
 {
+    KernelTimer::Scope timing("rvq_encode", stream_, static_cast<double>(frames) * books * 2.0 * (8192 + 8192 + 8192));
     require(books > 0 && books <= books_, "stream and prepared RVQ codebooks do not match");
     dev::rvq_encode(latent, frames, table_.as<dev::RvqBookDevice>(), books, tokens, stride,
                     error_word(), stream_);

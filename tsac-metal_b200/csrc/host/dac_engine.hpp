@@ -27,9 +27,10 @@ public:
     {
         return channels_;
     }
-    // Analysis: pcm windows [sum of window samples][C] (window w has
-    // frames[w]*512 samples) -> latent [sum of frames][1024].
-    void analyze(const float* pcm, const std::vector<int>& frames, float* latent);
+    // Analysis: window w reads frames[w]*512 PCM rows [C] starting at row
+    // offsets[w] of `pcm` -> latent [sum of frames][1024] (windows in order).
+    void analyze(const float* pcm, const std::vector<long long>& offsets,
+                 const std::vector<int>& frames, float* latent);
     // Synthesis: latent windows [sum of frames][1024] -> pcm [sum frames*512][C].
     void synthesize(const float* latent, const std::vector<int>& frames, float* pcm);
     unsigned* error_word() const
@@ -41,7 +42,8 @@ public:
 private:
     struct Layout; // per-layer sequence tables for one window set
     void conv(int index, const float* x, float* y, const float* residual,
-              const std::vector<int>& in_frames, std::vector<int>& out_frames);
+              const std::vector<int>& in_frames, std::vector<int>& out_frames,
+              const std::vector<long long>* in_offsets = nullptr);
     void snake(int index, const float* x, float* y, long long frames);
 
     bool synthesis_;

@@ -1,5 +1,7 @@
 #include "transformer_engine.hpp"
 
+#include "kernel_timer.hpp"
+
 #include "kernels/qlinear.cuh"
 #include "kernels/transformer_ops.cuh"
 
@@ -99,6 +101,11 @@ void TransformerEngine::run_linear(int projection, const std::int8_t* xq, const 
     a.m = rows;
     a.n = l.output;
     a.k = l.input;
+    const double n = l.output, k = l.input, m = rows;
+    // GEMV-shaped launches are weight-streaming (bytes); GEMM launches count int8 ops.
+    KernelTimer::Scope timing(rows <= 16 ? "qlinear_gemv" : "qlinear_gemm", stream_,
+                              rows <= 16 ? n * k + 4 * n * k / 256 + 4 * n + m * k + 4 * m * k / 256 + 2 * m * n
+                                         : 2.0 * m * n * k);
     dev::qlinear_matmul(a, stream_);
 }
 
@@ -128,7 +135,10 @@ void TransformerEngine::run_stack(bool temporal, int rows, std::uint16_t* h, con
                         error_word(), stream_);
         run_linear(projection_index(temporal, l, 0), xq, xs, rows, qkv, nullptr, false);
         dev::rotary_scatter(qkv, meta, rotations, rows, query, ck, cv, stream_);
-        dev::attention(query, meta, ck, cv, rows, max_time, partials, att, stream_);
+        {
+            KernelTimer::Scope timing("attention", stream_, 0.0);
+            dev::attention(query, meta, ck, cv, rows, max_time, partials, att, stream_);
+        }
         quantize(att, rows, 512, xq, xs);
         run_linear(projection_index(temporal, l, 1), xq, xs, rows, h, h, false);
         dev::layer_norm(h, model_->norm_gain[n2].as<std::uint16_t>(),

@@ -466,4 +466,46 @@ void check_finite(const float* x, long long count, unsigned* error_word, cudaStr
     if (count > 0)
         check_finite_kernel<<<148 * 4, 256, 0, stream>>>(x, count, error_word);
 }
+
+namespace
+{
+__global__ void pcm_regroup_kernel(const float* __restrict__ src, long long samples,
+                                   long long channel_stride, long long sample_stride, int groups,
+                                   int mc, long long padded, float* __restrict__ dst,
+                                   unsigned* error_word)
+{
+    const long long total = static_cast<long long>(groups) * padded * mc;
+    bool ok = true;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+    {
+        const int c = static_cast<int>(i % mc);
+        const long long f = (i / mc) % padded;
+        const int g = static_cast<int>(i / (static_cast<long long>(mc) * padded));
+        float v = 0.0f;
+        if (f < samples)
+        {
+            v = src[static_cast<long long>(g * mc + c) * channel_stride + f * sample_stride];
+            ok = ok && isfinite(v);
+        }
+        dst[i] = v;
+    }
+    if (!ok && error_word)
+        atomicOr(error_word, error_nonfinite);
+}
+} // namespace
+
+void pcm_regroup(const float* src, long long samples, long long channel_stride,
+                 long long sample_stride, int groups, int model_channels, long long padded,
+                 float* dst, unsigned* error_word, cudaStream_t stream)
+{
+    const long long total = static_cast<long long>(groups) * padded * model_channels;
+    if (total <= 0)
+        return;
+    long long blocks = (total + 255) / 256;
+    blocks = blocks > 148 * 8 ? 148 * 8 : blocks;
+    pcm_regroup_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(
+        src, samples, channel_stride, sample_stride, groups, model_channels, padded, dst,
+        error_word);
+}
 } // namespace tsacb::dev

@@ -72,4 +72,11 @@ void rvq_decode(const std::uint16_t* tokens, int token_stride, int frames,
                 const RvqBookDevice* books, int book_count, float* latent, cudaStream_t stream);
 // Nonfinite scan of a float tensor: sets error bit on any NaN/Inf.
 void check_finite(const float* x, long long count, unsigned* error_word, cudaStream_t stream);
+
+// padded_audio (src/common/audio_analyzer.cpp:118-139) on the device:
+// dst[(g*padded + f)*mc + c] = src[(g*mc + c)*channel_stride + f*sample_stride]
+// for f < samples, zero up to `padded`; nonfinite input sets the error bit.
+void pcm_regroup(const float* src, long long samples, long long channel_stride,
+                 long long sample_stride, int groups, int model_channels, long long padded,
+                 float* dst, unsigned* error_word, cudaStream_t stream);
 } // namespace tsacb::dev

@@ -309,3 +309,36 @@ class CudaAnalyzer:
                                               tokens.ctypes.data_as(ctypes.c_void_p),
                                               ctypes.byref(out), ctypes.byref(nbytes)))
         return _take(out, nbytes.value, np.uint8).tobytes()
+
+
+def stream_info(stream: bytes):
+    """(channels, samples_per_channel, symbols) of a .tsac stream."""
+    ch, spc, sym = ctypes.c_uint(), ctypes.c_size_t(), ctypes.c_size_t()
+    check(library().tsac_cuda_stream_info(stream, ctypes.c_size_t(len(stream)), ctypes.byref(ch),
+                                          ctypes.byref(spc), ctypes.byref(sym)))
+    return ch.value, spc.value, sym.value
+
+
+def encode_batch_device(analyzer: "CudaAnalyzer", pcm_tensors, options: EncodeOptions | None = None):
+    """Encode HBM-resident interleaved PCM (torch CUDA float32 [samples][channels])."""
+    n = len(pcm_tensors)
+    ptrs = (ctypes.c_void_p * n)(*[t.data_ptr() for t in pcm_tensors])
+    chans = (ctypes.c_size_t * n)(*[t.shape[1] for t in pcm_tensors])
+    sams = (ctypes.c_size_t * n)(*[t.shape[0] for t in pcm_tensors])
+    outs = (ctypes.c_void_p * n)()
+    sizes = (ctypes.c_size_t * n)()
+    opts = _options(options)
+    check(library().tsac_cuda_encode_batch_device(analyzer._ctx, ctypes.c_size_t(n), ptrs, chans,
+                                                  sams, ctypes.byref(opts), outs, sizes))
+    return [_take(ctypes.c_void_p(outs[i]), sizes[i], np.uint8).tobytes() for i in range(n)]
+
+
+def decode_batch_device(analyzer: "CudaAnalyzer", streams, out_tensors):
+    """Decode into HBM-resident PCM tensors (torch CUDA float32, channels x samples each)."""
+    n = len(streams)
+    bufs = [ctypes.create_string_buffer(s, len(s)) for s in streams]
+    ptrs = (ctypes.c_void_p * n)(*[ctypes.addressof(b) for b in bufs])
+    sizes = (ctypes.c_size_t * n)(*[len(s) for s in streams])
+    outs = (ctypes.c_void_p * n)(*[t.data_ptr() for t in out_tensors])
+    check(library().tsac_cuda_decode_batch_device(analyzer._ctx, ctypes.c_size_t(n), ptrs, sizes,
+                                                  outs))
