@@ -201,6 +201,30 @@ int tsac_cuda_qlinear(const int8_t* weights, const float* weight_scales, const f
                       uint16_t* y, void* scratch, size_t scratch_bytes, unsigned* error_word,
                       void* stream);
 
+/* Scratch bytes tsac_cuda_conv1d needs (its per-launch tile table). */
+size_t tsac_cuda_conv1d_scratch_bytes(size_t out_frames, int stride, int transposed);
+
+/* One exact-order convolution: scalar::Conv1d::sample (src/scalar/dsp.cpp:11-35)
+ * for every output, with the geometry of src/common/dsp.tpp:141-178.
+ *   x        device f32 [frames][cin]
+ *   weights  device f32 [kernel][cin][cout] (tap, input, output; the
+ *            reference stores [cout][kernel][cin] ordinary, [cin][kernel][cout]
+ *            transposed — the same values re-laid)
+ *   bias     device f32 [cout]; residual device f32 [out_frames][cout] or NULL
+ *            (y = residual + conv, the residual-unit add of src/common/analysis.tpp:59-66)
+ *   y        device f32 [out_frames][cout]
+ * Transposed convolutions require dilation 1.  Synchronous on `stream`. */
+int tsac_cuda_conv1d(const float* x, size_t frames, const float* weights, const float* bias,
+                     const float* residual, float* y, size_t cin, size_t cout, size_t kernel,
+                     size_t stride, size_t padding, size_t dilation, int transposed,
+                     void* scratch, size_t scratch_bytes, unsigned* error_word, void* stream);
+
+/* DAC Snake, y = x + sin^2(alpha x) / (alpha + eps) with the captured
+ * polynomial (scalar_snake_frames, src/scalar/dsp.cpp:93-119); x, y device
+ * f32 [frames][channels], alpha device f32 [channels]. */
+int tsac_cuda_snake(const float* x, size_t channels, size_t frames, const float* alpha, float* y,
+                    unsigned* error_word, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
