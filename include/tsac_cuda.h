@@ -201,6 +201,24 @@ int tsac_cuda_qlinear(const int8_t* weights, const float* weight_scales, const f
                       uint16_t* y, void* scratch, size_t scratch_bytes, unsigned* error_word,
                       void* stream);
 
+/* tsac_cuda_qlinear for callers that cannot allocate device memory: for
+ * example a service that reserves all of its GPU memory at start-up and then
+ * forbids cudaMalloc, or a real-time audio thread that must not wait on the
+ * driver's allocator.  This entry point has no counterpart in the reference.
+ * It allocates nothing: its scratch is a fixed 1 MiB + 16 KiB array in the
+ * library's device image, present on every GPU that loads the library until the
+ * process exits.  Limit: m * k <= tsac_cuda_qlinear_noalloc_max_elements()
+ * (1,048,576, e.g. 256 columns of 4096 inputs); larger calls fail with
+ * TSAC_CUDA_ERROR.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) and should come before any stream capture.
+ * All calls share the array, so calls that overlap on the GPU race; serialise
+ * them.  Other arguments and results are those of tsac_cuda_qlinear. */
+size_t tsac_cuda_qlinear_noalloc_max_elements(void);
+int tsac_cuda_qlinear_noalloc(const int8_t* weights, const float* weight_scales,
+                              const float* bias, size_t k, size_t n, const uint16_t* x, size_t m,
+                              const uint16_t* residual, uint16_t* y, unsigned* error_word,
+                              void* stream);
+
 /* Scratch bytes tsac_cuda_conv1d needs (its per-launch tile table). */
 size_t tsac_cuda_conv1d_scratch_bytes(size_t out_frames, int stride, int transposed);
 
