@@ -426,27 +426,19 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
             books = std::max<std::size_t>(books, h.codebooks);
             lanes += h.lanes();
         }
-        std::vector<float> masses(lanes * 1023);
+        (void)lanes;
         for (std::size_t step = 0; step < steps; ++step)
             for (std::size_t book = 0; book < books; ++book)
             {
-                const auto rows = engine.decode_predict(step, book, masses.data());
+                const float* masses = nullptr;
+                const auto rows = engine.decode_predict(step, book, &masses);
                 std::vector<std::uint16_t> decoded(rows.size());
-                // Rows are ordered recording, lane, group = stream order per recording.
-                std::vector<std::size_t> first(ids.size() + 1, rows.size());
-                for (std::size_t j = rows.size(); j-- > 0;)
-                    first[static_cast<std::size_t>(rows[j].recording)] = j;
-                const auto decode_one = [&](std::size_t r)
-                {
-                    for (std::size_t j = first[r];
-                         j < rows.size() && static_cast<std::size_t>(rows[j].recording) == r; ++j)
-                        decoded[j] = decode_categorical_tree(decoders[r], masses.data() + j * 1023);
-                };
-                if (ids.size() > 2)
-                    parallel_for(ids.size(), decode_one);
-                else
-                    for (std::size_t r = 0; r < ids.size(); ++r)
-                        decode_one(r);
+                // Rows are in stream order per recording (lane, then group); each
+                // recording's decoder consumes its rows in that order (~0.3 us per
+                // symbol, so the walk stays on this thread).
+                for (std::size_t j = 0; j < rows.size(); ++j)
+                    decoded[j] = decode_categorical_tree(
+                        decoders[static_cast<std::size_t>(rows[j].recording)], masses + j * 1023);
                 for (std::size_t j = 0; j < rows.size(); ++j)
                 {
                     const auto r = static_cast<std::size_t>(rows[j].recording);

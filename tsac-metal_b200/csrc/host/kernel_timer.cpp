@@ -84,6 +84,13 @@ KernelTimer::Scope::Scope(const char* name, cudaStream_t stream, double work)
     {
         return;
     }
+    // Launches recorded into a CUDA graph are timed as a whole by their caller.
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream_, &capture) != cudaSuccess ||
+        capture != cudaStreamCaptureStatusNone)
+    {
+        return;
+    }
     std::lock_guard lock(t.mutex_);
     start_ = t.take();
     cudaEventRecord(start_, stream_);

@@ -110,7 +110,8 @@ void TransformerEngine::run_linear(int projection, const std::int8_t* xq, const 
 }
 
 // evaluate_stack (src/common/cpu_transformer.tpp:99-141) over a set of rows.
-void TransformerEngine::run_stack(bool temporal, int rows, std::uint16_t* h, const void* meta_device,
+void TransformerEngine::run_stack(Workspace& ws_, bool temporal, int rows, std::uint16_t* h,
+                                  const void* meta_device,
                                   int max_time, std::uint16_t* cache_k, std::uint16_t* cache_v,
                                   std::size_t cache_layer_stride, std::uint16_t* final_out,
                                   std::int8_t* final_q, float* final_s)
@@ -248,7 +249,7 @@ void TransformerEngine::predict_known(const Header& header, std::span<const std:
     auto* tck = ws_.get<std::uint16_t>("tck", tstride * 12);
     auto* tcv = ws_.get<std::uint16_t>("tcv", tstride * 12);
     auto* cond = ws_.get<std::uint16_t>("cond", static_cast<std::size_t>(trows) * 512);
-    run_stack(true, trows, th, d_tmeta, max_time, tck, tcv, tstride, cond, nullptr, nullptr);
+    run_stack(ws_, true, trows, th, d_tmeta, max_time, tck, tcv, tstride, cond, nullptr, nullptr);
 
     // ---- codebook stack, chunked by (frame, group) sequences of Q rows.
     const int sequences = F * G;
@@ -319,7 +320,7 @@ void TransformerEngine::predict_known(const Header& header, std::span<const std:
         auto* ccv = ws_.get<std::uint16_t>("ccv", cstride * 3);
         auto* fq = ws_.get<std::int8_t>("fq", static_cast<std::size_t>(rows) * 512);
         auto* fs = ws_.get<float>("fs", static_cast<std::size_t>(rows) * 2);
-        run_stack(false, rows, ch, d_cmeta, Q, cck, ccv, cstride, nullptr, fq, fs);
+        run_stack(ws_, false, rows, ch, d_cmeta, Q, cck, ccv, cstride, nullptr, fq, fs);
         auto* logits = ws_.get<std::uint16_t>("logits", static_cast<std::size_t>(rows) * 1024);
         run_linear(62, fq, fs, rows, logits, nullptr, false);
         auto* tree = ws_.get<float>("tree", static_cast<std::size_t>(rows) * 1023);
@@ -350,6 +351,61 @@ void TransformerEngine::predict_known(const Header& header, std::span<const std:
 }
 
 // ------------------------------------------------------------------ decode --
+namespace
+{
+// Page-locked host staging (graph memcpy nodes need fixed host addresses).
+class PinnedBuffer
+{
+public:
+    explicit PinnedBuffer(std::size_t bytes) : bytes_(bytes)
+    {
+        cuda_ok(cudaHostAlloc(&ptr_, bytes ? bytes : 1, cudaHostAllocDefault), "cudaHostAlloc");
+    }
+    ~PinnedBuffer()
+    {
+        if (ptr_)
+            cudaFreeHost(ptr_);
+    }
+    PinnedBuffer(const PinnedBuffer&) = delete;
+    PinnedBuffer& operator=(const PinnedBuffer&) = delete;
+    template <class T> T* as() const
+    {
+        return static_cast<T*>(ptr_);
+    }
+    std::size_t bytes() const
+    {
+        return bytes_;
+    }
+
+private:
+    void* ptr_ = nullptr;
+    std::size_t bytes_;
+};
+
+// Packed per-step inputs: struct-of-arrays for up to `rows` rows and 12 books.
+struct StepBlock
+{
+    std::size_t meta, lane_rows, books, offsets, counts, tokens, bytes;
+    explicit StepBlock(std::size_t rows)
+    {
+        std::size_t at = 0;
+        const auto take = [&](std::size_t n)
+        {
+            const auto here = at;
+            at = align_up(at + n, 256);
+            return here;
+        };
+        meta = take(rows * sizeof(RowMeta));
+        lane_rows = take(rows * 4);
+        books = take(rows * 4);
+        offsets = take(rows * 4);
+        counts = take(rows * 4);
+        tokens = take(rows * 12 * 2);
+        bytes = at;
+    }
+};
+} // namespace
+
 struct TransformerEngine::DecodeState
 {
     struct Lane
@@ -359,21 +415,41 @@ struct TransformerEngine::DecodeState
         std::vector<std::uint16_t> current;
         std::deque<std::vector<std::uint16_t>> history;
         int tslot = 0; // first temporal cache slot (1024 per lane)
-        int cslot = 0; // first codebook cache slot (Q per lane)
+        int cslot = 0; // first codebook cache slot (books per lane)
     };
     std::vector<Header> headers;
     std::vector<Lane> lanes;
-    int max_books = 0;
+    int max_rows = 0, replay_rows = 0;
+    std::size_t tstride = 0, cstride = 0;
+    Workspace ws; // sized once per session: graph-captured pointers stay valid
+    std::uint16_t *tck = nullptr, *tcv = nullptr, *cck = nullptr, *ccv = nullptr,
+                  *cond = nullptr;
+    // Temporal and codebook inputs, staged together with one copy.
+    std::unique_ptr<StepBlock> temporal_block, codebook_block;
+    std::unique_ptr<PinnedBuffer> host_in, host_masses, host_error;
+    char* dev_in = nullptr;
+    int* identity = nullptr;
+    std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs; // (temporal, book, rows)
     std::vector<LaneRef> last;
     std::vector<int> last_lanes;
     std::size_t last_book = 0;
+
+    ~DecodeState()
+    {
+        for (auto& [key, exec] : graphs)
+            cudaGraphExecDestroy(exec);
+    }
 };
+
+TransformerEngine::~TransformerEngine() = default;
 
 void TransformerEngine::decode_begin(const std::vector<Header>& headers)
 {
-    auto state = std::make_shared<DecodeState>();
+    decode_.reset();
+    auto state = std::make_unique<DecodeState>();
     state->headers = headers;
     int tslots = 0, cslots = 0;
+    bool replay = false;
     for (std::size_t r = 0; r < headers.size(); ++r)
     {
         const auto& h = headers[r];
@@ -383,7 +459,6 @@ void TransformerEngine::decode_begin(const std::vector<Header>& headers)
                 "Transformer stream/model mismatch");
         const int F = static_cast<int>(h.frames), B = h.batch, G = h.groups;
         const int lanes_b = std::min(B, F), base = F / B, extra = F % B;
-        state->max_books = std::max<int>(state->max_books, h.codebooks);
         for (int lane = 0; lane < lanes_b; ++lane)
         {
             for (int g = 0; g < G; ++g)
@@ -399,79 +474,111 @@ void TransformerEngine::decode_begin(const std::vector<Header>& headers)
                 l.cslot = cslots;
                 tslots += context;
                 cslots += h.codebooks;
+                replay = replay || l.length > context;
                 state->lanes.push_back(std::move(l));
             }
         }
     }
-    const std::size_t tstride = static_cast<std::size_t>(tslots) * 512;
-    ws_.get<std::uint16_t>("dtck", tstride * 12);
-    ws_.get<std::uint16_t>("dtcv", tstride * 12);
-    const std::size_t cstride = static_cast<std::size_t>(cslots) * 512;
-    ws_.get<std::uint16_t>("dcck", cstride * 3);
-    ws_.get<std::uint16_t>("dccv", cstride * 3);
-    ws_.get<std::uint16_t>("dcond", state->lanes.size() * 512);
+    auto& st = *state;
+    st.max_rows = static_cast<int>(st.lanes.size());
+    st.replay_rows = st.max_rows * (replay ? replay_frames : 1);
+    const auto cap = static_cast<std::size_t>(std::max(st.replay_rows, 1));
+    st.tstride = static_cast<std::size_t>(tslots) * 512;
+    st.cstride = static_cast<std::size_t>(cslots) * 512;
+    st.tck = st.ws.get<std::uint16_t>("tck", st.tstride * 12);
+    st.tcv = st.ws.get<std::uint16_t>("tcv", st.tstride * 12);
+    st.cck = st.ws.get<std::uint16_t>("cck", st.cstride * 3);
+    st.ccv = st.ws.get<std::uint16_t>("ccv", st.cstride * 3);
+    st.cond = st.ws.get<std::uint16_t>("cond", cap * 512);
+    // Every scratch name at its session maximum, so no pointer moves later.
+    st.ws.get<std::int8_t>("xq", cap * 2048);
+    st.ws.get<float>("xs", cap * 8);
+    st.ws.get<std::uint16_t>("qkv", cap * 1536);
+    st.ws.get<std::uint16_t>("query", cap * 512);
+    st.ws.get<std::uint16_t>("att", cap * 512);
+    st.ws.get<std::uint16_t>("mlp", cap * 2048);
+    st.ws.get<float>("partials", dev::attention_partials_bytes(static_cast<int>(cap), context) / 4);
+    for (const char* name : {"emb", "pemb"})
+        st.ws.get<std::uint16_t>(name, cap * 1024);
+    for (const char* name : {"eq", "pq"})
+        st.ws.get<std::int8_t>(name, cap * 1024);
+    for (const char* name : {"es", "ps"})
+        st.ws.get<float>(name, cap * 4);
+    for (const char* name : {"th", "tout", "ch", "pproj"})
+        st.ws.get<std::uint16_t>(name, cap * 512);
+    st.ws.get<std::int8_t>("fq", cap * 512);
+    st.ws.get<float>("fs", cap * 2);
+    st.ws.get<std::uint16_t>("logits", cap * 1024);
+    st.ws.get<float>("tree", cap * 1023);
+    st.temporal_block = std::make_unique<StepBlock>(cap);
+    st.codebook_block = std::make_unique<StepBlock>(cap);
+    const auto in_bytes = st.temporal_block->bytes + st.codebook_block->bytes;
+    st.dev_in = st.ws.get<char>("in", in_bytes);
+    st.host_in = std::make_unique<PinnedBuffer>(in_bytes);
+    st.host_masses = std::make_unique<PinnedBuffer>(cap * 1023 * 4);
+    st.host_error = std::make_unique<PinnedBuffer>(4);
+    std::vector<int> ident(cap);
+    for (std::size_t i = 0; i < cap; ++i)
+        ident[i] = static_cast<int>(i);
+    st.identity = st.ws.get<int>("identity", cap);
+    cuda_ok(cudaMemcpyAsync(st.identity, ident.data(), cap * 4, cudaMemcpyHostToDevice, stream_),
+            "H2D");
+    cuda_ok(cudaStreamSynchronize(stream_), "decode session");
     decode_ = std::move(state);
 }
 
 std::vector<TransformerEngine::LaneRef>
-TransformerEngine::decode_predict(std::size_t step, std::size_t book, float* masses_host)
+TransformerEngine::decode_predict(std::size_t step, std::size_t book, const float** masses)
 {
     require(decode_ != nullptr, "decode session not started");
     auto& st = *decode_;
     auto s = stream_;
-    const int total_lanes = static_cast<int>(st.lanes.size());
-    int tslots = 0, cslots = 0;
-    for (const auto& l : st.lanes)
-    {
-        tslots += context;
-        cslots += static_cast<int>(l.current.size());
-    }
-    const std::size_t tstride = static_cast<std::size_t>(tslots) * 512;
-    const std::size_t cstride = static_cast<std::size_t>(cslots) * 512;
-    auto* tck = ws_.get<std::uint16_t>("dtck", tstride * 12);
-    auto* tcv = ws_.get<std::uint16_t>("dtcv", tstride * 12);
-    auto* cck = ws_.get<std::uint16_t>("dcck", cstride * 3);
-    auto* ccv = ws_.get<std::uint16_t>("dccv", cstride * 3);
-    auto* cond = ws_.get<std::uint16_t>("dcond", static_cast<std::size_t>(total_lanes) * 512);
-
     std::vector<int> active;
-    for (int i = 0; i < total_lanes; ++i)
+    for (int i = 0; i < static_cast<int>(st.lanes.size()); ++i)
     {
         const auto& l = st.lanes[static_cast<std::size_t>(i)];
         if (static_cast<int>(step) < l.length && book < l.current.size())
-        {
             active.push_back(i);
-        }
     }
     st.last.clear();
     st.last_lanes = active;
     st.last_book = book;
     if (active.empty())
-    {
         return {};
-    }
     const int n = static_cast<int>(active.size());
-    const int Qmax = st.max_books;
+    char* host = st.host_in->as<char>();
+    const auto& tb = *st.temporal_block;
+    const auto& cb = *st.codebook_block;
+    char* host_c = host + tb.bytes;
+    char* dev_t = st.dev_in;
+    char* dev_c = st.dev_in + tb.bytes;
+
+    // ---- temporal inputs (book 0): one row per lane, or a 256-row replay.
+    int temporal_rows = 0;
+    bool replay = false;
     if (book == 0)
     {
-        // Temporal step (or context reset + replay) for every active lane.
-        std::vector<RowMeta> meta;
-        std::vector<std::uint16_t> tok;
-        std::vector<int> off, cnt, out_row;
-        int max_time = 1;
-        for (int i : active)
+        auto* meta = reinterpret_cast<RowMeta*>(host + tb.meta);
+        auto* lane_rows = reinterpret_cast<int*>(host + tb.lane_rows);
+        auto* offsets = reinterpret_cast<int*>(host + tb.offsets);
+        auto* counts = reinterpret_cast<int*>(host + tb.counts);
+        auto* tokens = reinterpret_cast<std::uint16_t*>(host + tb.tokens);
+        int tok = 0;
+        for (std::size_t j = 0; j < active.size(); ++j)
         {
+            const int i = active[j];
             auto& l = st.lanes[static_cast<std::size_t>(i)];
             const int Q = static_cast<int>(l.current.size());
-            const auto add = [&](const std::vector<std::uint16_t>& fb, bool replay)
+            const auto add = [&](const std::vector<std::uint16_t>& fb, bool is_replay)
             {
                 const int position = l.used++;
-                meta.push_back({l.tslot + position, l.tslot, position + 1, position,
-                                (position + 1 > 64 || replay) ? 1 : 0});
-                off.push_back(static_cast<int>(tok.size()));
-                cnt.push_back(Q);
-                tok.insert(tok.end(), fb.begin(), fb.end());
-                max_time = std::max(max_time, position + 1);
+                meta[temporal_rows] = {l.tslot + position, l.tslot, position + 1, position,
+                                       (position + 1 > 64 || is_replay) ? 1 : 0};
+                offsets[temporal_rows] = tok;
+                counts[temporal_rows] = Q;
+                std::copy(fb.begin(), fb.end(), tokens + tok);
+                tok += 12;
+                ++temporal_rows;
             };
             std::fill(l.current.begin(), l.current.end(), 0);
             if (l.used == context)
@@ -479,108 +586,150 @@ TransformerEngine::decode_predict(std::size_t step, std::size_t book, float* mas
                 require(static_cast<int>(l.history.size()) == replay_frames,
                         "incomplete Transformer replay history");
                 l.used = 0;
+                replay = true;
                 for (const auto& fb : l.history)
-                {
                     add(fb, true);
-                }
             }
             else
             {
                 add(l.history.empty() ? l.current : l.history.back(), false);
             }
-            out_row.push_back(static_cast<int>(meta.size()) - 1);
-        }
-        const int rows = static_cast<int>(meta.size());
-        auto* d_tok = ws_.get<std::uint16_t>("dtok", tok.size());
-        cuda_ok(cudaMemcpyAsync(d_tok, tok.data(), tok.size() * 2, cudaMemcpyHostToDevice, s), "H2D");
-        auto* d_meta = ws_.get<RowMeta>("dtmeta", meta.size());
-        cuda_ok(cudaMemcpyAsync(d_meta, meta.data(), meta.size() * sizeof(RowMeta), cudaMemcpyHostToDevice, s), "H2D");
-        auto* d_off = ws_.get<int>("dtoff", off.size());
-        cuda_ok(cudaMemcpyAsync(d_off, off.data(), off.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
-        auto* d_cnt = ws_.get<int>("dtcnt", cnt.size());
-        cuda_ok(cudaMemcpyAsync(d_cnt, cnt.data(), cnt.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
-        auto* emb = ws_.get<std::uint16_t>("demb", static_cast<std::size_t>(rows) * 1024);
-        dev::embed_sum(model_->embeddings.as<std::uint16_t>(), d_tok, d_off, d_cnt, rows, emb, s);
-        auto* eq = ws_.get<std::int8_t>("deq", static_cast<std::size_t>(rows) * 1024);
-        auto* es = ws_.get<float>("des", static_cast<std::size_t>(rows) * 4);
-        quantize(emb, rows, 1024, eq, es);
-        auto* th = ws_.get<std::uint16_t>("dth", static_cast<std::size_t>(rows) * 512);
-        run_linear(60, eq, es, rows, th, nullptr, false);
-        auto* tout = ws_.get<std::uint16_t>("dtout", static_cast<std::size_t>(rows) * 512);
-        run_stack(true, rows, th, d_meta, max_time, tck, tcv, tstride, tout, nullptr, nullptr);
-        // Keep each lane's conditioning (the last row it produced).
-        for (std::size_t j = 0; j < active.size(); ++j)
-        {
-            cuda_ok(cudaMemcpyAsync(cond + static_cast<std::size_t>(active[j]) * 512,
-                                    tout + static_cast<std::size_t>(out_row[j]) * 512, 1024,
-                                    cudaMemcpyDeviceToDevice, s),
-                    "D2D");
+            // The lane's conditioning is its last temporal row: entry j of the
+            // scatter maps row (temporal_rows - 1) to lane i.
+            lane_rows[j] = i;
+            reinterpret_cast<int*>(host + tb.books)[j] = temporal_rows - 1;
         }
     }
-    // Codebook step for book `book` of every active lane.
-    std::vector<RowMeta> meta(static_cast<std::size_t>(n));
-    std::vector<int> lane_rows(static_cast<std::size_t>(n)), books(static_cast<std::size_t>(n), static_cast<int>(book));
-    std::vector<std::uint16_t> tok;
-    std::vector<int> off, cnt;
-    for (int j = 0; j < n; ++j)
+    // ---- codebook inputs: one row per active lane.
     {
-        const auto& l = st.lanes[static_cast<std::size_t>(active[static_cast<std::size_t>(j)])];
-        meta[static_cast<std::size_t>(j)] = {l.cslot + static_cast<int>(book), l.cslot,
-                                             static_cast<int>(book) + 1, -1, 0};
-        lane_rows[static_cast<std::size_t>(j)] = active[static_cast<std::size_t>(j)];
-        off.push_back(static_cast<int>(tok.size()));
-        cnt.push_back(static_cast<int>(book));
-        tok.insert(tok.end(), l.current.begin(), l.current.begin() + static_cast<std::ptrdiff_t>(book));
-        st.last.push_back({l.recording, l.lane_b * st.headers[static_cast<std::size_t>(l.recording)].groups + l.group});
+        auto* meta = reinterpret_cast<RowMeta*>(host_c + cb.meta);
+        auto* lane_rows = reinterpret_cast<int*>(host_c + cb.lane_rows);
+        auto* books = reinterpret_cast<int*>(host_c + cb.books);
+        auto* offsets = reinterpret_cast<int*>(host_c + cb.offsets);
+        auto* counts = reinterpret_cast<int*>(host_c + cb.counts);
+        auto* tokens = reinterpret_cast<std::uint16_t*>(host_c + cb.tokens);
+        for (int j = 0; j < n; ++j)
+        {
+            const auto& l = st.lanes[static_cast<std::size_t>(active[static_cast<std::size_t>(j)])];
+            meta[j] = {l.cslot + static_cast<int>(book), l.cslot, static_cast<int>(book) + 1, -1, 0};
+            lane_rows[j] = active[static_cast<std::size_t>(j)];
+            books[j] = static_cast<int>(book);
+            offsets[j] = j * 12;
+            counts[j] = static_cast<int>(book);
+            std::copy_n(l.current.begin(), book, tokens + j * 12);
+            st.last.push_back({l.recording,
+                               l.lane_b * st.headers[static_cast<std::size_t>(l.recording)].groups + l.group});
+        }
     }
-    auto* d_meta = ws_.get<RowMeta>("dcmeta", meta.size());
-    cuda_ok(cudaMemcpyAsync(d_meta, meta.data(), meta.size() * sizeof(RowMeta), cudaMemcpyHostToDevice, s), "H2D");
-    auto* d_books = ws_.get<int>("dcbook", books.size());
-    cuda_ok(cudaMemcpyAsync(d_books, books.data(), books.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
-    auto* ch = ws_.get<std::uint16_t>("dch", static_cast<std::size_t>(n) * 512);
+
+    const auto enqueue = [&](int trows)
+    {
+        cuda_ok(cudaMemcpyAsync(st.dev_in, host, tb.bytes + cb.bytes, cudaMemcpyHostToDevice, s), "H2D");
+        auto& ws = st.ws;
+        if (trows > 0)
+        {
+            const auto* d_meta = reinterpret_cast<const RowMeta*>(dev_t + tb.meta);
+            auto* emb = ws.get<std::uint16_t>("emb", static_cast<std::size_t>(trows) * 1024);
+            dev::embed_sum(model_->embeddings.as<std::uint16_t>(),
+                           reinterpret_cast<const std::uint16_t*>(dev_t + tb.tokens),
+                           reinterpret_cast<const int*>(dev_t + tb.offsets),
+                           reinterpret_cast<const int*>(dev_t + tb.counts), trows, emb, s);
+            auto* eq = ws.get<std::int8_t>("eq", static_cast<std::size_t>(trows) * 1024);
+            auto* es = ws.get<float>("es", static_cast<std::size_t>(trows) * 4);
+            quantize(emb, trows, 1024, eq, es);
+            auto* th = ws.get<std::uint16_t>("th", static_cast<std::size_t>(trows) * 512);
+            run_linear(60, eq, es, trows, th, nullptr, false);
+            auto* tout = ws.get<std::uint16_t>("tout", static_cast<std::size_t>(trows) * 512);
+            run_stack(ws, true, trows, th, d_meta, context, st.tck, st.tcv, st.tstride, tout,
+                      nullptr, nullptr);
+            // Conditioning: each active lane's last temporal row.
+            dev::scatter_rows(tout, reinterpret_cast<const int*>(dev_t + tb.books),
+                              reinterpret_cast<const int*>(dev_t + tb.lane_rows), n, st.cond, s);
+        }
+        const auto* d_meta = reinterpret_cast<const RowMeta*>(dev_c + cb.meta);
+        const auto* d_books = reinterpret_cast<const int*>(dev_c + cb.books);
+        auto* ch = ws.get<std::uint16_t>("ch", static_cast<std::size_t>(n) * 512);
+        if (book == 0)
+        {
+            dev::add_positions(st.cond, reinterpret_cast<const int*>(dev_c + cb.lane_rows), d_books,
+                               model_->positions.as<std::uint16_t>(), n, ch, s);
+        }
+        else
+        {
+            auto* pemb = ws.get<std::uint16_t>("pemb", static_cast<std::size_t>(n) * 1024);
+            dev::embed_sum(model_->embeddings.as<std::uint16_t>(),
+                           reinterpret_cast<const std::uint16_t*>(dev_c + cb.tokens),
+                           reinterpret_cast<const int*>(dev_c + cb.offsets),
+                           reinterpret_cast<const int*>(dev_c + cb.counts), n, pemb, s);
+            auto* pq = ws.get<std::int8_t>("pq", static_cast<std::size_t>(n) * 1024);
+            auto* ps = ws.get<float>("ps", static_cast<std::size_t>(n) * 4);
+            quantize(pemb, n, 1024, pq, ps);
+            auto* pproj = ws.get<std::uint16_t>("pproj", static_cast<std::size_t>(n) * 512);
+            run_linear(61, pq, ps, n, pproj, nullptr, false);
+            dev::add_positions(pproj, st.identity, d_books, model_->positions.as<std::uint16_t>(),
+                               n, ch, s);
+        }
+        auto* fq = ws.get<std::int8_t>("fq", static_cast<std::size_t>(n) * 512);
+        auto* fs = ws.get<float>("fs", static_cast<std::size_t>(n) * 2);
+        run_stack(ws, false, n, ch, d_meta, 12, st.cck, st.ccv, st.cstride, nullptr, fq, fs);
+        auto* logits = ws.get<std::uint16_t>("logits", static_cast<std::size_t>(n) * 1024);
+        run_linear(62, fq, fs, n, logits, nullptr, false);
+        auto* tree = ws.get<float>("tree", static_cast<std::size_t>(n) * 1023);
+        dev::softmax_tree(logits, n, nullptr, nullptr, tree, error_word(), s);
+        cuda_ok(cudaMemcpyAsync(st.host_masses->as<void>(), tree, static_cast<std::size_t>(n) * 1023 * 4,
+                                cudaMemcpyDeviceToHost, s),
+                "D2H");
+        cuda_ok(cudaMemcpyAsync(st.host_error->as<void>(), error_word(), 4, cudaMemcpyDeviceToHost, s),
+                "D2H");
+    };
+
+    // Algorithmic bytes of one step: the int8 weights it streams.
+    const auto weights = [&](int p)
+    {
+        const auto& l = model_->projections[static_cast<std::size_t>(p)];
+        return static_cast<double>(l.input) * l.output;
+    };
+    double weight_bytes = weights(61) + weights(62);
+    for (int p = 48; p < 60; ++p)
+        weight_bytes += weights(p);
     if (book == 0)
     {
-        auto* d_rows = ws_.get<int>("dcrows", lane_rows.size());
-        cuda_ok(cudaMemcpyAsync(d_rows, lane_rows.data(), lane_rows.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
-        dev::add_positions(cond, d_rows, d_books, model_->positions.as<std::uint16_t>(), n, ch, s);
+        weight_bytes += weights(60);
+        for (int p = 0; p < 48; ++p)
+            weight_bytes += weights(p);
+    }
+    if (replay)
+    {
+        // Rare (once per 768 frames of a lane): executed directly.
+        KernelTimer::Scope timing("decode_step_replay", s, weight_bytes);
+        enqueue(temporal_rows);
     }
     else
     {
-        std::vector<int> ident(static_cast<std::size_t>(n));
-        for (int j = 0; j < n; ++j)
-            ident[static_cast<std::size_t>(j)] = j;
-        if (tok.empty())
-            tok.push_back(0);
-        auto* d_tok = ws_.get<std::uint16_t>("dctok", tok.size());
-        cuda_ok(cudaMemcpyAsync(d_tok, tok.data(), tok.size() * 2, cudaMemcpyHostToDevice, s), "H2D");
-        auto* d_off = ws_.get<int>("dcoff", off.size());
-        cuda_ok(cudaMemcpyAsync(d_off, off.data(), off.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
-        auto* d_cnt = ws_.get<int>("dccnt", cnt.size());
-        cuda_ok(cudaMemcpyAsync(d_cnt, cnt.data(), cnt.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
-        auto* d_id = ws_.get<int>("dcid", ident.size());
-        cuda_ok(cudaMemcpyAsync(d_id, ident.data(), ident.size() * 4, cudaMemcpyHostToDevice, s), "H2D");
-        auto* pemb = ws_.get<std::uint16_t>("dpemb", static_cast<std::size_t>(n) * 1024);
-        dev::embed_sum(model_->embeddings.as<std::uint16_t>(), d_tok, d_off, d_cnt, n, pemb, s);
-        auto* pq = ws_.get<std::int8_t>("dpq", static_cast<std::size_t>(n) * 1024);
-        auto* ps = ws_.get<float>("dps", static_cast<std::size_t>(n) * 4);
-        quantize(pemb, n, 1024, pq, ps);
-        auto* pproj = ws_.get<std::uint16_t>("dpproj", static_cast<std::size_t>(n) * 512);
-        run_linear(61, pq, ps, n, pproj, nullptr, false);
-        dev::add_positions(pproj, d_id, d_books, model_->positions.as<std::uint16_t>(), n, ch, s);
+        const auto key = std::make_tuple(book == 0 ? 1 : 0, static_cast<int>(book), n);
+        auto found = st.graphs.find(key);
+        if (found == st.graphs.end())
+        {
+            cudaGraph_t graph = nullptr;
+            cuda_ok(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "capture");
+            enqueue(temporal_rows);
+            cuda_ok(cudaStreamEndCapture(s, &graph), "capture");
+            cudaGraphExec_t exec = nullptr;
+            const auto status = cudaGraphInstantiate(&exec, graph, 0);
+            cudaGraphDestroy(graph);
+            cuda_ok(status, "cudaGraphInstantiate");
+            found = st.graphs.emplace(key, exec).first;
+        }
+        KernelTimer::Scope timing("decode_step", s, weight_bytes);
+        cuda_ok(cudaGraphLaunch(found->second, s), "cudaGraphLaunch");
     }
-    auto* fq = ws_.get<std::int8_t>("dfq", static_cast<std::size_t>(n) * 512);
-    auto* fs = ws_.get<float>("dfs", static_cast<std::size_t>(n) * 2);
-    run_stack(false, n, ch, d_meta, static_cast<int>(book) + 1, cck, ccv, cstride, nullptr, fq, fs);
-    auto* logits = ws_.get<std::uint16_t>("dlogits", static_cast<std::size_t>(n) * 1024);
-    run_linear(62, fq, fs, n, logits, nullptr, false);
-    auto* tree = ws_.get<float>("dtree", static_cast<std::size_t>(n) * 1023);
-    dev::softmax_tree(logits, n, nullptr, nullptr, tree, error_word(), s);
-    cuda_ok(cudaGetLastError(), "transformer launch");
-    cuda_ok(cudaMemcpyAsync(masses_host, tree, static_cast<std::size_t>(n) * 1023 * 4,
-                            cudaMemcpyDeviceToHost, s),
-            "D2H");
-    (void)Qmax;
-    check_errors();
+    cuda_ok(cudaStreamSynchronize(s), "decode step");
+    if (*st.host_error->as<unsigned>())
+    {
+        cuda_ok(cudaMemset(error_word(), 0, 4), "memset");
+        throw NumericError("Transformer activations must be finite");
+    }
+    *masses = st.host_masses->as<float>();
     return st.last;
 }
 
@@ -598,9 +747,7 @@ void TransformerEngine::decode_commit(std::span<const std::uint16_t> tokens)
         {
             l.history.push_back(l.current);
             if (static_cast<int>(l.history.size()) > replay_frames)
-            {
                 l.history.pop_front();
-            }
         }
     }
 }

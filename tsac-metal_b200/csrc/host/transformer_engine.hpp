@@ -14,12 +14,17 @@
 //
 // Decode: one (step, book) at a time for all lanes of all recordings in the
 // batch; emits the left-child subtree masses the host range decoder walks.
+// Each step is a CUDA graph (captured once per (stack, book, rows), replayed
+// with its inputs staged through one pinned block), so a step costs one
+// launch and one synchronisation on the host.
 #pragma once
 #include "device.hpp"
 #include "format.hpp"
 #include "models.hpp"
 
+#include <map>
 #include <memory>
+#include <tuple>
 
 namespace tsacb
 {
@@ -39,13 +44,11 @@ struct DeviceTransformer
     DeviceTransformer(const PreparedTransformer& t, cudaStream_t stream);
 };
 
-// Rows of one stack evaluation with their cache metadata (host side).
-struct RowPlan;
-
 class TransformerEngine
 {
 public:
     TransformerEngine(std::shared_ptr<const DeviceTransformer> model, cudaStream_t stream);
+    ~TransformerEngine();
 
     // Known-token evaluation of whole recordings (encode).
     // tokens: [frames][groups][books] of each recording; outputs per recording
@@ -55,20 +58,16 @@ public:
                        std::uint16_t* q15, float* probabilities);
 
     // --- decode stepping for a batch of recordings (same model) -------------
-    struct Stream
-    {
-        Header header;
-    };
     void decode_begin(const std::vector<Header>& headers);
-    // Computes the distributions of book `book` at `step` for every lane of
-    // every recording that has that step; writes left-child masses
-    // [row][1023] (host pinned) and returns the lane ids (recording, lane) of
-    // the rows in order.
     struct LaneRef
     {
         int recording, lane;
     };
-    std::vector<LaneRef> decode_predict(std::size_t step, std::size_t book, float* masses_host);
+    // Computes the distributions of book `book` at `step` for every lane of
+    // every recording that has that step; returns the rows' lanes in stream
+    // order and a pointer to their left-child masses [row][1023] (pinned host
+    // memory, valid until the next call).
+    std::vector<LaneRef> decode_predict(std::size_t step, std::size_t book, const float** masses);
     // Commits the decoded tokens of the rows returned by the last decode_predict.
     void decode_commit(std::span<const std::uint16_t> tokens);
 
@@ -82,10 +81,10 @@ private:
     void run_linear(int projection, const std::int8_t* xq, const float* xs, int rows,
                     std::uint16_t* y, const std::uint16_t* residual, bool gelu);
     void quantize(const std::uint16_t* x, int rows, int k, std::int8_t* xq, float* xs);
-    void run_stack(bool temporal, int rows, std::uint16_t* h, const void* meta_device,
-                   int max_time, std::uint16_t* cache_k, std::uint16_t* cache_v,
-                   std::size_t cache_layer_stride, std::uint16_t* final_out,
-                   std::int8_t* final_q, float* final_s);
+    void run_stack(Workspace& ws, bool temporal, int rows, std::uint16_t* h,
+                   const void* meta_device, int max_time, std::uint16_t* cache_k,
+                   std::uint16_t* cache_v, std::size_t cache_layer_stride,
+                   std::uint16_t* final_out, std::int8_t* final_q, float* final_s);
 
     std::shared_ptr<const DeviceTransformer> model_;
     cudaStream_t stream_;
@@ -93,6 +92,6 @@ private:
     DeviceBuffer error_;
 
     struct DecodeState;
-    std::shared_ptr<DecodeState> decode_;
+    std::unique_ptr<DecodeState> decode_;
 };
 } // namespace tsacb

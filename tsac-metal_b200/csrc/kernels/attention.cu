@@ -34,12 +34,16 @@ __device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b)
     return (a.value < b.value || (a.value == b.value && b.index < a.index)) ? b : a;
 }
 
+// SINGLE: the whole history fits one 64-key block (codebook stack, short
+// temporal histories); the kernel then applies the one-block merge itself and
+// writes the bf16 output, with exactly the combine kernel's operations.
+template <bool SINGLE>
 __global__ void __launch_bounds__(128)
     attention_block_kernel(const std::uint16_t* __restrict__ query,
                            const RowMeta* __restrict__ meta,
                            const std::uint16_t* __restrict__ cache_k,
                            const std::uint16_t* __restrict__ cache_v, int max_blocks,
-                           float* __restrict__ partials)
+                           float* __restrict__ partials, std::uint16_t* __restrict__ output)
 {
     __shared__ unsigned ks[BLOCK][65];
     __shared__ unsigned vs[BLOCK][65];
@@ -122,6 +126,21 @@ __global__ void __launch_bounds__(128)
     if (m.round)
         sum = from_bf16(to_bf16(sum));
     __syncthreads();
+    if constexpr (SINGLE)
+    {
+        // The combine kernel's first (and only) merge step, from running = -inf.
+        const float running = -INFINITY;
+        const float difference = __fsub_rn(maximum, running);
+        const float factor = original_exp(-fabsf(difference));
+        const float old_scale = running > maximum ? 1.0f : factor;
+        const float new_scale = running > maximum ? factor : 1.0f;
+        const float total = __fmaf_rn(block_sum, new_scale, __fmul_rn(0.0f, old_scale));
+        const float numerator = __fmaf_rn(sum, new_scale, __fmul_rn(0.0f, old_scale));
+        const float reciprocal = __fdiv_rn(1.0f, total);
+        output[static_cast<size_t>(row) * WIDTH + head * HW + t] =
+            to_bf16(__fmul_rn(numerator, reciprocal));
+        return;
+    }
     float* out = partials + (static_cast<size_t>(task) * max_blocks + block) * PSTRIDE;
     out[2 + t] = sum;
     if (t == 0)
@@ -172,8 +191,14 @@ void attention(const std::uint16_t* query, const RowMeta* meta, const std::uint1
     if (rows <= 0)
         return;
     const int blocks = (max_time + BLOCK - 1) / BLOCK;
-    attention_block_kernel<<<dim3(rows * HEADS, blocks), 128, 0, stream>>>(query, meta, cache_k,
-                                                                          cache_v, blocks, partials);
+    if (blocks == 1)
+    {
+        attention_block_kernel<true><<<dim3(rows * HEADS, 1), 128, 0, stream>>>(
+            query, meta, cache_k, cache_v, 1, nullptr, out);
+        return;
+    }
+    attention_block_kernel<false><<<dim3(rows * HEADS, blocks), 128, 0, stream>>>(
+        query, meta, cache_k, cache_v, blocks, partials, nullptr);
     attention_combine_kernel<<<rows * HEADS, 128, 0, stream>>>(meta, partials, blocks, out);
 }
 } // namespace tsacb::dev

@@ -202,155 +202,83 @@ __global__ void __launch_bounds__(256)
     }
 }
 
-// GEMV-shaped launch for decode-sized M (<= 16 columns): one warp per output
-// row; lane l reads bytes [16l, 16l+16) of each 512-byte row segment with one
-// 128-bit load, so a 256-block is owned by 16 lanes and reduced exactly.
-constexpr int GEMV_MAX_M = 16;
+// Decode-shaped launch for up to 64 columns.  A CTA owns R output rows; every
+// (row, 256-block) item is one half-warp's job: each lane holds 16 weight
+// bytes and, column by column, forms its 16-byte int8 dot with the column's
+// activations (read through L1, shared by all rows of the CTA), reduced exactly
+// over the half-warp.  Block dots land in shared memory; then one thread per
+// (row, column) folds them in block order.  Short dependency chains and
+// (rows x blocks) items keep every warp busy at decode sizes.
+constexpr int SMALL_MAX_M = 64;
 
-template <int M>
 __global__ void __launch_bounds__(256)
-    qlinear_gemv_kernel(const std::int8_t* __restrict__ w, const float* __restrict__ wscale,
-                        const std::int8_t* __restrict__ xq, const float* __restrict__ xscale,
-                        int m_rows, int n_cols, int k, Epilogue e, std::uint16_t* __restrict__ y)
+    qlinear_small_kernel(const std::int8_t* __restrict__ w, const float* __restrict__ wscale,
+                         const std::int8_t* __restrict__ xq, const float* __restrict__ xscale,
+                         int m_rows, int n_cols, int k, int rows_per_cta, Epilogue e,
+                         std::uint16_t* __restrict__ y)
 {
-    extern __shared__ __align__(16) unsigned char smem[];
-    std::int8_t* xs = reinterpret_cast<std::int8_t*>(smem);             // [M][k]
-    float* ss = reinterpret_cast<float*>(smem + static_cast<size_t>(M) * k); // [M][k/256]
+    extern __shared__ int dots[]; // [rows_per_cta][blocks][m_rows]
     const int blocks = k / 256;
-    for (int i = threadIdx.x * 16; i < m_rows * k; i += blockDim.x * 16)
+    const int n0 = blockIdx.x * rows_per_cta;
+    const int half = threadIdx.x >> 4, l16 = threadIdx.x & 15;
+    const unsigned mask = (threadIdx.x & 16) ? 0xffff0000u : 0x0000ffffu;
+    const int items = rows_per_cta * blocks;
+    for (int item = half; item < items; item += 16)
     {
-        *reinterpret_cast<uint4*>(xs + i) = *reinterpret_cast<const uint4*>(xq + i);
-    }
-    for (int i = threadIdx.x; i < m_rows * blocks; i += blockDim.x)
-    {
-        ss[i] = xscale[i];
+        const int r = item / blocks, b = item % blocks;
+        const int n = n0 + r;
+        uint4 wv = make_uint4(0, 0, 0, 0);
+        if (n < n_cols)
+            wv = __ldg(reinterpret_cast<const uint4*>(w + static_cast<size_t>(n) * k + b * 256 + l16 * 16));
+        for (int c = 0; c < m_rows; ++c)
+        {
+            const uint4 xv = __ldg(reinterpret_cast<const uint4*>(xq + static_cast<size_t>(c) * k +
+                                                                  b * 256 + l16 * 16));
+            int d = __dp4a(static_cast<int>(wv.x), static_cast<int>(xv.x), 0);
+            d = __dp4a(static_cast<int>(wv.y), static_cast<int>(xv.y), d);
+            d = __dp4a(static_cast<int>(wv.z), static_cast<int>(xv.z), d);
+            d = __dp4a(static_cast<int>(wv.w), static_cast<int>(xv.w), d);
+            d += __shfl_xor_sync(mask, d, 8, 16);
+            d += __shfl_xor_sync(mask, d, 4, 16);
+            d += __shfl_xor_sync(mask, d, 2, 16);
+            d += __shfl_xor_sync(mask, d, 1, 16);
+            if (l16 == 0)
+                dots[(r * blocks + b) * m_rows + c] = d;
+        }
     }
     __syncthreads();
-    const int lane = threadIdx.x & 31;
-    const int warps = blockDim.x >> 5;
-    for (int n = blockIdx.x * warps + (threadIdx.x >> 5); n < n_cols; n += gridDim.x * warps)
+    for (int t = threadIdx.x; t < rows_per_cta * m_rows; t += blockDim.x)
     {
-        const std::int8_t* row = w + static_cast<size_t>(n) * k;
-        float sum[M];
-#pragma unroll
-        for (int c = 0; c < M; ++c)
+        const int r = t / m_rows, c = t % m_rows;
+        const int n = n0 + r;
+        if (n >= n_cols)
+            continue;
+        float sum = 0.0f;
+        for (int b = 0; b < blocks; ++b)
         {
-            sum[c] = 0.0f;
+            const float scale = __fmul_rn(wscale[b * n_cols + n], xscale[c * blocks + b]);
+            sum = __fmaf_rn(static_cast<float>(dots[(r * blocks + b) * m_rows + c]), scale, sum);
         }
-        // Two 256-blocks per 512-byte segment: lanes 0-15 block 2s, 16-31 block 2s+1.
-        for (int seg = 0; seg < k / 512; ++seg)
-        {
-            const uint4 wv = *reinterpret_cast<const uint4*>(row + seg * 512 + lane * 16);
-            const int wi[4] = {int(wv.x), int(wv.y), int(wv.z), int(wv.w)};
-            int dot[M];
-#pragma unroll
-            for (int c = 0; c < M; ++c)
-            {
-                dot[c] = 0;
-                if (c < m_rows)
-                {
-                    const int4 xv =
-                        *reinterpret_cast<const int4*>(xs + static_cast<size_t>(c) * k + seg * 512 + lane * 16);
-                    dot[c] = __dp4a(wi[0], xv.x, dot[c]);
-                    dot[c] = __dp4a(wi[1], xv.y, dot[c]);
-                    dot[c] = __dp4a(wi[2], xv.z, dot[c]);
-                    dot[c] = __dp4a(wi[3], xv.w, dot[c]);
-                }
-#pragma unroll
-                for (int offset = 8; offset > 0; offset >>= 1)
-                {
-                    dot[c] += __shfl_xor_sync(0xffffffffu, dot[c], offset);
-                }
-            }
-            // Lane 0 holds block 2*seg, lane 16 block 2*seg+1; fold in block order.
-#pragma unroll
-            for (int half = 0; half < 2; ++half)
-            {
-                const int b = 2 * seg + half;
-                const float ws = wscale[b * n_cols + n];
-#pragma unroll
-                for (int c = 0; c < M; ++c)
-                {
-                    const int d = __shfl_sync(0xffffffffu, dot[c], half * 16);
-                    if (c < m_rows)
-                    {
-                        const float scale = __fmul_rn(ws, ss[c * blocks + b]);
-                        sum[c] = __fmaf_rn(static_cast<float>(d), scale, sum[c]);
-                    }
-                }
-            }
-        }
-        if (k % 512)
-        {
-            // Trailing single 256-block (K = 256 + 512j): lanes 0-15 only.
-            const int b = blocks - 1;
-            int dot[M];
-            uint4 wv = make_uint4(0, 0, 0, 0);
-            if (lane < 16)
-            {
-                wv = *reinterpret_cast<const uint4*>(row + b * 256 + lane * 16);
-            }
-            const int wi[4] = {int(wv.x), int(wv.y), int(wv.z), int(wv.w)};
-#pragma unroll
-            for (int c = 0; c < M; ++c)
-            {
-                dot[c] = 0;
-                if (c < m_rows && lane < 16)
-                {
-                    const int4 xv =
-                        *reinterpret_cast<const int4*>(xs + static_cast<size_t>(c) * k + b * 256 + lane * 16);
-                    dot[c] = __dp4a(wi[0], xv.x, dot[c]);
-                    dot[c] = __dp4a(wi[1], xv.y, dot[c]);
-                    dot[c] = __dp4a(wi[2], xv.z, dot[c]);
-                    dot[c] = __dp4a(wi[3], xv.w, dot[c]);
-                }
-#pragma unroll
-                for (int offset = 8; offset > 0; offset >>= 1)
-                {
-                    dot[c] += __shfl_xor_sync(0xffffffffu, dot[c], offset);
-                }
-                const int d = __shfl_sync(0xffffffffu, dot[c], 0);
-                if (c < m_rows)
-                {
-                    const float scale = __fmul_rn(wscale[b * n_cols + n], ss[c * blocks + b]);
-                    sum[c] = __fmaf_rn(static_cast<float>(d), scale, sum[c]);
-                }
-            }
-        }
-        if (lane < M && lane < m_rows)
-        {
-            float s = sum[0];
-#pragma unroll
-            for (int c = 1; c < M; ++c)
-            {
-                s = lane == c ? sum[c] : s;
-            }
-            y[static_cast<size_t>(lane) * n_cols + n] = finish(s, lane, n, n_cols, e);
-        }
+        y[static_cast<size_t>(c) * n_cols + n] = finish(sum, c, n, n_cols, e);
     }
 }
 
-template <int M>
-void launch_gemv(const QLinearArgs& a, const Epilogue& e, cudaStream_t stream)
+void launch_small(const QLinearArgs& a, const Epilogue& e, cudaStream_t stream)
 {
-    const size_t smem = static_cast<size_t>(M) * a.k + static_cast<size_t>(M) * (a.k / 256) * 4;
-    const int warps = 8;
-    int grid = (a.n + warps - 1) / warps;
-    grid = grid > 148 * 4 ? 148 * 4 : grid;
-    qlinear_gemv_kernel<M><<<grid, warps * 32, smem, stream>>>(
-        a.weights, a.weight_scales, a.xq, a.xscale, a.m, a.n, a.k, e, a.y);
+    // Rows per CTA: enough (row, block) items for the 16 half-warps.
+    const int blocks = a.k / 256;
+    const int rows = blocks >= 16 ? 1 : 16 / blocks;
+    const size_t smem = static_cast<size_t>(rows) * blocks * a.m * sizeof(int);
+    qlinear_small_kernel<<<(a.n + rows - 1) / rows, 256, smem, stream>>>(
+        a.weights, a.weight_scales, a.xq, a.xscale, a.m, a.n, a.k, rows, e, a.y);
 }
+
 } // namespace
 
 void qlinear_init()
 {
-    // Decode-sized launches stage up to 16 x 4096 int8 activations in shared memory.
-    const int limit = 100 * 1024;
-    cudaFuncSetAttribute(qlinear_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, limit);
-    cudaFuncSetAttribute(qlinear_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, limit);
-    cudaFuncSetAttribute(qlinear_gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, limit);
-    cudaFuncSetAttribute(qlinear_gemv_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, limit);
-    cudaFuncSetAttribute(qlinear_gemv_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, limit);
+    // Nothing to configure: every launch fits the default shared-memory limit
+    // (the decode-shaped kernel needs at most 16 x 64 ints of block dots).
 }
 
 size_t qlinear_scratch_bytes(size_t m, size_t k)
@@ -370,16 +298,8 @@ void qlinear_quantize(const std::uint16_t* x, int m, int k, std::int8_t* xq, flo
 void qlinear_matmul(const QLinearArgs& a, cudaStream_t stream)
 {
     const Epilogue e{a.bias, a.residual, a.lut};
-    if (a.m <= 1)
-        launch_gemv<1>(a, e, stream);
-    else if (a.m <= 2)
-        launch_gemv<2>(a, e, stream);
-    else if (a.m <= 4)
-        launch_gemv<4>(a, e, stream);
-    else if (a.m <= 8)
-        launch_gemv<8>(a, e, stream);
-    else if (a.m <= GEMV_MAX_M)
-        launch_gemv<16>(a, e, stream);
+    if (a.m <= SMALL_MAX_M)
+        launch_small(a, e, stream);
     else
     {
         const dim3 grid(a.n / BN, (a.m + BM - 1) / BM);

@@ -454,6 +454,25 @@ void categorical_path_q15(const float* tree, const std::uint16_t* token, const i
                                                                         rows, q15);
 }
 
+namespace
+{
+__global__ void scatter_rows_kernel(const std::uint16_t* __restrict__ src,
+                                    const int* __restrict__ src_index,
+                                    const int* __restrict__ dst_index, std::uint16_t* __restrict__ dst)
+{
+    const int j = blockIdx.x;
+    reinterpret_cast<unsigned*>(dst + static_cast<size_t>(dst_index[j]) * 512)[threadIdx.x] =
+        reinterpret_cast<const unsigned*>(src + static_cast<size_t>(src_index[j]) * 512)[threadIdx.x];
+}
+} // namespace
+
+void scatter_rows(const std::uint16_t* src, const int* src_index, const int* dst_index, int rows,
+                  std::uint16_t* dst, cudaStream_t stream)
+{
+    if (rows > 0)
+        scatter_rows_kernel<<<rows, 256, 0, stream>>>(src, src_index, dst_index, dst);
+}
+
 void build_gelu_table(std::uint16_t* table, cudaStream_t stream)
 {
     gelu_table_kernel<<<256, 256, 0, stream>>>(table);

@@ -59,6 +59,10 @@ void softmax_tree(const std::uint16_t* logits, int rows, std::uint16_t* probs_bf
 void categorical_path_q15(const float* tree, const std::uint16_t* token, const int* token_index,
                           int rows, std::uint16_t* q15, cudaStream_t stream);
 
+// dst row dst_index[j] = src row src_index[j], j < rows (512-wide bf16 rows).
+void scatter_rows(const std::uint16_t* src, const int* src_index, const int* dst_index, int rows,
+                  std::uint16_t* dst, cudaStream_t stream);
+
 // 65536-entry bf16 GELU table computed on the device.
 void build_gelu_table(std::uint16_t* table, cudaStream_t stream);
 } // namespace tsacb::dev
