@@ -144,7 +144,7 @@ def codec_workload(args, rank, world, torch, dist):
     dev = torch.device("cuda", torch.cuda.current_device())
     clips = args.clips
     opts = tsac_cuda.EncodeOptions(method="normal", codebooks=12, entropy_batch=3)
-    host = [synthetic.music_like(rank * 100000 + i, CLIP_SECONDS, 2) for i in range(clips)]
+    host = [synthetic.music_like(rank * 100000 + i, args.seconds, 2) for i in range(clips)]
     device_pcm = [torch.from_numpy(p).to(dev) for p in host]
     analyzer = tsac_cuda.CudaAnalyzer(tsac_cuda.seeded_package(0), torch.cuda.current_device())
     streams = tsac_cuda.encode_batch_device(analyzer, device_pcm, opts)
@@ -182,7 +182,7 @@ def codec_workload(args, rank, world, torch, dist):
     elapsed_ms = max_over_ranks(start.elapsed_time(end), world, torch, dist)
     stats = kernel_stats()
     tsac_cuda.library().tsac_cuda_kernel_timing(0)
-    audio_seconds = clips * CLIP_SECONDS * args.steps * world
+    audio_seconds = clips * args.seconds * args.steps * world
     value = audio_seconds / (elapsed_ms / 1e3)
 
     # e2e: the host-buffer API, PCM H2D and PCM/streams D2H inside the region.
@@ -233,7 +233,7 @@ def codec_workload(args, rank, world, torch, dist):
         "ms_per_step": round(elapsed_ms / args.steps, 2),
         "dtype": "f32+int8 (exact reference arithmetic)",
         "config": {"workload": "cfg0/cfg4: encode+decode of 30 s stereo clips", "clips_per_gpu": clips,
-                   "codebooks": 12, "entropy_batch": 3, "seconds_per_clip": CLIP_SECONDS,
+                   "codebooks": 12, "entropy_batch": 3, "seconds_per_clip": args.seconds,
                    "l2": "working set (PCM, activations) far larger than L2 each step",
                    "parity_cfg0_stream_vs_reference": parity},
         "roofline": roofline,
@@ -292,6 +292,51 @@ def codec_cpu(steps: int, warmup: int = 0):
             "sample": f"{len(walls)} step(s) x {cores} processes, each the reference ScalarAnalyzer "
                       f"encode+decode of one {REFERENCE_SAMPLE_SECONDS} s stereo clip (q=12, batch 3); "
                       f"{wall:.1f} s wall"}
+
+
+def frontend_workload(args, rank, world, torch, dist):
+    """Encoder front end only (padding, DAC analysis, RVQ) of B clips per GPU:
+    the exact-order analysis convolutions in isolation (profiling workload)."""
+    import synthetic
+    import tsac_cuda
+
+    opts = tsac_cuda.EncodeOptions(method="fast", codebooks=12)
+    host = [synthetic.music_like(rank * 100000 + i, args.seconds, 2) for i in range(args.clips)]
+    analyzer = tsac_cuda.CudaAnalyzer(tsac_cuda.seeded_package(0), torch.cuda.current_device())
+    for _ in range(args.warmup):
+        for p in host:
+            analyzer.analyze_tokens(p, opts)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    tsac_cuda.library().tsac_cuda_kernel_timing(1)
+    start, end = event_pair(torch)
+    start.record()
+    for _ in range(args.steps):
+        for p in host:
+            analyzer.analyze_tokens(p, opts)
+    end.record()
+    torch.cuda.synchronize()
+    elapsed_ms = max_over_ranks(start.elapsed_time(end), world, torch, dist)
+    stats = kernel_stats()
+    tsac_cuda.library().tsac_cuda_kernel_timing(0)
+    conv = stats["conv_exact"]
+    peaks = measured_peaks()
+    achieved = conv["work"] / (conv["ms"] / 1e3) / 1e12
+    peak = SM_COUNT * 128 * peaks["sm_max_mhz"] * 1e6 / 1e12
+    return {
+        "metric": "x-realtime encoder front end (DAC analysis + RVQ)",
+        "value": round(args.clips * args.seconds * args.steps * world / (elapsed_ms / 1e3), 2),
+        "unit": "x realtime", "ms_per_step": round(elapsed_ms / args.steps, 2),
+        "dtype": "f32 (exact reference order)",
+        "config": {"workload": "encoder front end", "clips_per_gpu": args.clips,
+                   "seconds_per_clip": args.seconds},
+        "roofline": {"bound": "fp32", "achieved": round(achieved, 2), "peak": round(peak, 2),
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "kernel": "conv_exact", "peak_source": "nominal FP32 issue at max SM clock"},
+        "gpu_launches": sum(v["launches"] for v in stats.values()),
+        "e2e": None,
+    }
 
 
 # ------------------------------------------------------------------ qlinear --
@@ -401,8 +446,10 @@ def main():
     parser.add_argument("--steps", type=int, default=2)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--workload", choices=["codec", "qlinear"], default="codec")
-    parser.add_argument("--clips", type=int, default=8, help="30 s clips per GPU per step")
+    parser.add_argument("--workload", choices=["codec", "qlinear", "frontend"], default="codec")
+    parser.add_argument("--clips", type=int, default=8, help="clips per GPU per step")
+    parser.add_argument("--seconds", type=float, default=CLIP_SECONDS,
+                        help="clip length (30 s is the benchmark; shorter for profiling runs)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -441,6 +488,8 @@ def main():
         torch.cuda.set_device(0)
     if args.workload == "codec":
         result = codec_workload(args, rank, world, torch, dist)
+    elif args.workload == "frontend":
+        result = frontend_workload(args, rank, world, torch, dist)
     else:
         result = qlinear_workload(args, rank, world, torch, dist)
     if rank == 0:

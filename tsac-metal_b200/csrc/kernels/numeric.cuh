@@ -153,6 +153,15 @@ __device__ __forceinline__ float carry_combine(const float* block_sums, int bloc
     return value;
 }
 
+// The binary carry over 2^k block sums (k >= 1) leaves the total in slot k and
+// zeros below it; the final fold then adds the zero slots and the total to
+// partial[0] = 0, which reduces to ftz_add(0, balanced tree of the block sums).
+// `tree` is that balanced tree, already flushed by its last ftz_add.
+__device__ __forceinline__ float carry_fold_power_of_two(float tree)
+{
+    return ftz_add(0.0f, tree);
+}
+
 // probability_sum of `count` values in shared/global memory, one thread.
 __device__ __forceinline__ float probability_sum_serial(const float* values, int count)
 {

@@ -230,6 +230,7 @@ __global__ void __launch_bounds__(256)
         uint4 wv = make_uint4(0, 0, 0, 0);
         if (n < n_cols)
             wv = __ldg(reinterpret_cast<const uint4*>(w + static_cast<size_t>(n) * k + b * 256 + l16 * 16));
+#pragma unroll 4
         for (int c = 0; c < m_rows; ++c)
         {
             const uint4 xv = __ldg(reinterpret_cast<const uint4*>(xq + static_cast<size_t>(c) * k +
@@ -254,9 +255,10 @@ __global__ void __launch_bounds__(256)
         if (n >= n_cols)
             continue;
         float sum = 0.0f;
+#pragma unroll 8
         for (int b = 0; b < blocks; ++b)
         {
-            const float scale = __fmul_rn(wscale[b * n_cols + n], xscale[c * blocks + b]);
+            const float scale = __fmul_rn(__ldg(wscale + b * n_cols + n), __ldg(xscale + c * blocks + b));
             sum = __fmaf_rn(static_cast<float>(dots[(r * blocks + b) * m_rows + c]), scale, sum);
         }
         y[static_cast<size_t>(c) * n_cols + n] = finish(sum, c, n, n_cols, e);

@@ -72,13 +72,14 @@ __device__ __forceinline__ float lane_pair16(const float* v)
 __device__ __forceinline__ float warp_sum512(const float* v)
 {
     float s = lane_pair16(v);
-    s = ftz_add(s, __shfl_xor_sync(0xffffffffu, s, 1));
-    s = ftz_add(s, __shfl_xor_sync(0xffffffffu, s, 2));
-    float blocks[8];
-#pragma unroll
-    for (int b = 0; b < 8; ++b)
-        blocks[b] = __shfl_sync(0xffffffffu, s, 4 * b);
-    return carry_combine(blocks, 8);
+    s = ftz_add(s, __shfl_xor_sync(0xffffffffu, s, 1)); // 32-value subtrees
+    s = ftz_add(s, __shfl_xor_sync(0xffffffffu, s, 2)); // 64-value block sums (lanes 4b..4b+3)
+    // Eight block sums in block order: balanced tree over blocks, then the
+    // carry's final fold (numeric.cuh: carry_fold_power_of_two).
+    s = ftz_add(s, __shfl_xor_sync(0xffffffffu, s, 4));
+    s = ftz_add(s, __shfl_xor_sync(0xffffffffu, s, 8));
+    s = ftz_add(s, __shfl_xor_sync(0xffffffffu, s, 16));
+    return carry_fold_power_of_two(s);
 }
 
 __global__ void layer_norm_kernel(const std::uint16_t* __restrict__ x,
@@ -277,8 +278,17 @@ __global__ void softmax_tree_kernel(const std::uint16_t* __restrict__ logits,
     if ((lane & 15) == 0)
         block_sums[warp * 2 + lane / 16] = s;
     __syncthreads();
-    if (t == 0)
-        total_shared = carry_combine(block_sums, 16);
+    if (t < 8)
+    {
+        // Sixteen 64-blocks: balanced tree over blocks (lanes 0-7 of warp 0),
+        // then the carry's final fold (numeric.cuh: carry_fold_power_of_two).
+        float b = ftz_add(block_sums[2 * t], block_sums[2 * t + 1]);
+        b = ftz_add(b, __shfl_xor_sync(0x000000ffu, b, 1));
+        b = ftz_add(b, __shfl_xor_sync(0x000000ffu, b, 2));
+        b = ftz_add(b, __shfl_xor_sync(0x000000ffu, b, 4));
+        if (t == 0)
+            total_shared = carry_fold_power_of_two(b);
+    }
     __syncthreads();
     const float reciprocal = __fdiv_rn(1.0f, total_shared);
     std::uint16_t p[4];
