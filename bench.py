@@ -119,11 +119,24 @@ def event_pair(torch):
 
 
 def max_over_ranks(value, world, torch, dist):
+    """Slowest rank's time: every rank takes this collective at the same point."""
     if world == 1:
         return value
-    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], device=device, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def clip_seeds(rank, clips):
+    """PCM seeds of one rank's clips: disjoint across ranks (clip sharding with
+    no data-path exchange); rank 0's clip 0 is the cfg0 clip (seed 0)."""
+    return [rank * 100000 + i for i in range(clips)]
+
+
+def whole_job_rate(units_per_rank, world, elapsed_ms_max):
+    """Units all ranks processed / the slowest rank's time (units per second)."""
+    return units_per_rank * world / (elapsed_ms_max / 1e3)
 
 
 def kernel_stats():
@@ -144,7 +157,7 @@ def codec_workload(args, rank, world, torch, dist):
     dev = torch.device("cuda", torch.cuda.current_device())
     clips = args.clips
     opts = tsac_cuda.EncodeOptions(method="normal", codebooks=12, entropy_batch=3)
-    host = [synthetic.music_like(rank * 100000 + i, args.seconds, 2) for i in range(clips)]
+    host = [synthetic.music_like(seed, args.seconds, 2) for seed in clip_seeds(rank, clips)]
     device_pcm = [torch.from_numpy(p).to(dev) for p in host]
     analyzer = tsac_cuda.CudaAnalyzer(tsac_cuda.seeded_package(0), torch.cuda.current_device())
     streams = tsac_cuda.encode_batch_device(analyzer, device_pcm, opts)
@@ -182,8 +195,7 @@ def codec_workload(args, rank, world, torch, dist):
     elapsed_ms = max_over_ranks(start.elapsed_time(end), world, torch, dist)
     stats = kernel_stats()
     tsac_cuda.library().tsac_cuda_kernel_timing(0)
-    audio_seconds = clips * args.seconds * args.steps * world
-    value = audio_seconds / (elapsed_ms / 1e3)
+    value = whole_job_rate(clips * args.seconds * args.steps, world, elapsed_ms)
 
     # e2e: the host-buffer API, PCM H2D and PCM/streams D2H inside the region.
     if world > 1:
@@ -201,7 +213,7 @@ def codec_workload(args, rank, world, torch, dist):
     torch.cuda.synchronize()
     clocks.stop()
     e2e_ms = max_over_ranks(s2.elapsed_time(e2), world, torch, dist)
-    e2e_value = audio_seconds / (e2e_ms / 1e3)
+    e2e_value = whole_job_rate(clips * args.seconds * args.steps, world, e2e_ms)
 
     # Roofline of the dominant kernel family, from the live CUDA-event timing.
     peaks = measured_peaks()

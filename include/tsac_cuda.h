@@ -121,6 +121,15 @@ int tsac_cuda_decode_batch_device(tsac_cuda_context* context, size_t count,
 int tsac_cuda_stream_info(const uint8_t* stream, size_t bytes, unsigned* channels,
                           size_t* samples_per_channel, size_t* symbols);
 
+/* unpack_fast (src/format/container.hpp:28, src/format/container.cpp): the
+ * 10-bit token fields of a fast-method stream, after the header and CRC
+ * checks.  Host-only; *tokens is malloc'd, release with tsac_cuda_free. */
+int tsac_cuda_unpack_fast(const uint8_t* stream, size_t bytes, uint16_t** tokens, size_t* count);
+
+/* token_crc32 (src/format/container.hpp:32): the CRC-32 (polynomial
+ * 0x04c11db7) that a normal stream's header carries over its token indices. */
+uint32_t tsac_cuda_token_crc32(const uint16_t* tokens, size_t count);
+
 /* ---- pipeline stages (host buffers; synchronous) ----------------------- */
 
 /* Encoder front end: padding, 400-frame chunks with 8/9 context, DAC analysis

@@ -157,6 +157,23 @@ int tsac_cuda_stream_info(const uint8_t* stream, size_t bytes, unsigned* channel
         });
 }
 
+int tsac_cuda_unpack_fast(const uint8_t* stream, size_t bytes, uint16_t** tokens, size_t* count)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            tsacb::require(stream && tokens && count, "null argument");
+            const auto values = tsacb::unpack_fast(tsacb::ByteView(stream, bytes));
+            *tokens = tsacb::malloc_copy(values.data(), values.size());
+            *count = values.size();
+        });
+}
+
+uint32_t tsac_cuda_token_crc32(const uint16_t* tokens, size_t count)
+{
+    return tsacb::token_crc32(std::span<const std::uint16_t>(tokens, tokens ? count : 0));
+}
+
 int tsac_cuda_encode_batch_device(tsac_cuda_context* ctx, size_t count,
                                   const float* const* pcm_device, const size_t* channels,
                                   const size_t* samples, const tsac_cuda_encode_options* opts,

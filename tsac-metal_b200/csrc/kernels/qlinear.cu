@@ -18,6 +18,8 @@
 #include "kernels/qlinear.cuh"
 #include "kernels/numeric.cuh"
 
+#include <atomic>
+
 namespace tsacb::dev
 {
 namespace
@@ -217,12 +219,20 @@ __global__ void __launch_bounds__(256)
                          int m_rows, int n_cols, int k, int rows_per_cta, Epilogue e,
                          std::uint16_t* __restrict__ y)
 {
-    extern __shared__ int dots[]; // [rows_per_cta][blocks][m_rows]
+    // Shared memory: the quantized activations [m_rows][k] (staged once with
+    // independent 16-byte loads, so their L2 latency is paid once), then the
+    // block dots [rows_per_cta][blocks][m_rows].
+    extern __shared__ __align__(16) unsigned char small_smem[];
+    std::int8_t* xs = reinterpret_cast<std::int8_t*>(small_smem);
+    int* dots = reinterpret_cast<int*>(small_smem + static_cast<size_t>(m_rows) * k);
     const int blocks = k / 256;
     const int n0 = blockIdx.x * rows_per_cta;
     const int half = threadIdx.x >> 4, l16 = threadIdx.x & 15;
     const unsigned mask = (threadIdx.x & 16) ? 0xffff0000u : 0x0000ffffu;
     const int items = rows_per_cta * blocks;
+    for (int i = threadIdx.x * 16; i < m_rows * k; i += blockDim.x * 16)
+        *reinterpret_cast<uint4*>(xs + i) = __ldg(reinterpret_cast<const uint4*>(xq + i));
+    __syncthreads();
     for (int item = half; item < items; item += 16)
     {
         const int r = item / blocks, b = item % blocks;
@@ -233,8 +243,8 @@ __global__ void __launch_bounds__(256)
 #pragma unroll 4
         for (int c = 0; c < m_rows; ++c)
         {
-            const uint4 xv = __ldg(reinterpret_cast<const uint4*>(xq + static_cast<size_t>(c) * k +
-                                                                  b * 256 + l16 * 16));
+            const uint4 xv = *reinterpret_cast<const uint4*>(xs + static_cast<size_t>(c) * k +
+                                                             b * 256 + l16 * 16);
             int d = __dp4a(static_cast<int>(wv.x), static_cast<int>(xv.x), 0);
             d = __dp4a(static_cast<int>(wv.y), static_cast<int>(xv.y), d);
             d = __dp4a(static_cast<int>(wv.z), static_cast<int>(xv.z), d);
@@ -265,12 +275,27 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// Rows per CTA: enough (row, block) items for the 16 half-warps, and at least
+// 4 so that few CTAs restage the same activations.
+int small_rows(int k)
+{
+    const int blocks = k / 256;
+    return blocks >= 4 ? 4 : 16 / blocks;
+}
+
+size_t small_smem_bytes(int m, int k)
+{
+    return static_cast<size_t>(m) * k + static_cast<size_t>(small_rows(k)) * (k / 256) * m * sizeof(int);
+}
+
+constexpr size_t SMALL_MAX_SMEM = 200 * 1024;
+
 void launch_small(const QLinearArgs& a, const Epilogue& e, cudaStream_t stream)
 {
-    // Rows per CTA: enough (row, block) items for the 16 half-warps.
-    const int blocks = a.k / 256;
-    const int rows = blocks >= 16 ? 1 : 16 / blocks;
-    const size_t smem = static_cast<size_t>(rows) * blocks * a.m * sizeof(int);
+    const int rows = small_rows(a.k);
+    const size_t smem = small_smem_bytes(a.m, a.k);
+    if (smem > 48 * 1024)
+        qlinear_init();
     qlinear_small_kernel<<<(a.n + rows - 1) / rows, 256, smem, stream>>>(
         a.weights, a.weight_scales, a.xq, a.xscale, a.m, a.n, a.k, rows, e, a.y);
 }
@@ -279,8 +304,20 @@ void launch_small(const QLinearArgs& a, const Epilogue& e, cudaStream_t stream)
 
 void qlinear_init()
 {
-    // Nothing to configure: every launch fits the default shared-memory limit
-    // (the decode-shaped kernel needs at most 16 x 64 ints of block dots).
+    // The decode-shaped kernel stages its int8 activations plus the block dots
+    // in shared memory, up to SMALL_MAX_SMEM bytes.  The attribute belongs to
+    // each device's context, so it is set once per device (a bit per ordinal;
+    // setting it twice from racing threads is harmless).
+    static std::atomic<unsigned long long> ready{0};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
+        return;
+    const unsigned long long bit = 1ull << device;
+    if (ready.load(std::memory_order_acquire) & bit)
+        return;
+    if (cudaFuncSetAttribute(qlinear_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(SMALL_MAX_SMEM)) == cudaSuccess)
+        ready.fetch_or(bit, std::memory_order_acq_rel);
 }
 
 size_t qlinear_scratch_bytes(size_t m, size_t k)
@@ -300,7 +337,7 @@ void qlinear_quantize(const std::uint16_t* x, int m, int k, std::int8_t* xq, flo
 void qlinear_matmul(const QLinearArgs& a, cudaStream_t stream)
 {
     const Epilogue e{a.bias, a.residual, a.lut};
-    if (a.m <= SMALL_MAX_M)
+    if (a.m <= SMALL_MAX_M && small_smem_bytes(a.m, a.k) <= SMALL_MAX_SMEM)
         launch_small(a, e, stream);
     else
     {

@@ -319,6 +319,22 @@ def stream_info(stream: bytes):
     return ch.value, spc.value, sym.value
 
 
+def unpack_fast(stream: bytes) -> np.ndarray:
+    """Token indices of a fast-method stream (header and CRC checked)."""
+    ptr, n = ctypes.POINTER(ctypes.c_uint16)(), ctypes.c_size_t()
+    check(library().tsac_cuda_unpack_fast(stream, ctypes.c_size_t(len(stream)), ctypes.byref(ptr),
+                                          ctypes.byref(n)))
+    return _take(ptr, n.value, np.uint16)
+
+
+def token_crc32(tokens) -> int:
+    """CRC-32 (polynomial 0x04c11db7) of token indices, as a normal header stores it."""
+    t = np.ascontiguousarray(tokens, dtype=np.uint16)
+    fn = library().tsac_cuda_token_crc32
+    fn.restype = ctypes.c_uint32
+    return fn(t.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(t.size))
+
+
 def encode_batch_device(analyzer: "CudaAnalyzer", pcm_tensors, options: EncodeOptions | None = None):
     """Encode HBM-resident interleaved PCM (torch CUDA float32 [samples][channels])."""
     n = len(pcm_tensors)
