@@ -79,6 +79,14 @@ typedef struct tsac_cuda_encode_options
 int tsac_cuda_context_create(const char* package_directory, int device, tsac_cuda_context** out);
 void tsac_cuda_context_destroy(tsac_cuda_context* context);
 
+/* Decoder synthesis arithmetic of a context.  0 (the default): the wide DAC
+ * decoder convolutions run on the tensor cores in 3xTF32 (decoded PCM within
+ * 1e-4 * (1 + max(|a|, |b|)) of the reference, the reference's own pipeline
+ * tolerance, tests/metal_optimized.cpp:741-745).  Nonzero: the reference's
+ * serial fp32 order on CUDA cores (decoded PCM bit-identical).  Streams are
+ * unaffected either way. */
+int tsac_cuda_set_exact_synthesis(tsac_cuda_context* context, int exact);
+
 /* AudioAnalyzer::encode (include/tsac/audio_analyzer.hpp:33-34) for a host
  * PCM view [channel, sample] with the given strides (in floats, as
  * tsac::PcmView's layout_stride).  *out (free with tsac_cuda_free) receives the
@@ -185,6 +193,10 @@ int tsac_cuda_kernel_timing(int enable);
  * accumulated since the last tsac_cuda_kernel_timing call (free with tsac_cuda_free). */
 int tsac_cuda_kernel_stats(char** json);
 
+/* Kernels this library has launched in this process so far (every device and
+ * thread; a decode-step graph launch adds its kernel nodes). */
+uint64_t tsac_cuda_launch_count(void);
+
 /* ---- kernel-level entry points (device pointers, enqueue on `stream`) -- */
 
 /* Scratch bytes tsac_cuda_qlinear needs for m columns of k inputs (the BF8L
@@ -245,6 +257,18 @@ int tsac_cuda_conv1d(const float* x, size_t frames, const float* weights, const 
                      const float* residual, float* y, size_t cin, size_t cout, size_t kernel,
                      size_t stride, size_t padding, size_t dilation, int transposed,
                      void* scratch, size_t scratch_bytes, unsigned* error_word, void* stream);
+
+/* The decoder's tensor-core convolution (3xTF32 tcgen05 implicit GEMM, the
+ * kernel DAC synthesis runs) on one sequence, for accuracy tests and
+ * microbenchmarks; arguments as tsac_cuda_conv1d.  Ordinary convolutions need
+ * stride 1 and 'same' padding (2 padding = (kernel - 1) dilation); transposed
+ * ones kernel 2 stride and padding stride / 2.  cin % 32 == 0; cout a multiple
+ * of 128 or 96.  alpha (device f32 [cout]) or NULL: y = Snake(conv).
+ * Allocates and frees device memory per call.  Synchronous on `stream`. */
+int tsac_cuda_conv1d_tensor(const float* x, size_t frames, const float* weights, const float* bias,
+                            const float* residual, const float* alpha, float* y, size_t cin,
+                            size_t cout, size_t kernel, size_t stride, size_t padding,
+                            size_t dilation, int transposed, unsigned* error_word, void* stream);
 
 /* DAC Snake, y = x + sin^2(alpha x) / (alpha + eps) with the captured
  * polynomial (scalar_snake_frames, src/scalar/dsp.cpp:93-119); x, y device

@@ -305,6 +305,16 @@ int tsac_cuda_dac_analysis(tsac_cuda_context* ctx, unsigned channels, const floa
         });
 }
 
+int tsac_cuda_set_exact_synthesis(tsac_cuda_context* ctx, int exact)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            tsacb::require(ctx != nullptr, "null argument");
+            ctx->impl.set_exact_synthesis(exact != 0);
+        });
+}
+
 int tsac_cuda_dac_synthesis(tsac_cuda_context* ctx, unsigned channels, const float* latent,
                             size_t frames, float* pcm)
 {

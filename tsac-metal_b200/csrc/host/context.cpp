@@ -80,8 +80,19 @@ DacEngine& Context::synthesis(unsigned channels)
     require(channels == 1 || channels == 2, "invalid model variant");
     auto& e = synthesis_[channels - 1];
     if (!e)
+    {
         e = std::make_unique<DacEngine>(prepare_dac(package_, channels, true, limits_), stream_);
+        e->set_exact_synthesis(exact_synthesis_);
+    }
     return *e;
+}
+
+void Context::set_exact_synthesis(bool exact)
+{
+    exact_synthesis_ = exact;
+    for (auto& e : synthesis_)
+        if (e)
+            e->set_exact_synthesis(exact);
 }
 
 RvqEngine& Context::rvq(unsigned channels)

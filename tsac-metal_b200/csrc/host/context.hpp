@@ -34,6 +34,9 @@ public:
     TransformerEngine& transformer(unsigned channels);
     DacEngine& analysis(unsigned channels);
     DacEngine& synthesis(unsigned channels);
+    // Exact synthesis (bit-identical PCM, serial CUDA-core convolutions) or
+    // the default tensor-core synthesis (PCM within tolerance).
+    void set_exact_synthesis(bool exact);
     RvqEngine& rvq(unsigned channels);
     const Package& package() const
     {
@@ -48,6 +51,7 @@ private:
     std::shared_ptr<DeviceTransformer> transformers_[2];
     std::unique_ptr<TransformerEngine> engines_[2];
     std::unique_ptr<DacEngine> analysis_[2], synthesis_[2];
+    bool exact_synthesis_ = false;
     std::unique_ptr<RvqEngine> rvq_[2];
 };
 } // namespace tsacb

@@ -1,6 +1,9 @@
 #include "dac_engine.hpp"
 
 #include "kernel_timer.hpp"
+#include "tf32_split.hpp"
+#include "kernels/error_bits.hpp"
+#include "kernels/tc_conv.cuh"
 
 #include <algorithm>
 #include <array>
@@ -22,6 +25,64 @@ std::vector<float> device_layout(const PreparedConv& c)
                     s.transposed ? c.weights[o + tap * cout + in * cout * k]
                                  : c.weights[in + tap * cin + o * cin * k];
     return out;
+}
+
+// Tensor-core operands of a synthesis convolution (tc_conv.cuh geometry), or
+// false when the shape stays on the exact kernels.  Ordinary: "same" length
+// (2 padding == (kernel - 1) dilation, stride 1), slices = taps.  Transposed:
+// kernel 2s, padding s/2, output = input x s; phase r of the output takes taps
+// b = (r + p) mod s and b + s from input rows i + (r + p) div s and one less.
+bool build_tensor_operands(DeviceConv& d, const PreparedConv& c, cudaStream_t stream)
+{
+    const auto& s = c.spec;
+    const int cin = static_cast<int>(s.input_channels), cout = static_cast<int>(s.output_channels);
+    const int k = static_cast<int>(s.kernel);
+    if (!dev::tc_conv_supported(cin, cout))
+        return false;
+    std::vector<float> w;
+    if (!s.transposed)
+    {
+        if (s.stride != 1 || 2 * s.padding != (s.kernel - 1) * s.dilation || k > 16)
+            return false;
+        d.tc_taps = k;
+        d.tc_phases = 1;
+        d.tc_step = static_cast<int>(s.dilation);
+        d.tc_shift[0] = -static_cast<int>(s.padding);
+        w.resize(static_cast<std::size_t>(k) * cout * cin);
+        for (int tap = 0; tap < k; ++tap)
+            for (int o = 0; o < cout; ++o)
+                for (int in = 0; in < cin; ++in)
+                    w[(static_cast<std::size_t>(tap) * cout + o) * cin + in] =
+                        c.weights[in + static_cast<std::size_t>(tap) * cin + static_cast<std::size_t>(o) * cin * k];
+    }
+    else
+    {
+        const int st = static_cast<int>(s.stride), p = static_cast<int>(s.padding);
+        if (k != 2 * st || 2 * p != st || st > 8)
+            return false;
+        d.tc_taps = 2;
+        d.tc_phases = st;
+        d.tc_step = -1;
+        w.resize(static_cast<std::size_t>(st) * 2 * cout * cin);
+        for (int r = 0; r < st; ++r)
+        {
+            d.tc_shift[r] = (r + p) / st;
+            const int b = (r + p) % st;
+            for (int j = 0; j < 2; ++j)
+            {
+                const int tap = b + j * st, slice = r * 2 + j;
+                for (int o = 0; o < cout; ++o)
+                    for (int in = 0; in < cin; ++in)
+                        w[(static_cast<std::size_t>(slice) * cout + o) * cin + in] =
+                            c.weights[o + static_cast<std::size_t>(tap) * cout + static_cast<std::size_t>(in) * cout * k];
+            }
+        }
+    }
+    std::vector<float> hi, lo;
+    split_tf32(w, hi, lo);
+    d.tc_hi = upload(hi, stream);
+    d.tc_lo = upload(lo, stream);
+    return true;
 }
 
 // Output length of a convolution (src/common/dsp.tpp:141-156).
@@ -50,8 +111,13 @@ DacEngine::DacEngine(const PreparedDac& dac, cudaStream_t stream)
         d.spec = c.spec;
         d.weights = upload(device_layout(c), stream);
         d.bias = upload(c.bias, stream);
+        if (synthesis_ && c.spec.output_channels >= 16)
+            tensor_ready_ = build_tensor_operands(d, c, stream) && tensor_ready_;
         convs_.push_back(std::move(d));
     }
+    // The synthesis graph this engine drives: the entry convolution, then per
+    // stage one transposed convolution and three residual units, then the exit.
+    tensor_ready_ = tensor_ready_ && synthesis_ && convs_.size() == 30;
     for (const auto& a : dac.alphas)
     {
         alphas_.push_back(upload(a, stream));
@@ -69,6 +135,8 @@ void DacEngine::check_errors(const char* what)
     if (word)
     {
         cuda_ok(cudaMemsetAsync(error_.as<void>(), 0, 4, stream_), "memset");
+        if (word & dev::error_timeout)
+            throw DeviceError(std::string("tensor-core pipeline wait timed out (") + what + ")");
         throw NumericError(std::string("nonfinite DSP value (") + what + ")");
     }
 }
@@ -199,6 +267,125 @@ void DacEngine::analyze(const float* pcm, const std::vector<long long>& offsets,
 void DacEngine::synthesize(const float* latent, const std::vector<int>& frames, float* pcm)
 {
     require(synthesis_, "synthesis on an analysis model");
+    if (!exact_synthesis_ && tensor_ready_)
+        synthesize_tensor(latent, frames, pcm);
+    else
+        synthesize_exact(latent, frames, pcm);
+}
+
+void DacEngine::tc_conv(int index, const float* x_hi, const float* x_lo, long long in_rows,
+                        int in_scale, const float* residual, float* raw, int alpha, float* hi,
+                        float* lo, const unsigned char* valid)
+{
+    const auto& c = convs_[static_cast<std::size_t>(index)];
+    dev::TcConvGeometry g{};
+    g.rows = in_rows;
+    g.cin = static_cast<int>(c.spec.input_channels);
+    g.cout = static_cast<int>(c.spec.output_channels);
+    g.taps = c.tc_taps;
+    g.phases = c.tc_phases;
+    g.out_stride = c.tc_phases;
+    g.tap_step = c.tc_step;
+    for (int r = 0; r < 8; ++r)
+        g.row_shift[r] = c.tc_shift[r];
+    g.in_rows = in_rows;
+    g.out_rows = in_rows * c.tc_phases;
+    g.out_scale = in_scale * c.tc_phases;
+    const dev::TcConvEpilogue e{c.bias.as<float>(), residual, raw,
+                                alpha >= 0 ? alphas_[static_cast<std::size_t>(alpha)].as<float>() : nullptr,
+                                hi, lo, valid, error_word()};
+    const dev::TcConvOperands op{x_hi, x_lo, c.tc_hi.as<float>(), c.tc_lo.as<float>()};
+    // Useful MACs: valid output rows x cout x cin x taps per output.
+    const double macs = static_cast<double>(tc_valid_latent_) * g.out_scale * g.cout * g.cin * g.taps;
+    KernelTimer::Scope timing("conv_tc", stream_, 2.0 * macs);
+    cuda_ok(dev::tc_conv(op, g, e, stream_), "tensor-core convolution");
+}
+
+void DacEngine::synthesize_tensor(const float* latent, const std::vector<int>& frames, float* pcm)
+{
+    // Padded latent rows: G zero rows before, between and after the windows.
+    // At every stage the layout is this one scaled by the cumulative
+    // upsampling, so gaps grow to >= 32 rows, wider than any tap reach (27).
+    constexpr int G = 4;
+    const std::size_t count = frames.size();
+    std::vector<long long> base(count);
+    long long r0 = G, total = 0;
+    for (std::size_t q = 0; q < count; ++q)
+    {
+        require(frames[q] > 0, "synthesis window without frames");
+        base[q] = r0;
+        r0 += frames[q] + G;
+        total += frames[q];
+    }
+    std::vector<unsigned char> valid(static_cast<std::size_t>(r0), 0);
+    std::vector<long long> row_map(static_cast<std::size_t>(total));
+    long long k = 0;
+    for (std::size_t q = 0; q < count; ++q)
+        for (int f = 0; f < frames[q]; ++f)
+        {
+            valid[static_cast<std::size_t>(base[q] + f)] = 1;
+            row_map[static_cast<std::size_t>(k++)] = base[q] + f;
+        }
+    auto* d_valid = ws_.get<unsigned char>("tc_valid", valid.size());
+    auto* d_map = ws_.get<long long>("tc_map", row_map.size());
+    cuda_ok(cudaMemcpyAsync(d_valid, valid.data(), valid.size(), cudaMemcpyHostToDevice, stream_), "H2D");
+    cuda_ok(cudaMemcpyAsync(d_map, row_map.data(), row_map.size() * sizeof(long long),
+                            cudaMemcpyHostToDevice, stream_),
+            "H2D");
+    const std::size_t widest = static_cast<std::size_t>(r0) * 49152;
+    float* a = ws_.get<float>("tc_a", widest);
+    float* p[2][2] = {{ws_.get<float>("tc_p0h", widest), ws_.get<float>("tc_p0l", widest)},
+                      {ws_.get<float>("tc_p1h", widest), ws_.get<float>("tc_p1l", widest)}};
+    tc_valid_latent_ = total;
+    const std::size_t latent_bytes = static_cast<std::size_t>(r0) * 1024 * sizeof(float);
+    cuda_ok(cudaMemsetAsync(p[0][0], 0, latent_bytes, stream_), "memset");
+    cuda_ok(cudaMemsetAsync(p[0][1], 0, latent_bytes, stream_), "memset");
+    dev::pad_split_rows(latent, total, 1024, d_map, p[0][0], p[0][1], stream_);
+
+    int cur = 0;
+    long long rows = r0;
+    int scale = 1;
+    // Entry convolution; its epilogue applies stage 0's first Snake.
+    tc_conv(0, p[cur][0], p[cur][1], rows, scale, nullptr, nullptr, 0, p[1 - cur][0], p[1 - cur][1], d_valid);
+    cur ^= 1;
+    for (int stage = 0; stage < 4; ++stage)
+    {
+        const int up = 1 + stage * 7;
+        tc_conv(up, p[cur][0], p[cur][1], rows, scale, nullptr, a, stage * 7 + 1, p[1 - cur][0],
+                p[1 - cur][1], d_valid);
+        cur ^= 1;
+        rows *= convs_[static_cast<std::size_t>(up)].tc_phases;
+        scale *= convs_[static_cast<std::size_t>(up)].tc_phases;
+        for (int unit = 0; unit < 3; ++unit)
+        {
+            const int conv_index = up + 1 + unit * 2;
+            const int first_alpha = stage * 7 + 1 + unit * 2;
+            tc_conv(conv_index, p[cur][0], p[cur][1], rows, scale, nullptr, nullptr, first_alpha + 1,
+                    p[1 - cur][0], p[1 - cur][1], d_valid);
+            cur ^= 1;
+            const bool exit_next = stage == 3 && unit == 2;
+            const int next_alpha = unit < 2 ? first_alpha + 2 : (stage < 3 ? (stage + 1) * 7 : 28);
+            // Residual sum kept only while another residual unit of the stage reads it.
+            tc_conv(conv_index + 1, p[cur][0], p[cur][1], rows, scale, a, unit < 2 ? a : nullptr,
+                    next_alpha, p[1 - cur][0], exit_next ? nullptr : p[1 - cur][1], d_valid);
+            cur ^= 1;
+        }
+    }
+    // Exit convolution to PCM on the exact kernel, reading Snake(28) rows of
+    // the padded layout.
+    std::vector<int> in_frames(count), out_frames;
+    std::vector<long long> offsets(count);
+    for (std::size_t q = 0; q < count; ++q)
+    {
+        in_frames[q] = frames[q] * scale;
+        offsets[q] = base[q] * scale;
+    }
+    conv(29, p[cur][0], pcm, nullptr, in_frames, out_frames, &offsets);
+    cuda_ok(cudaGetLastError(), "synthesis launch");
+}
+
+void DacEngine::synthesize_exact(const float* latent, const std::vector<int>& frames, float* pcm)
+{
     long long total = 0;
     for (int v : frames)
         total += v;

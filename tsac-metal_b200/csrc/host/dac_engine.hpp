@@ -17,6 +17,11 @@ struct DeviceConv
     Conv1dSpec spec;
     DeviceBuffer weights; // [tap][in][out]
     DeviceBuffer bias;
+    // Tensor-core synthesis operands (empty when the shape stays on the exact
+    // kernels): [slice][out][in] TF32 head and fp32 tail; see tc_conv.cuh.
+    DeviceBuffer tc_hi, tc_lo;
+    int tc_taps = 0, tc_phases = 0, tc_step = 0;
+    int tc_shift[8] = {};
 };
 
 class DacEngine
@@ -32,7 +37,18 @@ public:
     void analyze(const float* pcm, const std::vector<long long>& offsets,
                  const std::vector<int>& frames, float* latent);
     // Synthesis: latent windows [sum of frames][1024] -> pcm [sum frames*512][C].
+    // Tensor-core mode (the default) runs the wide convolutions as 3xTF32
+    // tcgen05 GEMMs (PCM within tolerance of the reference); exact mode keeps
+    // the reference's serial arithmetic (PCM bit-identical).
     void synthesize(const float* latent, const std::vector<int>& frames, float* pcm);
+    void set_exact_synthesis(bool exact)
+    {
+        exact_synthesis_ = exact;
+    }
+    bool exact_synthesis() const
+    {
+        return exact_synthesis_;
+    }
     unsigned* error_word() const
     {
         return error_.as<unsigned>();
@@ -45,8 +61,16 @@ private:
               const std::vector<int>& in_frames, std::vector<int>& out_frames,
               const std::vector<long long>* in_offsets = nullptr);
     void snake(int index, const float* x, float* y, long long frames);
+    void synthesize_exact(const float* latent, const std::vector<int>& frames, float* pcm);
+    void synthesize_tensor(const float* latent, const std::vector<int>& frames, float* pcm);
+    void tc_conv(int index, const float* x_hi, const float* x_lo, long long in_rows, int in_scale,
+                 const float* residual, float* raw, int alpha, float* hi, float* lo,
+                 const unsigned char* valid);
 
     bool synthesis_;
+    bool exact_synthesis_ = false;
+    bool tensor_ready_ = true; // every wide synthesis convolution has tensor operands
+    long long tc_valid_latent_ = 0;
     unsigned channels_;
     std::vector<DeviceConv> convs_;
     std::vector<DeviceBuffer> alphas_;

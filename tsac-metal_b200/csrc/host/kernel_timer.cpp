@@ -1,7 +1,9 @@
 #include "kernel_timer.hpp"
 
 #include "abi_util.hpp"
+#include "kernels/launch_count.hpp"
 
+#include <atomic>
 #include <map>
 #include <sstream>
 
@@ -110,8 +112,50 @@ KernelTimer::Scope::~Scope()
 }
 } // namespace tsacb
 
+namespace tsacb::dev
+{
+namespace
+{
+std::atomic<unsigned long long> launches{0};
+thread_local CaptureTally* capturing = nullptr;
+} // namespace
+
+void note_launch(unsigned long long kernels)
+{
+    if (capturing)
+        capturing->kernels_ += kernels;
+    else
+        launches.fetch_add(kernels, std::memory_order_relaxed);
+}
+
+unsigned long long launch_count()
+{
+    return launches.load(std::memory_order_relaxed);
+}
+
+CaptureTally::CaptureTally() : outer_(capturing)
+{
+    capturing = this;
+}
+
+CaptureTally::~CaptureTally()
+{
+    capturing = outer_;
+}
+
+unsigned long long CaptureTally::kernels() const
+{
+    return kernels_;
+}
+} // namespace tsacb::dev
+
 extern "C"
 {
+uint64_t tsac_cuda_launch_count(void)
+{
+    return tsacb::dev::launch_count();
+}
+
 int tsac_cuda_kernel_timing(int enable)
 {
     return tsacb::guarded(

@@ -2,6 +2,7 @@
 
 #include "kernel_timer.hpp"
 
+#include "kernels/launch_count.hpp"
 #include "kernels/qlinear.cuh"
 #include "kernels/transformer_ops.cuh"
 
@@ -429,15 +430,20 @@ struct TransformerEngine::DecodeState
     std::unique_ptr<PinnedBuffer> host_in, host_masses, host_error;
     char* dev_in = nullptr;
     int* identity = nullptr;
-    std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs; // (temporal, book, rows)
+    struct StepGraph
+    {
+        cudaGraphExec_t exec;
+        unsigned long long kernels; // kernel nodes, for the launch tally
+    };
+    std::map<std::tuple<int, int, int>, StepGraph> graphs; // (temporal, book, rows)
     std::vector<LaneRef> last;
     std::vector<int> last_lanes;
     std::size_t last_book = 0;
 
     ~DecodeState()
     {
-        for (auto& [key, exec] : graphs)
-            cudaGraphExecDestroy(exec);
+        for (auto& [key, graph] : graphs)
+            cudaGraphExecDestroy(graph.exec);
     }
 };
 
@@ -711,17 +717,23 @@ TransformerEngine::decode_predict(std::size_t step, std::size_t book, const floa
         if (found == st.graphs.end())
         {
             cudaGraph_t graph = nullptr;
-            cuda_ok(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "capture");
-            enqueue(temporal_rows);
-            cuda_ok(cudaStreamEndCapture(s, &graph), "capture");
+            unsigned long long kernels = 0;
+            {
+                dev::CaptureTally tally;
+                cuda_ok(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "capture");
+                enqueue(temporal_rows);
+                cuda_ok(cudaStreamEndCapture(s, &graph), "capture");
+                kernels = tally.kernels();
+            }
             cudaGraphExec_t exec = nullptr;
             const auto status = cudaGraphInstantiate(&exec, graph, 0);
             cudaGraphDestroy(graph);
             cuda_ok(status, "cudaGraphInstantiate");
-            found = st.graphs.emplace(key, exec).first;
+            found = st.graphs.emplace(key, DecodeState::StepGraph{exec, kernels}).first;
         }
         KernelTimer::Scope timing("decode_step", s, weight_bytes);
-        cuda_ok(cudaGraphLaunch(found->second, s), "cudaGraphLaunch");
+        cuda_ok(cudaGraphLaunch(found->second.exec, s), "cudaGraphLaunch");
+        dev::note_launch(found->second.kernels);
     }
     cuda_ok(cudaStreamSynchronize(s), "decode step");
     if (*st.host_error->as<unsigned>())

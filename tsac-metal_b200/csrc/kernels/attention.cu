@@ -14,6 +14,7 @@
 //   kernel 2, one CTA per (row, head): the sequential merge over blocks, which
 //   is cheap (16 steps at 1024 keys) and keeps the reference's order.
 #include "kernels/numeric.cuh"
+#include "kernels/launch_count.hpp"
 #include "kernels/transformer_ops.cuh"
 
 namespace tsacb::dev
@@ -195,10 +196,13 @@ void attention(const std::uint16_t* query, const RowMeta* meta, const std::uint1
     {
         attention_block_kernel<true><<<dim3(rows * HEADS, 1), 128, 0, stream>>>(
             query, meta, cache_k, cache_v, 1, nullptr, out);
+        note_launch();
         return;
     }
     attention_block_kernel<false><<<dim3(rows * HEADS, blocks), 128, 0, stream>>>(
         query, meta, cache_k, cache_v, blocks, partials, nullptr);
+    note_launch();
     attention_combine_kernel<<<rows * HEADS, 128, 0, stream>>>(meta, partials, blocks, out);
+    note_launch();
 }
 } // namespace tsacb::dev

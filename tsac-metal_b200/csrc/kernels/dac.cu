@@ -20,40 +20,14 @@
 // reused 4x (inputs) or 8x (weights) from registers.  Device weights are laid
 // out [tap][in][out] so the weight slice loads are contiguous.
 #include "kernels/dac.cuh"
+#include "kernels/dac_math.cuh"
+#include "kernels/launch_count.hpp"
 #include "kernels/numeric.cuh"
 
 namespace tsacb::dev
 {
 namespace
 {
-__device__ __forceinline__ float sine_squared(float phase)
-{
-    const float reduced = __fmul_rn(phase, __uint_as_float(0x3f22f983u));
-    const float quadrant = rintf(reduced); // ties to even
-    const int q = (quadrant >= -2147483648.0f && quadrant < 2147483648.0f)
-                      ? static_cast<int>(quadrant)
-                      : INT_MIN;
-    float x = __fmaf_rn(quadrant, __uint_as_float(0xbfc90000u), phase);
-    x = __fmaf_rn(quadrant, __uint_as_float(0xb9fdaa22u), x);
-    const float x2 = __fmul_rn(x, x);
-    float value;
-    if ((q & 1) == 0)
-    {
-        float p = __fmaf_rn(__uint_as_float(0xb94ca1f9u), x2, __uint_as_float(0x3c08839eu));
-        p = __fmaf_rn(p, x2, __uint_as_float(0xbe2aaaa3u));
-        const float cube = __fmul_rn(x, x2);
-        value = __fmaf_rn(cube, p, x);
-    }
-    else
-    {
-        float p = __fmaf_rn(__uint_as_float(0x37ccf5ceu), x2, __uint_as_float(0xbab6061au));
-        p = __fmaf_rn(p, x2, __uint_as_float(0x3d2aaaa5u));
-        p = __fmaf_rn(p, x2, __uint_as_float(0xbf000000u));
-        value = __fmaf_rn(p, x2, 1.0f);
-    }
-    return __fmul_rn(value, value);
-}
-
 __global__ void snake_kernel(const float* __restrict__ x, const float* __restrict__ alpha,
                              int channels, long long count, float* __restrict__ y,
                              unsigned* error_word)
@@ -419,6 +393,7 @@ void snake(const float* x, const float* alpha, int channels, long long frames, f
     blocks = blocks > 148 * 16 ? 148 * 16 : blocks;
     snake_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(x, alpha, channels, count, y,
                                                                error_word);
+    note_launch();
 }
 
 int conv_tile_frames(const ConvShape&)
@@ -433,6 +408,7 @@ void conv1d(const ConvLaunch& l, cudaStream_t stream)
     const dim3 grid(l.tile_count, (l.shape.cout + TO - 1) / TO);
     conv1d_kernel<<<grid, 256, 0, stream>>>(l.x, l.weights, l.bias, l.residual, l.y, l.sequences,
                                             l.tiles, l.shape, l.error_word);
+    note_launch();
 }
 
 void conv1d_narrow(const float* x, const float* w, const float* bias, float* y,
@@ -443,28 +419,38 @@ void conv1d_narrow(const float* x, const float* w, const float* bias, float* y,
         return;
     conv1d_narrow_kernel<<<static_cast<int>((total_outputs + 127) / 128), 128, 0, stream>>>(
         x, w, bias, y, sequences, sequence_count, s, total_outputs, error_word);
+    note_launch();
 }
 
 void rvq_encode(const float* latent, int frames, const RvqBookDevice* books, int book_count,
                 std::uint16_t* tokens, int token_stride, unsigned* error_word, cudaStream_t stream)
 {
     if (frames > 0)
+    {
         rvq_encode_kernel<<<frames, 256, 0, stream>>>(latent, books, book_count, tokens,
                                                       token_stride, error_word);
+        note_launch();
+    }
 }
 
 void rvq_decode(const std::uint16_t* tokens, int token_stride, int frames,
                 const RvqBookDevice* books, int book_count, float* latent, cudaStream_t stream)
 {
     if (frames > 0)
+    {
         rvq_decode_kernel<<<frames, 256, 0, stream>>>(tokens, token_stride, books, book_count,
                                                       latent);
+        note_launch();
+    }
 }
 
 void check_finite(const float* x, long long count, unsigned* error_word, cudaStream_t stream)
 {
     if (count > 0)
+    {
         check_finite_kernel<<<148 * 4, 256, 0, stream>>>(x, count, error_word);
+        note_launch();
+    }
 }
 
 namespace
@@ -507,5 +493,6 @@ void pcm_regroup(const float* src, long long samples, long long channel_stride,
     pcm_regroup_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(
         src, samples, channel_stride, sample_stride, groups, model_channels, padded, dst,
         error_word);
+    note_launch();
 }
 } // namespace tsacb::dev

@@ -17,6 +17,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "kernels/error_bits.hpp"
+
 namespace tsacb::dev
 {
 __device__ __forceinline__ float flush(float x)
@@ -206,12 +208,4 @@ __device__ __forceinline__ float warp_probability_sum(const float* values, int c
     return carry_combine(sums, blocks);
 }
 
-// Device error word bits, OR-ed by kernels and checked by the host after
-// completion (the reference's Metal kernels use the same pattern,
-// src/metal/dac/snake.metal:49-52).
-enum ErrorBits : unsigned
-{
-    error_nonfinite = 1u,
-    error_range = 2u,
-};
 } // namespace tsacb::dev

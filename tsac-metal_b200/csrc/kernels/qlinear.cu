@@ -16,6 +16,7 @@
 // source plane), w_scale f32 [K/256][N], bias f32 [N], activations bf16 [M][K].
 // Quantized activations: int8 [M][K] + f32 scale [M][K/256] in caller scratch.
 #include "kernels/qlinear.cuh"
+#include "kernels/launch_count.hpp"
 #include "kernels/numeric.cuh"
 
 #include <atomic>
@@ -298,6 +299,7 @@ void launch_small(const QLinearArgs& a, const Epilogue& e, cudaStream_t stream)
         qlinear_init();
     qlinear_small_kernel<<<(a.n + rows - 1) / rows, 256, smem, stream>>>(
         a.weights, a.weight_scales, a.xq, a.xscale, a.m, a.n, a.k, rows, e, a.y);
+    note_launch();
 }
 
 } // namespace
@@ -332,6 +334,7 @@ void qlinear_quantize(const std::uint16_t* x, int m, int k, std::int8_t* xq, flo
     const int threads = 256;
     quantize_bf8l_kernel<<<(warps * 32 + threads - 1) / threads, threads, 0, stream>>>(
         x, k, m, xq, xscale, error_word);
+    note_launch();
 }
 
 void qlinear_matmul(const QLinearArgs& a, cudaStream_t stream)
@@ -344,6 +347,7 @@ void qlinear_matmul(const QLinearArgs& a, cudaStream_t stream)
         const dim3 grid(a.n / BN, (a.m + BM - 1) / BM);
         qlinear_gemm_kernel<<<grid, 256, 0, stream>>>(a.weights, a.weight_scales, a.xq, a.xscale,
                                                       a.m, a.n, a.k, e, a.y);
+        note_launch();
     }
 }
 } // namespace tsacb::dev

@@ -1,0 +1,654 @@
+// tcgen05 implicit-GEMM convolution (DAC synthesis), 3xTF32.
+//
+// One persistent CTA per SM, six warps:
+//   warp 0      TMA producer: per k-block (tap, 32 input channels) it loads the
+//               input head/tail tiles [128 rows][32 ch] and the weight head/tail
+//               tiles [BN out][32 ch], 128-byte swizzled, into a STAGES-deep ring.
+//   warp 1      TMEM owner and MMA issuer: 4 k-steps x 3 tcgen05.mma (kind::tf32,
+//               M=128, N=BN, K=8) per k-block into the tile's four TMEM
+//               accumulators; tcgen05.commit frees the smem stage and, per
+//               tile, hands the accumulators to the epilogue.
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (one TMEM lane = one
+//               output row per thread), + bias (+ residual), optional Snake of
+//               the next layer, head/tail split, zero rows outside sequences,
+//               fp32 stores; then the accumulators are released for the
+//               next tile (the epilogue is short next to a tile's K loop).
+// M = 128 output rows (time), N = BN output channels, K = taps x cin.
+//
+// Every wait is bounded (about one second of global time).  A wait that gives
+// up raises error_timeout in the error word and an abort flag that ends the
+// other roles' loops; the producer then waits (bounded) for its loads in
+// flight, the MMA warp for its MMAs, and the TMEM is freed before the CTA exits.
+#include "kernels/dac_math.cuh"
+#include "kernels/launch_count.hpp"
+#include "kernels/numeric.cuh"
+#include "kernels/tc_conv.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+namespace tsacb::dev
+{
+namespace
+{
+constexpr int BM = 128;        // rows per tile (TMEM lanes)
+constexpr int BK = 32;         // fp32 per k-block row: one 128-byte swizzle row
+constexpr int A_BYTES = BM * BK * 4;
+constexpr unsigned long long WAIT_NS = 1000000000ull;
+
+// Four TMEM accumulators per tile (BN columns each): the hi*hi products of
+// k-step j go to accumulator j mod 3 and the hi*lo + lo*hi corrections to the
+// fourth.  The tensor core's fp32 accumulation rounds toward zero, so its
+// error grows with the length of each accumulation chain; three short main
+// chains and a correction chain 2^11 times smaller in magnitude, summed with
+// round-to-nearest adds in the epilogue, keep the error near fp32 rounding.
+constexpr int ACCS = 4;
+template <int BN> struct Config;
+template <> struct Config<128>
+{
+    static constexpr int stages = 3, tmem_cols = 512;
+};
+template <> struct Config<96>
+{
+    static constexpr int stages = 3, tmem_cols = 512;
+};
+
+template <int BN> __host__ __device__ constexpr int stage_bytes()
+{
+    return 2 * A_BYTES + 2 * BN * BK * 4;
+}
+template <int BN> __host__ __device__ constexpr int smem_bytes()
+{
+    return Config<BN>::stages * stage_bytes<BN>() + 1024 /* alignment */ + 256 /* barriers */;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void bar_init(uint32_t bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok)
+                 : "r"(bar), "r"(parity)
+                 : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase of `parity` to complete.  Returns false after
+// about WAIT_NS of global time, or early when another role has aborted.
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag)
+{
+    if (bar_try(bar, parity))
+        return true;
+    const unsigned long long start = global_ns();
+    for (unsigned iter = 1;; ++iter)
+    {
+        if (bar_try(bar, parity))
+            return true;
+        if ((iter & 63u) == 0)
+        {
+            if (*abort_flag)
+                return false;
+            if (global_ns() - start > WAIT_NS)
+                return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void bar_expect_tx(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bar_arrive(uint32_t bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                       uint32_t bar)
+{
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                       uint32_t bar)
+{
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+                 : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
+// 128 bytes in 8-row (1024-byte) atoms stacked along M/N.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr)
+{
+    uint64_t d = static_cast<uint64_t>((saddr & 0x3ffffu) >> 4);
+    d |= static_cast<uint64_t>(1) << 16;           // leading byte offset (unused here)
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;   // stride byte offset: 8 rows x 128 B
+    d |= static_cast<uint64_t>(1) << 46;           // descriptor version
+    d |= static_cast<uint64_t>(2) << 61;           // 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor: D f32, A and B tf32, both K-major, M = 128, N = BN.
+template <int BN> __device__ __forceinline__ uint32_t tf32_idesc()
+{
+    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+           (static_cast<uint32_t>(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate)
+{
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                 "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before()
+{
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after()
+{
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_load16(uint32_t taddr, float (&v)[16])
+{
+    uint32_t r[16];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32"
+                 " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                   "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+                   "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+        v[j] = __uint_as_float(r[j]);
+}
+
+// Nearest TF32 value (ties away from zero) of a finite fp32; the truncated
+// value where rounding would overflow to infinity.
+__device__ __forceinline__ float tf32_round(float x)
+{
+    const unsigned bits = __float_as_uint(x);
+    const float r = __uint_as_float((bits + 0x1000u) & 0xffffe000u);
+    return isinf(r) && !isinf(x) ? __uint_as_float(bits & 0xffffe000u) : r;
+}
+
+// Head/tail split: hi = nearest TF32 of x, lo = nearest TF32 of the exact
+// remainder x - hi; x - (hi + lo) <= 2^-22 |x|.
+__device__ __forceinline__ void tf32_split(float x, float& hi, float& lo)
+{
+    hi = tf32_round(x);
+    lo = tf32_round(__fsub_rn(x, hi));
+}
+
+struct TileCoord
+{
+    int phase;
+    long long m;
+    int n;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(long long tile, long long m_tiles, int n_tiles)
+{
+    TileCoord t;
+    t.n = static_cast<int>(tile % n_tiles);
+    const long long pm = tile / n_tiles;
+    t.m = pm % m_tiles;
+    t.phase = static_cast<int>(pm / m_tiles);
+    return t;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    tc_conv_kernel(const __grid_constant__ CUtensorMap map_xhi,
+                   const __grid_constant__ CUtensorMap map_xlo,
+                   const __grid_constant__ CUtensorMap map_whi,
+                   const __grid_constant__ CUtensorMap map_wlo, const TcConvGeometry g,
+                   const TcConvEpilogue e)
+{
+    constexpr int STAGES = Config<BN>::stages;
+    constexpr int TMEM_COLS = Config<BN>::tmem_cols;
+    static_assert(ACCS * BN <= TMEM_COLS, "accumulators exceed the TMEM allocation");
+    constexpr int STAGE = stage_bytes<BN>();
+    constexpr int B_BYTES = BN * BK * 4;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
+    // bars: full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
+    const uint32_t acc_full0 = smem_u32(bars + 2 * STAGES), acc_empty0 = acc_full0 + 16;
+    const uint32_t drain = acc_full0 + 32;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long m_tiles = (g.rows + BM - 1) / BM;
+    const int n_tiles = g.cout / BN;
+    const long long tiles = m_tiles * n_tiles * g.phases;
+    const int kb_per_tap = g.cin / BK;
+    const int kblocks = g.taps * kb_per_tap;
+
+    if (threadIdx.x == 0)
+    {
+        for (int s = 0; s < STAGES; ++s)
+        {
+            bar_init(full0 + 8 * s, 1);
+            bar_init(empty0 + 8 * s, 1);
+        }
+        for (int a = 0; a < 2; ++a)
+        {
+            bar_init(acc_full0 + 8 * a, 1);
+            bar_init(acc_empty0 + 8 * a, 128);
+        }
+        bar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1)
+    {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0)
+    {
+        if (lane == 0)
+        {
+            // ---------------------------------------------------- producer --
+            int stage = 0;
+            uint32_t phase = 0;
+            long long issued = 0;
+            bool ok = true;
+            for (long long tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
+            {
+                const TileCoord t = tile_coord(tile, m_tiles, n_tiles);
+                const long long row0 = t.m * BM + g.row_shift[t.phase];
+                for (int kb = 0; kb < kblocks; ++kb)
+                {
+                    if (!bar_wait(empty0 + 8 * stage, phase ^ 1u, abort_flag))
+                    {
+                        ok = false;
+                        break;
+                    }
+                    const int tap = kb / kb_per_tap, cb = kb - tap * kb_per_tap;
+                    const int row = static_cast<int>(row0 + static_cast<long long>(tap) * g.tap_step);
+                    const int slice = t.phase * g.taps + tap;
+                    const uint32_t base = smem_u32(smem + stage * STAGE);
+                    const uint32_t bar = full0 + 8 * stage;
+                    bar_expect_tx(bar, STAGE);
+                    tma_2d(base, &map_xhi, cb * BK, row, bar);
+                    tma_2d(base + A_BYTES, &map_xlo, cb * BK, row, bar);
+                    tma_3d(base + 2 * A_BYTES, &map_whi, cb * BK, t.n * BN, slice, bar);
+                    tma_3d(base + 2 * A_BYTES + B_BYTES, &map_wlo, cb * BK, t.n * BN, slice, bar);
+                    ++issued;
+                    if (++stage == STAGES)
+                    {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok)
+            {
+                *abort_flag = 1;
+                if (e.error_word)
+                    atomicOr(e.error_word, error_timeout);
+                // Loads in flight land in the last (up to) STAGES stages issued;
+                // wait for them (bounded) before the CTA may exit.
+                const long long pending = issued < STAGES ? issued : STAGES;
+                volatile int never = 0;
+                for (long long k = 1; k <= pending; ++k)
+                {
+                    const long long n = issued - k;
+                    const int s = static_cast<int>(n % STAGES);
+                    const uint32_t par = static_cast<uint32_t>((n / STAGES) & 1);
+                    bar_wait(full0 + 8 * s, par, &never);
+                }
+            }
+        }
+    }
+    else if (warp == 1)
+    {
+        if (lane == 0)
+        {
+            // --------------------------------------------------------- MMA --
+            const uint32_t idesc = tf32_idesc<BN>();
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            bool ok = true, any = false;
+            for (long long tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local)
+            {
+                // One tile in flight: wait until the epilogue has read the
+                // previous tile's accumulators.
+                if (!bar_wait(acc_empty0, (static_cast<uint32_t>(local) & 1u) ^ 1u, abort_flag))
+                {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t corr = tmem + static_cast<uint32_t>(3 * BN);
+                int step = 0; // k-step within the tile
+                for (int kb = 0; kb < kblocks; ++kb)
+                {
+                    if (!bar_wait(full0 + 8 * stage, phase, abort_flag))
+                    {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t base = smem_u32(smem + stage * STAGE);
+#pragma unroll
+                    for (int k = 0; k < BK / 8; ++k, ++step)
+                    {
+                        const uint64_t ahi = sw128_desc(base + k * 32);
+                        const uint64_t alo = sw128_desc(base + A_BYTES + k * 32);
+                        const uint64_t bhi = sw128_desc(base + 2 * A_BYTES + k * 32);
+                        const uint64_t blo = sw128_desc(base + 2 * A_BYTES + B_BYTES + k * 32);
+                        const uint32_t main = tmem + static_cast<uint32_t>((step % 3) * BN);
+                        mma_tf32(main, ahi, bhi, idesc, step >= 3 ? 1u : 0u);
+                        mma_tf32(corr, ahi, blo, idesc, step > 0 ? 1u : 0u);
+                        mma_tf32(corr, alo, bhi, idesc, 1u);
+                    }
+                    any = true;
+                    mma_commit(empty0 + 8 * stage);
+                    if (++stage == STAGES)
+                    {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok)
+                    break;
+                mma_commit(acc_full0);
+            }
+            if (!ok)
+            {
+                *abort_flag = 1;
+                if (e.error_word)
+                    atomicOr(e.error_word, error_timeout);
+            }
+            if (any)
+            {
+                // All MMAs this thread issued complete before TMEM is freed.
+                mma_commit(drain);
+                volatile int never = 0;
+                bar_wait(drain, 0, &never);
+            }
+        }
+    }
+    else
+    {
+        // ---------------------------------------------------------- epilogue --
+        const int quarter = warp & 3;
+        const int row_in_tile = quarter * 32 + lane;
+        int local = 0;
+        bool finite = true;
+        for (long long tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local)
+        {
+            if (!bar_wait(acc_full0, static_cast<uint32_t>(local) & 1u, abort_flag))
+            {
+                *abort_flag = 1;
+                if (e.error_word)
+                    atomicOr(e.error_word, error_timeout);
+                break;
+            }
+            tc_fence_after();
+            const TileCoord t = tile_coord(tile, m_tiles, n_tiles);
+            const long long i = t.m * BM + row_in_tile;
+            const bool in_range = i < g.rows;
+            const long long o = i * g.out_stride + t.phase;
+            const bool valid = in_range && e.valid[o / g.out_scale] != 0;
+            const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16)
+            {
+                float v[16], m1[16], m2[16], cr[16];
+                tmem_load16(taddr + c0, v);
+                tmem_load16(taddr + BN + c0, m1);
+                tmem_load16(taddr + 2 * BN + c0, m2);
+                tmem_load16(taddr + 3 * BN + c0, cr);
+                if (!in_range)
+                    continue;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    v[j] = __fadd_rn(__fadd_rn(__fadd_rn(v[j], m1[j]), m2[j]), cr[j]);
+                const int col = t.n * BN + c0;
+                const size_t at = static_cast<size_t>(o) * g.cout + col;
+                float raw[16], act[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                {
+                    float r = 0.0f;
+                    if (valid)
+                    {
+                        r = __fadd_rn(v[j], __ldg(e.bias + col + j));
+                        if (e.residual)
+                            r = __fadd_rn(e.residual[at + j], r);
+                    }
+                    raw[j] = r;
+                    act[j] = (valid && e.alpha) ? snake_value(r, __ldg(e.alpha + col + j)) : r;
+                    finite = finite && isfinite(act[j]) && isfinite(r);
+                }
+                if (e.raw)
+                {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4)
+                        *reinterpret_cast<float4*>(e.raw + at + j) =
+                            make_float4(raw[j], raw[j + 1], raw[j + 2], raw[j + 3]);
+                }
+                if (e.hi)
+                {
+                    if (e.lo)
+                    {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4)
+                        {
+                            float h[4], l[4];
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                tf32_split(act[j + q], h[q], l[q]);
+                            *reinterpret_cast<float4*>(e.hi + at + j) = make_float4(h[0], h[1], h[2], h[3]);
+                            *reinterpret_cast<float4*>(e.lo + at + j) = make_float4(l[0], l[1], l[2], l[3]);
+                        }
+                    }
+                    else
+                    {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4)
+                            *reinterpret_cast<float4*>(e.hi + at + j) =
+                                make_float4(act[j], act[j + 1], act[j + 2], act[j + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            bar_arrive(acc_empty0);
+        }
+        if (!finite && e.error_word)
+            atomicOr(e.error_word, error_nonfinite);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(TMEM_COLS));
+}
+
+__global__ void pad_split_rows_kernel(const float* __restrict__ src, long long rows, int channels,
+                                      const long long* __restrict__ row_map, float* __restrict__ hi,
+                                      float* __restrict__ lo)
+{
+    const long long total = rows * channels;
+    for (long long k = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; k < total;
+         k += static_cast<long long>(gridDim.x) * blockDim.x)
+    {
+        const long long r = k / channels;
+        const int c = static_cast<int>(k - r * channels);
+        const float v = src[k];
+        const size_t at = static_cast<size_t>(row_map[r]) * channels + c;
+        if (lo)
+        {
+            float h, l;
+            tf32_split(v, h, l);
+            hi[at] = h;
+            lo[at] = l;
+        }
+        else
+        {
+            hi[at] = v;
+        }
+    }
+}
+
+// ------------------------------------------------------------ host side --
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once,
+                   []
+                   {
+                       void* p = nullptr;
+                       cudaDriverEntryPointQueryResult q{};
+                       if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                                            cudaEnableDefault, &q) == cudaSuccess &&
+                           q == cudaDriverEntryPointSuccess)
+                           fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+                   });
+    return fn;
+}
+
+bool make_map(CUtensorMap* map, const float* base, int rank, const cuuint64_t* dims,
+              const cuuint64_t* strides, const cuuint32_t* box)
+{
+    const auto fn = encode_fn();
+    if (!fn)
+        return false;
+    const cuuint32_t elem[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<float*>(base), dims, strides,
+              box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count()
+{
+    int device = 0, count = 148;
+    if (cudaGetDevice(&device) == cudaSuccess)
+        cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device);
+    return count;
+}
+
+template <int BN>
+cudaError_t launch(const TcConvOperands& op, const TcConvGeometry& g, const TcConvEpilogue& e,
+                   cudaStream_t stream)
+{
+    CUtensorMap xhi, xlo, whi, wlo;
+    const cuuint64_t xdims[2] = {static_cast<cuuint64_t>(g.cin), static_cast<cuuint64_t>(g.in_rows)};
+    const cuuint64_t xstrides[1] = {static_cast<cuuint64_t>(g.cin) * 4};
+    const cuuint32_t xbox[2] = {BK, BM};
+    const int slices = g.taps * g.phases;
+    const cuuint64_t wdims[3] = {static_cast<cuuint64_t>(g.cin), static_cast<cuuint64_t>(g.cout),
+                                 static_cast<cuuint64_t>(slices)};
+    const cuuint64_t wstrides[2] = {static_cast<cuuint64_t>(g.cin) * 4,
+                                    static_cast<cuuint64_t>(g.cin) * g.cout * 4};
+    const cuuint32_t wbox[3] = {BK, BN, 1};
+    if (!make_map(&xhi, op.x_hi, 2, xdims, xstrides, xbox) ||
+        !make_map(&xlo, op.x_lo, 2, xdims, xstrides, xbox) ||
+        !make_map(&whi, op.w_hi, 3, wdims, wstrides, wbox) ||
+        !make_map(&wlo, op.w_lo, 3, wdims, wstrides, wbox))
+        return cudaErrorInvalidValue;
+    constexpr int smem = smem_bytes<BN>();
+    static std::once_flag attr_once[64];
+    int device = 0;
+    cudaGetDevice(&device);
+    if (device >= 0 && device < 64)
+        std::call_once(attr_once[device],
+                       []
+                       {
+                           cudaFuncSetAttribute(tc_conv_kernel<BN>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+                       });
+    const long long tiles = ((g.rows + BM - 1) / BM) * (g.cout / BN) * g.phases;
+    const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+    tc_conv_kernel<BN><<<grid, 192, smem, stream>>>(xhi, xlo, whi, wlo, g, e);
+    note_launch();
+    return cudaGetLastError();
+}
+} // namespace
+
+bool tc_conv_supported(int cin, int cout)
+{
+    return cin >= BK && cin % BK == 0 && cout > 0 && (cout % 128 == 0 || cout % 96 == 0);
+}
+
+cudaError_t tc_conv(const TcConvOperands& op, const TcConvGeometry& g, const TcConvEpilogue& e,
+                    cudaStream_t stream)
+{
+    if (!tc_conv_supported(g.cin, g.cout) || g.rows <= 0 || g.phases < 1 || g.phases > 8 ||
+        g.taps < 1 || g.taps * g.phases > 16 || g.out_scale < 1 || g.in_rows >= (1ll << 31))
+        return cudaErrorInvalidValue;
+    if (g.cout % 128 == 0)
+        return launch<128>(op, g, e, stream);
+    return launch<96>(op, g, e, stream);
+}
+
+void pad_split_rows(const float* src, long long rows, int channels, const long long* row_map,
+                    float* hi, float* lo, cudaStream_t stream)
+{
+    if (rows <= 0)
+        return;
+    const long long total = rows * channels;
+    long long blocks = (total + 255) / 256;
+    blocks = blocks > 148 * 16 ? 148 * 16 : blocks;
+    pad_split_rows_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(src, rows, channels,
+                                                                         row_map, hi, lo);
+    note_launch();
+}
+} // namespace tsacb::dev

@@ -11,6 +11,7 @@
 //   probability_gelu_bf16                 src/common/probability.cpp:45-63
 //   encode_categorical / conditional_q15  src/format/categorical.cpp:76-117
 #include "kernels/numeric.cuh"
+#include "kernels/launch_count.hpp"
 #include "kernels/transformer_ops.cuh"
 
 namespace tsacb::dev
@@ -419,7 +420,10 @@ void embed_sum(const std::uint16_t* embeddings, const std::uint16_t* tokens, con
                const int* counts, int rows, std::uint16_t* out, cudaStream_t stream)
 {
     if (rows > 0)
+    {
         embed_sum_kernel<<<rows, 128, 0, stream>>>(embeddings, tokens, offsets, counts, out);
+        note_launch();
+    }
 }
 
 void layer_norm(const std::uint16_t* x, const std::uint16_t* gain, const std::uint16_t* bias,
@@ -427,8 +431,11 @@ void layer_norm(const std::uint16_t* x, const std::uint16_t* gain, const std::ui
                 cudaStream_t stream)
 {
     if (rows > 0)
+    {
         layer_norm_kernel<<<(rows * 32 + 255) / 256, 256, 0, stream>>>(x, gain, bias, rows, y, yq,
                                                                         yscale, error_word);
+        note_launch();
+    }
 }
 
 void rotary_scatter(const std::uint16_t* qkv, const RowMeta* meta, const std::uint16_t* rotations,
@@ -436,8 +443,11 @@ void rotary_scatter(const std::uint16_t* qkv, const RowMeta* meta, const std::ui
                     cudaStream_t stream)
 {
     if (rows > 0)
+    {
         rotary_scatter_kernel<<<rows, 256, 0, stream>>>(qkv, meta, rotations, query, cache_k,
                                                         cache_v);
+        note_launch();
+    }
 }
 
 void add_positions(const std::uint16_t* src, const int* source_row, const int* book,
@@ -445,23 +455,32 @@ void add_positions(const std::uint16_t* src, const int* source_row, const int* b
                    cudaStream_t stream)
 {
     if (rows > 0)
+    {
         add_positions_kernel<<<rows, 256, 0, stream>>>(src, source_row, book, positions, out);
+        note_launch();
+    }
 }
 
 void softmax_tree(const std::uint16_t* logits, int rows, std::uint16_t* probs_bf16,
                   float* probs_f32, float* tree, unsigned* error_word, cudaStream_t stream)
 {
     if (rows > 0)
+    {
         softmax_tree_kernel<<<rows, 256, 0, stream>>>(logits, probs_bf16, probs_f32, tree,
                                                       error_word);
+        note_launch();
+    }
 }
 
 void categorical_path_q15(const float* tree, const std::uint16_t* token, const int* token_index,
                           int rows, std::uint16_t* q15, cudaStream_t stream)
 {
     if (rows > 0)
+    {
         categorical_path_kernel<<<(rows + 127) / 128, 128, 0, stream>>>(tree, token, token_index,
                                                                         rows, q15);
+        note_launch();
+    }
 }
 
 namespace
@@ -480,11 +499,15 @@ void scatter_rows(const std::uint16_t* src, const int* src_index, const int* dst
                   std::uint16_t* dst, cudaStream_t stream)
 {
     if (rows > 0)
+    {
         scatter_rows_kernel<<<rows, 256, 0, stream>>>(src, src_index, dst_index, dst);
+        note_launch();
+    }
 }
 
 void build_gelu_table(std::uint16_t* table, cudaStream_t stream)
 {
     gelu_table_kernel<<<256, 256, 0, stream>>>(table);
+    note_launch();
 }
 } // namespace tsacb::dev

@@ -172,6 +172,10 @@ class CudaAnalyzer:
         self._ctx = ctypes.c_void_p()
         check(lib.tsac_cuda_context_create(str(package).encode(), device, ctypes.byref(self._ctx)))
 
+    def set_exact_synthesis(self, exact: bool) -> None:
+        """Exact (bit-identical PCM) or tensor-core (within tolerance) synthesis."""
+        check(library().tsac_cuda_set_exact_synthesis(self._ctx, 1 if exact else 0))
+
     def close(self):
         if self._ctx:
             library().tsac_cuda_context_destroy(self._ctx)
