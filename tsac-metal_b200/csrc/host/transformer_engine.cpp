@@ -7,6 +7,7 @@
 #include "kernels/transformer_ops.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 #include <deque>
 
 namespace tsacb
@@ -82,6 +83,7 @@ void TransformerEngine::check_errors()
 
 void TransformerEngine::quantize(const std::uint16_t* x, int rows, int k, std::int8_t* xq, float* xs)
 {
+    KernelTimer::Scope timing("quantize", stream_, 0.0);
     dev::qlinear_quantize(x, rows, k, xq, xs, error_word(), stream_);
 }
 
@@ -104,8 +106,8 @@ void TransformerEngine::run_linear(int projection, const std::int8_t* xq, const 
     a.k = l.input;
     const double n = l.output, k = l.input, m = rows;
     // GEMV-shaped launches are weight-streaming (bytes); GEMM launches count int8 ops.
-    KernelTimer::Scope timing(rows <= 16 ? "qlinear_gemv" : "qlinear_gemm", stream_,
-                              rows <= 16 ? n * k + 4 * n * k / 256 + 4 * n + m * k + 4 * m * k / 256 + 2 * m * n
+    KernelTimer::Scope timing(rows <= 256 ? "qlinear_small" : "qlinear_gemm", stream_,
+                              rows <= 256 ? n * k + 4 * n * k / 256 + 4 * n + m * k + 4 * m * k / 256 + 2 * m * n
                                          : 2.0 * m * n * k);
     dev::qlinear_matmul(a, stream_);
 }
@@ -132,20 +134,29 @@ void TransformerEngine::run_stack(Workspace& ws_, bool temporal, int rows, std::
         const int n1 = norm_index(temporal, l, false), n2 = norm_index(temporal, l, true);
         auto* ck = cache_k + cache_layer_stride * static_cast<std::size_t>(l);
         auto* cv = cache_v + cache_layer_stride * static_cast<std::size_t>(l);
-        dev::layer_norm(h, model_->norm_gain[n1].as<std::uint16_t>(),
-                        model_->norm_bias[n1].as<std::uint16_t>(), rows, nullptr, xq, xs,
-                        error_word(), stream_);
+        {
+            KernelTimer::Scope timing("layer_norm", stream_, 0.0);
+            dev::layer_norm(h, model_->norm_gain[n1].as<std::uint16_t>(),
+                            model_->norm_bias[n1].as<std::uint16_t>(), rows, nullptr, xq, xs,
+                            error_word(), stream_);
+        }
         run_linear(projection_index(temporal, l, 0), xq, xs, rows, qkv, nullptr, false);
-        dev::rotary_scatter(qkv, meta, rotations, rows, query, ck, cv, stream_);
+        {
+            KernelTimer::Scope timing("rotary_scatter", stream_, 0.0);
+            dev::rotary_scatter(qkv, meta, rotations, rows, query, ck, cv, stream_);
+        }
         {
             KernelTimer::Scope timing("attention", stream_, 0.0);
             dev::attention(query, meta, ck, cv, rows, max_time, partials, att, stream_);
         }
         quantize(att, rows, 512, xq, xs);
         run_linear(projection_index(temporal, l, 1), xq, xs, rows, h, h, false);
-        dev::layer_norm(h, model_->norm_gain[n2].as<std::uint16_t>(),
-                        model_->norm_bias[n2].as<std::uint16_t>(), rows, nullptr, xq, xs,
-                        error_word(), stream_);
+        {
+            KernelTimer::Scope timing("layer_norm", stream_, 0.0);
+            dev::layer_norm(h, model_->norm_gain[n2].as<std::uint16_t>(),
+                            model_->norm_bias[n2].as<std::uint16_t>(), rows, nullptr, xq, xs,
+                            error_word(), stream_);
+        }
         run_linear(projection_index(temporal, l, 2), xq, xs, rows, mlp, nullptr, true);
         quantize(mlp, rows, 2048, xq, xs);
         run_linear(projection_index(temporal, l, 3), xq, xs, rows, h, h, false);
@@ -681,7 +692,10 @@ TransformerEngine::decode_predict(std::size_t step, std::size_t book, const floa
         auto* logits = ws.get<std::uint16_t>("logits", static_cast<std::size_t>(n) * 1024);
         run_linear(62, fq, fs, n, logits, nullptr, false);
         auto* tree = ws.get<float>("tree", static_cast<std::size_t>(n) * 1023);
-        dev::softmax_tree(logits, n, nullptr, nullptr, tree, error_word(), s);
+        {
+            KernelTimer::Scope timing("softmax_tree", s, 0.0);
+            dev::softmax_tree(logits, n, nullptr, nullptr, tree, error_word(), s);
+        }
         cuda_ok(cudaMemcpyAsync(st.host_masses->as<void>(), tree, static_cast<std::size_t>(n) * 1023 * 4,
                                 cudaMemcpyDeviceToHost, s),
                 "D2H");
@@ -704,10 +718,16 @@ TransformerEngine::decode_predict(std::size_t step, std::size_t book, const floa
         for (int p = 0; p < 48; ++p)
             weight_bytes += weights(p);
     }
-    if (replay)
+    // TSAC_CUDA_DECODE_GRAPHS=0 runs every step's kernels directly (each
+    // kernel family then shows in the kernel timing); replay steps (once per
+    // 768 frames of a lane) always run directly.
+    static const bool graphs_enabled = []
     {
-        // Rare (once per 768 frames of a lane): executed directly.
-        KernelTimer::Scope timing("decode_step_replay", s, weight_bytes);
+        const char* e = std::getenv("TSAC_CUDA_DECODE_GRAPHS");
+        return !(e && e[0] == '0');
+    }();
+    if (replay || !graphs_enabled)
+    {
         enqueue(temporal_rows);
     }
     else

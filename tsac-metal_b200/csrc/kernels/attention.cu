@@ -15,6 +15,7 @@
 //   is cheap (16 steps at 1024 keys) and keeps the reference's order.
 #include "kernels/numeric.cuh"
 #include "kernels/launch_count.hpp"
+#include "kernels/pdl.cuh"
 #include "kernels/transformer_ops.cuh"
 
 namespace tsacb::dev
@@ -46,6 +47,7 @@ __global__ void __launch_bounds__(128)
                            const std::uint16_t* __restrict__ cache_v, int max_blocks,
                            float* __restrict__ partials, std::uint16_t* __restrict__ output)
 {
+    pdl_prologue();
     __shared__ unsigned ks[BLOCK][65];
     __shared__ unsigned vs[BLOCK][65];
     __shared__ float q[HW];
@@ -155,6 +157,7 @@ __global__ void __launch_bounds__(128)
     attention_combine_kernel(const RowMeta* __restrict__ meta, const float* __restrict__ partials,
                              int max_blocks, std::uint16_t* __restrict__ out)
 {
+    pdl_prologue();
     const int task = blockIdx.x;
     const int row = task / HEADS, head = task % HEADS;
     const int t = threadIdx.x;
@@ -194,15 +197,16 @@ void attention(const std::uint16_t* query, const RowMeta* meta, const std::uint1
     const int blocks = (max_time + BLOCK - 1) / BLOCK;
     if (blocks == 1)
     {
-        attention_block_kernel<true><<<dim3(rows * HEADS, 1), 128, 0, stream>>>(
-            query, meta, cache_k, cache_v, 1, nullptr, out);
+        launch_pdl(attention_block_kernel<true>, dim3(rows * HEADS, 1), dim3(128), 0, stream, query,
+                   meta, cache_k, cache_v, 1, static_cast<float*>(nullptr), out);
         note_launch();
         return;
     }
-    attention_block_kernel<false><<<dim3(rows * HEADS, blocks), 128, 0, stream>>>(
-        query, meta, cache_k, cache_v, blocks, partials, nullptr);
+    launch_pdl(attention_block_kernel<false>, dim3(rows * HEADS, blocks), dim3(128), 0, stream, query,
+               meta, cache_k, cache_v, blocks, partials, static_cast<std::uint16_t*>(nullptr));
     note_launch();
-    attention_combine_kernel<<<rows * HEADS, 128, 0, stream>>>(meta, partials, blocks, out);
+    launch_pdl(attention_combine_kernel, dim3(rows * HEADS), dim3(128), 0, stream, meta,
+               static_cast<const float*>(partials), blocks, out);
     note_launch();
 }
 } // namespace tsacb::dev

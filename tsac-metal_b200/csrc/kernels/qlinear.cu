@@ -18,6 +18,7 @@
 #include "kernels/qlinear.cuh"
 #include "kernels/launch_count.hpp"
 #include "kernels/numeric.cuh"
+#include "kernels/pdl.cuh"
 
 #include <atomic>
 
@@ -30,6 +31,7 @@ __global__ void quantize_bf8l_kernel(const std::uint16_t* __restrict__ x, int k,
                                      std::int8_t* __restrict__ q, float* __restrict__ scales,
                                      unsigned* error_word)
 {
+    pdl_prologue();
     const int blocks = k / 256;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -114,6 +116,7 @@ __global__ void __launch_bounds__(256)
                         const std::int8_t* __restrict__ xq, const float* __restrict__ xscale,
                         int m_rows, int n_cols, int k, Epilogue e, std::uint16_t* __restrict__ y)
 {
+    pdl_prologue();
     __shared__ __align__(16) int As[BK / 4][BM];
     __shared__ __align__(16) int Bs[BK / 4][BN];
     const int tid = threadIdx.x;
@@ -205,100 +208,109 @@ __global__ void __launch_bounds__(256)
     }
 }
 
-// Decode-shaped launch for up to 64 columns.  A CTA owns R output rows; every
-// (row, 256-block) item is one half-warp's job: each lane holds 16 weight
-// bytes and, column by column, forms its 16-byte int8 dot with the column's
-// activations (read through L1, shared by all rows of the CTA), reduced exactly
-// over the half-warp.  Block dots land in shared memory; then one thread per
-// (row, column) folds them in block order.  Short dependency chains and
-// (rows x blocks) items keep every warp busy at decode sizes.
-constexpr int SMALL_MAX_M = 64;
+// Decode-shaped launch (m <= 256 columns).  A CTA owns 16 output features x
+// 32 columns (four 8-column m-tiles).  Its 8 warps split K into 64-byte chunks
+// (warp w takes quarter w % 4 of the 256-blocks b = w / 4, w / 4 + 2, ...) and
+// form int8 dots on the tensor cores with mma.sync m16n8k32 (s8 x s8 -> s32:
+// integer sums are exact in any order, so each block dot equals the
+// reference's).  Each lane loads 16 contiguous bytes of a weight row and of an
+// activation row per chunk and feeds them to two MMAs; A and B use the same
+// byte-to-k assignment, so every byte pair meets exactly once.  Quarter dots
+// meet in shared memory (integer atomics, exact), and 256 threads then fold
+// the blocks in order, two outputs each: sum = fma(dot, w_scale * x_scale, sum).
+constexpr int SMALL_MAX_M = 256;
+constexpr int MMA_MT = 4; // 8-column m-tiles per CTA
+
+__device__ __forceinline__ void mma_s8(int (&d)[4], unsigned a0, unsigned a1, unsigned a2,
+                                       unsigned a3, unsigned b0, unsigned b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32"
+                 " {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+                 : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 
 __global__ void __launch_bounds__(256)
-    qlinear_small_kernel(const std::int8_t* __restrict__ w, const float* __restrict__ wscale,
-                         const std::int8_t* __restrict__ xq, const float* __restrict__ xscale,
-                         int m_rows, int n_cols, int k, int rows_per_cta, Epilogue e,
-                         std::uint16_t* __restrict__ y)
+    qlinear_mma_kernel(const std::int8_t* __restrict__ w, const float* __restrict__ wscale,
+                       const std::int8_t* __restrict__ xq, const float* __restrict__ xscale,
+                       int m_rows, int n_cols, int k, Epilogue e, std::uint16_t* __restrict__ y)
 {
-    // Shared memory: the quantized activations [m_rows][k] (staged once with
-    // independent 16-byte loads, so their L2 latency is paid once), then the
-    // block dots [rows_per_cta][blocks][m_rows].
-    extern __shared__ __align__(16) unsigned char small_smem[];
-    std::int8_t* xs = reinterpret_cast<std::int8_t*>(small_smem);
-    int* dots = reinterpret_cast<int*>(small_smem + static_cast<size_t>(m_rows) * k);
+    pdl_prologue();
+    extern __shared__ int dots[]; // [block][m-tile][lane][4]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int n0 = blockIdx.x * 16, m0 = blockIdx.y * (8 * MMA_MT);
     const int blocks = k / 256;
-    const int n0 = blockIdx.x * rows_per_cta;
-    const int half = threadIdx.x >> 4, l16 = threadIdx.x & 15;
-    const unsigned mask = (threadIdx.x & 16) ? 0xffff0000u : 0x0000ffffu;
-    const int items = rows_per_cta * blocks;
-    for (int i = threadIdx.x * 16; i < m_rows * k; i += blockDim.x * 16)
-        *reinterpret_cast<uint4*>(xs + i) = __ldg(reinterpret_cast<const uint4*>(xq + i));
+    for (int i = threadIdx.x; i < blocks * MMA_MT * 128; i += 256)
+        dots[i] = 0;
     __syncthreads();
-    for (int item = half; item < items; item += 16)
+    const int quarter = warp & 3;
+    const std::int8_t* wa = w + static_cast<size_t>(n0 + g) * k + quarter * 64 + t * 16;
+    const std::int8_t* wb = wa + static_cast<size_t>(8) * k;
+    for (int b = warp >> 2; b < blocks; b += 2)
     {
-        const int r = item / blocks, b = item % blocks;
-        const int n = n0 + r;
-        uint4 wv = make_uint4(0, 0, 0, 0);
-        if (n < n_cols)
-            wv = __ldg(reinterpret_cast<const uint4*>(w + static_cast<size_t>(n) * k + b * 256 + l16 * 16));
-#pragma unroll 4
-        for (int c = 0; c < m_rows; ++c)
+        const uint4 a_lo = __ldg(reinterpret_cast<const uint4*>(wa + b * 256));
+        const uint4 a_hi = __ldg(reinterpret_cast<const uint4*>(wb + b * 256));
+        uint4 x[MMA_MT];
+#pragma unroll
+        for (int mt = 0; mt < MMA_MT; ++mt)
         {
-            const uint4 xv = *reinterpret_cast<const uint4*>(xs + static_cast<size_t>(c) * k +
-                                                             b * 256 + l16 * 16);
-            int d = __dp4a(static_cast<int>(wv.x), static_cast<int>(xv.x), 0);
-            d = __dp4a(static_cast<int>(wv.y), static_cast<int>(xv.y), d);
-            d = __dp4a(static_cast<int>(wv.z), static_cast<int>(xv.z), d);
-            d = __dp4a(static_cast<int>(wv.w), static_cast<int>(xv.w), d);
-            d += __shfl_xor_sync(mask, d, 8, 16);
-            d += __shfl_xor_sync(mask, d, 4, 16);
-            d += __shfl_xor_sync(mask, d, 2, 16);
-            d += __shfl_xor_sync(mask, d, 1, 16);
-            if (l16 == 0)
-                dots[(r * blocks + b) * m_rows + c] = d;
+            const int m = m0 + mt * 8 + g;
+            x[mt] = m < m_rows ? __ldg(reinterpret_cast<const uint4*>(
+                                     xq + static_cast<size_t>(m) * k + b * 256 + quarter * 64 + t * 16))
+                               : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int mt = 0; mt < MMA_MT; ++mt)
+        {
+            int d[4] = {0, 0, 0, 0};
+            mma_s8(d, a_lo.x, a_hi.x, a_lo.y, a_hi.y, x[mt].x, x[mt].y);
+            mma_s8(d, a_lo.z, a_hi.z, a_lo.w, a_hi.w, x[mt].z, x[mt].w);
+            int* slot = dots + ((b * MMA_MT + mt) * 32 + lane) * 4;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                atomicAdd(slot + c, d[c]);
         }
     }
     __syncthreads();
-    for (int t = threadIdx.x; t < rows_per_cta * m_rows; t += blockDim.x)
+    // Fold: output (nl, ml), nl = 0..15, ml = 0..31; fragment element c of
+    // lane (g, t) holds (n = g + 8 (c / 2), m = 2 t + c % 2) of its m-tile.
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
     {
-        const int r = t / m_rows, c = t % m_rows;
-        const int n = n0 + r;
-        if (n >= n_cols)
+        const int id = threadIdx.x + half * 256;
+        const int nl = id & 15, ml = id >> 4;
+        const int n = n0 + nl, m = m0 + ml;
+        if (m >= m_rows)
             continue;
+        const int mt = ml >> 3, col = ml & 7;
+        const int frag_lane = (nl & 7) * 4 + (col >> 1);
+        const int c = (nl >> 3) * 2 + (col & 1);
         float sum = 0.0f;
-#pragma unroll 8
+#pragma unroll 4
         for (int b = 0; b < blocks; ++b)
         {
-            const float scale = __fmul_rn(__ldg(wscale + b * n_cols + n), __ldg(xscale + c * blocks + b));
-            sum = __fmaf_rn(static_cast<float>(dots[(r * blocks + b) * m_rows + c]), scale, sum);
+            const float scale = __fmul_rn(__ldg(wscale + b * n_cols + n), __ldg(xscale + m * blocks + b));
+            const int dot = dots[((b * MMA_MT + mt) * 32 + frag_lane) * 4 + c];
+            sum = __fmaf_rn(static_cast<float>(dot), scale, sum);
         }
-        y[static_cast<size_t>(c) * n_cols + n] = finish(sum, c, n, n_cols, e);
+        y[static_cast<size_t>(m) * n_cols + n] = finish(sum, m, n, n_cols, e);
     }
 }
 
-// Rows per CTA: enough (row, block) items for the 16 half-warps, and at least
-// 4 so that few CTAs restage the same activations.
-int small_rows(int k)
+size_t mma_smem_bytes(int k)
 {
-    const int blocks = k / 256;
-    return blocks >= 4 ? 4 : 16 / blocks;
+    return static_cast<size_t>(k / 256) * MMA_MT * 128 * sizeof(int);
 }
-
-size_t small_smem_bytes(int m, int k)
-{
-    return static_cast<size_t>(m) * k + static_cast<size_t>(small_rows(k)) * (k / 256) * m * sizeof(int);
-}
-
-constexpr size_t SMALL_MAX_SMEM = 200 * 1024;
 
 void launch_small(const QLinearArgs& a, const Epilogue& e, cudaStream_t stream)
 {
-    const int rows = small_rows(a.k);
-    const size_t smem = small_smem_bytes(a.m, a.k);
+    const size_t smem = mma_smem_bytes(a.k);
     if (smem > 48 * 1024)
         qlinear_init();
-    qlinear_small_kernel<<<(a.n + rows - 1) / rows, 256, smem, stream>>>(
-        a.weights, a.weight_scales, a.xq, a.xscale, a.m, a.n, a.k, rows, e, a.y);
+    const dim3 grid(a.n / 16, (a.m + 8 * MMA_MT - 1) / (8 * MMA_MT));
+    launch_pdl(qlinear_mma_kernel, grid, dim3(256), smem, stream, a.weights, a.weight_scales, a.xq,
+               a.xscale, a.m, a.n, a.k, e, a.y);
     note_launch();
 }
 
@@ -306,10 +318,10 @@ void launch_small(const QLinearArgs& a, const Epilogue& e, cudaStream_t stream)
 
 void qlinear_init()
 {
-    // The decode-shaped kernel stages its int8 activations plus the block dots
-    // in shared memory, up to SMALL_MAX_SMEM bytes.  The attribute belongs to
-    // each device's context, so it is set once per device (a bit per ordinal;
-    // setting it twice from racing threads is harmless).
+    // The decode-shaped kernel keeps its block dots in shared memory (64 KB
+    // at k = 8192).  The attribute belongs to each device's context, so it is
+    // set once per device (a bit per ordinal; setting it twice from racing
+    // threads is harmless).
     static std::atomic<unsigned long long> ready{0};
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
@@ -317,8 +329,8 @@ void qlinear_init()
     const unsigned long long bit = 1ull << device;
     if (ready.load(std::memory_order_acquire) & bit)
         return;
-    if (cudaFuncSetAttribute(qlinear_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(SMALL_MAX_SMEM)) == cudaSuccess)
+    if (cudaFuncSetAttribute(qlinear_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(mma_smem_bytes(8192))) == cudaSuccess)
         ready.fetch_or(bit, std::memory_order_acq_rel);
 }
 
@@ -332,21 +344,21 @@ void qlinear_quantize(const std::uint16_t* x, int m, int k, std::int8_t* xq, flo
 {
     const int warps = m * (k / 256);
     const int threads = 256;
-    quantize_bf8l_kernel<<<(warps * 32 + threads - 1) / threads, threads, 0, stream>>>(
-        x, k, m, xq, xscale, error_word);
+    launch_pdl(quantize_bf8l_kernel, dim3((warps * 32 + threads - 1) / threads), dim3(threads), 0,
+               stream, x, k, m, xq, xscale, error_word);
     note_launch();
 }
 
 void qlinear_matmul(const QLinearArgs& a, cudaStream_t stream)
 {
     const Epilogue e{a.bias, a.residual, a.lut};
-    if (a.m <= SMALL_MAX_M && small_smem_bytes(a.m, a.k) <= SMALL_MAX_SMEM)
+    if (a.m <= SMALL_MAX_M && a.n % 16 == 0)
         launch_small(a, e, stream);
     else
     {
         const dim3 grid(a.n / BN, (a.m + BM - 1) / BM);
-        qlinear_gemm_kernel<<<grid, 256, 0, stream>>>(a.weights, a.weight_scales, a.xq, a.xscale,
-                                                      a.m, a.n, a.k, e, a.y);
+        launch_pdl(qlinear_gemm_kernel, grid, dim3(256), 0, stream, a.weights, a.weight_scales,
+                   a.xq, a.xscale, a.m, a.n, a.k, e, a.y);
         note_launch();
     }
 }

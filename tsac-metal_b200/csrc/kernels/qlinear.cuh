@@ -24,7 +24,8 @@ size_t qlinear_scratch_bytes(size_t m, size_t k);
 // BF8L quantization of bf16 activations [m][k] into int8 + per-block scales.
 void qlinear_quantize(const std::uint16_t* x, int m, int k, std::int8_t* xq, float* xscale,
                       unsigned* error_word, cudaStream_t stream);
-// Exact int8 block dots + ordered FP32 epilogue (GEMV for m <= 16, tiled GEMM above).
+// Exact int8 block dots + ordered FP32 epilogue (int8 tensor-core split-K tiles for
+// m <= 256, tiled dp4a GEMM above).
 void qlinear_matmul(const QLinearArgs& args, cudaStream_t stream);
 // One-time kernel attribute setup (dynamic shared memory limits).
 void qlinear_init();

@@ -12,6 +12,7 @@
 //   encode_categorical / conditional_q15  src/format/categorical.cpp:76-117
 #include "kernels/numeric.cuh"
 #include "kernels/launch_count.hpp"
+#include "kernels/pdl.cuh"
 #include "kernels/transformer_ops.cuh"
 
 namespace tsacb::dev
@@ -30,6 +31,7 @@ __global__ void embed_sum_kernel(const std::uint16_t* __restrict__ table,
                                  const int* __restrict__ offsets, const int* __restrict__ counts,
                                  std::uint16_t* __restrict__ out)
 {
+    pdl_prologue();
     const int row = blockIdx.x;
     const int count = counts[row];
     const int c0 = threadIdx.x * 8;
@@ -89,6 +91,7 @@ __global__ void layer_norm_kernel(const std::uint16_t* __restrict__ x,
                                   std::uint16_t* __restrict__ y, std::int8_t* __restrict__ yq,
                                   float* __restrict__ yscale, unsigned* error_word)
 {
+    pdl_prologue();
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= rows)
@@ -169,6 +172,7 @@ __global__ void rotary_scatter_kernel(const std::uint16_t* __restrict__ qkv,
                                       std::uint16_t* __restrict__ cache_k,
                                       std::uint16_t* __restrict__ cache_v)
 {
+    pdl_prologue();
     const int row = blockIdx.x;
     const int t = threadIdx.x;
     const RowMeta m = meta[row];
@@ -204,6 +208,7 @@ __global__ void add_positions_kernel(const std::uint16_t* __restrict__ src,
                                      const std::uint16_t* __restrict__ positions,
                                      std::uint16_t* __restrict__ out)
 {
+    pdl_prologue();
     const int row = blockIdx.x;
     const int t = threadIdx.x; // 256 threads x 2 values
     const unsigned a =
@@ -233,6 +238,7 @@ __global__ void softmax_tree_kernel(const std::uint16_t* __restrict__ logits,
                                     float* __restrict__ probs_f32, float* __restrict__ tree,
                                     unsigned* error_word)
 {
+    pdl_prologue();
     __shared__ ArgMax warp_best[8];
     __shared__ float block_sums[16];
     __shared__ float level_sums[8]; // 128-wide sums (one per warp)
@@ -369,6 +375,7 @@ __global__ void categorical_path_kernel(const float* __restrict__ tree,
                                         const int* __restrict__ token_index, int rows,
                                         std::uint16_t* __restrict__ q15)
 {
+    pdl_prologue();
     const int row = blockIdx.x * blockDim.x + threadIdx.x;
     if (row >= rows)
         return;
@@ -421,7 +428,7 @@ void embed_sum(const std::uint16_t* embeddings, const std::uint16_t* tokens, con
 {
     if (rows > 0)
     {
-        embed_sum_kernel<<<rows, 128, 0, stream>>>(embeddings, tokens, offsets, counts, out);
+        launch_pdl(embed_sum_kernel, dim3(rows), dim3(128), 0, stream, embeddings, tokens, offsets, counts, out);
         note_launch();
     }
 }
@@ -432,8 +439,8 @@ void layer_norm(const std::uint16_t* x, const std::uint16_t* gain, const std::ui
 {
     if (rows > 0)
     {
-        layer_norm_kernel<<<(rows * 32 + 255) / 256, 256, 0, stream>>>(x, gain, bias, rows, y, yq,
-                                                                        yscale, error_word);
+        launch_pdl(layer_norm_kernel, dim3((rows * 32 + 255) / 256), dim3(256), 0, stream, x, gain, bias,
+                   rows, y, yq, yscale, error_word);
         note_launch();
     }
 }
@@ -444,8 +451,8 @@ void rotary_scatter(const std::uint16_t* qkv, const RowMeta* meta, const std::ui
 {
     if (rows > 0)
     {
-        rotary_scatter_kernel<<<rows, 256, 0, stream>>>(qkv, meta, rotations, query, cache_k,
-                                                        cache_v);
+        launch_pdl(rotary_scatter_kernel, dim3(rows), dim3(256), 0, stream, qkv, meta, rotations, query,
+                   cache_k, cache_v);
         note_launch();
     }
 }
@@ -456,7 +463,7 @@ void add_positions(const std::uint16_t* src, const int* source_row, const int* b
 {
     if (rows > 0)
     {
-        add_positions_kernel<<<rows, 256, 0, stream>>>(src, source_row, book, positions, out);
+        launch_pdl(add_positions_kernel, dim3(rows), dim3(256), 0, stream, src, source_row, book, positions, out);
         note_launch();
     }
 }
@@ -466,8 +473,8 @@ void softmax_tree(const std::uint16_t* logits, int rows, std::uint16_t* probs_bf
 {
     if (rows > 0)
     {
-        softmax_tree_kernel<<<rows, 256, 0, stream>>>(logits, probs_bf16, probs_f32, tree,
-                                                      error_word);
+        launch_pdl(softmax_tree_kernel, dim3(rows), dim3(256), 0, stream, logits, probs_bf16, probs_f32,
+                   tree, error_word);
         note_launch();
     }
 }
@@ -477,8 +484,8 @@ void categorical_path_q15(const float* tree, const std::uint16_t* token, const i
 {
     if (rows > 0)
     {
-        categorical_path_kernel<<<(rows + 127) / 128, 128, 0, stream>>>(tree, token, token_index,
-                                                                        rows, q15);
+        launch_pdl(categorical_path_kernel, dim3((rows + 127) / 128), dim3(128), 0, stream, tree, token,
+                   token_index, rows, q15);
         note_launch();
     }
 }
@@ -489,6 +496,7 @@ __global__ void scatter_rows_kernel(const std::uint16_t* __restrict__ src,
                                     const int* __restrict__ src_index,
                                     const int* __restrict__ dst_index, std::uint16_t* __restrict__ dst)
 {
+    pdl_prologue();
     const int j = blockIdx.x;
     reinterpret_cast<unsigned*>(dst + static_cast<size_t>(dst_index[j]) * 512)[threadIdx.x] =
         reinterpret_cast<const unsigned*>(src + static_cast<size_t>(src_index[j]) * 512)[threadIdx.x];
@@ -500,7 +508,7 @@ void scatter_rows(const std::uint16_t* src, const int* src_index, const int* dst
 {
     if (rows > 0)
     {
-        scatter_rows_kernel<<<rows, 256, 0, stream>>>(src, src_index, dst_index, dst);
+        launch_pdl(scatter_rows_kernel, dim3(rows), dim3(256), 0, stream, src, src_index, dst_index, dst);
         note_launch();
     }
 }
