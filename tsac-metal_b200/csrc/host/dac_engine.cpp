@@ -151,7 +151,7 @@ void DacEngine::snake(int index, const float* x, float* y, long long frames)
 
 void DacEngine::conv(int index, const float* x, float* y, const float* residual,
                      const std::vector<int>& in_frames, std::vector<int>& out_frames,
-                     const std::vector<long long>* in_offsets)
+                     const std::vector<long long>* in_offsets, int alpha, float* act)
 {
     const auto& c = convs_[static_cast<std::size_t>(index)];
     const auto& sp = c.spec;
@@ -203,7 +203,7 @@ void DacEngine::conv(int index, const float* x, float* y, const float* residual,
         dev::conv1d_narrow(x, c.weights.as<float>(), c.bias.as<float>(), y, d_seq,
                            static_cast<int>(seqs.size()), shape,
                            static_cast<long long>(out_off) * shape.cout, error_word(), stream_);
-        require(residual == nullptr, "narrow convolution has no residual input");
+        require(residual == nullptr && act == nullptr, "narrow convolution has no residual or Snake output");
         return;
     }
     auto* d_tiles = ws_.get<int4>(key + "t", tiles.size());
@@ -212,6 +212,11 @@ void DacEngine::conv(int index, const float* x, float* y, const float* residual,
             "H2D");
     dev::ConvLaunch l{error_word(), x, c.weights.as<float>(), c.bias.as<float>(), residual, y,
                       d_seq, d_tiles, static_cast<int>(tiles.size()), shape};
+    if (act)
+    {
+        l.alpha = alphas_[static_cast<std::size_t>(alpha)].as<float>();
+        l.act = act;
+    }
     dev::conv1d(l, stream_);
 }
 
@@ -230,37 +235,30 @@ void DacEngine::analyze(const float* pcm, const std::vector<long long>& offsets,
     // Widest activation: 64 channels at full rate (= 512*64 per frame ... all
     // stages hold frames*512*64/... floats; stage sizes shrink as width grows).
     const std::size_t biggest = static_cast<std::size_t>(total) * 64;
+    // a: the residual stream (raw sums); p / q: Snake of it for the next
+    // convolution, written by the producing convolution's epilogue.
     auto* a = ws_.get<float>("a", biggest);
-    auto* t1 = ws_.get<float>("t1", biggest);
-    auto* t2 = ws_.get<float>("t2", biggest);
+    float* p = ws_.get<float>("t1", biggest);
+    float* q = ws_.get<float>("t2", biggest);
     std::vector<int> cur = f0;
-    conv(0, pcm, a, nullptr, cur, f1, &offsets);
+    conv(0, pcm, a, nullptr, cur, f1, &offsets, 0, p);
     cur = f1;
-    int width = 64;
     for (int stage = 0; stage < 4; ++stage)
     {
-        long long n = 0;
-        for (int v : cur)
-            n += v;
         for (int unit = 0; unit < 3; ++unit)
         {
             const int base = 1 + stage * 7 + unit * 2; // convolution index
-            const int alpha = stage * 7 + unit * 2;    // activation index
-            snake(alpha, a, t1, n);
-            conv(base, t1, t2, nullptr, cur, f1);
-            snake(alpha + 1, t2, t1, n);
-            conv(base + 1, t1, a, a, cur, f1);
+            const int alpha = stage * 7 + unit * 2;    // activation index of the unit's first Snake
+            conv(base, p, nullptr, nullptr, cur, f1, nullptr, alpha + 1, q);
+            const int next = unit < 2 ? alpha + 2 : stage * 7 + 6;
+            conv(base + 1, q, a, a, cur, f1, nullptr, next, p);
         }
-        snake(stage * 7 + 6, a, t1, n);
-        conv(1 + stage * 7 + 6, t1, a, nullptr, cur, f1);
+        const int next = stage < 3 ? (stage + 1) * 7 : 28;
+        conv(1 + stage * 7 + 6, p, a, nullptr, cur, f1, nullptr, next, q);
+        std::swap(p, q);
         cur = f1;
-        width *= 2;
     }
-    long long n = 0;
-    for (int v : cur)
-        n += v;
-    snake(28, a, t1, n);
-    conv(29, t1, latent, nullptr, cur, f1);
+    conv(29, p, latent, nullptr, cur, f1);
     cuda_ok(cudaGetLastError(), "analysis launch");
 }
 

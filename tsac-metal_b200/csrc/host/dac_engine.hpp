@@ -57,9 +57,11 @@ public:
 
 private:
     struct Layout; // per-layer sequence tables for one window set
+    // y (raw result, or null) and optionally act = Snake(alpha)(result).
     void conv(int index, const float* x, float* y, const float* residual,
               const std::vector<int>& in_frames, std::vector<int>& out_frames,
-              const std::vector<long long>* in_offsets = nullptr);
+              const std::vector<long long>* in_offsets = nullptr, int alpha = -1,
+              float* act = nullptr);
     void snake(int index, const float* x, float* y, long long frames);
     void synthesize_exact(const float* latent, const std::vector<int>& frames, float* pcm);
     void synthesize_tensor(const float* latent, const std::vector<int>& frames, float* pcm);

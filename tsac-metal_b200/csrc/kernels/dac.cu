@@ -14,15 +14,19 @@
 // B200 mapping of the exact-order convolution: the reference's per-output
 // serial chain is kept (products and sums rounded separately, taps outer,
 // input channels inner), and parallelism comes from outputs.  A CTA owns a
-// 128-frame x 64-channel output tile, 256 threads each accumulating 8 frames x
-// 4 channels in registers; per (tap, 32-channel chunk) it stages the needed
-// input rows and the weight slice in shared memory, so every staged value is
-// reused 4x (inputs) or 8x (weights) from registers.  Device weights are laid
-// out [tap][in][out] so the weight slice loads are contiguous.
+// 128-frame x 128-channel output tile (64 for 64-channel layers), 256 threads
+// each accumulating 8 (4) frames x 8 channels in registers; per (tap,
+// 32-channel chunk) it stages the input rows channel-major and the weight
+// slice in shared memory, double-buffered through registers, so every staged
+// value is reused 8x from registers and a thread's operands are 16-byte loads.
+// Device weights are laid out [tap][in][out] so the weight slice loads are
+// contiguous.
 #include "kernels/dac.cuh"
 #include "kernels/dac_math.cuh"
 #include "kernels/launch_count.hpp"
 #include "kernels/numeric.cuh"
+
+#include <mutex>
 
 namespace tsacb::dev
 {
@@ -49,7 +53,7 @@ __global__ void snake_kernel(const float* __restrict__ x, const float* __restric
         atomicOr(error_word, error_nonfinite);
 }
 
-constexpr int TF = 128, TO = 64, CK = 32;
+constexpr int TF = 128, CK = 32;
 
 // Output frame of tile row r and the input frame feeding it through `tap`.
 struct TileGeometry
@@ -68,134 +72,257 @@ struct TileGeometry
         }
         return (f_first + r) * s.stride + tap * s.dilation - s.padding;
     }
+    // Row r of the tile takes `tap` (the reference skips taps outside the window).
+    __device__ __forceinline__ bool takes(const ConvShape& s, const Sequence& q, int r, int tap) const
+    {
+        const int src = in_frame(s, r, tap);
+        const int f = out_frame(s, r);
+        return f < q.out_frames && src >= 0 && src < q.in_frames &&
+               (!s.transposed || f + s.padding >= tap);
+    }
 };
 
-__global__ void __launch_bounds__(256)
-    conv1d_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                  const float* __restrict__ bias, const float* __restrict__ residual,
-                  float* __restrict__ y, const Sequence* __restrict__ sequences,
-                  const int4* __restrict__ tiles, ConvShape s, unsigned* error_word)
+// Shared memory of one pipeline stage: the input chunk stored channel-major
+// (xs[c][row], so a thread's TR consecutive rows are one or two 16-byte
+// loads) and the weight chunk [c][output].
+template <int TO> struct ConvStage
 {
-    __shared__ float xs[TF][CK + 1];
-    __shared__ __align__(16) float ws[CK][TO];
-    const int4 tile = tiles[blockIdx.x];
-    const Sequence seq = sequences[tile.x];
+    float xs[CK][TF + 4];
+    float ws[CK][TO];
+};
+
+template <int TO> constexpr size_t conv_smem_bytes()
+{
+    return 2 * sizeof(ConvStage<TO>);
+}
+
+// Exact-order convolution.  A CTA owns a 128-frame x TO-channel output tile;
+// its 256 threads each hold TR frames x 8 channels of serial chains in
+// registers (TR = 8 for TO = 128, 4 for TO = 64).  Per (tap, 32-channel chunk)
+// "step", the chunk's inputs and weights are staged in shared memory; the next
+// step's global loads are issued into registers before the current step's
+// arithmetic and stored after it (two stages, one barrier per step).  Per
+// output the order is the reference's: taps ascending, channels ascending,
+// sum = sum + x * w with the product and the sum each rounded; a row skips
+// taps whose input frame lies outside its window.
+template <int TO>
+__global__ void __launch_bounds__(256, 1)
+    conv1d_kernel(ConvLaunch l)
+{
+    constexpr int TR = TO == 128 ? 8 : 4;
+    constexpr int CG = TO / 8; // column groups (threads across outputs)
+    extern __shared__ __align__(16) unsigned char conv_smem[];
+    auto* stage = reinterpret_cast<ConvStage<TO>*>(conv_smem);
+    const ConvShape s = l.shape;
+    const int4 tile = l.tiles[blockIdx.x];
+    const Sequence seq = l.sequences[tile.x];
     const TileGeometry g{tile.y, tile.z};
     const int o0 = blockIdx.y * TO;
-    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    float sum[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            sum[i][j] = 0.0f;
-    // Taps in ascending order; a transposed tile uses its phase's two taps.
+    const int tid = threadIdx.x, tx = tid % CG, ty = tid / CG;
+
+    // Taps used by any / every row of the tile (uniform across the CTA).
     const int tap_count = s.transposed ? 2 : s.kernel;
     const int tap_first = s.transposed ? (g.phase + s.padding) % s.stride : 0;
+    unsigned any_mask = 0, all_mask = 0;
     for (int ti = 0; ti < tap_count; ++ti)
     {
         const int tap = s.transposed ? tap_first + ti * s.stride : ti;
-        unsigned valid = 0; // bit i: this thread's frame row ty*8+i takes this tap
+        const bool mine = tid < TF && g.takes(s, seq, tid, tap);
+        const bool row_ok = tid >= TF || mine;
+        if (__syncthreads_or(mine))
+            any_mask |= 1u << ti;
+        if (__syncthreads_and(row_ok))
+            all_mask |= 1u << ti;
+    }
+    const int chunks = (s.cin + CK - 1) / CK;
+    const int steps = __popc(any_mask) * chunks;
+
+    float sum[TR][8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < TR; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            sum[i][j] = 0.0f;
+
+    // Step k -> (tap index, chunk): taps in ascending order, skipping unused ones.
+    auto step_tap = [&](int k, int& ti, int& c0)
+    {
+        int n = k / chunks;
+        c0 = (k - n * chunks) * CK;
+        unsigned m = any_mask;
+        for (; n > 0; --n)
+            m &= m - 1;
+        ti = __ffs(m) - 1;
+    };
+    // Register prefetch of one step: 16 inputs and 4 x 4 weights per thread.
+    float xr[16];
+    float4 wr[TO / 32];
+    auto load = [&](int k)
+    {
+        int ti, c0;
+        step_tap(k, ti, c0);
+        const int tap = s.transposed ? tap_first + ti * s.stride : ti;
+        const int cn = s.cin - c0 < CK ? s.cin - c0 : CK;
+#pragma unroll
+        for (int it = 0; it < 4; ++it)
         {
-            const int r = ty * 8 + i;
+            const int idx = it * 256 + tid;
+            const int r = idx & (TF - 1), cg = idx >> 7; // channels 4cg .. 4cg+3
             const int src = g.in_frame(s, r, tap);
-            const int f = g.out_frame(s, r);
-            if (f < seq.out_frames && src >= 0 && src < seq.in_frames &&
-                (!s.transposed || f + s.padding >= tap))
-                valid |= 1u << i;
-        }
-        const bool any = __syncthreads_or(valid != 0);
-        if (!any)
-            continue;
-        const bool all = __syncthreads_and(valid == 0xffu);
-        for (int c0 = 0; c0 < s.cin; c0 += CK)
-        {
-            const int cn = s.cin - c0 < CK ? s.cin - c0 : CK;
-            // Stage input rows (zeros where the tap is invalid; never added).
-            for (int e = tid; e < TF * CK; e += 256)
+            const bool in = src >= 0 && src < seq.in_frames;
+            const float* xp = l.x + static_cast<size_t>(seq.in_offset + (in ? src : 0)) * s.cin + c0 + 4 * cg;
+            if (in && 4 * cg + 3 < cn && (s.cin & 3) == 0)
             {
-                const int c = e & (CK - 1), r = e >> 5;
-                const int src = g.in_frame(s, r, tap);
-                float v = 0.0f;
-                if (c < cn && src >= 0 && src < seq.in_frames)
-                    v = x[static_cast<size_t>(seq.in_offset + src) * s.cin + c0 + c];
-                xs[r][c] = v;
-            }
-            for (int e = tid; e < CK * TO; e += 256)
-            {
-                const int o = e & (TO - 1), c = e >> 6;
-                float v = 0.0f;
-                if (c < cn && o0 + o < s.cout)
-                    v = w[(static_cast<size_t>(tap) * s.cin + c0 + c) * s.cout + o0 + o];
-                ws[c][o] = v;
-            }
-            __syncthreads();
-            if (all)
-            {
-#pragma unroll 4
-                for (int c = 0; c < cn; ++c)
-                {
-                    const float4 wv = *reinterpret_cast<const float4*>(&ws[c][tx * 4]);
-                    const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                    {
-                        const float xv = xs[ty * 8 + i][c];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            sum[i][j] = __fadd_rn(sum[i][j], __fmul_rn(xv, wa[j]));
-                    }
-                }
+                const float4 v = __ldg(reinterpret_cast<const float4*>(xp));
+                xr[4 * it] = v.x;
+                xr[4 * it + 1] = v.y;
+                xr[4 * it + 2] = v.z;
+                xr[4 * it + 3] = v.w;
             }
             else
             {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    xr[4 * it + j] = in && 4 * cg + j < cn ? __ldg(xp + j) : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int it = 0; it < TO / 32; ++it)
+        {
+            const int idx = it * 256 + tid;
+            const int c = idx / (TO / 4), o4 = idx % (TO / 4);
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (c < cn && o0 + 4 * o4 < s.cout)
+                v = __ldg(reinterpret_cast<const float4*>(
+                    l.weights + (static_cast<size_t>(tap) * s.cin + c0 + c) * s.cout + o0 + 4 * o4));
+            wr[it] = v;
+        }
+    };
+    auto store = [&](ConvStage<TO>& st)
+    {
+#pragma unroll
+        for (int it = 0; it < 4; ++it)
+        {
+            const int idx = it * 256 + tid;
+            const int r = idx & (TF - 1), cg = idx >> 7;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                st.xs[4 * cg + j][r] = xr[4 * it + j];
+        }
+#pragma unroll
+        for (int it = 0; it < TO / 32; ++it)
+        {
+            const int idx = it * 256 + tid;
+            const int c = idx / (TO / 4), o4 = idx % (TO / 4);
+            *reinterpret_cast<float4*>(&st.ws[c][4 * o4]) = wr[it];
+        }
+    };
+
+    if (steps > 0)
+    {
+        load(0);
+        store(stage[0]);
+    }
+    __syncthreads();
+    for (int k = 0; k < steps; ++k)
+    {
+        const ConvStage<TO>& st = stage[k & 1];
+        if (k + 1 < steps)
+            load(k + 1);
+        int ti, c0;
+        step_tap(k, ti, c0);
+        const int cn = s.cin - c0 < CK ? s.cin - c0 : CK;
+        if ((all_mask >> ti) & 1u)
+        {
 #pragma unroll 2
-                for (int c = 0; c < cn; ++c)
+            for (int c = 0; c < cn; ++c)
+            {
+                const float4 w0 = *reinterpret_cast<const float4*>(&st.ws[c][tx * 8]);
+                const float4 w1 = *reinterpret_cast<const float4*>(&st.ws[c][tx * 8 + 4]);
+                const float wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                float xa[TR];
+#pragma unroll
+                for (int i = 0; i < TR; i += 4)
                 {
-                    const float4 wv = *reinterpret_cast<const float4*>(&ws[c][tx * 4]);
-                    const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
+                    const float4 v = *reinterpret_cast<const float4*>(&st.xs[c][ty * TR + i]);
+                    xa[i] = v.x;
+                    xa[i + 1] = v.y;
+                    xa[i + 2] = v.z;
+                    xa[i + 3] = v.w;
+                }
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
+                for (int i = 0; i < TR; ++i)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        sum[i][j] = __fadd_rn(sum[i][j], __fmul_rn(xa[i], wa[j]));
+            }
+        }
+        else
+        {
+            const int tap = s.transposed ? tap_first + ti * s.stride : ti;
+            unsigned valid = 0;
+#pragma unroll
+            for (int i = 0; i < TR; ++i)
+                if (g.takes(s, seq, ty * TR + i, tap))
+                    valid |= 1u << i;
+#pragma unroll 1
+            for (int c = 0; c < cn; ++c)
+            {
+                const float4 w0 = *reinterpret_cast<const float4*>(&st.ws[c][tx * 8]);
+                const float4 w1 = *reinterpret_cast<const float4*>(&st.ws[c][tx * 8 + 4]);
+                const float wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int i = 0; i < TR; ++i)
+                {
+                    const float xv = st.xs[c][ty * TR + i];
+                    const bool take = (valid >> i) & 1u;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
                     {
-                        const float xv = xs[ty * 8 + i][c];
-                        const bool take = (valid >> i) & 1u;
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                        {
-                            const float n = __fadd_rn(sum[i][j], __fmul_rn(xv, wa[j]));
-                            sum[i][j] = take ? n : sum[i][j];
-                        }
+                        const float n = __fadd_rn(sum[i][j], __fmul_rn(xv, wa[j]));
+                        sum[i][j] = take ? n : sum[i][j];
                     }
                 }
             }
-            __syncthreads();
         }
+        if (k + 1 < steps)
+            store(stage[(k + 1) & 1]);
+        __syncthreads();
     }
+
+    // Epilogue: + bias, then residual + result; optionally Snake of the next
+    // layer into `act` (the reference applies it to the stored sum).
     bool ok = true;
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < TR; ++i)
     {
-        const int f = g.out_frame(s, ty * 8 + i);
+        const int r = ty * TR + i;
+        const int f = g.out_frame(s, r);
         if (f >= seq.out_frames)
             continue;
         const size_t row = static_cast<size_t>(seq.out_offset + f) * s.cout;
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < 8; ++j)
         {
-            const int o = o0 + tx * 4 + j;
+            const int o = o0 + tx * 8 + j;
             if (o >= s.cout)
                 continue;
-            float v = __fadd_rn(sum[i][j], bias[o]);
-            if (residual)
-                v = __fadd_rn(residual[row + o], v);
+            float v = __fadd_rn(sum[i][j], __ldg(l.bias + o));
+            if (l.residual)
+                v = __fadd_rn(l.residual[row + o], v);
             ok = ok && isfinite(v);
-            y[row + o] = v;
+            if (l.y)
+                l.y[row + o] = v;
+            if (l.act)
+            {
+                const float a = snake_value(v, __ldg(l.alpha + o));
+                ok = ok && isfinite(a);
+                l.act[row + o] = a;
+            }
         }
     }
-    if (!ok && error_word)
-        atomicOr(error_word, error_nonfinite);
+    if (!ok && l.error_word)
+        atomicOr(l.error_word, error_nonfinite);
 }
 
 // Narrow outputs (DAC exit convolution to 1-2 PCM channels): one thread per
@@ -401,14 +528,35 @@ int conv_tile_frames(const ConvShape&)
     return TF;
 }
 
+template <int TO> void launch_conv(const ConvLaunch& l, cudaStream_t stream)
+{
+    constexpr size_t smem = conv_smem_bytes<TO>();
+    static std::once_flag attr_once[64];
+    int device = 0;
+    cudaGetDevice(&device);
+    if (device >= 0 && device < 64)
+        std::call_once(attr_once[device],
+                       []
+                       {
+                           cudaFuncSetAttribute(conv1d_kernel<TO>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(smem));
+                       });
+    const dim3 grid(l.tile_count, (l.shape.cout + TO - 1) / TO);
+    conv1d_kernel<TO><<<grid, 256, smem, stream>>>(l);
+    note_launch();
+}
+
 void conv1d(const ConvLaunch& l, cudaStream_t stream)
 {
     if (l.tile_count <= 0)
         return;
-    const dim3 grid(l.tile_count, (l.shape.cout + TO - 1) / TO);
-    conv1d_kernel<<<grid, 256, 0, stream>>>(l.x, l.weights, l.bias, l.residual, l.y, l.sequences,
-                                            l.tiles, l.shape, l.error_word);
-    note_launch();
+    // 128-channel tiles (8 x 8 chains per thread) where the layer is at least
+    // that wide; 64-channel tiles (4 x 8) for the 64-channel layers.
+    if (l.shape.cout >= 128)
+        launch_conv<128>(l, stream);
+    else
+        launch_conv<64>(l, stream);
 }
 
 void conv1d_narrow(const float* x, const float* w, const float* bias, float* y,

@@ -39,11 +39,13 @@ struct ConvLaunch
     const float* weights;
     const float* bias;
     const float* residual; // same shape as y, or null
-    float* y;
+    float* y;              // raw result, or null when only `act` is wanted
     const Sequence* sequences;
     const int4* tiles; // {sequence, first output frame (per phase for transposed), phase, 0}
     int tile_count;
     ConvShape shape;
+    const float* alpha = nullptr; // next layer's Snake alpha [cout], with act
+    float* act = nullptr;         // Snake(result) (same shape as y), or null
 };
 void conv1d(const ConvLaunch& launch, cudaStream_t stream);
 // Output channels < 16 (DAC exit to PCM): one thread per output.
