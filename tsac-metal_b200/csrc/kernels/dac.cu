@@ -14,11 +14,11 @@
 // B200 mapping of the exact-order convolution: the reference's per-output
 // serial chain is kept (products and sums rounded separately, taps outer,
 // input channels inner), and parallelism comes from outputs.  A CTA owns a
-// 128-frame x 128-channel output tile (64 for 64-channel layers), 256 threads
-// each accumulating 8 (4) frames x 8 channels in registers; per (tap,
+// 128-frame x 128-channel output tile (64 for 64-channel layers), 512 (256)
+// threads each accumulating 4 frames x 8 channels in registers; per (tap,
 // 32-channel chunk) it stages the input rows channel-major and the weight
 // slice in shared memory, double-buffered through registers, so every staged
-// value is reused 8x from registers and a thread's operands are 16-byte loads.
+// value is reused 4x or 8x from registers and a thread's operands are 16-byte loads.
 // Device weights are laid out [tap][in][out] so the weight slice loads are
 // contiguous.
 #include "kernels/dac.cuh"
@@ -53,7 +53,7 @@ __global__ void snake_kernel(const float* __restrict__ x, const float* __restric
         atomicOr(error_word, error_nonfinite);
 }
 
-constexpr int TF = 128, CK = 32;
+constexpr int TF = 128, CK = 64;
 
 // Output frame of tile row r and the input frame feeding it through `tap`.
 struct TileGeometry
@@ -83,8 +83,8 @@ struct TileGeometry
 };
 
 // Shared memory of one pipeline stage: the input chunk stored channel-major
-// (xs[c][row], so a thread's TR consecutive rows are one or two 16-byte
-// loads) and the weight chunk [c][output].
+// (xs[c][row], so a thread's 4 consecutive rows are one 16-byte load) and the
+// weight chunk [c][output].
 template <int TO> struct ConvStage
 {
     float xs[CK][TF + 4];
@@ -96,21 +96,26 @@ template <int TO> constexpr size_t conv_smem_bytes()
     return 2 * sizeof(ConvStage<TO>);
 }
 
-// Exact-order convolution.  A CTA owns a 128-frame x TO-channel output tile;
-// its 256 threads each hold TR frames x 8 channels of serial chains in
-// registers (TR = 8 for TO = 128, 4 for TO = 64).  Per (tap, 32-channel chunk)
-// "step", the chunk's inputs and weights are staged in shared memory; the next
-// step's global loads are issued into registers before the current step's
-// arithmetic and stored after it (two stages, one barrier per step).  Per
-// output the order is the reference's: taps ascending, channels ascending,
-// sum = sum + x * w with the product and the sum each rounded; a row skips
-// taps whose input frame lies outside its window.
-template <int TO>
-__global__ void __launch_bounds__(256, 1)
+// Exact-order convolution.  A CTA owns a 128-frame x TO-channel output tile
+// (TO = 128 with 512 threads, 64 with 256); each thread holds 4 frames x 8
+// channels of serial chains in registers: channels tx*4..tx*4+3 and
+// TO/2 + tx*4..+3, so the 8 threads of a shared-memory wavefront read 128
+// contiguous weight bytes (no bank conflicts).  Per (tap, 32-channel chunk)
+// "step", the chunk's inputs and weights are staged in shared memory; the
+// next step's global loads are issued into registers before the current
+// step's arithmetic and stored after it (two stages, one barrier per step).
+// Per output the order is the reference's: taps ascending, channels
+// ascending, sum = sum + x * w with the product and the sum each rounded; a
+// row skips taps whose input frame lies outside its window.
+template <int TO, int THREADS>
+__global__ void __launch_bounds__(THREADS, 512 / THREADS)
     conv1d_kernel(ConvLaunch l)
 {
-    constexpr int TR = TO == 128 ? 8 : 4;
-    constexpr int CG = TO / 8; // column groups (threads across outputs)
+    constexpr int TR = 4;
+    constexpr int CG = TO / 8;           // column groups (threads across outputs)
+    static_assert(THREADS / CG * TR == TF, "tile rows");
+    constexpr int XV = TF * CK / 4 / THREADS; // input float4 per thread per step
+    constexpr int WV = CK * TO / 4 / THREADS; // weight float4 per thread per step
     extern __shared__ __align__(16) unsigned char conv_smem[];
     auto* stage = reinterpret_cast<ConvStage<TO>*>(conv_smem);
     const ConvShape s = l.shape;
@@ -154,9 +159,8 @@ __global__ void __launch_bounds__(256, 1)
             m &= m - 1;
         ti = __ffs(m) - 1;
     };
-    // Register prefetch of one step: 16 inputs and 4 x 4 weights per thread.
-    float xr[16];
-    float4 wr[TO / 32];
+    float xr[4 * XV];
+    float4 wr[WV];
     auto load = [&](int k)
     {
         int ti, c0;
@@ -164,9 +168,9 @@ __global__ void __launch_bounds__(256, 1)
         const int tap = s.transposed ? tap_first + ti * s.stride : ti;
         const int cn = s.cin - c0 < CK ? s.cin - c0 : CK;
 #pragma unroll
-        for (int it = 0; it < 4; ++it)
+        for (int it = 0; it < XV; ++it)
         {
-            const int idx = it * 256 + tid;
+            const int idx = it * THREADS + tid;
             const int r = idx & (TF - 1), cg = idx >> 7; // channels 4cg .. 4cg+3
             const int src = g.in_frame(s, r, tap);
             const bool in = src >= 0 && src < seq.in_frames;
@@ -187,9 +191,9 @@ __global__ void __launch_bounds__(256, 1)
             }
         }
 #pragma unroll
-        for (int it = 0; it < TO / 32; ++it)
+        for (int it = 0; it < WV; ++it)
         {
-            const int idx = it * 256 + tid;
+            const int idx = it * THREADS + tid;
             const int c = idx / (TO / 4), o4 = idx % (TO / 4);
             float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             if (c < cn && o0 + 4 * o4 < s.cout)
@@ -201,18 +205,18 @@ __global__ void __launch_bounds__(256, 1)
     auto store = [&](ConvStage<TO>& st)
     {
 #pragma unroll
-        for (int it = 0; it < 4; ++it)
+        for (int it = 0; it < XV; ++it)
         {
-            const int idx = it * 256 + tid;
+            const int idx = it * THREADS + tid;
             const int r = idx & (TF - 1), cg = idx >> 7;
 #pragma unroll
             for (int j = 0; j < 4; ++j)
                 st.xs[4 * cg + j][r] = xr[4 * it + j];
         }
 #pragma unroll
-        for (int it = 0; it < TO / 32; ++it)
+        for (int it = 0; it < WV; ++it)
         {
-            const int idx = it * 256 + tid;
+            const int idx = it * THREADS + tid;
             const int c = idx / (TO / 4), o4 = idx % (TO / 4);
             *reinterpret_cast<float4*>(&st.ws[c][4 * o4]) = wr[it];
         }
@@ -234,22 +238,14 @@ __global__ void __launch_bounds__(256, 1)
         const int cn = s.cin - c0 < CK ? s.cin - c0 : CK;
         if ((all_mask >> ti) & 1u)
         {
-#pragma unroll 2
+#pragma unroll 4
             for (int c = 0; c < cn; ++c)
             {
-                const float4 w0 = *reinterpret_cast<const float4*>(&st.ws[c][tx * 8]);
-                const float4 w1 = *reinterpret_cast<const float4*>(&st.ws[c][tx * 8 + 4]);
+                const float4 w0 = *reinterpret_cast<const float4*>(&st.ws[c][tx * 4]);
+                const float4 w1 = *reinterpret_cast<const float4*>(&st.ws[c][TO / 2 + tx * 4]);
+                const float4 xv = *reinterpret_cast<const float4*>(&st.xs[c][ty * TR]);
                 const float wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-                float xa[TR];
-#pragma unroll
-                for (int i = 0; i < TR; i += 4)
-                {
-                    const float4 v = *reinterpret_cast<const float4*>(&st.xs[c][ty * TR + i]);
-                    xa[i] = v.x;
-                    xa[i + 1] = v.y;
-                    xa[i + 2] = v.z;
-                    xa[i + 3] = v.w;
-                }
+                const float xa[TR] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
                 for (int i = 0; i < TR; ++i)
 #pragma unroll
@@ -268,8 +264,8 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll 1
             for (int c = 0; c < cn; ++c)
             {
-                const float4 w0 = *reinterpret_cast<const float4*>(&st.ws[c][tx * 8]);
-                const float4 w1 = *reinterpret_cast<const float4*>(&st.ws[c][tx * 8 + 4]);
+                const float4 w0 = *reinterpret_cast<const float4*>(&st.ws[c][tx * 4]);
+                const float4 w1 = *reinterpret_cast<const float4*>(&st.ws[c][TO / 2 + tx * 4]);
                 const float wa[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
                 for (int i = 0; i < TR; ++i)
@@ -304,7 +300,7 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
         for (int j = 0; j < 8; ++j)
         {
-            const int o = o0 + tx * 8 + j;
+            const int o = o0 + (j < 4 ? tx * 4 + j : TO / 2 + tx * 4 + j - 4);
             if (o >= s.cout)
                 continue;
             float v = __fadd_rn(sum[i][j], __ldg(l.bias + o));
@@ -528,7 +524,7 @@ int conv_tile_frames(const ConvShape&)
     return TF;
 }
 
-template <int TO> void launch_conv(const ConvLaunch& l, cudaStream_t stream)
+template <int TO, int THREADS> void launch_conv(const ConvLaunch& l, cudaStream_t stream)
 {
     constexpr size_t smem = conv_smem_bytes<TO>();
     static std::once_flag attr_once[64];
@@ -538,12 +534,12 @@ template <int TO> void launch_conv(const ConvLaunch& l, cudaStream_t stream)
         std::call_once(attr_once[device],
                        []
                        {
-                           cudaFuncSetAttribute(conv1d_kernel<TO>,
+                           cudaFuncSetAttribute(conv1d_kernel<TO, THREADS>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 static_cast<int>(smem));
                        });
     const dim3 grid(l.tile_count, (l.shape.cout + TO - 1) / TO);
-    conv1d_kernel<TO><<<grid, 256, smem, stream>>>(l);
+    conv1d_kernel<TO, THREADS><<<grid, THREADS, smem, stream>>>(l);
     note_launch();
 }
 
@@ -554,9 +550,9 @@ void conv1d(const ConvLaunch& l, cudaStream_t stream)
     // 128-channel tiles (8 x 8 chains per thread) where the layer is at least
     // that wide; 64-channel tiles (4 x 8) for the 64-channel layers.
     if (l.shape.cout >= 128)
-        launch_conv<128>(l, stream);
+        launch_conv<128, 512>(l, stream);
     else
-        launch_conv<64>(l, stream);
+        launch_conv<64, 256>(l, stream);
 }
 
 void conv1d_narrow(const float* x, const float* w, const float* bias, float* y,
