@@ -131,6 +131,35 @@ def max_over_ranks(value, world, torch, dist):
     return float(t.item())
 
 
+def gather_streams(streams, world, rank, torch, dist):
+    """All ranks' encoded streams, gathered to every rank over the process
+    group (NCCL on GPUs: the only collective on the data path, used to collect
+    results); returns the list of all streams in rank order on rank 0, else None.
+    Each rank sends one byte tensor of its length-prefixed streams."""
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    payload = b"".join(len(x).to_bytes(8, "little") + bytes(x) for x in streams)
+    size = torch.tensor([len(payload)], device=device, dtype=torch.int64)
+    sizes = [torch.zeros_like(size) for _ in range(world)]
+    dist.all_gather(sizes, size)
+    longest = int(max(int(x.item()) for x in sizes))
+    buf = torch.zeros(longest, dtype=torch.uint8, device=device)
+    if payload:
+        buf[: len(payload)] = torch.frombuffer(bytearray(payload), dtype=torch.uint8).to(device)
+    parts = [torch.zeros_like(buf) for _ in range(world)]
+    dist.all_gather(parts, buf)
+    if rank != 0:
+        return None
+    out = []
+    for n, part in zip(sizes, parts):
+        raw = part[: int(n.item())].cpu().numpy().tobytes()
+        at = 0
+        while at < len(raw):
+            length = int.from_bytes(raw[at: at + 8], "little")
+            out.append(raw[at + 8: at + 8 + length])
+            at += 8 + length
+    return out
+
+
 def clip_seeds(rank, clips):
     """PCM seeds of one rank's clips: disjoint across ranks (clip sharding with
     no data-path exchange); rank 0's clip 0 is the cfg0 clip (seed 0)."""
@@ -221,9 +250,12 @@ def codec_workload(args, rank, world, torch, dist):
     s2.record()
     h2d = d2h = 0
     e2e_steps = min(args.steps, 2)
+    gathered = None
     for _ in range(e2e_steps):
         st = analyzer.encode_batch(host, opts)
         decoded = analyzer.decode_batch(st)
+        if world > 1:
+            gathered = gather_streams(st, world, rank, torch, dist)
         h2d = sum(p.nbytes for p in host)
         d2h = sum(d.samples.nbytes for d in decoded) + sum(len(x) for x in st)
     e2.record()
@@ -287,7 +319,8 @@ def codec_workload(args, rank, world, torch, dist):
         "launches_before_timed": launches_before,
         "clocks": clock_info,
         "e2e": {"value": round(e2e_value, 2), "unit": "x realtime", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "streams_gathered_on_rank0": len(gathered) if gathered is not None else None},
     }
 
 

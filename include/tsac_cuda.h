@@ -97,6 +97,16 @@ int tsac_cuda_encode(tsac_cuda_context* context, const float* pcm, size_t channe
                      const tsac_cuda_encode_options* options, uint8_t** out, size_t* out_bytes,
                      size_t* symbol_bits);
 
+/* tsac_cuda_encode plus the per-codebook totals an EntropyObserver would
+ * accumulate from after_symbol (include/tsac/observer.hpp:12-16; the bits of a
+ * symbol are the range encoder's bit-position difference,
+ * src/format/entropy.cpp:93-98): codebook_bits[b] for b < codebooks (entries
+ * past the stream's codebook count are 0; all 0 for fast streams). */
+int tsac_cuda_encode_observed(tsac_cuda_context* context, const float* pcm, size_t channels,
+                              size_t samples, ptrdiff_t channel_stride, ptrdiff_t sample_stride,
+                              const tsac_cuda_encode_options* options, uint8_t** out,
+                              size_t* out_bytes, uint64_t* codebook_bits, size_t codebooks);
+
 /* AudioAnalyzer::decode (include/tsac/audio_analyzer.hpp:35): stream ->
  * interleaved float PCM [sample][channel], padding retained. */
 int tsac_cuda_decode(tsac_cuda_context* context, const uint8_t* stream, size_t bytes,
@@ -128,6 +138,18 @@ int tsac_cuda_decode_batch_device(tsac_cuda_context* context, size_t count,
  * channel and symbol count of a stream, without decoding it. */
 int tsac_cuda_stream_info(const uint8_t* stream, size_t bytes, unsigned* channels,
                           size_t* samples_per_channel, size_t* symbols);
+
+/* Header fields of a .tsac stream (parse_header, src/format/container.cpp:43-80). */
+typedef struct tsac_cuda_stream_header
+{
+    unsigned method;         /* 0 fast, 1 normal */
+    unsigned model_channels; /* 1 or 2 */
+    unsigned groups;         /* channel groups (separate channels / mono layouts) */
+    unsigned codebooks;
+    uint64_t frames;         /* 512-sample frames */
+    unsigned batch;          /* entropy batch (lanes) */
+} tsac_cuda_stream_header;
+int tsac_cuda_stream_header_info(const uint8_t* stream, size_t bytes, tsac_cuda_stream_header* out);
 
 /* unpack_fast (src/format/container.hpp:28, src/format/container.cpp): the
  * 10-bit token fields of a fast-method stream, after the header and CRC

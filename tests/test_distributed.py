@@ -1,7 +1,8 @@
 """Multi-process host logic of the clip-sharded benchmark on CPU (gloo, two
 ranks): each rank codes its own clips with no data-path exchange, the timed
-region ends in a max over ranks, and the whole-job rate counts every rank's
-clips against the slowest rank's time."""
+region ends in a max over ranks, the whole-job rate counts every rank's clips
+against the slowest rank's time, and the result gather (the one collective on
+the data path) delivers every rank's streams to rank 0."""
 from __future__ import annotations
 
 import os
@@ -40,7 +41,11 @@ def _rank_main(rank, world, port, results):
         elapsed = 100.0 + 50.0 * rank
         slowest = bench.max_over_ranks(elapsed, world, torch, dist)
         rate = bench.whole_job_rate(4 * 30.0, world, slowest)
-        results[rank] = {"gathered": gathered, "slowest": slowest, "rate": rate}
+        # Result gather: ragged per-rank stream lists reach rank 0 intact.
+        mine = [bytes([rank, i]) * (i + 1) for i in range(rank + 2)]
+        streams = bench.gather_streams(mine, world, rank, torch, dist)
+        results[rank] = {"gathered": gathered, "slowest": slowest, "rate": rate,
+                         "streams": streams}
     finally:
         dist.destroy_process_group()
 
@@ -61,3 +66,6 @@ def test_clip_sharding_and_max_over_ranks():
         assert r["gathered"][0][0] == 0  # rank 0 clip 0 is the cfg0 clip
         assert r["slowest"] == pytest.approx(150.0)
         assert r["rate"] == pytest.approx(4 * 30.0 * world / 0.150)
+    expected = [bytes([r, i]) * (i + 1) for r in range(world) for i in range(r + 2)]
+    assert results[0]["streams"] == expected
+    assert results[1]["streams"] is None

@@ -85,6 +85,28 @@ int tsac_cuda_encode(tsac_cuda_context* ctx, const float* pcm, size_t channels, 
         });
 }
 
+int tsac_cuda_encode_observed(tsac_cuda_context* ctx, const float* pcm, size_t channels,
+                              size_t samples, ptrdiff_t channel_stride, ptrdiff_t sample_stride,
+                              const tsac_cuda_encode_options* opts, uint8_t** out,
+                              size_t* out_bytes, uint64_t* codebook_bits, size_t codebooks)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            tsacb::require(ctx && out && out_bytes && (codebook_bits || codebooks == 0),
+                           "null argument");
+            std::vector<std::size_t> bits;
+            std::vector<std::vector<std::size_t>> book_bits;
+            auto r = tsacb::encode_batch(ctx->impl,
+                                         {pcm_input(pcm, channels, samples, channel_stride, sample_stride)},
+                                         options(opts), &bits, &book_bits);
+            for (size_t b = 0; b < codebooks; ++b)
+                codebook_bits[b] = b < book_bits[0].size() ? book_bits[0][b] : 0;
+            *out = tsacb::malloc_copy(r[0].data(), r[0].size());
+            *out_bytes = r[0].size();
+        });
+}
+
 int tsac_cuda_decode(tsac_cuda_context* ctx, const uint8_t* stream, size_t bytes, float** out,
                      size_t* samples, unsigned* channels)
 {
@@ -154,6 +176,22 @@ int tsac_cuda_stream_info(const uint8_t* stream, size_t bytes, unsigned* channel
             *samples_per_channel = h.samples_per_channel();
             if (symbols)
                 *symbols = h.symbol_count();
+        });
+}
+
+int tsac_cuda_stream_header_info(const uint8_t* stream, size_t bytes, tsac_cuda_stream_header* out)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            tsacb::require(stream && out, "null argument");
+            const auto h = tsacb::parse_header(tsacb::ByteView(stream, bytes));
+            out->method = h.method;
+            out->model_channels = h.model_channels;
+            out->groups = h.groups;
+            out->codebooks = h.codebooks;
+            out->frames = h.frames;
+            out->batch = h.batch;
         });
 }
 

@@ -254,17 +254,23 @@ void analyze_recordings(Context& ctx, const std::vector<PcmInput>& pcm,
 }
 
 Bytes range_code(const Header& h, std::span<const std::uint16_t> tok, const std::uint16_t* q,
-                 const Limits& limits, std::size_t* bits)
+                 const Limits& limits, std::size_t* bits, std::size_t* book_bits = nullptr)
 {
     require(limits.file_bytes >= 19, "normal framing exceeds file limit");
     RangeEncoder encoder(limits.file_bytes - 18);
     visit_entropy_positions(h,
                             [&](const EntropyPosition& p)
                             {
+                                // Bits of one symbol: the encoder's bit position
+                                // difference (EntropyObserver::after_symbol,
+                                // src/format/entropy.cpp:93-98).
+                                const auto before = book_bits ? encoder.bit_position() : 0;
                                 const unsigned token = tok[p.token_offset];
                                 const auto* path = q + p.token_offset * 10;
                                 for (int d = 0; d < 10; ++d)
                                     encoder.put(path[d], (token >> (9 - d)) & 1u);
+                                if (book_bits)
+                                    book_bits[p.codebook] += encoder.bit_position() - before;
                             });
     if (bits)
         *bits = encoder.bit_position();
@@ -329,7 +335,8 @@ Bytes pack_normal(Context& ctx, Header header, std::span<const std::uint16_t> to
 }
 
 std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
-                                const EncodeOptions& options, std::vector<std::size_t>* bits)
+                                const EncodeOptions& options, std::vector<std::size_t>* bits,
+                                std::vector<std::vector<std::size_t>>* book_bits)
 {
     ctx.bind();
     Profile profile(ctx.stream(), "encode");
@@ -358,6 +365,12 @@ std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
     std::vector<Bytes> out(n);
     if (bits)
         bits->assign(n, 0);
+    if (book_bits)
+    {
+        book_bits->assign(n, {});
+        for (std::size_t i = 0; i < n; ++i)
+            (*book_bits)[i].assign(headers[i].codebooks, 0);
+    }
     std::vector<std::vector<std::uint16_t>> q15(n);
     for (std::size_t i = 0; i < n; ++i)
     {
@@ -379,7 +392,8 @@ std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
                  {
                      if (headers[i].method == 1)
                          out[i] = range_code(headers[i], tokens[i], q15[i].data(), ctx.limits(),
-                                             bits ? &(*bits)[i] : nullptr);
+                                             bits ? &(*bits)[i] : nullptr,
+                                             book_bits ? (*book_bits)[i].data() : nullptr);
                  });
     profile.mark("range encode");
     return out;

@@ -42,7 +42,8 @@ Header audio_header(const PcmInput& pcm, const EncodeOptions& options, const Lim
 
 // Batched entry points (one call = many independent recordings).
 std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
-                                const EncodeOptions& options, std::vector<std::size_t>* bits);
+                                const EncodeOptions& options, std::vector<std::size_t>* bits,
+                                std::vector<std::vector<std::size_t>>* book_bits = nullptr);
 // With device_out, recording i is written to device_out[i] (interleaved,
 // channels x padded samples floats) and DecodedAudio::samples stays empty.
 std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>& streams,

@@ -87,6 +87,17 @@ void TransformerEngine::quantize(const std::uint16_t* x, int rows, int k, std::i
     dev::qlinear_quantize(x, rows, k, xq, xs, error_word(), stream_);
 }
 
+namespace
+{
+double linear_work(int rows, double n, double k)
+{
+    const double m = rows;
+    // GEMV-shaped launches are weight-streaming (bytes); GEMM launches count int8 ops.
+    return rows <= 256 ? n * k + 4 * n * k / 256 + 4 * n + m * k + 4 * m * k / 256 + 2 * m * n
+                       : 2.0 * m * n * k;
+}
+} // namespace
+
 void TransformerEngine::run_linear(int projection, const std::int8_t* xq, const float* xs,
                                    int rows, std::uint16_t* y, const std::uint16_t* residual,
                                    bool gelu)
@@ -104,11 +115,47 @@ void TransformerEngine::run_linear(int projection, const std::int8_t* xq, const 
     a.m = rows;
     a.n = l.output;
     a.k = l.input;
-    const double n = l.output, k = l.input, m = rows;
-    // GEMV-shaped launches are weight-streaming (bytes); GEMM launches count int8 ops.
     KernelTimer::Scope timing(rows <= 256 ? "qlinear_small" : "qlinear_gemm", stream_,
-                              rows <= 256 ? n * k + 4 * n * k / 256 + 4 * n + m * k + 4 * m * k / 256 + 2 * m * n
-                                         : 2.0 * m * n * k);
+                              linear_work(rows, l.output, l.input));
+    dev::qlinear_matmul(a, stream_);
+}
+
+void TransformerEngine::run_linear_bf16(int projection, const std::uint16_t* x, int rows,
+                                        std::uint16_t* y, const std::uint16_t* residual,
+                                        bool gelu, std::int8_t* xq, float* xs)
+{
+    // A separate BF8L pass: quantizing inside the linear kernel was measured
+    // slower on B200 (each CTA re-quantizes its rows on its critical path).
+    const auto& l = model_->projections.at(static_cast<std::size_t>(projection));
+    quantize(x, rows, static_cast<int>(l.input), xq, xs);
+    run_linear(projection, xq, xs, rows, y, residual, gelu);
+}
+
+void TransformerEngine::run_qkv(int projection, const std::int8_t* xq, const float* xs, int rows,
+                                const dev::RowMeta* meta, std::uint16_t* query,
+                                std::uint16_t* cache_k, std::uint16_t* cache_v, std::uint16_t* qkv)
+{
+    const auto& l = model_->projections.at(static_cast<std::size_t>(projection));
+    const auto* rotations = model_->rotations.as<std::uint16_t>();
+    if (!dev::qlinear_qkv_fusable(rows, static_cast<int>(l.output)))
+    {
+        run_linear(projection, xq, xs, rows, qkv, nullptr, false);
+        KernelTimer::Scope timing("rotary_scatter", stream_, 0.0);
+        dev::rotary_scatter(qkv, meta, rotations, rows, query, cache_k, cache_v, stream_);
+        return;
+    }
+    require(l.output == 1536, "QKV projection must have 1536 outputs");
+    dev::QLinearArgs a;
+    a.weights = l.weights.as<std::int8_t>();
+    a.weight_scales = l.scales.as<float>();
+    a.bias = l.bias.as<float>();
+    a.xq = xq;
+    a.xscale = xs;
+    a.m = rows;
+    a.n = l.output;
+    a.k = l.input;
+    a.qkv = dev::QkvScatter{meta, rotations, query, cache_k, cache_v};
+    KernelTimer::Scope timing("qlinear_small", stream_, linear_work(rows, l.output, l.input));
     dev::qlinear_matmul(a, stream_);
 }
 
@@ -128,7 +175,6 @@ void TransformerEngine::run_stack(Workspace& ws_, bool temporal, int rows, std::
     auto* att = ws_.get<std::uint16_t>("att", static_cast<std::size_t>(rows) * 512);
     auto* mlp = ws_.get<std::uint16_t>("mlp", static_cast<std::size_t>(rows) * 2048);
     auto* partials = ws_.get<float>("partials", dev::attention_partials_bytes(rows, max_time) / 4);
-    const auto* rotations = model_->rotations.as<std::uint16_t>();
     for (int l = 0; l < layers; ++l)
     {
         const int n1 = norm_index(temporal, l, false), n2 = norm_index(temporal, l, true);
@@ -140,17 +186,12 @@ void TransformerEngine::run_stack(Workspace& ws_, bool temporal, int rows, std::
                             model_->norm_bias[n1].as<std::uint16_t>(), rows, nullptr, xq, xs,
                             error_word(), stream_);
         }
-        run_linear(projection_index(temporal, l, 0), xq, xs, rows, qkv, nullptr, false);
-        {
-            KernelTimer::Scope timing("rotary_scatter", stream_, 0.0);
-            dev::rotary_scatter(qkv, meta, rotations, rows, query, ck, cv, stream_);
-        }
+        run_qkv(projection_index(temporal, l, 0), xq, xs, rows, meta, query, ck, cv, qkv);
         {
             KernelTimer::Scope timing("attention", stream_, 0.0);
             dev::attention(query, meta, ck, cv, rows, max_time, partials, att, stream_);
         }
-        quantize(att, rows, 512, xq, xs);
-        run_linear(projection_index(temporal, l, 1), xq, xs, rows, h, h, false);
+        run_linear_bf16(projection_index(temporal, l, 1), att, rows, h, h, false, xq, xs);
         {
             KernelTimer::Scope timing("layer_norm", stream_, 0.0);
             dev::layer_norm(h, model_->norm_gain[n2].as<std::uint16_t>(),
@@ -158,8 +199,7 @@ void TransformerEngine::run_stack(Workspace& ws_, bool temporal, int rows, std::
                             error_word(), stream_);
         }
         run_linear(projection_index(temporal, l, 2), xq, xs, rows, mlp, nullptr, true);
-        quantize(mlp, rows, 2048, xq, xs);
-        run_linear(projection_index(temporal, l, 3), xq, xs, rows, h, h, false);
+        run_linear_bf16(projection_index(temporal, l, 3), mlp, rows, h, h, false, xq, xs);
     }
     const int f = final_norm(temporal);
     dev::layer_norm(h, model_->norm_gain[f].as<std::uint16_t>(),
@@ -254,9 +294,8 @@ void TransformerEngine::predict_known(const Header& header, std::span<const std:
     dev::embed_sum(model_->embeddings.as<std::uint16_t>(), d_pool, d_toff, d_tcnt, trows, emb, s);
     auto* eq = ws_.get<std::int8_t>("eq", static_cast<std::size_t>(trows) * 1024);
     auto* es = ws_.get<float>("es", static_cast<std::size_t>(trows) * 4);
-    quantize(emb, trows, 1024, eq, es);
     auto* th = ws_.get<std::uint16_t>("th", static_cast<std::size_t>(trows) * 512);
-    run_linear(60, eq, es, trows, th, nullptr, false);
+    run_linear_bf16(60, emb, trows, th, nullptr, false, eq, es);
     const std::size_t tstride = static_cast<std::size_t>(next_slot) * 512;
     auto* tck = ws_.get<std::uint16_t>("tck", tstride * 12);
     auto* tcv = ws_.get<std::uint16_t>("tcv", tstride * 12);
@@ -321,9 +360,8 @@ void TransformerEngine::predict_known(const Header& header, std::span<const std:
             dev::embed_sum(model_->embeddings.as<std::uint16_t>(), d_pool, d_poff, d_pcnt, prows, pemb, s);
             auto* pq = ws_.get<std::int8_t>("pq", static_cast<std::size_t>(prows) * 1024);
             auto* ps = ws_.get<float>("ps", static_cast<std::size_t>(prows) * 4);
-            quantize(pemb, prows, 1024, pq, ps);
             auto* pproj = ws_.get<std::uint16_t>("pproj", static_cast<std::size_t>(prows) * 512);
-            run_linear(61, pq, ps, prows, pproj, nullptr, false);
+            run_linear_bf16(61, pemb, prows, pproj, nullptr, false, pq, ps);
             dev::add_positions(pproj, d_pid, d_pbook, model_->positions.as<std::uint16_t>(), prows,
                                ch + static_cast<std::size_t>(count) * 512, s);
         }
@@ -653,9 +691,8 @@ TransformerEngine::decode_predict(std::size_t step, std::size_t book, const floa
                            reinterpret_cast<const int*>(dev_t + tb.counts), trows, emb, s);
             auto* eq = ws.get<std::int8_t>("eq", static_cast<std::size_t>(trows) * 1024);
             auto* es = ws.get<float>("es", static_cast<std::size_t>(trows) * 4);
-            quantize(emb, trows, 1024, eq, es);
             auto* th = ws.get<std::uint16_t>("th", static_cast<std::size_t>(trows) * 512);
-            run_linear(60, eq, es, trows, th, nullptr, false);
+            run_linear_bf16(60, emb, trows, th, nullptr, false, eq, es);
             auto* tout = ws.get<std::uint16_t>("tout", static_cast<std::size_t>(trows) * 512);
             run_stack(ws, true, trows, th, d_meta, context, st.tck, st.tcv, st.tstride, tout,
                       nullptr, nullptr);
@@ -680,9 +717,8 @@ TransformerEngine::decode_predict(std::size_t step, std::size_t book, const floa
                            reinterpret_cast<const int*>(dev_c + cb.counts), n, pemb, s);
             auto* pq = ws.get<std::int8_t>("pq", static_cast<std::size_t>(n) * 1024);
             auto* ps = ws.get<float>("ps", static_cast<std::size_t>(n) * 4);
-            quantize(pemb, n, 1024, pq, ps);
             auto* pproj = ws.get<std::uint16_t>("pproj", static_cast<std::size_t>(n) * 512);
-            run_linear(61, pq, ps, n, pproj, nullptr, false);
+            run_linear_bf16(61, pemb, n, pproj, nullptr, false, pq, ps);
             dev::add_positions(pproj, st.identity, d_books, model_->positions.as<std::uint16_t>(),
                                n, ch, s);
         }

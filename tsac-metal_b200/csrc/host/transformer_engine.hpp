@@ -19,6 +19,7 @@
 // launch and one synchronisation on the host.
 #pragma once
 #include "device.hpp"
+#include "kernels/row_meta.hpp"
 #include "format.hpp"
 #include "models.hpp"
 
@@ -80,6 +81,14 @@ public:
 private:
     void run_linear(int projection, const std::int8_t* xq, const float* xs, int rows,
                     std::uint16_t* y, const std::uint16_t* residual, bool gelu);
+    // bf16 input: BF8L pass into xq / xs (scratch of rows x K), then the linear.
+    void run_linear_bf16(int projection, const std::uint16_t* x, int rows, std::uint16_t* y,
+                         const std::uint16_t* residual, bool gelu, std::int8_t* xq, float* xs);
+    // QKV projection + rotary + K/V cache scatter (fused where it fits; else
+    // through `qkv` scratch [rows][1536] and the rotary kernel).
+    void run_qkv(int projection, const std::int8_t* xq, const float* xs, int rows,
+                 const dev::RowMeta* meta, std::uint16_t* query, std::uint16_t* cache_k,
+                 std::uint16_t* cache_v, std::uint16_t* qkv);
     void quantize(const std::uint16_t* x, int rows, int k, std::int8_t* xq, float* xs);
     void run_stack(Workspace& ws, bool temporal, int rows, std::uint16_t* h,
                    const void* meta_device, int max_time, std::uint16_t* cache_k,

@@ -26,7 +26,47 @@ namespace tsacb::dev
 {
 namespace
 {
-// One warp per (row, 256-block): lane holds 8 consecutive values.
+// BF8L quantization of one 256-value block by one warp: lane l holds values
+// 8l..8l+7 of the block (a 16-byte load).  Returns the lane's 8 int8 values
+// packed in two words and the block scale; nonfinite inputs clear `finite`.
+struct Bf8lLane
+{
+    unsigned packed[2];
+    float scale;
+};
+
+__device__ __forceinline__ Bf8lLane bf8l_block(uint4 raw, bool& finite)
+{
+    const std::uint16_t* h = reinterpret_cast<const std::uint16_t*>(&raw);
+    float v[8];
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+    {
+        v[i] = from_bf16(h[i]);
+        finite = finite && isfinite(v[i]);
+        m = fmaxf(m, fabsf(flush(v[i])));
+    }
+#pragma unroll
+    for (int offset = 16; offset > 0; offset >>= 1)
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, offset));
+    float d = ftz_div(m, 127.0f);
+    d = d < 1e-35f ? 1e-35f : d;
+    Bf8lLane out;
+    out.scale = from_bf16(to_bf16(d));
+    const float reciprocal = ftz_div(1.0f, out.scale);
+    out.packed[0] = out.packed[1] = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+    {
+        float r = rintf(ftz_mul(v[i], reciprocal));
+        r = r < -128.0f ? -128.0f : (r > 127.0f ? 127.0f : r);
+        out.packed[i / 4] |= (static_cast<unsigned>(static_cast<int>(r)) & 0xffu) << (8 * (i % 4));
+    }
+    return out;
+}
+
+// One warp per (row, 256-block).
 __global__ void quantize_bf8l_kernel(const std::uint16_t* __restrict__ x, int k, int rows,
                                      std::int8_t* __restrict__ q, float* __restrict__ scales,
                                      unsigned* error_word)
@@ -40,47 +80,18 @@ __global__ void quantize_bf8l_kernel(const std::uint16_t* __restrict__ x, int k,
         return;
     }
     const int row = warp / blocks, block = warp % blocks;
-    const std::uint16_t* src = x + static_cast<size_t>(row) * k + block * 256 + lane * 8;
-    const uint4 raw = *reinterpret_cast<const uint4*>(src);
-    const std::uint16_t* h = reinterpret_cast<const std::uint16_t*>(&raw);
-    float v[8];
-    float m = 0.0f;
+    const uint4 raw = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * k + block * 256 + lane * 8);
     bool finite = true;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-    {
-        v[i] = from_bf16(h[i]);
-        finite = finite && isfinite(v[i]);
-        m = fmaxf(m, fabsf(flush(v[i])));
-    }
-#pragma unroll
-    for (int offset = 16; offset > 0; offset >>= 1)
-    {
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, offset));
-    }
+    const Bf8lLane r = bf8l_block(raw, finite);
     if (!__all_sync(0xffffffffu, finite) && lane == 0 && error_word)
     {
         atomicOr(error_word, error_nonfinite);
     }
-    float d = ftz_div(m, 127.0f);
-    d = d < 1e-35f ? 1e-35f : d;
-    const std::uint16_t s = to_bf16(d);
-    const float scale = from_bf16(s);
-    const float reciprocal = ftz_div(1.0f, scale);
-    unsigned packed[2] = {0, 0};
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-    {
-        float r = rintf(ftz_mul(v[i], reciprocal));
-        r = r < -128.0f ? -128.0f : (r > 127.0f ? 127.0f : r);
-        const unsigned byte = static_cast<unsigned>(static_cast<int>(r)) & 0xffu;
-        packed[i / 4] |= byte << (8 * (i % 4));
-    }
     *reinterpret_cast<uint2*>(q + static_cast<size_t>(row) * k + block * 256 + lane * 8) =
-        make_uint2(packed[0], packed[1]);
+        make_uint2(r.packed[0], r.packed[1]);
     if (lane == 0)
     {
-        scales[row * blocks + block] = scale;
+        scales[row * blocks + block] = r.scale;
     }
 }
 
@@ -230,13 +241,31 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], unsigned a0, unsigned a1, un
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__global__ void __launch_bounds__(256)
-    qlinear_mma_kernel(const std::int8_t* __restrict__ w, const float* __restrict__ wscale,
-                       const std::int8_t* __restrict__ xq, const float* __restrict__ xscale,
-                       int m_rows, int n_cols, int k, Epilogue e, std::uint16_t* __restrict__ y)
+struct MmaArgs
+{
+    const std::int8_t* w;
+    const float* wscale;
+    const std::int8_t* xq; // quantized activations
+    const float* xscale;
+    int m_rows, n_cols, k;
+    Epilogue e;
+    std::uint16_t* y;
+    QkvScatter qkv; // QKV_OUT destinations
+};
+
+// Shared memory of the decode-shaped kernel: the block dots.
+__host__ __device__ constexpr size_t mma_smem_bytes(int k)
+{
+    return static_cast<size_t>(k / 256) * MMA_MT * 128 * sizeof(int);
+}
+
+template <bool QKV_OUT>
+__global__ void __launch_bounds__(256) qlinear_mma_kernel(MmaArgs a)
 {
     pdl_prologue();
-    extern __shared__ int dots[]; // [block][m-tile][lane][4]
+    extern __shared__ __align__(16) unsigned char mma_smem[];
+    int* dots = reinterpret_cast<int*>(mma_smem); // [block][m-tile][lane][4]
+    const int k = a.k, m_rows = a.m_rows, n_cols = a.n_cols;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int n0 = blockIdx.x * 16, m0 = blockIdx.y * (8 * MMA_MT);
@@ -245,7 +274,7 @@ __global__ void __launch_bounds__(256)
         dots[i] = 0;
     __syncthreads();
     const int quarter = warp & 3;
-    const std::int8_t* wa = w + static_cast<size_t>(n0 + g) * k + quarter * 64 + t * 16;
+    const std::int8_t* wa = a.w + static_cast<size_t>(n0 + g) * k + quarter * 64 + t * 16;
     const std::int8_t* wb = wa + static_cast<size_t>(8) * k;
     for (int b = warp >> 2; b < blocks; b += 2)
     {
@@ -257,7 +286,7 @@ __global__ void __launch_bounds__(256)
         {
             const int m = m0 + mt * 8 + g;
             x[mt] = m < m_rows ? __ldg(reinterpret_cast<const uint4*>(
-                                     xq + static_cast<size_t>(m) * k + b * 256 + quarter * 64 + t * 16))
+                                     a.xq + static_cast<size_t>(m) * k + b * 256 + quarter * 64 + t * 16))
                                : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
@@ -281,26 +310,71 @@ __global__ void __launch_bounds__(256)
         const int id = threadIdx.x + half * 256;
         const int nl = id & 15, ml = id >> 4;
         const int n = n0 + nl, m = m0 + ml;
-        if (m >= m_rows)
-            continue;
-        const int mt = ml >> 3, col = ml & 7;
-        const int frag_lane = (nl & 7) * 4 + (col >> 1);
-        const int c = (nl >> 3) * 2 + (col & 1);
-        float sum = 0.0f;
-#pragma unroll 4
-        for (int b = 0; b < blocks; ++b)
+        const bool valid = m < m_rows;
+        std::uint16_t out = 0;
+        if (valid)
         {
-            const float scale = __fmul_rn(__ldg(wscale + b * n_cols + n), __ldg(xscale + m * blocks + b));
-            const int dot = dots[((b * MMA_MT + mt) * 32 + frag_lane) * 4 + c];
-            sum = __fmaf_rn(static_cast<float>(dot), scale, sum);
+            const int mt = ml >> 3, col = ml & 7;
+            const int frag_lane = (nl & 7) * 4 + (col >> 1);
+            const int c = (nl >> 3) * 2 + (col & 1);
+            float sum = 0.0f;
+#pragma unroll 4
+            for (int b = 0; b < blocks; ++b)
+            {
+                const float scale = __fmul_rn(__ldg(a.wscale + b * n_cols + n),
+                                              __ldg(a.xscale + m * blocks + b));
+                const int dot = dots[((b * MMA_MT + mt) * 32 + frag_lane) * 4 + c];
+                sum = __fmaf_rn(static_cast<float>(dot), scale, sum);
+            }
+            out = finish(sum, m, n, n_cols, a.e);
         }
-        y[static_cast<size_t>(m) * n_cols + n] = finish(sum, m, n, n_cols, e);
+        if constexpr (QKV_OUT)
+        {
+            // Rotary + K/V cache scatter of the bf16 projection (the
+            // rotary_scatter_kernel's operations): lanes n and n ^ 1 hold a
+            // (real, imaginary) pair.
+            const unsigned other = __shfl_xor_sync(0xffffffffu, static_cast<unsigned>(out), 1);
+            if (!valid)
+                continue;
+            const RowMeta rm = a.qkv.meta[m];
+            if (n < 1024)
+            {
+                const bool even = (n & 1) == 0;
+                std::uint16_t result = out;
+                if (rm.rotary >= 0)
+                {
+                    const int pair = (n & 511) >> 1;
+                    const unsigned cs = reinterpret_cast<const unsigned*>(a.qkv.rotations + rm.rotary * 128)[pair & 63];
+                    const float cosine = from_bf16(cs & 0xffffu), sine = from_bf16(cs >> 16);
+                    const float real = from_bf16(even ? out : static_cast<std::uint16_t>(other));
+                    const float imaginary = from_bf16(even ? static_cast<std::uint16_t>(other) : out);
+                    if (even)
+                        result = to_bf16(__fmaf_rn(real, cosine, -__fmul_rn(imaginary, sine)));
+                    else
+                        result = to_bf16(__fmaf_rn(imaginary, cosine, __fmul_rn(real, sine)));
+                }
+                if (n < 512)
+                    a.qkv.query[static_cast<size_t>(m) * 512 + n] = result;
+                else
+                    a.qkv.cache_k[static_cast<size_t>(rm.slot) * 512 + (n - 512)] = result;
+            }
+            else
+            {
+                a.qkv.cache_v[static_cast<size_t>(rm.slot) * 512 + (n - 1024)] = out;
+            }
+        }
+        else
+        {
+            if (valid)
+                a.y[static_cast<size_t>(m) * n_cols + n] = out;
+        }
     }
 }
 
-size_t mma_smem_bytes(int k)
+template <bool QKV_OUT> void set_mma_smem_limit()
 {
-    return static_cast<size_t>(k / 256) * MMA_MT * 128 * sizeof(int);
+    cudaFuncSetAttribute(qlinear_mma_kernel<QKV_OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(mma_smem_bytes(8192)));
 }
 
 void launch_small(const QLinearArgs& a, const Epilogue& e, cudaStream_t stream)
@@ -309,8 +383,11 @@ void launch_small(const QLinearArgs& a, const Epilogue& e, cudaStream_t stream)
     if (smem > 48 * 1024)
         qlinear_init();
     const dim3 grid(a.n / 16, (a.m + 8 * MMA_MT - 1) / (8 * MMA_MT));
-    launch_pdl(qlinear_mma_kernel, grid, dim3(256), smem, stream, a.weights, a.weight_scales, a.xq,
-               a.xscale, a.m, a.n, a.k, e, a.y);
+    const MmaArgs args{a.weights, a.weight_scales, a.xq, a.xscale, a.m, a.n, a.k, e, a.y, a.qkv};
+    if (a.qkv.meta)
+        launch_pdl(qlinear_mma_kernel<true>, grid, dim3(256), smem, stream, args);
+    else
+        launch_pdl(qlinear_mma_kernel<false>, grid, dim3(256), smem, stream, args);
     note_launch();
 }
 
@@ -329,8 +406,9 @@ void qlinear_init()
     const unsigned long long bit = 1ull << device;
     if (ready.load(std::memory_order_acquire) & bit)
         return;
-    if (cudaFuncSetAttribute(qlinear_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(mma_smem_bytes(8192))) == cudaSuccess)
+    set_mma_smem_limit<false>();
+    set_mma_smem_limit<true>();
+    if (cudaGetLastError() == cudaSuccess)
         ready.fetch_or(bit, std::memory_order_acq_rel);
 }
 
@@ -347,6 +425,11 @@ void qlinear_quantize(const std::uint16_t* x, int m, int k, std::int8_t* xq, flo
     launch_pdl(quantize_bf8l_kernel, dim3((warps * 32 + threads - 1) / threads), dim3(threads), 0,
                stream, x, k, m, xq, xscale, error_word);
     note_launch();
+}
+
+bool qlinear_qkv_fusable(int m, int n)
+{
+    return m >= 1 && m <= SMALL_MAX_M && n == 1536;
 }
 
 void qlinear_matmul(const QLinearArgs& a, cudaStream_t stream)

@@ -4,8 +4,21 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "kernels/row_meta.hpp"
+
 namespace tsacb::dev
 {
+// Fused QKV epilogue: rotary on q and k, then q to `query` [row][512] and k,
+// v to the caches at the row's slot (the rotary_scatter operations).
+struct QkvScatter
+{
+    const RowMeta* meta = nullptr; // null: plain output to y
+    const std::uint16_t* rotations = nullptr;
+    std::uint16_t* query = nullptr;
+    std::uint16_t* cache_k = nullptr;
+    std::uint16_t* cache_v = nullptr;
+};
+
 struct QLinearArgs
 {
     const std::int8_t* weights = nullptr;     // [n][k] int8
@@ -17,7 +30,11 @@ struct QLinearArgs
     const std::uint16_t* lut = nullptr;       // bf16 -> bf16 map applied last (GELU)
     std::uint16_t* y = nullptr;               // [m][n] bf16
     int m = 0, n = 0, k = 0;
+    QkvScatter qkv;                           // only where qlinear_qkv_fusable
 };
+
+// True when the decode-shaped kernel can apply the fused QKV epilogue.
+bool qlinear_qkv_fusable(int m, int n);
 
 // Bytes of scratch holding the quantized activations of m columns of k inputs.
 size_t qlinear_scratch_bytes(size_t m, size_t k);

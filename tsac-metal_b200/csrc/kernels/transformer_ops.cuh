@@ -8,18 +8,10 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "kernels/row_meta.hpp"
+
 namespace tsacb::dev
 {
-// Per-row attention/cache metadata.
-struct RowMeta
-{
-    int slot;      // cache slot receiving this row's key/value
-    int base;      // cache slot of position 0 of the row's sequence
-    int time;      // number of keys visible to the row (position + 1)
-    int rotary;    // rotary coefficient row (position), -1 = no rotary
-    int round;     // 1: bf16-round block value sums (time > 64 or replay prefill)
-};
-
 // out[r][0:1024] = sum over j < count[r] of E[j][tokens[offset[r] + j]] with
 // bf16 adds in book order (first term copied); count 0 gives zeros.
 void embed_sum(const std::uint16_t* embeddings, const std::uint16_t* tokens, const int* offsets,
