@@ -86,6 +86,21 @@ def test_decode_reference_stream_bit_exact(exact_analyzer, case):
     assert hashlib.sha256(flat.astype("<f4").tobytes()).hexdigest() == g["pcm_sha256"]
 
 
+def test_cfg0_full_clip_stream_and_pcm(analyzer, exact_analyzer):
+    """cfg0: 30 s joint stereo, seed 0, q=12, batch 3 (2,584 frames, lanes
+    862/861/861): the stream is byte-identical to the reference's, and exact
+    decoding reproduces the reference's PCM bit for bit."""
+    g = _golden("cfg0_stereo_30s")
+    pcm = synthetic.music_like(g["pcm_seed"], g["seconds"], g["channels"])
+    stream = analyzer.encode(pcm, _options(g))
+    assert hashlib.sha256(stream).hexdigest() == g["stream_sha256"]
+    audio = exact_analyzer.decode(stream)
+    flat = audio.samples.ravel()
+    assert hashlib.sha256(flat.astype("<f4").tobytes()).hexdigest() == g["pcm_sha256"]
+    fast = analyzer.decode(stream)
+    assert_pcm_close(fast.samples, audio.samples)
+
+
 @pytest.mark.parametrize("case", CASES)
 def test_decode_tensor_synthesis_within_tolerance(analyzer, exact_analyzer, case):
     stream = (GOLDEN / f"{case}.tsac").read_bytes()
