@@ -11,6 +11,7 @@ follow tests/audio_analyzer.cpp:307-425 of the reference.
 """
 import hashlib
 import json
+import pathlib
 
 import numpy as np
 import pytest
@@ -161,3 +162,29 @@ def test_failures_are_errors_and_analyzer_is_reusable(analyzer):
     # Reuse after failures.
     good = analyzer.encode(pcm)
     assert analyzer.decode(good).samples.shape == (512 * 5, 2)
+
+
+def test_fused_codebook_step_decodes_identically(tmp_path):
+    """The opt-in fused codebook-step kernel (one cluster launch per step)
+    produces the same PCM as the default separate kernels."""
+    import os
+    import subprocess
+    import sys
+    stream = (GOLDEN / "stereo_q12_b3_1s.tsac").read_bytes()
+    (tmp_path / "in.tsac").write_bytes(stream)
+    script = (
+        "import sys, numpy as np; sys.path.insert(0, %r)\n"
+        "import tsac_cuda\n"
+        "a = tsac_cuda.CudaAnalyzer(tsac_cuda.seeded_package(0), 0)\n"
+        "a.set_exact_synthesis(True)\n"
+        "d = a.decode(open(%r, 'rb').read())\n"
+        "np.save(%r, d.samples)\n"
+    ) % (str(pathlib.Path(tsac_cuda.__file__).parent), str(tmp_path / "in.tsac"), str(tmp_path / "out.npy"))
+    env = dict(os.environ, TSAC_CUDA_FUSED_CODEBOOK="1")
+    subprocess.run([sys.executable, "-c", script], env=env, check=True, timeout=600)
+    fused = np.load(tmp_path / "out.npy")
+    a = tsac_cuda.CudaAnalyzer(tsac_cuda.seeded_package(0), 0)
+    a.set_exact_synthesis(True)
+    default = a.decode(stream).samples
+    a.close()
+    assert np.array_equal(fused.view(np.uint32), default.view(np.uint32))

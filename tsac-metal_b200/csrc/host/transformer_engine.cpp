@@ -2,6 +2,7 @@
 
 #include "kernel_timer.hpp"
 
+#include "kernels/codebook_step.cuh"
 #include "kernels/launch_count.hpp"
 #include "kernels/qlinear.cuh"
 #include "kernels/transformer_ops.cuh"
@@ -677,6 +678,16 @@ TransformerEngine::decode_predict(std::size_t step, std::size_t book, const floa
         }
     }
 
+    // TSAC_CUDA_FUSED_CODEBOOK=1 runs each codebook step as one cluster
+    // launch (codebook_step.cu).  Bit-identical, but measured slower on B200
+    // (about 178 us against 150 us per step at 48 lanes: each cluster's
+    // phases are serial dependent chains on a few SMs, while the separate
+    // kernels spread every phase over 100+ CTAs), so it is off by default.
+    static const bool fused_codebook_step = []
+    {
+        const char* e = std::getenv("TSAC_CUDA_FUSED_CODEBOOK");
+        return e && e[0] == '1';
+    }();
     const auto enqueue = [&](int trows)
     {
         cuda_ok(cudaMemcpyAsync(st.dev_in, host, tb.bytes + cb.bytes, cudaMemcpyHostToDevice, s), "H2D");
@@ -702,33 +713,79 @@ TransformerEngine::decode_predict(std::size_t step, std::size_t book, const floa
         }
         const auto* d_meta = reinterpret_cast<const RowMeta*>(dev_c + cb.meta);
         const auto* d_books = reinterpret_cast<const int*>(dev_c + cb.books);
-        auto* ch = ws.get<std::uint16_t>("ch", static_cast<std::size_t>(n) * 512);
-        if (book == 0)
+        auto* tree = ws.get<float>("tree", static_cast<std::size_t>(n) * 1023);
+        if (fused_codebook_step)
         {
-            dev::add_positions(st.cond, reinterpret_cast<const int*>(dev_c + cb.lane_rows), d_books,
-                               model_->positions.as<std::uint16_t>(), n, ch, s);
+            // The whole codebook step in one cluster launch (codebook_step.cu).
+            dev::CodebookStepArgs a{};
+            a.rows = n;
+            a.book = static_cast<int>(book);
+            a.cond = st.cond;
+            a.lane_rows = reinterpret_cast<const int*>(dev_c + cb.lane_rows);
+            a.embeddings = model_->embeddings.as<std::uint16_t>();
+            a.tokens = reinterpret_cast<const std::uint16_t*>(dev_c + cb.tokens);
+            a.offsets = reinterpret_cast<const int*>(dev_c + cb.offsets);
+            a.counts = reinterpret_cast<const int*>(dev_c + cb.counts);
+            const auto linear = [&](int p)
+            {
+                const auto& l = model_->projections[static_cast<std::size_t>(p)];
+                return dev::CodebookLinear{l.weights.as<std::int8_t>(), l.scales.as<float>(),
+                                           l.bias.as<float>()};
+            };
+            a.proj61 = linear(61);
+            a.positions = model_->positions.as<std::uint16_t>();
+            a.books = d_books;
+            for (int l = 0; l < 3; ++l)
+            {
+                for (int op = 0; op < 4; ++op)
+                    a.layer[l][op] = linear(projection_index(false, l, op));
+                for (int second = 0; second < 2; ++second)
+                {
+                    const int nrm = norm_index(false, l, second != 0);
+                    a.norm_gain[2 * l + second] = model_->norm_gain[static_cast<std::size_t>(nrm)].as<std::uint16_t>();
+                    a.norm_bias[2 * l + second] = model_->norm_bias[static_cast<std::size_t>(nrm)].as<std::uint16_t>();
+                }
+            }
+            a.norm_gain[6] = model_->norm_gain[static_cast<std::size_t>(final_norm(false))].as<std::uint16_t>();
+            a.norm_bias[6] = model_->norm_bias[static_cast<std::size_t>(final_norm(false))].as<std::uint16_t>();
+            a.proj62 = linear(62);
+            a.gelu = model_->gelu.as<std::uint16_t>();
+            a.meta = d_meta;
+            a.cache_k = st.cck;
+            a.cache_v = st.ccv;
+            a.cache_stride = st.cstride;
+            a.tree = tree;
+            a.error_word = error_word();
+            KernelTimer::Scope timing("codebook_step", s, 0.0);
+            dev::codebook_step(a, s);
         }
         else
         {
-            auto* pemb = ws.get<std::uint16_t>("pemb", static_cast<std::size_t>(n) * 1024);
-            dev::embed_sum(model_->embeddings.as<std::uint16_t>(),
-                           reinterpret_cast<const std::uint16_t*>(dev_c + cb.tokens),
-                           reinterpret_cast<const int*>(dev_c + cb.offsets),
-                           reinterpret_cast<const int*>(dev_c + cb.counts), n, pemb, s);
-            auto* pq = ws.get<std::int8_t>("pq", static_cast<std::size_t>(n) * 1024);
-            auto* ps = ws.get<float>("ps", static_cast<std::size_t>(n) * 4);
-            auto* pproj = ws.get<std::uint16_t>("pproj", static_cast<std::size_t>(n) * 512);
-            run_linear_bf16(61, pemb, n, pproj, nullptr, false, pq, ps);
-            dev::add_positions(pproj, st.identity, d_books, model_->positions.as<std::uint16_t>(),
-                               n, ch, s);
-        }
-        auto* fq = ws.get<std::int8_t>("fq", static_cast<std::size_t>(n) * 512);
-        auto* fs = ws.get<float>("fs", static_cast<std::size_t>(n) * 2);
-        run_stack(ws, false, n, ch, d_meta, 12, st.cck, st.ccv, st.cstride, nullptr, fq, fs);
-        auto* logits = ws.get<std::uint16_t>("logits", static_cast<std::size_t>(n) * 1024);
-        run_linear(62, fq, fs, n, logits, nullptr, false);
-        auto* tree = ws.get<float>("tree", static_cast<std::size_t>(n) * 1023);
-        {
+            auto* ch = ws.get<std::uint16_t>("ch", static_cast<std::size_t>(n) * 512);
+            if (book == 0)
+            {
+                dev::add_positions(st.cond, reinterpret_cast<const int*>(dev_c + cb.lane_rows), d_books,
+                                   model_->positions.as<std::uint16_t>(), n, ch, s);
+            }
+            else
+            {
+                auto* pemb = ws.get<std::uint16_t>("pemb", static_cast<std::size_t>(n) * 1024);
+                dev::embed_sum(model_->embeddings.as<std::uint16_t>(),
+                               reinterpret_cast<const std::uint16_t*>(dev_c + cb.tokens),
+                               reinterpret_cast<const int*>(dev_c + cb.offsets),
+                               reinterpret_cast<const int*>(dev_c + cb.counts), n, pemb, s);
+                auto* pq = ws.get<std::int8_t>("pq", static_cast<std::size_t>(n) * 1024);
+                auto* ps = ws.get<float>("ps", static_cast<std::size_t>(n) * 4);
+                auto* pproj = ws.get<std::uint16_t>("pproj", static_cast<std::size_t>(n) * 512);
+                run_linear_bf16(61, pemb, n, pproj, nullptr, false, pq, ps);
+                dev::add_positions(pproj, st.identity, d_books, model_->positions.as<std::uint16_t>(),
+                                   n, ch, s);
+            }
+            auto* fq = ws.get<std::int8_t>("fq", static_cast<std::size_t>(n) * 512);
+            auto* fs = ws.get<float>("fs", static_cast<std::size_t>(n) * 2);
+            run_stack(ws, false, n, ch, d_meta, 12, st.cck, st.ccv, st.cstride, nullptr, fq, fs);
+            auto* logits = ws.get<std::uint16_t>("logits", static_cast<std::size_t>(n) * 1024);
+            run_linear(62, fq, fs, n, logits, nullptr, false);
             KernelTimer::Scope timing("softmax_tree", s, 0.0);
             dev::softmax_tree(logits, n, nullptr, nullptr, tree, error_word(), s);
         }

@@ -14,6 +14,7 @@
 //   kernel 2, one CTA per (row, head): the sequential merge over blocks, which
 //   is cheap (16 steps at 1024 keys) and keeps the reference's order.
 #include "kernels/numeric.cuh"
+#include "kernels/row_ops.cuh"
 #include "kernels/launch_count.hpp"
 #include "kernels/pdl.cuh"
 #include "kernels/transformer_ops.cuh"
@@ -22,20 +23,9 @@ namespace tsacb::dev
 {
 namespace
 {
-constexpr int HEADS = 4, HW = 128, WIDTH = 512, BLOCK = 64, PSTRIDE = HW + 2;
-constexpr float SCALE = 0.0883883461356163f;
+constexpr int HEADS = ATT_HEADS, HW = ATT_HW, WIDTH = ATT_WIDTH, BLOCK = ATT_BLOCK, PSTRIDE = HW + 2;
 
-struct ArgMax
-{
-    float value;
-    int index;
-};
-
-__device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b)
-{
-    return (a.value < b.value || (a.value == b.value && b.index < a.index)) ? b : a;
-}
-
+// One CTA per (row, head, 64-key block) (row_ops.cuh: attention_block_core).
 // SINGLE: the whole history fits one 64-key block (codebook stack, short
 // temporal histories); the kernel then applies the one-block merge itself and
 // writes the bf16 output, with exactly the combine kernel's operations.
@@ -48,12 +38,7 @@ __global__ void __launch_bounds__(128)
                            float* __restrict__ partials, std::uint16_t* __restrict__ output)
 {
     pdl_prologue();
-    __shared__ unsigned ks[BLOCK][65];
-    __shared__ unsigned vs[BLOCK][65];
-    __shared__ float q[HW];
-    __shared__ float scores[BLOCK];
-    __shared__ ArgMax warp_best[2];
-    __shared__ float block_sum;
+    __shared__ AttentionShared sh;
     const int block = blockIdx.y;
     const int task = blockIdx.x; // row * HEADS + head
     const int row = task / HEADS, head = task % HEADS;
@@ -63,93 +48,19 @@ __global__ void __launch_bounds__(128)
         return;
     const int count = m.time - start < BLOCK ? m.time - start : BLOCK;
     const int t = threadIdx.x;
-    q[t] = from_bf16(query[static_cast<size_t>(row) * WIDTH + head * HW + t]);
-    // Stage K and V rows [start, start+count) of this head: 64 words per row.
-    for (int i = t; i < count * 64; i += 128)
-    {
-        const int r = i >> 6, w = i & 63;
-        const size_t slot = static_cast<size_t>(m.base + start + r) * WIDTH + head * HW;
-        ks[r][w] = reinterpret_cast<const unsigned*>(cache_k + slot)[w];
-        vs[r][w] = reinterpret_cast<const unsigned*>(cache_v + slot)[w];
-    }
-    __syncthreads();
-    ArgMax best{-INFINITY, BLOCK};
-    if (t < count)
-    {
-        float dot = 0.0f;
-#pragma unroll 8
-        for (int w = 0; w < 64; ++w)
-        {
-            const unsigned pair = ks[t][w];
-            dot = __fmaf_rn(q[2 * w], from_bf16(pair & 0xffffu), dot);
-            dot = __fmaf_rn(q[2 * w + 1], from_bf16(pair >> 16), dot);
-        }
-        const float s = __fmul_rn(dot, SCALE);
-        scores[t] = s;
-        best = ArgMax{s, t};
-    }
-    if (t < 64)
-    {
-#pragma unroll
-        for (int offset = 16; offset > 0; offset >>= 1)
-        {
-            ArgMax other{__shfl_xor_sync(0xffffffffu, best.value, offset),
-                         __shfl_xor_sync(0xffffffffu, best.index, offset)};
-            best = better(best, other);
-        }
-        if ((t & 31) == 0)
-            warp_best[t >> 5] = best;
-    }
-    __syncthreads();
-    const float maximum = better(warp_best[0], warp_best[1]).value;
-    if (t < count)
-        scores[t] = original_exp(__fsub_rn(scores[t], maximum));
-    __syncthreads();
-    if (t < 32)
-    {
-        float s;
-        if (count <= 8)
-            s = t == 0 ? pair_sum_serial(scores, count, 8) : 0.0f;
-        else
-            s = warp_pair_sum64(2 * t < count ? scores[2 * t] : 0.0f,
-                                2 * t + 1 < count ? scores[2 * t + 1] : 0.0f);
-        if (t == 0)
-            block_sum = s;
-    }
-    // Value sums: thread t owns coordinate t, serial over the block's keys.
-    float sum = 0.0f;
-    const int w = t >> 1;
-    const bool high = t & 1;
-#pragma unroll 4
-    for (int r = 0; r < count; ++r)
-    {
-        const unsigned pair = vs[r][w];
-        sum = __fmaf_rn(from_bf16(high ? (pair >> 16) : (pair & 0xffffu)), scores[r], sum);
-    }
-    if (m.round)
-        sum = from_bf16(to_bf16(sum));
-    __syncthreads();
+    const AttentionBlock b = attention_block_core(query + static_cast<size_t>(row) * WIDTH + head * HW, m, head,
+                                                  cache_k, cache_v, start, count, sh, 0, t);
     if constexpr (SINGLE)
     {
-        // The combine kernel's first (and only) merge step, from running = -inf.
-        const float running = -INFINITY;
-        const float difference = __fsub_rn(maximum, running);
-        const float factor = original_exp(-fabsf(difference));
-        const float old_scale = running > maximum ? 1.0f : factor;
-        const float new_scale = running > maximum ? factor : 1.0f;
-        const float total = __fmaf_rn(block_sum, new_scale, __fmul_rn(0.0f, old_scale));
-        const float numerator = __fmaf_rn(sum, new_scale, __fmul_rn(0.0f, old_scale));
-        const float reciprocal = __fdiv_rn(1.0f, total);
-        output[static_cast<size_t>(row) * WIDTH + head * HW + t] =
-            to_bf16(__fmul_rn(numerator, reciprocal));
+        output[static_cast<size_t>(row) * WIDTH + head * HW + t] = attention_single_output(b);
         return;
     }
     float* out = partials + (static_cast<size_t>(task) * max_blocks + block) * PSTRIDE;
-    out[2 + t] = sum;
+    out[2 + t] = b.sum;
     if (t == 0)
     {
-        out[0] = maximum;
-        out[1] = block_sum;
+        out[0] = b.maximum;
+        out[1] = b.block_sum;
     }
 }
 

@@ -18,6 +18,7 @@
 #include "kernels/qlinear.cuh"
 #include "kernels/launch_count.hpp"
 #include "kernels/numeric.cuh"
+#include "kernels/row_ops.cuh"
 #include "kernels/pdl.cuh"
 
 #include <atomic>
@@ -26,46 +27,6 @@ namespace tsacb::dev
 {
 namespace
 {
-// BF8L quantization of one 256-value block by one warp: lane l holds values
-// 8l..8l+7 of the block (a 16-byte load).  Returns the lane's 8 int8 values
-// packed in two words and the block scale; nonfinite inputs clear `finite`.
-struct Bf8lLane
-{
-    unsigned packed[2];
-    float scale;
-};
-
-__device__ __forceinline__ Bf8lLane bf8l_block(uint4 raw, bool& finite)
-{
-    const std::uint16_t* h = reinterpret_cast<const std::uint16_t*>(&raw);
-    float v[8];
-    float m = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-    {
-        v[i] = from_bf16(h[i]);
-        finite = finite && isfinite(v[i]);
-        m = fmaxf(m, fabsf(flush(v[i])));
-    }
-#pragma unroll
-    for (int offset = 16; offset > 0; offset >>= 1)
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, offset));
-    float d = ftz_div(m, 127.0f);
-    d = d < 1e-35f ? 1e-35f : d;
-    Bf8lLane out;
-    out.scale = from_bf16(to_bf16(d));
-    const float reciprocal = ftz_div(1.0f, out.scale);
-    out.packed[0] = out.packed[1] = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-    {
-        float r = rintf(ftz_mul(v[i], reciprocal));
-        r = r < -128.0f ? -128.0f : (r > 127.0f ? 127.0f : r);
-        out.packed[i / 4] |= (static_cast<unsigned>(static_cast<int>(r)) & 0xffu) << (8 * (i % 4));
-    }
-    return out;
-}
-
 // One warp per (row, 256-block).
 __global__ void quantize_bf8l_kernel(const std::uint16_t* __restrict__ x, int k, int rows,
                                      std::int8_t* __restrict__ q, float* __restrict__ scales,

@@ -11,6 +11,7 @@
 //   probability_gelu_bf16                 src/common/probability.cpp:45-63
 //   encode_categorical / conditional_q15  src/format/categorical.cpp:76-117
 #include "kernels/numeric.cuh"
+#include "kernels/row_ops.cuh"
 #include "kernels/launch_count.hpp"
 #include "kernels/pdl.cuh"
 #include "kernels/transformer_ops.cuh"
@@ -54,37 +55,7 @@ __global__ void embed_sum_kernel(const std::uint16_t* __restrict__ table,
 }
 
 // ------------------------------------------------------------ layer norm --
-// One warp per 512-wide row; lane l owns values [16l, 16l+16).  The 16-value
-// lane partials are subtrees of the 64-wide pair tree, lanes 4i..4i+3 form
-// 64-block i, and the eight block sums go through the binary carry.
-__device__ __forceinline__ float lane_pair16(const float* v)
-{
-    float s[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-        s[i] = ftz_add(v[2 * i], v[2 * i + 1]);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        s[i] = ftz_add(s[2 * i], s[2 * i + 1]);
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-        s[i] = ftz_add(s[2 * i], s[2 * i + 1]);
-    return ftz_add(s[0], s[1]);
-}
-
-__device__ __forceinline__ float warp_sum512(const float* v)
-{
-    float s = lane_pair16(v);
-    s = ftz_add(s, __shfl_xor_sync(0xffffffffu, s, 1)); // 32-value subtrees
-    s = ftz_add(s, __shfl_xor_sync(0xffffffffu, s, 2)); // 64-value block sums (lanes 4b..4b+3)
-    // Eight block sums in block order: balanced tree over blocks, then the
-    // carry's final fold (numeric.cuh: carry_fold_power_of_two).
-    s = ftz_add(s, __shfl_xor_sync(0xffffffffu, s, 4));
-    s = ftz_add(s, __shfl_xor_sync(0xffffffffu, s, 8));
-    s = ftz_add(s, __shfl_xor_sync(0xffffffffu, s, 16));
-    return carry_fold_power_of_two(s);
-}
-
+// One warp per row (row_ops.cuh: layer_norm_row).
 __global__ void layer_norm_kernel(const std::uint16_t* __restrict__ x,
                                   const std::uint16_t* __restrict__ gain,
                                   const std::uint16_t* __restrict__ bias, int rows,
@@ -96,70 +67,12 @@ __global__ void layer_norm_kernel(const std::uint16_t* __restrict__ x,
     const int lane = threadIdx.x & 31;
     if (row >= rows)
         return;
-    const std::uint16_t* src = x + static_cast<size_t>(row) * 512 + lane * 16;
-    const uint4 r0 = *reinterpret_cast<const uint4*>(src);
-    const uint4 r1 = *reinterpret_cast<const uint4*>(src + 8);
-    std::uint16_t h[16];
-    *reinterpret_cast<uint4*>(h) = r0;
-    *reinterpret_cast<uint4*>(h + 8) = r1;
-    float v[16], sq[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-    {
-        v[i] = from_bf16(h[i]);
-        sq[i] = __fmul_rn(v[i], v[i]);
-    }
-    const float reciprocal = 1.0f / 512.0f;
-    const float mean = __fmul_rn(warp_sum512(v), reciprocal);
-    float variance = __fmaf_rn(warp_sum512(sq), reciprocal, 0.0f);
-    variance = __fmaf_rn(mean, -mean, variance);
-    variance = __fadd_rn(variance, 1e-5f);
-    const float inverse = __fdiv_rn(1.0f, __fsqrt_rn(variance));
-    const float offset = __fmul_rn(-mean, inverse);
-    std::uint16_t out[16];
-    float m = 0.0f;
-    bool finite = true;
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-    {
-        const int c = lane * 16 + i;
-        const float normalized = __fmaf_rn(v[i], inverse, offset);
-        out[i] = to_bf16(__fmaf_rn(normalized, from_bf16(gain[c]), from_bf16(bias[c])));
-        const float o = from_bf16(out[i]);
-        finite = finite && isfinite(o);
-        m = fmaxf(m, fabsf(flush(o)));
-    }
-    if (y)
-    {
-        std::uint16_t* dst = y + static_cast<size_t>(row) * 512 + lane * 16;
-        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(out);
-        *reinterpret_cast<uint4*>(dst + 8) = *reinterpret_cast<const uint4*>(out + 8);
-    }
-    if (yq)
-    {
-        // BF8L of the bf16 output: 256-blocks = lanes 0-15 and 16-31.
-#pragma unroll
-        for (int offset_ = 8; offset_ > 0; offset_ >>= 1)
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, offset_));
-        if (!__all_sync(0xffffffffu, finite) && lane == 0 && error_word)
-            atomicOr(error_word, error_nonfinite);
-        float d = ftz_div(m, 127.0f);
-        d = d < 1e-35f ? 1e-35f : d;
-        const float scale = from_bf16(to_bf16(d));
-        const float recip = ftz_div(1.0f, scale);
-        unsigned packed[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-        {
-            float r = rintf(ftz_mul(from_bf16(out[i]), recip));
-            r = r < -128.0f ? -128.0f : (r > 127.0f ? 127.0f : r);
-            packed[i / 4] |= (static_cast<unsigned>(static_cast<int>(r)) & 0xffu) << (8 * (i % 4));
-        }
-        *reinterpret_cast<uint4*>(yq + static_cast<size_t>(row) * 512 + lane * 16) =
-            make_uint4(packed[0], packed[1], packed[2], packed[3]);
-        if ((lane & 15) == 0)
-            yscale[row * 2 + lane / 16] = scale;
-    }
+    const bool finite = layer_norm_row(x + static_cast<size_t>(row) * 512, gain, bias,
+                                       y ? y + static_cast<size_t>(row) * 512 : nullptr,
+                                       yq ? yq + static_cast<size_t>(row) * 512 : nullptr,
+                                       yq ? yscale + row * 2 : nullptr);
+    if (!finite && lane == 0 && error_word && yq)
+        atomicOr(error_word, error_nonfinite);
 }
 
 // ------------------------------------------------------- rotary + scatter --
@@ -220,144 +133,20 @@ __global__ void add_positions_kernel(const std::uint16_t* __restrict__ src,
 }
 
 // ------------------------------------------------------ softmax + masses --
-// 256 threads per 1024-wide row; thread t owns entries [4t, 4t+4).
-struct ArgMax
-{
-    float value;
-    int index;
-};
-
-// Reference max: sequential (m < x ? x : m) keeps the earliest maximal entry.
-__device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b)
-{
-    return (a.value < b.value || (a.value == b.value && b.index < a.index)) ? b : a;
-}
-
+// 256 threads per 1024-wide row (row_ops.cuh: softmax_tree_row).
 __global__ void softmax_tree_kernel(const std::uint16_t* __restrict__ logits,
                                     std::uint16_t* __restrict__ probs_bf16,
                                     float* __restrict__ probs_f32, float* __restrict__ tree,
                                     unsigned* error_word)
 {
     pdl_prologue();
-    __shared__ ArgMax warp_best[8];
-    __shared__ float block_sums[16];
-    __shared__ float level_sums[8]; // 128-wide sums (one per warp)
-    __shared__ float total_shared;
-    const int row = blockIdx.x;
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const uint2 raw = reinterpret_cast<const uint2*>(logits + static_cast<size_t>(row) * 1024)[t];
-    float x[4] = {from_bf16(raw.x & 0xffffu), from_bf16(raw.x >> 16), from_bf16(raw.y & 0xffffu),
-                  from_bf16(raw.y >> 16)};
-    bool finite = isfinite(x[0]) && isfinite(x[1]) && isfinite(x[2]) && isfinite(x[3]);
-    if (!__syncthreads_and(finite))
-    {
-        if (t == 0 && error_word)
-            atomicOr(error_word, error_nonfinite);
-    }
-    ArgMax best{x[0], 4 * t};
-#pragma unroll
-    for (int i = 1; i < 4; ++i)
-        best = better(best, ArgMax{x[i], 4 * t + i});
-#pragma unroll
-    for (int offset = 16; offset > 0; offset >>= 1)
-    {
-        ArgMax other{__shfl_xor_sync(0xffffffffu, best.value, offset),
-                     __shfl_xor_sync(0xffffffffu, best.index, offset)};
-        best = better(best, other);
-    }
-    if (lane == 0)
-        warp_best[warp] = best;
-    __syncthreads();
-    best = warp_best[0];
-#pragma unroll
-    for (int w = 1; w < 8; ++w)
-        best = better(best, warp_best[w]);
-    const float maximum = best.value;
-    float e[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        e[i] = original_exp(__fsub_rn(x[i], maximum));
-    // 64-blocks: lanes 16h..16h+15 of a warp hold block 2*warp+h; pair tree.
-    float s = ftz_add(ftz_add(e[0], e[1]), ftz_add(e[2], e[3]));
-#pragma unroll
-    for (int offset = 1; offset < 16; offset <<= 1)
-        s = ftz_add(s, __shfl_xor_sync(0xffffffffu, s, offset));
-    if ((lane & 15) == 0)
-        block_sums[warp * 2 + lane / 16] = s;
-    __syncthreads();
-    if (t < 8)
-    {
-        // Sixteen 64-blocks: balanced tree over blocks (lanes 0-7 of warp 0),
-        // then the carry's final fold (numeric.cuh: carry_fold_power_of_two).
-        float b = ftz_add(block_sums[2 * t], block_sums[2 * t + 1]);
-        b = ftz_add(b, __shfl_xor_sync(0x000000ffu, b, 1));
-        b = ftz_add(b, __shfl_xor_sync(0x000000ffu, b, 2));
-        b = ftz_add(b, __shfl_xor_sync(0x000000ffu, b, 4));
-        if (t == 0)
-            total_shared = carry_fold_power_of_two(b);
-    }
-    __syncthreads();
-    const float reciprocal = __fdiv_rn(1.0f, total_shared);
-    std::uint16_t p[4];
-    float pf[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-    {
-        p[i] = to_bf16(__fmul_rn(e[i], reciprocal));
-        pf[i] = from_bf16(p[i]);
-    }
-    if (probs_bf16)
-        reinterpret_cast<uint2*>(probs_bf16 + static_cast<size_t>(row) * 1024)[t] =
-            make_uint2(pack2(p[0], p[1]), pack2(p[2], p[3]));
-    if (probs_f32)
-        reinterpret_cast<float4*>(probs_f32 + static_cast<size_t>(row) * 1024)[t] =
-            make_float4(pf[0], pf[1], pf[2], pf[3]);
-    if (!tree)
-        return;
-    // Left-child masses of the 1023 internal nodes of the bisection heap:
-    // internal node i covers an aligned range; its left child is heap node
-    // 2i+1.  An aligned range of size 2^L starting at b is heap node
-    // (2^(10-L) - 1) + b / 2^L; when that node is a left child (odd heap
-    // index) its mass goes to slot (heap - 1) / 2.
-    float* out = tree + static_cast<size_t>(row) * 1023;
-    auto emit = [&](int level, int begin, float mass)
-    {
-        const int heap = ((1 << (10 - level)) - 1) + (begin >> level);
-        if (heap & 1)
-            out[(heap - 1) >> 1] = mass;
-    };
-    const float l0[4] = {flush(pf[0]), flush(pf[1]), flush(pf[2]), flush(pf[3])};
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        emit(0, 4 * t + i, l0[i]);
-    const float a1 = ftz_add(pf[0], pf[1]), b1 = ftz_add(pf[2], pf[3]);
-    emit(1, 4 * t, a1);
-    emit(1, 4 * t + 2, b1);
-    float m = ftz_add(a1, b1); // level 2, range [4t, 4t+4)
-    emit(2, 4 * t, m);
-#pragma unroll
-    for (int level = 3; level <= 7; ++level)
-    {
-        const int span = 1 << (level - 2); // lanes per range at this level
-        m = ftz_add(m, __shfl_xor_sync(0xffffffffu, m, span >> 1));
-        if ((lane & (span - 1)) == 0)
-            emit(level, 4 * t, m);
-    }
-    if (lane == 0)
-        level_sums[warp] = m; // 128-wide range [128w, 128w+128)
-    __syncthreads();
-    if (t == 0)
-    {
-        const float l8[4] = {ftz_add(level_sums[0], level_sums[1]),
-                             ftz_add(level_sums[2], level_sums[3]),
-                             ftz_add(level_sums[4], level_sums[5]),
-                             ftz_add(level_sums[6], level_sums[7])};
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            emit(8, 256 * i, l8[i]);
-        emit(9, 0, ftz_add(l8[0], l8[1]));
-        emit(9, 512, ftz_add(l8[2], l8[3]));
-    }
+    __shared__ SoftmaxShared sh;
+    const size_t row = blockIdx.x;
+    const bool finite = softmax_tree_row(logits + row * 1024, probs_bf16 ? probs_bf16 + row * 1024 : nullptr,
+                                         probs_f32 ? probs_f32 + row * 1024 : nullptr,
+                                         tree ? tree + row * 1023 : nullptr, sh);
+    if (!finite && threadIdx.x == 0 && error_word)
+        atomicOr(error_word, error_nonfinite);
 }
 
 __device__ __forceinline__ std::uint16_t conditional_q15(float left, float mass)
