@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(256)
 // byte-to-k assignment, so every byte pair meets exactly once.  Quarter dots
 // meet in shared memory (integer atomics, exact), and 256 threads then fold
 // the blocks in order, two outputs each: sum = fma(dot, w_scale * x_scale, sum).
-constexpr int SMALL_MAX_M = 256;
+constexpr int SMALL_MAX_M = 1 << 20;
 constexpr int MMA_MT = 4; // 8-column m-tiles per CTA
 
 __device__ __forceinline__ void mma_s8(int (&d)[4], unsigned a0, unsigned a1, unsigned a2,

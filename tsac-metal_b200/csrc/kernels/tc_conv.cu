@@ -1,6 +1,6 @@
 // tcgen05 implicit-GEMM convolution (DAC synthesis), 3xTF32.
 //
-// One persistent CTA per SM, six warps:
+// One persistent CTA per SM, ten warps:
 //   warp 0      TMA producer: per k-block (tap, 32 input channels) it loads the
 //               input head/tail tiles [128 rows][32 ch] and the weight head/tail
 //               tiles [BN out][32 ch], 128-byte swizzled, into a STAGES-deep ring.
@@ -8,7 +8,8 @@
 //               M=128, N=BN, K=8) per k-block into the tile's four TMEM
 //               accumulators; tcgen05.commit frees the smem stage and, per
 //               tile, hands the accumulators to the epilogue.
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (one TMEM lane = one
+//   warps 2..9  epilogue, two warps per TMEM lane quarter splitting the
+//               columns: tcgen05.ld of the accumulators (one TMEM lane = one
 //               output row per thread), + bias (+ residual), optional Snake of
 //               the next layer, head/tail split, zero rows outside sequences,
 //               fp32 stores; then the accumulators are released for the
@@ -34,6 +35,7 @@ namespace tsacb::dev
 namespace
 {
 constexpr int BM = 128;        // rows per tile (TMEM lanes)
+constexpr int TC_THREADS = 320; // producer warp, MMA warp, 8 epilogue warps
 constexpr int BK = 32;         // fp32 per k-block row: one 128-byte swizzle row
 constexpr int A_BYTES = BM * BK * 4;
 constexpr unsigned long long WAIT_NS = 1000000000ull;
@@ -237,7 +239,7 @@ __device__ __forceinline__ TileCoord tile_coord(long long tile, long long m_tile
 }
 
 template <int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(TC_THREADS, 1)
     tc_conv_kernel(const __grid_constant__ CUtensorMap map_xhi,
                    const __grid_constant__ CUtensorMap map_xlo,
                    const __grid_constant__ CUtensorMap map_whi,
@@ -247,6 +249,7 @@ __global__ void __launch_bounds__(192, 1)
     constexpr int STAGES = Config<BN>::stages;
     constexpr int TMEM_COLS = Config<BN>::tmem_cols;
     static_assert(ACCS * BN <= TMEM_COLS, "accumulators exceed the TMEM allocation");
+    static_assert((BN / 2) % 16 == 0, "each epilogue warp takes whole 16-column chunks");
     constexpr int STAGE = stage_bytes<BN>();
     constexpr int B_BYTES = BN * BK * 4;
     extern __shared__ unsigned char smem_raw[];
@@ -277,7 +280,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int a = 0; a < 2; ++a)
         {
             bar_init(acc_full0 + 8 * a, 1);
-            bar_init(acc_empty0 + 8 * a, 128);
+            bar_init(acc_empty0 + 8 * a, TC_THREADS - 64);
         }
         bar_init(drain, 1);
         *abort_flag = 0;
@@ -425,8 +428,11 @@ __global__ void __launch_bounds__(192, 1)
     else
     {
         // ---------------------------------------------------------- epilogue --
+        // Two warps per TMEM lane quarter (a warp reaches lanes 32 (warp % 4)
+        // .. +31), each taking half of the tile's columns.
         const int quarter = warp & 3;
         const int row_in_tile = quarter * 32 + lane;
+        const int col_begin = ((warp - 2) / 4) * (BN / 2), col_end = col_begin + BN / 2;
         int local = 0;
         bool finite = true;
         for (long long tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local)
@@ -446,7 +452,7 @@ __global__ void __launch_bounds__(192, 1)
             const bool valid = in_range && e.valid[o / g.out_scale] != 0;
             const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 16)
+            for (int c0 = col_begin; c0 < col_end; c0 += 16)
             {
                 float v[16], m1[16], m2[16], cr[16];
                 tmem_load16(taddr + c0, v);
@@ -617,7 +623,7 @@ cudaError_t launch(const TcConvOperands& op, const TcConvGeometry& g, const TcCo
                        });
     const long long tiles = ((g.rows + BM - 1) / BM) * (g.cout / BN) * g.phases;
     const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-    tc_conv_kernel<BN><<<grid, 192, smem, stream>>>(xhi, xlo, whi, wlo, g, e);
+    tc_conv_kernel<BN><<<grid, TC_THREADS, smem, stream>>>(xhi, xlo, whi, wlo, g, e);
     note_launch();
     return cudaGetLastError();
 }
