@@ -111,9 +111,9 @@ void check_word(cudaStream_t s, unsigned* word, const char* message)
 
 // padded_audio on the device for every recording of one variant, laid end to
 // end: recording r, group g starts at PCM row base[r] + g * padded_samples.
-DeviceBuffer padded_device(Context& ctx, const std::vector<PcmInput>& pcm,
-                           const std::vector<Header>& headers, std::vector<long long>& base,
-                           unsigned* error_word)
+float* padded_device(Context& ctx, const std::vector<PcmInput>& pcm,
+                     const std::vector<Header>& headers, std::vector<long long>& base,
+                     unsigned* error_word)
 {
     auto s = ctx.stream();
     long long rows = 0;
@@ -124,45 +124,51 @@ DeviceBuffer padded_device(Context& ctx, const std::vector<PcmInput>& pcm,
         rows += static_cast<long long>(h.groups) * static_cast<long long>(h.samples_per_channel());
     }
     const unsigned mc = headers.empty() ? 1 : headers[0].model_channels;
-    DeviceBuffer out(static_cast<std::size_t>(rows) * mc * 4 + 4);
+    float* out = ctx.workspace().get<float>("pcm_padded", static_cast<std::size_t>(rows) * mc + 1);
+    // Host views are copied into one staging area (interleaved, contiguous),
+    // all copies queued back to back, then regrouped on the device.
+    std::size_t staged_floats = 0;
+    for (const auto& p : pcm)
+        if (!p.device)
+            staged_floats += p.samples * p.channels;
+    float* staging = staged_floats ? ctx.workspace().get<float>("pcm_staging", staged_floats) : nullptr;
+    std::vector<std::vector<float>> packed(pcm.size());
+    std::size_t at = 0;
     for (std::size_t r = 0; r < pcm.size(); ++r)
     {
         const auto& p = pcm[r];
         const auto& h = headers[r];
         const float* src = p.data;
         long long cs = p.channel_stride, ss = p.sample_stride;
-        DeviceBuffer staged;
         if (!p.device && p.samples)
         {
-            // Host view -> contiguous interleaved device copy, then regroup there.
-            std::vector<float> packed;
             const float* host = p.data;
             if (!(cs == 1 && ss == static_cast<long long>(p.channels)))
             {
-                packed.resize(p.samples * p.channels);
+                packed[r].resize(p.samples * p.channels);
                 for (std::size_t f = 0; f < p.samples; ++f)
                     for (std::size_t c = 0; c < p.channels; ++c)
-                        packed[f * p.channels + c] =
+                        packed[r][f * p.channels + c] =
                             p.data[static_cast<std::ptrdiff_t>(c) * p.channel_stride +
                                    static_cast<std::ptrdiff_t>(f) * p.sample_stride];
-                host = packed.data();
+                host = packed[r].data();
             }
-            staged.resize(p.samples * p.channels * 4);
-            cuda_ok(cudaMemcpyAsync(staged.as<void>(), host, p.samples * p.channels * 4,
+            cuda_ok(cudaMemcpyAsync(staging + at, host, p.samples * p.channels * 4,
                                     cudaMemcpyHostToDevice, s),
                     "H2D");
-            src = staged.as<float>();
+            src = staging + at;
+            at += p.samples * p.channels;
             cs = 1;
             ss = static_cast<long long>(p.channels);
         }
         dev::pcm_regroup(src, static_cast<long long>(p.samples), cs, ss, h.groups, mc,
                          static_cast<long long>(h.samples_per_channel()),
-                         out.as<float>() + base[r] * mc, error_word, s);
-        if (staged.bytes())
-        {
-            // The staging copy must finish before `staged` is released.
-            cuda_ok(cudaStreamSynchronize(s), "PCM upload");
-        }
+                         out + base[r] * mc, error_word, s);
+    }
+    if (staged_floats)
+    {
+        // Host copies of strided views must outlive their asynchronous upload.
+        cuda_ok(cudaStreamSynchronize(s), "PCM upload");
     }
     return out;
 }
@@ -212,15 +218,17 @@ void analyze_recordings(Context& ctx, const std::vector<PcmInput>& pcm,
             latent_frames += w.chunk.right - w.chunk.left;
             central += w.chunk.count;
         }
-        DeviceBuffer d_latent(latent_frames * 1024 * 4), d_central(central * 1024 * 4);
-        dac.analyze(padded.as<float>(), offsets, frames, d_latent.as<float>());
+        auto& ws = ctx.workspace();
+        float* d_latent = ws.get<float>("enc_latent", latent_frames * 1024);
+        float* d_central = ws.get<float>("enc_central", central * 1024);
+        dac.analyze(padded, offsets, frames, d_latent);
         // Keep each window's central latents (src/common/audio_pipeline.hpp:49-56).
         std::size_t lat = 0, cen = 0;
         for (std::size_t i = 0; i < wn; ++i)
         {
             const auto& c = windows[w0 + i].chunk;
-            cuda_ok(cudaMemcpyAsync(d_central.as<float>() + cen * 1024,
-                                    d_latent.as<float>() + (lat + c.begin - c.left) * 1024,
+            cuda_ok(cudaMemcpyAsync(d_central + cen * 1024,
+                                    d_latent + (lat + c.begin - c.left) * 1024,
                                     c.count * 1024 * 4, cudaMemcpyDeviceToDevice, s),
                     "D2D");
             lat += c.right - c.left;
@@ -228,11 +236,11 @@ void analyze_recordings(Context& ctx, const std::vector<PcmInput>& pcm,
         }
         profile.mark("dac analysis");
         const int books = headers[0].codebooks;
-        DeviceBuffer d_tok(central * static_cast<std::size_t>(books) * 2);
-        rvq.encode(d_central.as<float>(), static_cast<int>(central), books,
-                   d_tok.as<std::uint16_t>(), books);
+        auto* d_tok = ws.get<std::uint16_t>("enc_tokens", central * static_cast<std::size_t>(books));
+        rvq.encode(d_central, static_cast<int>(central), books,
+                   d_tok, books);
         std::vector<std::uint16_t> host_tok(central * static_cast<std::size_t>(books));
-        cuda_ok(cudaMemcpyAsync(host_tok.data(), d_tok.as<void>(), host_tok.size() * 2,
+        cuda_ok(cudaMemcpyAsync(host_tok.data(), d_tok, host_tok.size() * 2,
                                 cudaMemcpyDeviceToHost, s),
                 "D2H");
         check_word(s, dac.error_word(), "nonfinite DSP value");
@@ -441,11 +449,18 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
             lanes += h.lanes();
         }
         (void)lanes;
+        // Host-side split of the step loop (TSAC_CUDA_PROFILE): time in
+        // decode_predict (input staging, graph launch, waiting for the masses),
+        // in the range decoders, and in commit.
+        double t_predict = 0, t_range = 0, t_commit = 0;
+        using clock = std::chrono::steady_clock;
         for (std::size_t step = 0; step < steps; ++step)
             for (std::size_t book = 0; book < books; ++book)
             {
                 const float* masses = nullptr;
+                const auto t0 = clock::now();
                 const auto rows = engine.decode_predict(step, book, &masses);
+                const auto t1 = clock::now();
                 std::vector<std::uint16_t> decoded(rows.size());
                 // Rows are in stream order per recording (lane, then group); each
                 // recording's decoder consumes its rows in that order (~0.3 us per
@@ -463,8 +478,16 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
                     const std::size_t frame = lane_b * base + std::min(lane_b, extra) + step;
                     tokens[ids[r]][(frame * h.groups + g) * h.codebooks + book] = decoded[j];
                 }
+                const auto t2 = clock::now();
                 engine.decode_commit(decoded);
+                const auto t3 = clock::now();
+                t_predict += std::chrono::duration<double, std::milli>(t1 - t0).count();
+                t_range += std::chrono::duration<double, std::milli>(t2 - t1).count();
+                t_commit += std::chrono::duration<double, std::milli>(t3 - t2).count();
             }
+        if (const char* e = std::getenv("TSAC_CUDA_PROFILE"); e && *e && *e != '0')
+            std::fprintf(stderr, "tsac_cuda decode steps %zu: predict %.1f ms, range %.1f ms, commit %.1f ms\n",
+                         steps * books, t_predict, t_range, t_commit);
         for (auto i : ids)
             verify_token_crc(headers[i], tokens[i]);
     }
@@ -535,9 +558,11 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
                     std::copy_n(tokens[w.recording].data() + (f * h.groups + w.group) * h.codebooks,
                                 h.codebooks, wt.data() + at * books);
             }
-            DeviceBuffer d_tok(wt.size() * 2), d_latent(total * 1024 * 4),
-                d_pcm(total * 512 * mc * 4);
-            cuda_ok(cudaMemcpyAsync(d_tok.as<void>(), wt.data(), wt.size() * 2,
+            auto& ws = ctx.workspace();
+            auto* d_tok = ws.get<std::uint16_t>("dec_tokens", wt.size());
+            float* d_latent = ws.get<float>("dec_latent", total * 1024);
+            float* d_pcm = ws.get<float>("dec_pcm", total * 512 * mc);
+            cuda_ok(cudaMemcpyAsync(d_tok, wt.data(), wt.size() * 2,
                                     cudaMemcpyHostToDevice, s),
                     "H2D");
             std::size_t off = 0;
@@ -551,13 +576,13 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
                     len += windows[w0 + j].chunk.right - windows[w0 + j].chunk.left;
                     ++j;
                 }
-                rvq.decode(d_tok.as<std::uint16_t>() + off * books, books, static_cast<int>(len), q,
-                           d_latent.as<float>() + off * 1024);
+                rvq.decode(d_tok + off * books, books, static_cast<int>(len), q,
+                           d_latent + off * 1024);
                 off += len;
                 i = j;
             }
             profile.mark("rvq decode");
-            dac.synthesize(d_latent.as<float>(), frames, d_pcm.as<float>());
+            dac.synthesize(d_latent, frames, d_pcm);
             // store_pcm (src/common/audio_analyzer.cpp:185-199): central samples
             // of each window into the interleaved output, channel g*mc + c.
             off = 0;
@@ -567,7 +592,7 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
                 const auto channels = headers[w.recording].channels();
                 cuda_ok(cudaMemcpy2DAsync(dst[w.recording] + w.chunk.begin * 512 * channels + w.group * mc,
                                           channels * 4,
-                                          d_pcm.as<float>() + (off + (w.chunk.begin - w.chunk.left) * 512) * mc,
+                                          d_pcm + (off + (w.chunk.begin - w.chunk.left) * 512) * mc,
                                           mc * 4, mc * 4, w.chunk.count * 512,
                                           cudaMemcpyDeviceToDevice, s),
                         "D2D");

@@ -42,6 +42,13 @@ public:
     {
         return package_;
     }
+    // Grow-only device buffers of the codec's staging (PCM, window tokens,
+    // latents, PCM windows), kept across calls so a call allocates nothing
+    // once warm.  Valid until the next get() of the same name.
+    Workspace& workspace()
+    {
+        return workspace_;
+    }
 
 private:
     Package package_;
@@ -53,5 +60,6 @@ private:
     std::unique_ptr<DacEngine> analysis_[2], synthesis_[2];
     bool exact_synthesis_ = false;
     std::unique_ptr<RvqEngine> rvq_[2];
+    Workspace workspace_;
 };
 } // namespace tsacb
