@@ -16,7 +16,7 @@
 // input channels inner), and parallelism comes from outputs.  A CTA owns a
 // 128-frame x 128-channel output tile (64 for 64-channel layers), 512 (256)
 // threads each accumulating 4 frames x 8 channels in registers; per (tap,
-// 32-channel chunk) it stages the input rows channel-major and the weight
+// 64-channel chunk) it stages the input rows channel-major and the weight
 // slice in shared memory, double-buffered through registers, so every staged
 // value is reused 4x or 8x from registers and a thread's operands are 16-byte loads.
 // Device weights are laid out [tap][in][out] so the weight slice loads are
@@ -100,7 +100,7 @@ template <int TO> constexpr size_t conv_smem_bytes()
 // (TO = 128 with 512 threads, 64 with 256); each thread holds 4 frames x 8
 // channels of serial chains in registers: channels tx*4..tx*4+3 and
 // TO/2 + tx*4..+3, so the 8 threads of a shared-memory wavefront read 128
-// contiguous weight bytes (no bank conflicts).  Per (tap, 32-channel chunk)
+// contiguous weight bytes (no bank conflicts).  Per (tap, 64-channel chunk)
 // "step", the chunk's inputs and weights are staged in shared memory; the
 // next step's global loads are issued into registers before the current
 // step's arithmetic and stored after it (two stages, one barrier per step).
