@@ -8,8 +8,11 @@
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
+#include <exception>
+#include <functional>
 #include <future>
 #include <thread>
+#include <utility>
 
 namespace tsacb
 {
@@ -62,6 +65,82 @@ template <class F> void parallel_for(std::size_t n, F&& f)
     for (auto& j : jobs)
         j.get();
 }
+
+// Persistent workers for the decode loop's per-step range decoding.  A step
+// is a few microseconds of host work between two GPU predictions, too short
+// for thread creation, so the workers live for the whole loop and wait for
+// the next step by spinning on a generation counter (yielding after a short
+// spin).  run(f) calls f(w) for every worker w, w = 0 on the caller, and
+// returns when all have finished; the first exception is rethrown.
+class StepPool
+{
+public:
+    explicit StepPool(std::size_t workers) : errors_(std::max<std::size_t>(workers, 1))
+    {
+        for (std::size_t w = 1; w < errors_.size(); ++w)
+            threads_.emplace_back([this, w] { work(w); });
+    }
+    ~StepPool()
+    {
+        stop_.store(true, std::memory_order_release);
+        generation_.fetch_add(1, std::memory_order_acq_rel);
+        for (auto& t : threads_)
+            t.join();
+    }
+    StepPool(const StepPool&) = delete;
+    StepPool& operator=(const StepPool&) = delete;
+
+    std::size_t size() const { return errors_.size(); }
+
+    template <class F> void run(F&& f)
+    {
+        job_ = std::function<void(std::size_t)>(std::forward<F>(f));
+        pending_.store(threads_.size(), std::memory_order_relaxed);
+        generation_.fetch_add(1, std::memory_order_acq_rel);
+        call(0);
+        for (unsigned spin = 0; pending_.load(std::memory_order_acquire) != 0; ++spin)
+            if (spin > 4096)
+                std::this_thread::yield();
+        for (auto& e : errors_)
+            if (e)
+                std::rethrow_exception(std::exchange(e, nullptr));
+    }
+
+private:
+    void call(std::size_t w)
+    {
+        try
+        {
+            job_(w);
+        }
+        catch (...)
+        {
+            errors_[w] = std::current_exception();
+        }
+    }
+    void work(std::size_t w)
+    {
+        std::uint64_t seen = 0;
+        for (;;)
+        {
+            std::uint64_t g;
+            for (unsigned spin = 0; (g = generation_.load(std::memory_order_acquire)) == seen; ++spin)
+                if (spin > 4096)
+                    std::this_thread::yield();
+            seen = g;
+            if (stop_.load(std::memory_order_acquire))
+                return;
+            call(w);
+            pending_.fetch_sub(1, std::memory_order_acq_rel);
+        }
+    }
+    std::vector<std::exception_ptr> errors_;
+    std::vector<std::thread> threads_;
+    std::function<void(std::size_t)> job_;
+    std::atomic<std::uint64_t> generation_{0};
+    std::atomic<std::size_t> pending_{0};
+    std::atomic<bool> stop_{false};
+};
 
 // Stage timing (TSAC_CUDA_PROFILE=1): synchronises the stream at each mark.
 class Profile
@@ -449,6 +528,10 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
             lanes += h.lanes();
         }
         (void)lanes;
+        // Recordings are independent streams: worker w range-decodes the rows
+        // of recordings r with r % workers == w, each in stream order.
+        const auto hw = static_cast<std::size_t>(std::thread::hardware_concurrency());
+        StepPool pool(std::min<std::size_t>({ids.size(), 8, hw > 1 ? hw - 1 : 1}));
         // Host-side split of the step loop (TSAC_CUDA_PROFILE): time in
         // decode_predict (input staging, graph launch, waiting for the masses),
         // in the range decoders, and in commit.
@@ -463,11 +546,22 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
                 const auto t1 = clock::now();
                 std::vector<std::uint16_t> decoded(rows.size());
                 // Rows are in stream order per recording (lane, then group); each
-                // recording's decoder consumes its rows in that order (~0.3 us per
-                // symbol, so the walk stays on this thread).
-                for (std::size_t j = 0; j < rows.size(); ++j)
-                    decoded[j] = decode_categorical_tree(
-                        decoders[static_cast<std::size_t>(rows[j].recording)], masses + j * 1023);
+                // recording's decoder consumes its rows in that order (~0.2 us
+                // per symbol).
+                const std::size_t workers = pool.size();
+                auto walk = [&](std::size_t w)
+                {
+                    for (std::size_t j = 0; j < rows.size(); ++j)
+                    {
+                        const auto r = static_cast<std::size_t>(rows[j].recording);
+                        if (r % workers == w)
+                            decoded[j] = decode_categorical_tree(decoders[r], masses + j * 1023);
+                    }
+                };
+                if (workers > 1)
+                    pool.run(walk);
+                else
+                    walk(0);
                 for (std::size_t j = 0; j < rows.size(); ++j)
                 {
                     const auto r = static_cast<std::size_t>(rows[j].recording);
