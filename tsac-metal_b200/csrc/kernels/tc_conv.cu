@@ -12,8 +12,8 @@
 //               columns: tcgen05.ld of the accumulators (one TMEM lane = one
 //               output row per thread), + bias (+ residual), optional Snake of
 //               the next layer, head/tail split, zero rows outside sequences,
-//               fp32 stores; then the accumulators are released for the
-//               next tile (the epilogue is short next to a tile's K loop).
+//               fp32 stores.  The accumulators are summed into registers and
+//               released first, so the rest overlaps the next tile's MMAs.
 // M = 128 output rows (time), N = BN output channels, K = taps x cin.
 //
 // Every wait is bounded (about one second of global time).  A wait that gives
@@ -189,19 +189,21 @@ __device__ __forceinline__ void tc_fence_after()
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-__device__ __forceinline__ void tmem_load16(uint32_t taddr, float (&v)[16])
+// 16 consecutive TMEM columns of this thread's lane; the values are valid
+// after tmem_wait_loads().
+__device__ __forceinline__ void tmem_load16(uint32_t taddr, uint32_t (&r)[16])
 {
-    uint32_t r[16];
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32"
                  " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
                    "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
                    "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
                  : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_loads()
+{
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-        v[j] = __uint_as_float(r[j]);
 }
 
 // Nearest TF32 value (ties away from zero) of a finite fp32; the truncated
@@ -429,10 +431,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     {
         // ---------------------------------------------------------- epilogue --
         // Two warps per TMEM lane quarter (a warp reaches lanes 32 (warp % 4)
-        // .. +31), each taking half of the tile's columns.
+        // .. +31), each taking half of the tile's columns.  The four
+        // accumulators are first combined into registers and the TMEM is
+        // released, so the next tile's MMAs run while this tile's bias,
+        // residual, Snake, split and stores complete.
+        constexpr int COLS = BN / 2, CHUNKS = COLS / 16;
         const int quarter = warp & 3;
         const int row_in_tile = quarter * 32 + lane;
-        const int col_begin = ((warp - 2) / 4) * (BN / 2), col_end = col_begin + BN / 2;
+        const int col_begin = ((warp - 2) / 4) * COLS;
         int local = 0;
         bool finite = true;
         for (long long tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local)
@@ -451,19 +457,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const long long o = i * g.out_stride + t.phase;
             const bool valid = in_range && e.valid[o / g.out_scale] != 0;
             const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-#pragma unroll 1
-            for (int c0 = col_begin; c0 < col_end; c0 += 16)
+            float sum[COLS];
+#pragma unroll
+            for (int c = 0; c < CHUNKS; ++c)
             {
-                float v[16], m1[16], m2[16], cr[16];
-                tmem_load16(taddr + c0, v);
-                tmem_load16(taddr + BN + c0, m1);
-                tmem_load16(taddr + 2 * BN + c0, m2);
-                tmem_load16(taddr + 3 * BN + c0, cr);
-                if (!in_range)
-                    continue;
+                const uint32_t at = taddr + static_cast<uint32_t>(col_begin + 16 * c);
+                uint32_t a0[16], a1[16], a2[16], a3[16];
+                tmem_load16(at, a0);
+                tmem_load16(at + BN, a1);
+                tmem_load16(at + 2 * BN, a2);
+                tmem_load16(at + 3 * BN, a3);
+                tmem_wait_loads();
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
-                    v[j] = __fadd_rn(__fadd_rn(__fadd_rn(v[j], m1[j]), m2[j]), cr[j]);
+                    sum[16 * c + j] = __fadd_rn(__fadd_rn(__fadd_rn(__uint_as_float(a0[j]), __uint_as_float(a1[j])),
+                                                          __uint_as_float(a2[j])),
+                                                __uint_as_float(a3[j]));
+            }
+            tc_fence_before();
+            bar_arrive(acc_empty0);
+            if (!in_range)
+                continue;
+#pragma unroll
+            for (int c = 0; c < CHUNKS; ++c)
+            {
+                const int c0 = col_begin + 16 * c;
+                const float* v = sum + 16 * c;
                 const int col = t.n * BN + c0;
                 const size_t at = static_cast<size_t>(o) * g.cout + col;
                 float raw[16], act[16];
@@ -512,8 +531,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                 }
             }
-            tc_fence_before();
-            bar_arrive(acc_empty0);
         }
         if (!finite && e.error_word)
             atomicOr(e.error_word, error_nonfinite);
