@@ -65,6 +65,8 @@ template <int BN> __host__ __device__ constexpr int smem_bytes()
 {
     return Config<BN>::stages * stage_bytes<BN>() + 1024 /* alignment */ + 256 /* barriers */;
 }
+static_assert(smem_bytes<128>() <= 227 * 1024 && smem_bytes<96>() <= 227 * 1024,
+              "stage ring exceeds the per-CTA shared memory limit");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p)
 {
