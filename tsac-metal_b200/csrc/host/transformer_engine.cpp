@@ -101,7 +101,7 @@ double linear_work(int rows, double n, double k)
 
 void TransformerEngine::run_linear(int projection, const std::int8_t* xq, const float* xs,
                                    int rows, std::uint16_t* y, const std::uint16_t* residual,
-                                   bool gelu)
+                                   bool gelu, int residual_stride)
 {
     const auto& l = model_->projections.at(static_cast<std::size_t>(projection));
     dev::QLinearArgs a;
@@ -116,6 +116,7 @@ void TransformerEngine::run_linear(int projection, const std::int8_t* xq, const 
     a.m = rows;
     a.n = l.output;
     a.k = l.input;
+    a.residual_stride = residual_stride;
     KernelTimer::Scope timing(rows <= 256 ? "qlinear_small" : "qlinear_gemm", stream_,
                               linear_work(rows, l.output, l.input));
     dev::qlinear_matmul(a, stream_);
@@ -188,11 +189,16 @@ void TransformerEngine::run_stack(Workspace& ws_, bool temporal, int rows, std::
                             error_word(), stream_);
         }
         run_qkv(projection_index(temporal, l, 0), xq, xs, rows, meta, query, ck, cv, qkv);
+        bool quantized = false; // one-block histories: attention emits the BF8L input itself
         {
             KernelTimer::Scope timing("attention", stream_, 0.0);
-            dev::attention(query, meta, ck, cv, rows, max_time, partials, att, stream_);
+            quantized = dev::attention(query, meta, ck, cv, rows, max_time, partials, att, stream_, xq, xs,
+                                       error_word());
         }
-        run_linear_bf16(projection_index(temporal, l, 1), att, rows, h, h, false, xq, xs);
+        if (quantized)
+            run_linear(projection_index(temporal, l, 1), xq, xs, rows, h, h, false);
+        else
+            run_linear_bf16(projection_index(temporal, l, 1), att, rows, h, h, false, xq, xs);
         {
             KernelTimer::Scope timing("layer_norm", stream_, 0.0);
             dev::layer_norm(h, model_->norm_gain[n2].as<std::uint16_t>(),
@@ -560,7 +566,7 @@ void TransformerEngine::decode_begin(const std::vector<Header>& headers)
         st.ws.get<std::int8_t>(name, cap * 1024);
     for (const char* name : {"es", "ps"})
         st.ws.get<float>(name, cap * 4);
-    for (const char* name : {"th", "tout", "ch", "pproj"})
+    for (const char* name : {"th", "tout", "ch"})
         st.ws.get<std::uint16_t>(name, cap * 512);
     st.ws.get<std::int8_t>("fq", cap * 512);
     st.ws.get<float>("fs", cap * 2);
@@ -769,17 +775,19 @@ TransformerEngine::decode_predict(std::size_t step, std::size_t book, const floa
             }
             else
             {
+                // Prefix embedding sum (BF8L-quantized in the same kernel),
+                // cb_proj, and the book's position row added as a residual
+                // broadcast to every row: all rows of a step share `book`, and
+                // bf16(pos + y) is add_positions' bf16(y + pos).
                 auto* pemb = ws.get<std::uint16_t>("pemb", static_cast<std::size_t>(n) * 1024);
+                auto* pq = ws.get<std::int8_t>("pq", static_cast<std::size_t>(n) * 1024);
+                auto* ps = ws.get<float>("ps", static_cast<std::size_t>(n) * 4);
                 dev::embed_sum(model_->embeddings.as<std::uint16_t>(),
                                reinterpret_cast<const std::uint16_t*>(dev_c + cb.tokens),
                                reinterpret_cast<const int*>(dev_c + cb.offsets),
-                               reinterpret_cast<const int*>(dev_c + cb.counts), n, pemb, s);
-                auto* pq = ws.get<std::int8_t>("pq", static_cast<std::size_t>(n) * 1024);
-                auto* ps = ws.get<float>("ps", static_cast<std::size_t>(n) * 4);
-                auto* pproj = ws.get<std::uint16_t>("pproj", static_cast<std::size_t>(n) * 512);
-                run_linear_bf16(61, pemb, n, pproj, nullptr, false, pq, ps);
-                dev::add_positions(pproj, st.identity, d_books, model_->positions.as<std::uint16_t>(),
-                                   n, ch, s);
+                               reinterpret_cast<const int*>(dev_c + cb.counts), n, pemb, s, pq, ps,
+                               error_word());
+                run_linear(61, pq, ps, n, ch, model_->positions.as<std::uint16_t>() + book * 512, false, 0);
             }
             auto* fq = ws.get<std::int8_t>("fq", static_cast<std::size_t>(n) * 512);
             auto* fs = ws.get<float>("fs", static_cast<std::size_t>(n) * 2);

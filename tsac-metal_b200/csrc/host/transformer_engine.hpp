@@ -79,8 +79,11 @@ public:
     void check_errors();
 
 private:
+    // residual_stride: elements per residual row (-1: the output width; 0: one
+    // residual row added to every row).
     void run_linear(int projection, const std::int8_t* xq, const float* xs, int rows,
-                    std::uint16_t* y, const std::uint16_t* residual, bool gelu);
+                    std::uint16_t* y, const std::uint16_t* residual, bool gelu,
+                    int residual_stride = -1);
     // bf16 input: BF8L pass into xq / xs (scratch of rows x K), then the linear.
     void run_linear_bf16(int projection, const std::uint16_t* x, int rows, std::uint16_t* y,
                          const std::uint16_t* residual, bool gelu, std::int8_t* xq, float* xs);

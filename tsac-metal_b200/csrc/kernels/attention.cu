@@ -13,11 +13,16 @@
 //   (block max, block sum, 128 value sums).
 //   kernel 2, one CTA per (row, head): the sequential merge over blocks, which
 //   is cheap (16 steps at 1024 keys) and keeps the reference's order.
+//   Histories of one block skip kernel 2; when the caller wants the output
+//   BF8L-quantized for the next projection, one CTA per (row, head pair)
+//   also quantizes its 256 outputs, saving the separate quantize pass.
 #include "kernels/numeric.cuh"
 #include "kernels/row_ops.cuh"
 #include "kernels/launch_count.hpp"
 #include "kernels/pdl.cuh"
 #include "kernels/transformer_ops.cuh"
+
+#include <mutex>
 
 namespace tsacb::dev
 {
@@ -64,6 +69,59 @@ __global__ void __launch_bounds__(128)
     }
 }
 
+// One-block histories with the output BF8L-quantized for the next
+// projection: one CTA per (row, head pair), i.e. per 256-value quantization
+// block.  Two 128-thread groups (named barriers 1 and 2) each run one head's
+// block and its one-block merge, exactly as attention_block_kernel<true>;
+// the 256 bf16 outputs are then quantized with the quantize_bf8l_kernel
+// operations (block max of |flush(v)|, bf16 scale, rint(v / scale) clamped).
+__global__ void __launch_bounds__(256)
+    attention_pair_quantize_kernel(const std::uint16_t* __restrict__ query,
+                                   const RowMeta* __restrict__ meta,
+                                   const std::uint16_t* __restrict__ cache_k,
+                                   const std::uint16_t* __restrict__ cache_v,
+                                   std::int8_t* __restrict__ yq, float* __restrict__ yscale,
+                                   unsigned* error_word)
+{
+    pdl_prologue();
+    extern __shared__ __align__(16) unsigned char attention_smem[];
+    auto* groups = reinterpret_cast<AttentionShared*>(attention_smem);
+    __shared__ float warp_max[8];
+    const int row = blockIdx.x >> 1, pair = blockIdx.x & 1;
+    const int group = threadIdx.x >> 7, t = threadIdx.x & 127;
+    const int head = 2 * pair + group;
+    const RowMeta m = meta[row];
+    if (m.time <= 0) // uniform across the CTA: both groups share the row
+        return;
+    const int count = m.time < BLOCK ? m.time : BLOCK;
+    const AttentionBlock b = attention_block_core(query + static_cast<size_t>(row) * WIDTH + head * HW, m, head,
+                                                  cache_k, cache_v, 0, count, groups[group], 1 + group, t);
+    const float x = from_bf16(attention_single_output(b));
+    float block_max = fmaxf(0.0f, fabsf(flush(x)));
+#pragma unroll
+    for (int offset = 16; offset > 0; offset >>= 1)
+        block_max = fmaxf(block_max, __shfl_xor_sync(0xffffffffu, block_max, offset));
+    if ((threadIdx.x & 31) == 0)
+        warp_max[threadIdx.x >> 5] = block_max;
+    const bool finite = __syncthreads_and(isfinite(x));
+#pragma unroll
+    for (int w = 0; w < 8; ++w)
+        block_max = fmaxf(block_max, warp_max[w]);
+    float d = ftz_div(block_max, 127.0f);
+    d = d < 1e-35f ? 1e-35f : d;
+    const float scale = from_bf16(to_bf16(d));
+    const float reciprocal = ftz_div(1.0f, scale);
+    float r = rintf(ftz_mul(x, reciprocal));
+    r = r < -128.0f ? -128.0f : (r > 127.0f ? 127.0f : r);
+    yq[static_cast<size_t>(row) * WIDTH + pair * 256 + threadIdx.x] = static_cast<std::int8_t>(static_cast<int>(r));
+    if (threadIdx.x == 0)
+    {
+        yscale[row * 2 + pair] = scale;
+        if (!finite && error_word)
+            atomicOr(error_word, error_nonfinite);
+    }
+}
+
 __global__ void __launch_bounds__(128)
     attention_combine_kernel(const RowMeta* __restrict__ meta, const float* __restrict__ partials,
                              int max_blocks, std::uint16_t* __restrict__ out)
@@ -99,19 +157,39 @@ size_t attention_partials_bytes(int rows, int max_time)
     return static_cast<size_t>(rows) * HEADS * blocks * PSTRIDE * sizeof(float);
 }
 
-void attention(const std::uint16_t* query, const RowMeta* meta, const std::uint16_t* cache_k,
+bool attention(const std::uint16_t* query, const RowMeta* meta, const std::uint16_t* cache_k,
                const std::uint16_t* cache_v, int rows, int max_time, float* partials,
-               std::uint16_t* out, cudaStream_t stream)
+               std::uint16_t* out, cudaStream_t stream, std::int8_t* yq, float* yscale,
+               unsigned* error_word)
 {
     if (rows <= 0)
-        return;
+        return false;
     const int blocks = (max_time + BLOCK - 1) / BLOCK;
+    if (blocks == 1 && yq)
+    {
+        constexpr size_t smem = 2 * sizeof(AttentionShared);
+        static std::once_flag attribute_once[64];
+        int device = 0;
+        cudaGetDevice(&device);
+        if (device >= 0 && device < 64)
+            std::call_once(attribute_once[device],
+                           []
+                           {
+                               cudaFuncSetAttribute(attention_pair_quantize_kernel,
+                                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    static_cast<int>(smem));
+                           });
+        launch_pdl(attention_pair_quantize_kernel, dim3(rows * 2), dim3(256), smem, stream, query, meta,
+                   cache_k, cache_v, yq, yscale, error_word);
+        note_launch();
+        return true;
+    }
     if (blocks == 1)
     {
         launch_pdl(attention_block_kernel<true>, dim3(rows * HEADS, 1), dim3(128), 0, stream, query,
                    meta, cache_k, cache_v, 1, static_cast<float*>(nullptr), out);
         note_launch();
-        return;
+        return false;
     }
     launch_pdl(attention_block_kernel<false>, dim3(rows * HEADS, blocks), dim3(128), 0, stream, query,
                meta, cache_k, cache_v, blocks, partials, static_cast<std::uint16_t*>(nullptr));
@@ -119,5 +197,6 @@ void attention(const std::uint16_t* query, const RowMeta* meta, const std::uint1
     launch_pdl(attention_combine_kernel, dim3(rows * HEADS), dim3(128), 0, stream, meta,
                static_cast<const float*>(partials), blocks, out);
     note_launch();
+    return false;
 }
 } // namespace tsacb::dev

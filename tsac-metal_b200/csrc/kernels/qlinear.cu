@@ -59,17 +59,17 @@ __global__ void quantize_bf8l_kernel(const std::uint16_t* __restrict__ x, int k,
 struct Epilogue
 {
     const float* bias;
-    const std::uint16_t* residual; // [M][N] or null
+    const std::uint16_t* residual; // [M][residual_stride] or null
     const std::uint16_t* lut;      // 65536-entry bf16 map or null
+    int residual_stride;           // 0: one residual row for every column
 };
 
-__device__ __forceinline__ std::uint16_t finish(float sum, int m, int n, int ncols,
-                                                const Epilogue& e)
+__device__ __forceinline__ std::uint16_t finish(float sum, int m, int n, const Epilogue& e)
 {
     std::uint16_t y = to_bf16(__fadd_rn(sum, e.bias[n]));
     if (e.residual)
     {
-        y = to_bf16(__fadd_rn(from_bf16(e.residual[static_cast<size_t>(m) * ncols + n]),
+        y = to_bf16(__fadd_rn(from_bf16(e.residual[static_cast<size_t>(m) * e.residual_stride + n]),
                               from_bf16(y)));
     }
     if (e.lut)
@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
         for (int j = 0; j < 4; ++j)
         {
-            out[j] = finish(sum[i][j], m, n0 + tx * 4 + j, n_cols, e);
+            out[j] = finish(sum[i][j], m, n0 + tx * 4 + j, e);
         }
         *reinterpret_cast<uint2*>(y + static_cast<size_t>(m) * n_cols + n0 + tx * 4) =
             make_uint2(out[0] | (unsigned(out[1]) << 16), out[2] | (unsigned(out[3]) << 16));
@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(256) qlinear_mma_kernel(MmaArgs a)
                 const int dot = dots[((b * MMA_MT + mt) * 32 + frag_lane) * 4 + c];
                 sum = __fmaf_rn(static_cast<float>(dot), scale, sum);
             }
-            out = finish(sum, m, n, n_cols, a.e);
+            out = finish(sum, m, n, a.e);
         }
         if constexpr (QKV_OUT)
         {
@@ -395,7 +395,7 @@ bool qlinear_qkv_fusable(int m, int n)
 
 void qlinear_matmul(const QLinearArgs& a, cudaStream_t stream)
 {
-    const Epilogue e{a.bias, a.residual, a.lut};
+    const Epilogue e{a.bias, a.residual, a.lut, a.residual_stride < 0 ? a.n : a.residual_stride};
     if (a.m <= SMALL_MAX_M && a.n % 16 == 0)
         launch_small(a, e, stream);
     else

@@ -26,10 +26,11 @@ struct QLinearArgs
     const float* bias = nullptr;              // [n]
     const std::int8_t* xq = nullptr;          // [m][k] quantized activations
     const float* xscale = nullptr;            // [m][k/256]
-    const std::uint16_t* residual = nullptr;  // [m][n] bf16, added after rounding
+    const std::uint16_t* residual = nullptr;  // [m][residual_stride] bf16, added after rounding
     const std::uint16_t* lut = nullptr;       // bf16 -> bf16 map applied last (GELU)
     std::uint16_t* y = nullptr;               // [m][n] bf16
     int m = 0, n = 0, k = 0;
+    int residual_stride = -1;                 // elements per residual row; -1: n, 0: one row for all
     QkvScatter qkv;                           // only where qlinear_qkv_fusable
 };
 

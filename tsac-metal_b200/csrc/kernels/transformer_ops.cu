@@ -26,11 +26,14 @@ __device__ __forceinline__ unsigned pack2(std::uint16_t a, std::uint16_t b)
 }
 
 // ------------------------------------------------------------ embeddings --
-// 128 threads x 8 values per 1024-wide row.
+// 128 threads x 8 values per 1024-wide row.  With `yq`, the row is also
+// BF8L-quantized (the quantize_bf8l_kernel operations): warp w holds 256-block
+// w with lane l owning values 8l..8l+7, the bf8l_block layout.
 __global__ void embed_sum_kernel(const std::uint16_t* __restrict__ table,
                                  const std::uint16_t* __restrict__ tokens,
                                  const int* __restrict__ offsets, const int* __restrict__ counts,
-                                 std::uint16_t* __restrict__ out)
+                                 std::uint16_t* __restrict__ out, std::int8_t* __restrict__ yq,
+                                 float* __restrict__ yscale, unsigned* error_word)
 {
     pdl_prologue();
     const int row = blockIdx.x;
@@ -49,9 +52,20 @@ __global__ void embed_sum_kernel(const std::uint16_t* __restrict__ table,
             acc[i] = j == 0 ? e[i] : to_bf16(__fadd_rn(from_bf16(acc[i]), from_bf16(e[i])));
         }
     }
-    *reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * 1024 + c0) =
-        make_uint4(pack2(acc[0], acc[1]), pack2(acc[2], acc[3]), pack2(acc[4], acc[5]),
-                   pack2(acc[6], acc[7]));
+    const uint4 packed = make_uint4(pack2(acc[0], acc[1]), pack2(acc[2], acc[3]), pack2(acc[4], acc[5]),
+                                    pack2(acc[6], acc[7]));
+    *reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * 1024 + c0) = packed;
+    if (yq)
+    {
+        const int lane = threadIdx.x & 31, block = threadIdx.x >> 5;
+        bool finite = true;
+        const Bf8lLane q = bf8l_block(packed, finite);
+        if (!__all_sync(0xffffffffu, finite) && lane == 0 && error_word)
+            atomicOr(error_word, error_nonfinite);
+        *reinterpret_cast<uint2*>(yq + static_cast<size_t>(row) * 1024 + c0) = make_uint2(q.packed[0], q.packed[1]);
+        if (lane == 0)
+            yscale[row * 4 + block] = q.scale;
+    }
 }
 
 // ------------------------------------------------------------ layer norm --
@@ -213,11 +227,13 @@ __global__ void gelu_table_kernel(std::uint16_t* table)
 } // namespace
 
 void embed_sum(const std::uint16_t* embeddings, const std::uint16_t* tokens, const int* offsets,
-               const int* counts, int rows, std::uint16_t* out, cudaStream_t stream)
+               const int* counts, int rows, std::uint16_t* out, cudaStream_t stream,
+               std::int8_t* yq, float* yscale, unsigned* error_word)
 {
     if (rows > 0)
     {
-        launch_pdl(embed_sum_kernel, dim3(rows), dim3(128), 0, stream, embeddings, tokens, offsets, counts, out);
+        launch_pdl(embed_sum_kernel, dim3(rows), dim3(128), 0, stream, embeddings, tokens, offsets, counts, out,
+                   yq, yscale, error_word);
         note_launch();
     }
 }

@@ -13,9 +13,13 @@
 namespace tsacb::dev
 {
 // out[r][0:1024] = sum over j < count[r] of E[j][tokens[offset[r] + j]] with
-// bf16 adds in book order (first term copied); count 0 gives zeros.
+// bf16 adds in book order (first term copied); count 0 gives zeros.  With yq
+// non-null the rows are also BF8L-quantized into yq [rows][1024] and
+// yscale [rows][4] (qlinear_quantize's result, nonfinite values flagged in
+// error_word).
 void embed_sum(const std::uint16_t* embeddings, const std::uint16_t* tokens, const int* offsets,
-               const int* counts, int rows, std::uint16_t* out, cudaStream_t stream);
+               const int* counts, int rows, std::uint16_t* out, cudaStream_t stream,
+               std::int8_t* yq = nullptr, float* yscale = nullptr, unsigned* error_word = nullptr);
 
 // LayerNorm(512) per row; writes bf16 output and/or BF8L-quantized output.
 void layer_norm(const std::uint16_t* x, const std::uint16_t* gain, const std::uint16_t* bias,
@@ -29,10 +33,16 @@ void rotary_scatter(const std::uint16_t* qkv, const RowMeta* meta, const std::ui
                     cudaStream_t stream);
 
 // Causal attention over the cache, 4 heads x 128, 64-key blocks merged in order.
-// `partials` scratch: rows * 4 heads * 16 blocks * 130 floats.
-void attention(const std::uint16_t* query, const RowMeta* meta, const std::uint16_t* cache_k,
+// `partials` scratch: rows * 4 heads * 16 blocks * 130 floats.  With yq
+// non-null and every history within one 64-key block (max_time <= 64), the
+// output goes BF8L-quantized to yq [rows][512] and yscale [rows][2] instead
+// of bf16 to `out` (qlinear_quantize's result; nonfinite values flagged in
+// error_word), and the call returns true; otherwise it writes `out` and
+// returns false.
+bool attention(const std::uint16_t* query, const RowMeta* meta, const std::uint16_t* cache_k,
                const std::uint16_t* cache_v, int rows, int max_time, float* partials,
-               std::uint16_t* out, cudaStream_t stream);
+               std::uint16_t* out, cudaStream_t stream, std::int8_t* yq = nullptr,
+               float* yscale = nullptr, unsigned* error_word = nullptr);
 size_t attention_partials_bytes(int rows, int max_time);
 
 // out[r] = bf16(src[source_row[r]] + positions[book[r]]) (512 wide).
