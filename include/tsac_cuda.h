@@ -87,6 +87,14 @@ void tsac_cuda_context_destroy(tsac_cuda_context* context);
  * unaffected either way. */
 int tsac_cuda_set_exact_synthesis(tsac_cuda_context* context, int exact);
 
+/* Host worker budget of a context (the reference CLI's -T, src/cli.cpp:66-68,
+ * passed to AppleArmAnalyzer, src/codec.cpp:117-120, which accepts 1-256,
+ * src/apple-arm/audio_analyzer.cpp:93): range encoding of a batch's recordings
+ * and each decode step's range decoding use at most `threads` host threads.
+ * 0 (the default): automatic (all hardware threads for encoding, up to 8 for
+ * the per-step decoding).  More than 256 is TSAC_CUDA_ERROR. */
+int tsac_cuda_set_host_threads(tsac_cuda_context* context, unsigned threads);
+
 /* AudioAnalyzer::encode (include/tsac/audio_analyzer.hpp:33-34) for a host
  * PCM view [channel, sample] with the given strides (in floats, as
  * tsac::PcmView's layout_stride).  *out (free with tsac_cuda_free) receives the

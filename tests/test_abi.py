@@ -65,3 +65,10 @@ def test_kernel_entry_point_without_gpu_fails_loudly():
     status = lib.tsac_cuda_snake(p, ctypes.c_size_t(1), ctypes.c_size_t(1), p, p, p,
                                  ctypes.c_void_p(0))
     assert status == 2  # TSAC_CUDA_ERROR_DEVICE: no device, nothing computed on the host
+
+
+def test_context_setters_reject_null_context():
+    lib = tsac_cuda.library()
+    assert lib.tsac_cuda_set_host_threads(None, ctypes.c_uint(4)) == 1  # TSAC_CUDA_ERROR
+    assert b"null" in lib.tsac_cuda_last_error()
+    assert lib.tsac_cuda_set_exact_synthesis(None, 1) == 1

@@ -62,7 +62,7 @@ def test_compress_matches_golden_stream(tmp_path, case):
     g = json.loads((GOLDEN / f"{case}.json").read_text())
     pcm = synthetic.music_like(g["pcm_seed"], g["seconds"], g["channels"])
     write_wave(tmp_path / "in.wav", pcm)
-    args = ["-q", str(g["codebooks"])]
+    args = ["-q", str(g["codebooks"]), "-T", "3"]  # a host thread budget changes no byte
     if g["method"] == 0:
         args.append("-f")
     if g["separate"]:
@@ -90,7 +90,7 @@ def test_decompress_exact_writes_reference_pcm16(tmp_path):
 def test_round_trip_and_statistics(tmp_path):
     pcm = synthetic.music_like(77, 0.7, 2)
     write_wave(tmp_path / "in.wav", pcm)
-    out = cli("-vv", "-q", "6", "t", str(tmp_path / "in.wav"), str(tmp_path / "rt.wav"))
+    out = cli("-vv", "-T", "1", "-q", "6", "t", str(tmp_path / "in.wav"), str(tmp_path / "rt.wav"))
     lines = out.splitlines()
     assert lines[0].startswith("batch_size=") and " n_cb=6 " in lines[0]
     assert "CB AVG_BITS" in lines

@@ -164,6 +164,24 @@ def test_failures_are_errors_and_analyzer_is_reusable(analyzer):
     assert analyzer.decode(good).samples.shape == (512 * 5, 2)
 
 
+def test_host_thread_budget(analyzer):
+    """Range coding under a host thread budget (the reference CLI's -T, 1-256)
+    gives the same streams and the same decoded PCM; larger budgets are errors."""
+    pcms = [synthetic.music_like(40 + i, 0.3, 2) for i in range(3)]
+    automatic = analyzer.encode_batch(pcms)
+    reference = analyzer.decode_batch(automatic)
+    try:
+        for threads in (1, 2, 3):
+            analyzer.set_host_threads(threads)
+            assert analyzer.encode_batch(pcms) == automatic
+            for got, want in zip(analyzer.decode_batch(automatic), reference):
+                assert np.array_equal(got.samples, want.samples)
+        with pytest.raises(tsac_cuda.TsacError, match="256"):
+            analyzer.set_host_threads(257)
+    finally:
+        analyzer.set_host_threads(0)
+
+
 def test_fused_codebook_step_decodes_identically(tmp_path):
     """The opt-in fused codebook-step kernel (one cluster launch per step)
     produces the same PCM as the default separate kernels."""

@@ -182,7 +182,7 @@ or $TSAC_CUDA_MODELS).
 
 Available options:
 -h --help               show the help
--T n                    number of threads (accepted; the GPU path sizes its own host workers)
+-T n                    number of host threads for range coding (default: automatic)
 -q --n_codebooks n      quality (1-12 for joint stereo, 1-9 otherwise; 0=max)
 -s --separate_channels  encode stereo as separate channels
 -c --channels n         force input channels through FFmpeg
@@ -487,6 +487,10 @@ int run(const Options& options)
     check(tsac_cuda_context_create(models.c_str(), options.device, &c.ctx));
     if (options.exact)
         check(tsac_cuda_set_exact_synthesis(c.ctx, 1));
+    // The reference passes a positive -T to its analyzer and uses the default
+    // otherwise (src/codec.cpp:117-120).
+    if (options.threads > 0)
+        check(tsac_cuda_set_host_threads(c.ctx, static_cast<unsigned>(options.threads)));
     Bytes output;
     if (options.command == 'c' || options.command == 't')
     {

@@ -353,6 +353,16 @@ int tsac_cuda_set_exact_synthesis(tsac_cuda_context* ctx, int exact)
         });
 }
 
+int tsac_cuda_set_host_threads(tsac_cuda_context* ctx, unsigned threads)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            tsacb::require(ctx != nullptr, "null argument");
+            ctx->impl.set_host_threads(threads);
+        });
+}
+
 int tsac_cuda_dac_synthesis(tsac_cuda_context* ctx, unsigned channels, const float* latent,
                             size_t frames, float* pcm)
 {

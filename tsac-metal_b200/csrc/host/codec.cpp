@@ -41,10 +41,16 @@ std::size_t audio_chunk_frames(std::size_t target, const Limits& limits)
 // Windows per DAC launch group: bounds device scratch (~250 MB per window).
 constexpr std::size_t window_group = 48;
 
-template <class F> void parallel_for(std::size_t n, F&& f)
+// Host worker count: the context's budget, else every hardware thread.
+std::size_t host_workers(const Context& ctx)
 {
-    const std::size_t workers =
-        std::max<std::size_t>(1, std::min<std::size_t>(n, std::thread::hardware_concurrency()));
+    const std::size_t hw = std::max(1u, std::thread::hardware_concurrency());
+    return ctx.host_threads() ? ctx.host_threads() : hw;
+}
+
+template <class F> void parallel_for(std::size_t n, std::size_t max_workers, F&& f)
+{
+    const std::size_t workers = std::max<std::size_t>(1, std::min(n, max_workers));
     if (workers <= 1)
     {
         for (std::size_t i = 0; i < n; ++i)
@@ -474,7 +480,7 @@ std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
     profile.mark("transformer (known)");
     // Sequential range coding per recording on host cores (pack_normal,
     // src/format/entropy.cpp:57-123), recordings in parallel.
-    parallel_for(n,
+    parallel_for(n, host_workers(ctx),
                  [&](std::size_t i)
                  {
                      if (headers[i].method == 1)
@@ -529,9 +535,12 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
         }
         (void)lanes;
         // Recordings are independent streams: worker w range-decodes the rows
-        // of recordings r with r % workers == w, each in stream order.
-        const auto hw = static_cast<std::size_t>(std::thread::hardware_concurrency());
-        StepPool pool(std::min<std::size_t>({ids.size(), 8, hw > 1 ? hw - 1 : 1}));
+        // of recordings r with r % workers == w, each in stream order.  The
+        // caller is worker 0; automatically up to 8 (a step is a few
+        // microseconds of work, spread thinner it costs more than it saves).
+        const std::size_t budget = ctx.host_threads() ? ctx.host_threads()
+                                                      : std::min<std::size_t>(8, host_workers(ctx));
+        StepPool pool(std::min<std::size_t>(ids.size(), budget));
         // Host-side split of the step loop (TSAC_CUDA_PROFILE): time in
         // decode_predict (input staging, graph launch, waiting for the masses),
         // in the range decoders, and in commit.

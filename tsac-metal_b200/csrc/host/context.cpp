@@ -95,6 +95,12 @@ void Context::set_exact_synthesis(bool exact)
             e->set_exact_synthesis(exact);
 }
 
+void Context::set_host_threads(unsigned threads)
+{
+    require(threads <= 256, "CPU thread count exceeds supported limit (256)");
+    host_threads_ = threads;
+}
+
 RvqEngine& Context::rvq(unsigned channels)
 {
     require(channels == 1 || channels == 2, "invalid model variant");

@@ -37,6 +37,14 @@ public:
     // Exact synthesis (bit-identical PCM, serial CUDA-core convolutions) or
     // the default tensor-core synthesis (PCM within tolerance).
     void set_exact_synthesis(bool exact);
+    // Host worker budget for range coding (the -T thread count of the
+    // reference CLI, AppleArmAnalyzer's 1-256 bound,
+    // src/apple-arm/audio_analyzer.cpp:93); 0: automatic.
+    void set_host_threads(unsigned threads);
+    unsigned host_threads() const
+    {
+        return host_threads_;
+    }
     RvqEngine& rvq(unsigned channels);
     const Package& package() const
     {
@@ -53,6 +61,7 @@ public:
 private:
     Package package_;
     int device_;
+    unsigned host_threads_ = 0;
     Limits limits_;
     cudaStream_t stream_ = nullptr;
     std::shared_ptr<DeviceTransformer> transformers_[2];

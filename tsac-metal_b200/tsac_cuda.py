@@ -176,6 +176,13 @@ class CudaAnalyzer:
         """Exact (bit-identical PCM) or tensor-core (within tolerance) synthesis."""
         check(library().tsac_cuda_set_exact_synthesis(self._ctx, 1 if exact else 0))
 
+    def set_host_threads(self, threads: int) -> None:
+        """Host range-coding worker budget (0: automatic, at most 256), the
+        thread count AppleArmAnalyzer takes (src/apple-arm/audio_analyzer.cpp:93)."""
+        if threads < 0:
+            raise TsacError("invalid thread count")
+        check(library().tsac_cuda_set_host_threads(self._ctx, ctypes.c_uint(threads)))
+
     def close(self):
         if self._ctx:
             library().tsac_cuda_context_destroy(self._ctx)
