@@ -5,8 +5,8 @@
                     [--workload codec|qlinear|frontend] [--clips B] [--seconds S]
 
 Workloads
-  codec    (default) BASELINE metric "x-realtime encode+decode per GPU at q=12
-           stereo": one step = encode + decode of B independent 30 s 44.1 kHz
+  codec    (default) the headline metric "x-realtime encode+decode per GPU at
+           q=12 stereo": one step = encode + decode of B independent 30 s 44.1 kHz
            joint-stereo clips (cfg0 settings: q=12, --batch_size 3) per GPU,
            through the library's batched C ABI.  `value` is measured with PCM
            resident in HBM (tsac_cuda_encode_batch_device /
@@ -17,7 +17,10 @@ Workloads
            package 0.  Default B = 48 clips per GPU (the decoder's Transformer
            steps are latency-bound, so throughput grows with the batch).  The
            timed steps sit in the NVTX range "timed".
-  qlinear  BASELINE cfg1 quantized-linear microbench (aggregate HBM GB/s).
+  qlinear  cfg1 quantized-linear microbench (aggregate HBM GB/s).
+  frontend encoder front end only (padding, DAC analysis, RVQ) of B clips per
+           GPU: the exact-order analysis convolutions in isolation, for
+           profiling.
 
 Multi-GPU: one process per GPU (torchrun); each rank codes its own clips
 (clips shard with no data-path collective: "scaling": "weak"); the timed region
