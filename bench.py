@@ -169,6 +169,21 @@ def clip_seeds(rank, clips):
     return [rank * 100000 + i for i in range(clips)]
 
 
+def host_thread_share(world):
+    """Host threads one rank may use for range coding: with several ranks on
+    one host, an even share of the CPUs this process may run on (the decode
+    loop's workers spin between steps, so oversubscribing the host would slow
+    every rank); alone, 0 = the library's automatic choice."""
+    local = int(os.environ.get("LOCAL_WORLD_SIZE", world))
+    if local <= 1:
+        return 0
+    try:
+        cpus = len(os.sched_getaffinity(0))
+    except AttributeError:
+        cpus = os.cpu_count() or 1
+    return max(1, cpus // local)
+
+
 def whole_job_rate(units_per_rank, world, elapsed_ms_max):
     """Units all ranks processed / the slowest rank's time (units per second)."""
     return units_per_rank * world / (elapsed_ms_max / 1e3)
@@ -204,6 +219,8 @@ def codec_workload(args, rank, world, torch, dist):
     host = [synthetic.music_like(seed, args.seconds, 2) for seed in clip_seeds(rank, clips)]
     device_pcm = [torch.from_numpy(p).to(dev) for p in host]
     analyzer = tsac_cuda.CudaAnalyzer(tsac_cuda.seeded_package(0), torch.cuda.current_device())
+    threads = host_thread_share(world)
+    analyzer.set_host_threads(threads)
     streams = tsac_cuda.encode_batch_device(analyzer, device_pcm, opts)
     outs = []
     for s in streams:
@@ -315,6 +332,7 @@ def codec_workload(args, rank, world, torch, dist):
         "config": {"workload": "cfg0/cfg4: encode+decode of 30 s stereo clips", "clips_per_gpu": clips,
                    "codebooks": 12, "entropy_batch": 3, "seconds_per_clip": args.seconds,
                    "l2": "working set (PCM, activations) far larger than L2 each step",
+                   "host_threads_per_rank": threads or "auto",
                    "parity_cfg0_stream_vs_reference": parity},
         "roofline": roofline,
         "kernel_time_shares": shares,

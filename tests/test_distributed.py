@@ -69,3 +69,16 @@ def test_clip_sharding_and_max_over_ranks():
     expected = [bytes([r, i]) * (i + 1) for r in range(world) for i in range(r + 2)]
     assert results[0]["streams"] == expected
     assert results[1]["streams"] is None
+
+
+def test_host_thread_share(monkeypatch):
+    import bench
+
+    monkeypatch.delenv("LOCAL_WORLD_SIZE", raising=False)
+    assert bench.host_thread_share(1) == 0  # alone: the library chooses
+    cpus = len(os.sched_getaffinity(0))
+    for world in (2, 4, 8):
+        share = bench.host_thread_share(world)
+        assert 1 <= share and (share * world <= cpus or share == 1)
+    monkeypatch.setenv("LOCAL_WORLD_SIZE", "1")
+    assert bench.host_thread_share(8) == 0  # one rank per host
