@@ -306,6 +306,38 @@ int tsac_cuda_conv1d_tensor(const float* x, size_t frames, const float* weights,
 int tsac_cuda_snake(const float* x, size_t channels, size_t frames, const float* alpha, float* y,
                     unsigned* error_word, void* stream);
 
+/* Range decoding of normal-stream symbols on the device, the optional
+ * GPU-resident alternative to the host decoders (the reference's Metal
+ * range_decode, src/metal/probability/range.metal:12-77: one serialized
+ * RangeDecoder per stream, src/format/range.cpp:118-157, walking the
+ * bisection heap of decode_categorical, src/format/categorical.cpp:119-142).
+ * Payload s of `streams` is bytes[offsets[s], offsets[s] + sizes[s]); bytes,
+ * offsets, sizes, cursors (tsac_cuda_range_cursor_bytes() each) are device
+ * memory.  tsac_cuda_range_start reads each payload's first three bytes;
+ * tsac_cuda_range_decode then decodes `count` symbols: row r belongs to stream
+ * rows[r] (device int32), a stream's rows in increasing r, its left-child
+ * masses masses[r][1023] (device f32, the softmax tree's heap), symbol to
+ * symbols[r] (device u16).  The cursors carry each decoder across calls.  A
+ * stream whose code leaves its interval stops (cursor status 1, symbols 0)
+ * and ORs 2 (the range-error bit) into *error_word (nullable).  Asynchronous
+ * on `stream`. */
+size_t tsac_cuda_range_cursor_bytes(void);
+int tsac_cuda_range_start(const uint8_t* bytes, const uint64_t* offsets, const uint64_t* sizes,
+                          void* cursors, size_t streams, unsigned* error_word, void* stream);
+int tsac_cuda_range_decode(const uint8_t* bytes, const uint64_t* offsets, const uint64_t* sizes,
+                           void* cursors, size_t streams, const int* rows, size_t count,
+                           const float* masses, uint16_t* symbols, unsigned* error_word, void* stream);
+
+/* Host range coding over given bisection masses (host memory, [count][1023]
+ * heap order), the coder the decode loop runs: tsac_cuda_range_encode_tree
+ * codes count symbols (encode_categorical's 10 decisions each) into *out
+ * (free with tsac_cuda_free); tsac_cuda_range_decode_tree decodes them back.
+ * Host only; for round-trip tests of either decoder. */
+int tsac_cuda_range_encode_tree(const float* masses, const uint16_t* symbols, size_t count,
+                                uint8_t** out, size_t* out_bytes);
+int tsac_cuda_range_decode_tree(const uint8_t* bytes, size_t size, const float* masses, size_t count,
+                                uint16_t* symbols);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,83 @@
+"""Host range coding over bisection masses (the coder the decode loop runs):
+symbols drawn from random distributions survive encode -> decode through the
+library's RangeEncoder / RangeDecoder with the heap masses the softmax kernel
+emits (left child of node 2^d - 1 + k = the first half of its aligned range)."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+import tsac_cuda
+
+
+def heap_masses(p):
+    """Left-child masses [1023] of a 1024-entry distribution, heap order."""
+    out = np.zeros(1023, np.float32)
+    for depth in range(10):
+        width = 1024 >> depth
+        for k in range(1 << depth):
+            lo = k * width
+            out[(1 << depth) - 1 + k] = np.float32(p[lo:lo + width // 2].sum(dtype=np.float64))
+    return out
+
+
+def random_rows(rng, count):
+    masses = np.zeros((count, 1023), np.float32)
+    symbols = np.zeros(count, np.uint16)
+    for i in range(count):
+        p = rng.dirichlet(np.full(1024, rng.choice([0.02, 0.3, 5.0])))
+        masses[i] = heap_masses(p)
+        symbols[i] = rng.choice(1024, p=p)
+    return masses, symbols
+
+
+def encode(masses, symbols):
+    lib = tsac_cuda.library()
+    out, size = ctypes.c_void_p(), ctypes.c_size_t()
+    tsac_cuda.check(lib.tsac_cuda_range_encode_tree(masses.ctypes.data_as(ctypes.c_void_p),
+                                                    symbols.ctypes.data_as(ctypes.c_void_p),
+                                                    ctypes.c_size_t(len(symbols)), ctypes.byref(out),
+                                                    ctypes.byref(size)))
+    data = ctypes.string_at(out, size.value)
+    lib.tsac_cuda_free(out)
+    return data
+
+
+def decode(stream, masses):
+    lib = tsac_cuda.library()
+    got = np.zeros(len(masses), np.uint16)
+    buf = ctypes.create_string_buffer(stream, len(stream))
+    tsac_cuda.check(lib.tsac_cuda_range_decode_tree(buf, ctypes.c_size_t(len(stream)),
+                                                    masses.ctypes.data_as(ctypes.c_void_p),
+                                                    ctypes.c_size_t(len(masses)),
+                                                    got.ctypes.data_as(ctypes.c_void_p)))
+    return got
+
+
+@pytest.mark.parametrize("seed,count", [(0, 1), (1, 40), (2, 200)])
+def test_round_trip(seed, count):
+    rng = np.random.default_rng(seed)
+    masses, symbols = random_rows(rng, count)
+    stream = encode(masses, symbols)
+    assert np.array_equal(decode(stream, masses), symbols)
+
+
+def test_extreme_symbols_round_trip():
+    """Improbable symbols (Q15 clamped to 1 or 32767 on the path) and both ends
+    of the alphabet."""
+    rng = np.random.default_rng(3)
+    p = np.full(1024, 1e-9)
+    p[500] = 1.0
+    p /= p.sum()
+    masses = np.repeat(heap_masses(p)[None], 6, axis=0)
+    symbols = np.array([0, 1023, 500, 7, 500, 1022], np.uint16)
+    assert np.array_equal(decode(encode(masses, symbols), masses), symbols)
+    assert len(encode(masses, symbols[2:3])) < len(encode(masses, symbols[:1]))
+
+
+def test_symbol_outside_alphabet_rejected():
+    masses = np.zeros((1, 1023), np.float32)
+    with pytest.raises(tsac_cuda.TsacError, match="alphabet"):
+        encode(masses, np.array([1024], np.uint16))

@@ -4,6 +4,7 @@
 #include "cuda_util.cuh"
 #include "kernels/dac.cuh"
 #include "kernels/qlinear.cuh"
+#include "kernels/range_decode.cuh"
 
 #include <vector>
 
@@ -142,6 +143,46 @@ int tsac_cuda_conv1d(const float* x, size_t frames, const float* weights, const 
             }
             // The host tile table must outlive the asynchronous copy.
             cuda_check(cudaStreamSynchronize(s), "conv1d");
+        });
+}
+
+size_t tsac_cuda_range_cursor_bytes(void)
+{
+    return sizeof(tsacb::dev::RangeCursor);
+}
+
+int tsac_cuda_range_start(const uint8_t* bytes, const uint64_t* offsets, const uint64_t* sizes,
+                          void* cursors, size_t streams, unsigned* error_word, void* stream)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            using namespace tsacb;
+            require_device();
+            require(bytes && offsets && sizes && cursors, "null argument");
+            require(streams <= (1u << 24), "range decoder stream count out of range");
+            dev::range_start(bytes, offsets, sizes, static_cast<dev::RangeCursor*>(cursors),
+                             static_cast<int>(streams), error_word, static_cast<cudaStream_t>(stream));
+            cuda_check(cudaGetLastError(), "range start launch");
+        });
+}
+
+int tsac_cuda_range_decode(const uint8_t* bytes, const uint64_t* offsets, const uint64_t* sizes,
+                           void* cursors, size_t streams, const int* rows, size_t count,
+                           const float* masses, uint16_t* symbols, unsigned* error_word, void* stream)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            using namespace tsacb;
+            require_device();
+            require(bytes && offsets && sizes && cursors && (count == 0 || (rows && masses && symbols)),
+                    "null argument");
+            require(streams <= (1u << 24) && count <= (1u << 24), "range decoder size out of range");
+            dev::range_decode(bytes, offsets, sizes, static_cast<dev::RangeCursor*>(cursors),
+                              static_cast<int>(streams), rows, static_cast<int>(count), masses, symbols,
+                              error_word, static_cast<cudaStream_t>(stream));
+            cuda_check(cudaGetLastError(), "range decode launch");
         });
 }
 

@@ -207,6 +207,38 @@ int tsac_cuda_unpack_fast(const uint8_t* stream, size_t bytes, uint16_t** tokens
         });
 }
 
+int tsac_cuda_range_encode_tree(const float* masses, const uint16_t* symbols, size_t count, uint8_t** out,
+                                size_t* out_bytes)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            tsacb::require(out && out_bytes && (count == 0 || (masses && symbols)), "null argument");
+            tsacb::RangeEncoder encoder;
+            for (size_t i = 0; i < count; ++i)
+            {
+                tsacb::require(symbols[i] < 1024, "symbol exceeds alphabet");
+                tsacb::encode_categorical_tree(encoder, masses + i * 1023, symbols[i]);
+            }
+            const auto bytes = encoder.finish();
+            *out = tsacb::malloc_copy(bytes.data(), bytes.size());
+            *out_bytes = bytes.size();
+        });
+}
+
+int tsac_cuda_range_decode_tree(const uint8_t* bytes, size_t size, const float* masses, size_t count,
+                                uint16_t* symbols)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            tsacb::require((bytes || size == 0) && (count == 0 || (masses && symbols)), "null argument");
+            tsacb::RangeDecoder decoder(tsacb::ByteView(bytes, size));
+            for (size_t i = 0; i < count; ++i)
+                symbols[i] = tsacb::decode_categorical_tree(decoder, masses + i * 1023);
+        });
+}
+
 uint32_t tsac_cuda_token_crc32(const uint16_t* tokens, size_t count)
 {
     return tsacb::token_crc32(std::span<const std::uint16_t>(tokens, tokens ? count : 0));

@@ -367,6 +367,32 @@ std::uint16_t conditional_q15(float left_mass, float mass)
     return static_cast<std::uint16_t>(std::clamp(low, 1, 32767));
 }
 
+void encode_categorical_tree(RangeEncoder& encoder, const float* left_masses, std::uint16_t symbol)
+{
+    std::size_t node = 0, base = 0, count = 1024;
+    float mass = 1;
+    while (count > 1)
+    {
+        const auto half = count / 2;
+        const float left = left_masses[node];
+        const bool bit = symbol >= base + half;
+        encoder.put(conditional_q15(left, mass), bit);
+        if (bit)
+        {
+            base += half;
+            count -= half;
+            mass = ftz_sub(mass, left);
+            node = 2 * node + 2;
+        }
+        else
+        {
+            count = half;
+            mass = left;
+            node = 2 * node + 1;
+        }
+    }
+}
+
 std::uint16_t decode_categorical_tree(RangeDecoder& decoder, const float* left_masses)
 {
     std::size_t node = 0, base = 0, count = 1024;

@@ -105,6 +105,10 @@ std::uint16_t conditional_q15(float left_mass, float mass);
 // Decodes one symbol of a 1024-entry alphabet from the left-child masses of
 // the 1023 internal bisection nodes (heap order: children 2i+1, 2i+2).
 std::uint16_t decode_categorical_tree(RangeDecoder& decoder, const float* left_masses);
+// The encoding counterpart (encode_categorical, src/format/categorical.cpp:91-117):
+// the 10 decisions of `symbol`'s path, each with conditional_q15 of the node's
+// left mass and the path mass.
+void encode_categorical_tree(RangeEncoder& encoder, const float* left_masses, std::uint16_t symbol);
 // Host probability_sum (64-value FTZ pair trees + binary carry).
 float probability_sum(std::span<const float> values);
 } // namespace tsacb

@@ -9,6 +9,7 @@
 //   scalar::Attention (one block)     src/scalar/attention.cpp:12-131
 //   probability_softmax_bf16_into     src/common/probability.cpp:96-122
 //   probability_sum / pair trees      src/format/categorical.cpp:17-74
+//   conditional_q15                   src/format/categorical.cpp:76-89
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -159,6 +160,20 @@ __device__ __forceinline__ Bf8lLane bf8l_block(uint4 raw, bool& finite)
         out.packed[i / 4] |= (static_cast<unsigned>(static_cast<int>(r)) & 0xffu) << (8 * (i % 4));
     }
     return out;
+}
+
+// ------------------------------------------------------- categorical Q15 --
+// conditional_q15 (src/format/categorical.cpp:76-89): the Q15 probability of
+// the left child, round(flush(flush(left * 32768) / mass)) clamped to
+// [1, 32767]; nonfinite or out-of-range ratios give 1.
+__device__ __forceinline__ std::uint16_t conditional_q15(float left, float mass)
+{
+    const float value = ftz_div(ftz_mul(left, 32768.0f), mass);
+    if (!isfinite(value) || value >= 0x1p63f || value < -0x1p63f)
+        return 1;
+    const long long integer = __float2ll_rn(value);
+    const int low = static_cast<int>(static_cast<unsigned>(static_cast<unsigned long long>(integer)));
+    return static_cast<std::uint16_t>(low < 1 ? 1 : (low > 32767 ? 32767 : low));
 }
 
 // -------------------------------------------------------------- attention --

@@ -163,16 +163,6 @@ __global__ void softmax_tree_kernel(const std::uint16_t* __restrict__ logits,
         atomicOr(error_word, error_nonfinite);
 }
 
-__device__ __forceinline__ std::uint16_t conditional_q15(float left, float mass)
-{
-    const float value = ftz_div(ftz_mul(left, 32768.0f), mass);
-    if (!isfinite(value) || value >= 0x1p63f || value < -0x1p63f)
-        return 1;
-    const long long integer = __float2ll_rn(value);
-    const int low = static_cast<int>(static_cast<unsigned>(static_cast<unsigned long long>(integer)));
-    return static_cast<std::uint16_t>(low < 1 ? 1 : (low > 32767 ? 32767 : low));
-}
-
 __global__ void categorical_path_kernel(const float* __restrict__ tree,
                                         const std::uint16_t* __restrict__ token,
                                         const int* __restrict__ token_index, int rows,
