@@ -309,9 +309,10 @@ void TransformerEngine::predict_known(const Header& header, std::span<const std:
     auto* cond = ws_.get<std::uint16_t>("cond", static_cast<std::size_t>(trows) * 512);
     run_stack(ws_, true, trows, th, d_tmeta, max_time, tck, tcv, tstride, cond, nullptr, nullptr);
 
-    // ---- codebook stack, chunked by (frame, group) sequences of Q rows.
+    // ---- codebook stack, chunked by (frame, group) sequences of Q rows
+    // (2048 sequences per launch group bound the per-chunk scratch).
     const int sequences = F * G;
-    const int chunk = std::max(1, 2048 / 1);
+    constexpr int chunk = 2048;
     for (int first = 0; first < sequences; first += chunk)
     {
         const int count = std::min(chunk, sequences - first);
