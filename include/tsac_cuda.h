@@ -115,6 +115,17 @@ int tsac_cuda_encode_observed(tsac_cuda_context* context, const float* pcm, size
                               const tsac_cuda_encode_options* options, uint8_t** out,
                               size_t* out_bytes, uint64_t* codebook_bits, size_t codebooks);
 
+/* tsac_cuda_encode plus every symbol's bits in entropy order
+ * (visit_entropy_positions, src/format/entropy.cpp:26-55): the value an
+ * EntropyObserver's after_symbol receives for it while encoding
+ * (src/format/entropy.cpp:93-98).  *symbol_bits (free with tsac_cuda_free)
+ * holds *symbols values, the stream's symbol count; fast streams have none
+ * (NULL, 0: fast coding emits no entropy callbacks). */
+int tsac_cuda_encode_symbol_bits(tsac_cuda_context* context, const float* pcm, size_t channels,
+                                 size_t samples, ptrdiff_t channel_stride, ptrdiff_t sample_stride,
+                                 const tsac_cuda_encode_options* options, uint8_t** out,
+                                 size_t* out_bytes, uint32_t** symbol_bits, size_t* symbols);
+
 /* AudioAnalyzer::decode (include/tsac/audio_analyzer.hpp:35): stream ->
  * interleaved float PCM [sample][channel], padding retained. */
 int tsac_cuda_decode(tsac_cuda_context* context, const uint8_t* stream, size_t bytes,

@@ -164,6 +164,55 @@ def test_failures_are_errors_and_analyzer_is_reusable(analyzer):
     assert analyzer.decode(good).samples.shape == (512 * 5, 2)
 
 
+def _entropy_books(frames, batch, groups, books):
+    """Codebook of each symbol in visit_entropy_positions order (step, book,
+    lane, group; src/format/entropy.cpp:26-55)."""
+    lanes = min(batch, frames)
+    base, extra = divmod(frames, batch)
+    length = [base + (lane < extra) for lane in range(lanes)]
+    order = []
+    for step in range(max(length)):
+        for book in range(books):
+            for lane in range(lanes):
+                if step < length[lane]:
+                    order += [book] * groups
+    return np.array(order)
+
+
+@pytest.mark.parametrize("case", ["stereo_q12_b3_1s", "separate_q5_b2_0p5s", "stereo_fast_q3_0p5s"])
+def test_symbol_bits_for_observers(analyzer, case):
+    """Each symbol's bits in entropy order, what an EntropyObserver's
+    after_symbol receives: one per symbol, summing to the reference's payload
+    bit count and, per codebook, to the observed per-codebook totals; fast
+    streams have none."""
+    import ctypes
+
+    g = _golden(case)
+    pcm = synthetic.music_like(g["pcm_seed"], g["seconds"], g["channels"])
+    stream, per_symbol = analyzer.encode_symbol_bits(pcm, _options(g))
+    assert hashlib.sha256(stream).hexdigest() == g["stream_sha256"]
+    if g["method"] == 0:
+        assert per_symbol.size == 0
+        return
+    assert per_symbol.size == g["tokens"]
+    assert int(per_symbol.sum(dtype=np.int64)) == g["symbol_bits"]
+    channels, _, _ = tsac_cuda.stream_info(stream)
+    groups = channels if (g["separate"] or channels == 1) else 1
+    frames = (int(pcm.shape[0]) + 511) // 512
+    books = _entropy_books(frames, g["batch"], groups, g["codebooks"])
+    totals = (ctypes.c_uint64 * g["codebooks"])()
+    out, nbytes = ctypes.c_void_p(), ctypes.c_size_t()
+    pcm32 = np.ascontiguousarray(pcm, dtype=np.float32)
+    opts = tsac_cuda._options(_options(g))
+    tsac_cuda.check(tsac_cuda.library().tsac_cuda_encode_observed(
+        analyzer._ctx, pcm32.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(pcm32.shape[1]),
+        ctypes.c_size_t(pcm32.shape[0]), ctypes.c_ssize_t(1), ctypes.c_ssize_t(pcm32.shape[1]),
+        ctypes.byref(opts), ctypes.byref(out), ctypes.byref(nbytes), totals, ctypes.c_size_t(g["codebooks"])))
+    tsac_cuda.library().tsac_cuda_free(out)
+    expected = np.bincount(books, weights=per_symbol, minlength=g["codebooks"]).astype(np.int64)
+    assert list(expected) == list(totals)
+
+
 def test_host_thread_budget(analyzer):
     """Range coding under a host thread budget (the reference CLI's -T, 1-256)
     gives the same streams and the same decoded PCM; larger budgets are errors."""

@@ -107,6 +107,28 @@ int tsac_cuda_encode_observed(tsac_cuda_context* ctx, const float* pcm, size_t c
         });
 }
 
+int tsac_cuda_encode_symbol_bits(tsac_cuda_context* ctx, const float* pcm, size_t channels,
+                                 size_t samples, ptrdiff_t channel_stride, ptrdiff_t sample_stride,
+                                 const tsac_cuda_encode_options* opts, uint8_t** out, size_t* out_bytes,
+                                 uint32_t** symbol_bits, size_t* symbols)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            tsacb::require(ctx && out && out_bytes && symbol_bits && symbols, "null argument");
+            std::vector<std::size_t> bits;
+            std::vector<std::vector<std::uint32_t>> per_symbol;
+            auto r = tsacb::encode_batch(ctx->impl,
+                                         {pcm_input(pcm, channels, samples, channel_stride, sample_stride)},
+                                         options(opts), &bits, nullptr, &per_symbol);
+            *symbol_bits = per_symbol[0].empty() ? nullptr
+                                                 : tsacb::malloc_copy(per_symbol[0].data(), per_symbol[0].size());
+            *symbols = per_symbol[0].size();
+            *out = tsacb::malloc_copy(r[0].data(), r[0].size());
+            *out_bytes = r[0].size();
+        });
+}
+
 int tsac_cuda_decode(tsac_cuda_context* ctx, const uint8_t* stream, size_t bytes, float** out,
                      size_t* samples, unsigned* channels)
 {

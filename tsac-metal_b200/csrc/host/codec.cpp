@@ -347,23 +347,29 @@ void analyze_recordings(Context& ctx, const std::vector<PcmInput>& pcm,
 }
 
 Bytes range_code(const Header& h, std::span<const std::uint16_t> tok, const std::uint16_t* q,
-                 const Limits& limits, std::size_t* bits, std::size_t* book_bits = nullptr)
+                 const Limits& limits, std::size_t* bits, std::size_t* book_bits = nullptr,
+                 std::uint32_t* symbol_bits = nullptr)
 {
     require(limits.file_bytes >= 19, "normal framing exceeds file limit");
     RangeEncoder encoder(limits.file_bytes - 18);
+    const bool observed = book_bits || symbol_bits;
+    std::size_t index = 0;
     visit_entropy_positions(h,
                             [&](const EntropyPosition& p)
                             {
                                 // Bits of one symbol: the encoder's bit position
                                 // difference (EntropyObserver::after_symbol,
                                 // src/format/entropy.cpp:93-98).
-                                const auto before = book_bits ? encoder.bit_position() : 0;
+                                const auto before = observed ? encoder.bit_position() : 0;
                                 const unsigned token = tok[p.token_offset];
                                 const auto* path = q + p.token_offset * 10;
                                 for (int d = 0; d < 10; ++d)
                                     encoder.put(path[d], (token >> (9 - d)) & 1u);
+                                const auto used = observed ? encoder.bit_position() - before : 0;
                                 if (book_bits)
-                                    book_bits[p.codebook] += encoder.bit_position() - before;
+                                    book_bits[p.codebook] += used;
+                                if (symbol_bits)
+                                    symbol_bits[index++] = static_cast<std::uint32_t>(used);
                             });
     if (bits)
         *bits = encoder.bit_position();
@@ -429,7 +435,8 @@ Bytes pack_normal(Context& ctx, Header header, std::span<const std::uint16_t> to
 
 std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
                                 const EncodeOptions& options, std::vector<std::size_t>* bits,
-                                std::vector<std::vector<std::size_t>>* book_bits)
+                                std::vector<std::vector<std::size_t>>* book_bits,
+                                std::vector<std::vector<std::uint32_t>>* symbol_bits)
 {
     ctx.bind();
     Profile profile(ctx.stream(), "encode");
@@ -464,6 +471,13 @@ std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
         for (std::size_t i = 0; i < n; ++i)
             (*book_bits)[i].assign(headers[i].codebooks, 0);
     }
+    if (symbol_bits)
+    {
+        symbol_bits->assign(n, {});
+        for (std::size_t i = 0; i < n; ++i)
+            if (headers[i].method == 1)
+                (*symbol_bits)[i].assign(headers[i].symbol_count(), 0);
+    }
     std::vector<std::vector<std::uint16_t>> q15(n);
     for (std::size_t i = 0; i < n; ++i)
     {
@@ -486,7 +500,8 @@ std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
                      if (headers[i].method == 1)
                          out[i] = range_code(headers[i], tokens[i], q15[i].data(), ctx.limits(),
                                              bits ? &(*bits)[i] : nullptr,
-                                             book_bits ? (*book_bits)[i].data() : nullptr);
+                                             book_bits ? (*book_bits)[i].data() : nullptr,
+                                             symbol_bits ? (*symbol_bits)[i].data() : nullptr);
                  });
     profile.mark("range encode");
     return out;

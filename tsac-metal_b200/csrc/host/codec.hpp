@@ -41,9 +41,13 @@ struct DecodedAudio
 Header audio_header(const PcmInput& pcm, const EncodeOptions& options, const Limits& limits);
 
 // Batched entry points (one call = many independent recordings).
+// bits: each stream's payload bit position before termination; book_bits:
+// per-codebook sums and symbol_bits: per-symbol bits in entropy order, the
+// values an EntropyObserver's after_symbol receives (empty for fast streams).
 std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
                                 const EncodeOptions& options, std::vector<std::size_t>* bits,
-                                std::vector<std::vector<std::size_t>>* book_bits = nullptr);
+                                std::vector<std::vector<std::size_t>>* book_bits = nullptr,
+                                std::vector<std::vector<std::uint32_t>>* symbol_bits = nullptr);
 // With device_out, recording i is written to device_out[i] (interleaved,
 // channels x padded samples floats) and DecodedAudio::samples stays empty.
 std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>& streams,

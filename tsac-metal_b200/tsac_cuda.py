@@ -212,6 +212,24 @@ class CudaAnalyzer:
         data = _take(out, nbytes.value, np.uint8).tobytes()
         return (data, bits.value) if with_bits else data
 
+    def encode_symbol_bits(self, pcm: np.ndarray, options: EncodeOptions | None = None):
+        """encode() plus each symbol's bits in entropy order (what an
+        EntropyObserver's after_symbol receives); an empty array for fast streams."""
+        pcm = np.asarray(pcm, dtype=np.float32)
+        if pcm.ndim == 1:
+            pcm = pcm[:, None]
+        samples, channels = pcm.shape
+        out, per_symbol = ctypes.c_void_p(), ctypes.c_void_p()
+        nbytes, count = ctypes.c_size_t(), ctypes.c_size_t()
+        opts = _options(options)
+        check(library().tsac_cuda_encode_symbol_bits(
+            self._ctx, pcm.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(channels),
+            ctypes.c_size_t(samples), ctypes.c_ssize_t(pcm.strides[1] // 4),
+            ctypes.c_ssize_t(pcm.strides[0] // 4), ctypes.byref(opts), ctypes.byref(out),
+            ctypes.byref(nbytes), ctypes.byref(per_symbol), ctypes.byref(count)))
+        data = _take(out, nbytes.value, np.uint8).tobytes()
+        return data, _take(per_symbol, count.value, np.uint32)
+
     def decode(self, stream: bytes) -> PcmAudio:
         out = ctypes.c_void_p()
         samples, channels = ctypes.c_size_t(), ctypes.c_uint()
