@@ -14,9 +14,15 @@
 #include "scalar/pipeline.hpp"
 #include "tsac/scalar_analyzer.hpp"
 #include "weights/normalization.hpp"
+#include "weights/preparation.hpp"
 
 #include <cstdlib>
 #include <cstring>
+
+namespace tsac
+{
+std::uint16_t nearest_rvq_index(std::span<const float, 8>, std::span<const float>);
+}
 
 namespace
 {
@@ -424,6 +430,46 @@ int ref_conv1d(std::size_t input_channels, std::size_t output_channels, std::siz
                                       {input_channels, frames, 1});
             std::memcpy(out, r.values.data(), r.values.size() * 4);
             *out_frames = r.shape.frames;
+        });
+}
+
+// A RangeEncoder stream of `count` symbols, each coded by encode_categorical
+// (src/format/categorical.cpp:91-117) over its 1024 probabilities.
+int ref_encode_categorical(const float* probabilities, const std::uint16_t* symbols, std::size_t count,
+                           std::uint8_t** out, std::size_t* out_bytes)
+{
+    return guarded(
+        [&]
+        {
+            tsac::RangeEncoder encoder;
+            for (std::size_t i = 0; i < count; ++i)
+                tsac::encode_categorical(encoder, std::span<const float>(probabilities + i * 1024, 1024),
+                                         symbols[i]);
+            const auto bytes = encoder.finish();
+            *out = copy_out(bytes);
+            *out_bytes = bytes.size();
+        });
+}
+
+// nearest_rvq_index (src/common/rvq.cpp:126-146) over 1024 search vectors.
+std::uint16_t ref_rvq_nearest(const float* projected8, const float* search)
+{
+    return tsac::nearest_rvq_index(std::span<const float, 8>(projected8, 8),
+                                   std::span<const float>(search, 1024 * 8));
+}
+
+// project_codebook, fused (src/weights/preparation.cpp:95-114): codebook
+// [1024][8], weights [1024][8], bias [1024] -> out [1024].
+int ref_rvq_project(std::uint16_t index, const float* codebook, const float* weights, const float* bias,
+                    float* out)
+{
+    return guarded(
+        [&]
+        {
+            tsac::weights::project_codebook(index, std::span<const float>(codebook, 1024 * 8),
+                                            std::span<const float>(weights, 1024 * 8),
+                                            std::span<const float>(bias, 1024), std::span<float>(out, 1024),
+                                            true);
         });
 }
 

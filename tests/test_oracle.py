@@ -184,3 +184,29 @@ def test_snake_matches_reference():
     oracle().oracle_snake(ptr(x), channels, frames, ptr(a), ptr(y0))
     ref_check(ref().ref_snake(ptr(x), c_size_t(channels), c_size_t(frames), ptr(a), ptr(y1)))
     assert np.array_equal(y0.view(np.uint32), y1.view(np.uint32))
+
+
+def test_rvq_nearest_and_projection_match_reference():
+    """nearest_rvq_index (normalised query, ordered 8-FMA similarities, strict >
+    so the lowest index wins ties) and the fused codebook projection."""
+    lib_o, lib_r = oracle(), ref()
+    lib_o.oracle_rvq_nearest.restype = ctypes.c_uint16
+    lib_r.ref_rvq_nearest.restype = ctypes.c_uint16
+    search = rng.standard_normal((1024, 8)).astype(np.float32)
+    search /= np.linalg.norm(search, axis=1, keepdims=True)
+    search[900] = search[5]  # an exact tie: index 5 must win
+    queries = [rng.standard_normal(8).astype(np.float32) * s for s in (1e-3, 1.0, 40.0)]
+    queries += [search[5] * np.float32(3.0), np.zeros(8, np.float32), search[1023].copy()]
+    for q in queries:
+        q = np.ascontiguousarray(q, dtype=np.float32)
+        want = lib_r.ref_rvq_nearest(ptr(q), ptr(search))
+        assert lib_o.oracle_rvq_nearest(ptr(q), ptr(search)) == want
+    assert lib_r.ref_rvq_nearest(ptr(np.ascontiguousarray(search[5] * np.float32(3.0))), ptr(search)) == 5
+    codebook = rng.standard_normal((1024, 8)).astype(np.float32)
+    weights = (rng.standard_normal((1024, 8)) / 3).astype(np.float32)
+    bias = (rng.standard_normal(1024) * 0.1).astype(np.float32)
+    for index in (0, 17, 1023):
+        y0, y1 = np.zeros(1024, np.float32), np.zeros(1024, np.float32)
+        lib_o.oracle_rvq_project(ctypes.c_uint16(index), ptr(codebook), ptr(weights), ptr(bias), ptr(y0))
+        ref_check(lib_r.ref_rvq_project(ctypes.c_uint16(index), ptr(codebook), ptr(weights), ptr(bias), ptr(y1)))
+        assert np.array_equal(y0.view(np.uint32), y1.view(np.uint32))

@@ -81,3 +81,40 @@ def test_symbol_outside_alphabet_rejected():
     masses = np.zeros((1, 1023), np.float32)
     with pytest.raises(tsac_cuda.TsacError, match="alphabet"):
         encode(masses, np.array([1024], np.uint16))
+
+
+def test_host_coder_matches_reference_encode_categorical():
+    """The library's host coder over heap masses built with the reference's
+    probability_sum (the oracle's restatement, pinned separately) writes the
+    same bytes as the reference's own encode_categorical over the
+    probabilities, and decodes that stream back."""
+    from support import oracle, ptr, ref, ref_check
+
+    rng = np.random.default_rng(7)
+    count = 24
+    probabilities = np.zeros((count, 1024), np.float32)
+    symbols = np.zeros(count, np.uint16)
+    for i in range(count):
+        logits = rng.standard_normal(1024) * rng.choice([0.5, 3.0, 12.0])
+        p = np.exp(logits - logits.max())
+        p = (p / p.sum()).astype(np.float32)
+        p[rng.random(1024) < 0.02] = np.float32(1e-41)  # subnormals exercise the FTZ sums
+        probabilities[i] = p
+        symbols[i] = rng.choice(1024, p=p.astype(np.float64) / p.astype(np.float64).sum())
+    symbols[0], symbols[1] = 0, 1023
+    lib = oracle()
+    masses = np.zeros((count, 1023), np.float32)
+    for i in range(count):
+        row = probabilities[i]
+        for depth in range(10):
+            width = 1024 >> depth
+            for k in range(1 << depth):
+                left = np.ascontiguousarray(row[k * width:k * width + width // 2])
+                masses[i, (1 << depth) - 1 + k] = lib.oracle_probability_sum(ptr(left), left.size)
+    out, size = ctypes.c_void_p(), ctypes.c_size_t()
+    ref_check(ref().ref_encode_categorical(ptr(probabilities), ptr(symbols), ctypes.c_size_t(count),
+                                           ctypes.byref(out), ctypes.byref(size)))
+    reference_stream = ctypes.string_at(out, size.value)
+    ref().ref_free(out)
+    assert encode(masses, symbols) == reference_stream
+    assert np.array_equal(decode(reference_stream, masses), symbols)
