@@ -34,6 +34,7 @@ def test_help_and_usage_exit_1():
     (["--batch_size"], "option '--batch_size' must have an argument"),
     (["z", "a", "b"], "unknown command: z"),
     (["--metal", "c", "a", "b"], "Metal execution is not available"),
+    (["-T", "257", "c", "a", "b"], "CPU thread count exceeds supported limit (256)"),
 ])
 def test_rejected_arguments(args, message):
     r = run(*args)

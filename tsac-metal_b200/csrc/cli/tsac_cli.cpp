@@ -482,6 +482,10 @@ Bytes decompress(Context& c, const Bytes& stream, const Options& options)
 
 int run(const Options& options)
 {
+    // The reference's analyzer rejects a thread budget above 256 when it is
+    // constructed, before any file is read (src/apple-arm/audio_analyzer.cpp:93).
+    if (options.threads > 256)
+        throw Error("CPU thread count exceeds supported limit (256)");
     Context c;
     const auto models = options.models.empty() ? default_models() : std::filesystem::path(options.models);
     check(tsac_cuda_context_create(models.c_str(), options.device, &c.ctx));
