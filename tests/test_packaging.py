@@ -92,3 +92,29 @@ def test_packer_matches_reference_packer(tmp_path):
         assert filecmp.cmp(ours / name, theirs / name, shallow=False), name
     total = sum((ours / n).stat().st_size for n in ours_files if n.endswith(".weights"))
     assert total == 317_259_776
+
+
+def _generate_package(args):
+    cache, seed = args
+    import os
+
+    os.environ["TSAC_B200_CACHE"] = cache
+    import tsac_cuda
+
+    return str(tsac_cuda.seeded_package(seed))
+
+
+@pytest.mark.slow
+def test_seeded_package_concurrent_generation(tmp_path):
+    """One process per GPU on a fresh host may ask for the seeded package at
+    once: one generates it, the others wait and reuse it, and no partial
+    directory is left behind."""
+    import multiprocessing
+
+    with multiprocessing.get_context("spawn").Pool(4) as pool:
+        paths = pool.map(_generate_package, [(str(tmp_path), 3)] * 4)
+    package = tmp_path / "seed3" / "package"
+    assert set(paths) == {str(package)}
+    assert (package / "weights-manifest.cmake").exists()
+    assert len(list(package.glob("*.weights"))) == 20
+    assert not list((tmp_path / "seed3").glob("package.tmp*"))

@@ -12,6 +12,7 @@ import ctypes
 import dataclasses
 import os
 import pathlib
+import shutil
 import threading
 
 import numpy as np
@@ -76,16 +77,32 @@ def cache_root() -> pathlib.Path:
 
 
 def seeded_package(seed: int = 0) -> pathlib.Path:
-    """Directory of the seeded 20-file package (generated once, then cached)."""
-    package = cache_root() / f"seed{seed}" / "package"
+    """Directory of the seeded 20-file package (generated once, then cached).
+
+    Safe under concurrent callers (one process per GPU on a fresh host): an
+    exclusive lock on a file beside the cache serialises generation, the
+    package is published by renaming a finished directory, and a process that
+    waited finds it done."""
+    import fcntl
+
+    base = cache_root() / f"seed{seed}"
+    package = base / "package"
     marker = package / "weights-manifest.cmake"
     if marker.exists():
         return package
-    source = cache_root() / f"seed{seed}" / "source"
-    tmp = package.with_name(f"package.tmp{os.getpid()}")
-    write_seeded_sources(source, seed)
-    pack_models(source, tmp)
-    if not marker.exists():
+    base.mkdir(parents=True, exist_ok=True)
+    with open(base / "generate.lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)  # released when the file closes, or the process ends
+        if marker.exists():
+            return package
+        source = base / "source"
+        tmp = base / f"package.tmp{os.getpid()}"
+        if tmp.exists():
+            shutil.rmtree(tmp)
+        if package.exists():  # left by an interrupted earlier attempt
+            shutil.rmtree(package)
+        write_seeded_sources(source, seed)
+        pack_models(source, tmp)
         tmp.rename(package)
     return package
 
