@@ -14,7 +14,8 @@ Workloads
            (CudaAnalyzer.encode_batch / decode_batch: PCM H2D, streams and
            decoded PCM D2H inside the timed region; min(K, 2) steps).  Clips:
            synthetic.music_like with seeds rank*100000 + i; weights: seeded
-           package 0.  Default B = 48 clips per GPU (the decoder's Transformer
+           package 0.  Default B = 64 clips per GPU, so an 8-GPU step codes
+           exactly cfg4's box batch of 512 clips (the decoder's Transformer
            steps are latency-bound, so throughput grows with the batch).  The
            timed steps sit in the NVTX range "timed".
   qlinear  cfg1 quantized-linear microbench (aggregate HBM GB/s).
@@ -549,7 +550,7 @@ def main():
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--workload", choices=["codec", "qlinear", "frontend"], default="codec")
-    parser.add_argument("--clips", type=int, default=48, help="clips per GPU per step")
+    parser.add_argument("--clips", type=int, default=64, help="clips per GPU per step (8 x 64 = cfg4's 512)")
     parser.add_argument("--seconds", type=float, default=CLIP_SECONDS,
                         help="clip length (30 s is the benchmark; shorter for profiling runs)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
