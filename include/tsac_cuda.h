@@ -273,6 +273,8 @@ int tsac_cuda_qlinear(const int8_t* weights, const float* weight_scales, const f
  * (1,048,576, e.g. 256 columns of 4096 inputs); larger calls fail with
  * TSAC_CUDA_ERROR.  The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress) and should come before any stream capture.
+ * That address belongs to the device's primary context, so do not use this
+ * entry point on a device after cudaDeviceReset in the same process.
  * All calls share the array, so calls that overlap on the GPU race; serialise
  * them.  Other arguments and results are those of tsac_cuda_qlinear. */
 size_t tsac_cuda_qlinear_noalloc_max_elements(void);

@@ -503,3 +503,23 @@ size_t oracle_categorical_path(const float* p, size_t n, size_t symbol, uint16_t
     }
     return nodes;
 }
+
+/* Left-child masses of the 1023 bisection nodes of each 1024-entry row, heap
+ * order (node i's children at 2i+1, 2i+2): node (depth d, index k) covers the
+ * aligned range [k*w, (k+1)*w) with w = 1024 >> d, and its left mass is
+ * probability_sum over the first half of that range, as encode_categorical
+ * sums it (src/format/categorical.cpp:91-117). */
+void oracle_bisection_masses(const float* p, size_t rows, float* out)
+{
+    for (size_t r = 0; r < rows; ++r)
+    {
+        const float* row = p + r * 1024;
+        float* heap = out + r * 1023;
+        for (unsigned depth = 0; depth < 10; ++depth)
+        {
+            const size_t width = (size_t)1024 >> depth;
+            for (size_t k = 0; k < ((size_t)1 << depth); ++k)
+                heap[((size_t)1 << depth) - 1 + k] = oracle_probability_sum(row + k * width, width / 2);
+        }
+    }
+}

@@ -20,6 +20,7 @@ float oracle_float(uint16_t x);
 float oracle_flush(float x);
 float oracle_exp(float z);
 float oracle_probability_sum(const float* x, size_t n);
+void oracle_bisection_masses(const float* p, size_t rows, float* out);
 uint16_t oracle_conditional_q15(float left, float mass);
 
 void oracle_bf8l(const float* x, size_t n, int8_t* q, uint16_t* scales);

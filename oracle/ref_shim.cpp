@@ -546,3 +546,147 @@ int ref_pack_normal(const char* package, unsigned channels, unsigned groups, uns
         });
 }
 }
+
+extern "C"
+{
+// pack_fast (src/format/container.cpp:105-135): a method-0 stream of tokens
+// [frame][group][book], 10 bits each.
+int ref_pack_fast(unsigned channels, unsigned groups, unsigned books, std::size_t frames,
+                  const std::uint16_t* tokens, std::uint8_t** out, std::size_t* out_bytes)
+{
+    return guarded(
+        [&]
+        {
+            tsac::Header header;
+            header.method = 0;
+            header.model_channels = static_cast<std::uint8_t>(channels);
+            header.groups = static_cast<std::uint8_t>(groups);
+            header.codebooks = static_cast<std::uint8_t>(books);
+            header.frames = frames;
+            header.batch = 1;
+            const auto bytes =
+                tsac::pack_fast(header, std::span<const std::uint16_t>(tokens, header.symbol_count()));
+            *out = copy_out(bytes);
+            *out_bytes = bytes.size();
+        });
+}
+}
+
+namespace
+{
+// The five prepared models ScalarAnalyzer builds inside every encode/decode
+// call (src/scalar/audio_analyzer.cpp:14-63), built once for one (variant,
+// codebooks) so that a timing loop measures coding, not model preparation.
+struct RefSession
+{
+    tsac::ModelDirectory directory;
+    tsac::ModelVariant variant;
+    unsigned books;
+    tsac::scalar::DacAnalysis analysis;
+    tsac::scalar::RvqEncoder encoder;
+    tsac::scalar::CpuTransformer transformer;
+    tsac::RvqDecoder decoder;
+    tsac::scalar::DacSynthesis synthesis;
+
+    RefSession(const char* package, unsigned channels, unsigned codebooks)
+        : directory(package),
+          variant(channels == 1 ? tsac::ModelVariant::mono : tsac::ModelVariant::stereo),
+          books(codebooks),
+          analysis(tsac::scalar::DacAnalysis::from_model(tsac::DacAnalysisModel(directory, variant))),
+          encoder(tsac::scalar::RvqEncoder::from_model(tsac::RvqEncoderModel(
+              directory, variant, tsac::RvqInputLayout::input_major, codebooks))),
+          transformer(tsac::scalar::CpuTransformer::from_model(
+              tsac::TransformerModel(directory, variant, codebooks))),
+          decoder(tsac::RvqDecoder::from_model(tsac::RvqDecoderModel(directory, variant, codebooks))),
+          synthesis(
+              tsac::scalar::DacSynthesis::from_model(tsac::DacSynthesisModel(directory, variant)))
+    {
+    }
+};
+} // namespace
+
+extern "C"
+{
+int ref_session_create(const char* package, unsigned channels, unsigned codebooks, void** out)
+{
+    return guarded([&] { *out = new RefSession(package, channels, codebooks); });
+}
+
+void ref_session_destroy(void* session)
+{
+    delete static_cast<RefSession*>(session);
+}
+
+// The body of ScalarAnalyzer::encode (src/scalar/audio_analyzer.cpp:14-39) on
+// the session's prepared models; the options must select the session's
+// variant and codebook count.
+int ref_session_encode(void* handle, const float* interleaved, std::size_t channels,
+                       std::size_t samples, int method, int batch, std::uint8_t** out,
+                       std::size_t* out_bytes)
+{
+    return guarded(
+        [&]
+        {
+            auto& s = *static_cast<RefSession*>(handle);
+            const tsac::Limits limits{};
+            const auto pcm = tsac::interleaved_pcm(
+                std::span<const float>(interleaved, channels * samples), channels);
+            const auto header =
+                tsac::detail::audio_header(pcm, options(method, s.books, 0, batch), limits);
+            if (tsac::detail::audio_variant(header) != s.variant || header.codebooks != s.books)
+            {
+                throw std::runtime_error("options do not match the prepared session");
+            }
+            const auto padded = tsac::detail::padded_audio(pcm, header, limits);
+            const auto tokens = tsac::detail::analyze_audio(
+                padded, header, s.analysis, s.encoder, tsac::detail::audio_chunk_frames(400, limits),
+                limits);
+            tsac::Bytes bytes;
+            if (header.method == 0)
+            {
+                bytes = tsac::pack_fast(header, tokens, limits);
+            }
+            else
+            {
+                tsac::TransformerPredictor predictor(s.transformer, limits);
+                bytes = tsac::pack_normal(header, tokens, predictor, limits, {});
+            }
+            *out = copy_out(bytes);
+            *out_bytes = bytes.size();
+        });
+}
+
+// The body of ScalarAnalyzer::decode (src/scalar/audio_analyzer.cpp:41-63).
+int ref_session_decode(void* handle, const std::uint8_t* stream, std::size_t bytes, float** out,
+                       std::size_t* out_samples, unsigned* out_channels)
+{
+    return guarded(
+        [&]
+        {
+            auto& s = *static_cast<RefSession*>(handle);
+            const tsac::Limits limits{};
+            const std::span<const std::uint8_t> view(stream, bytes);
+            const auto header = tsac::parse_header(view, limits);
+            if (tsac::detail::audio_variant(header) != s.variant || header.codebooks != s.books)
+            {
+                throw std::runtime_error("stream does not match the prepared session");
+            }
+            std::vector<std::uint16_t> tokens;
+            if (header.method == 0)
+            {
+                tokens = tsac::unpack_fast(view, limits);
+            }
+            else
+            {
+                tsac::TransformerPredictor predictor(s.transformer, limits);
+                tokens = tsac::unpack_normal(view, predictor, limits, {});
+            }
+            const auto audio = tsac::detail::synthesize_audio(
+                tokens, header, s.decoder, s.synthesis, tsac::detail::audio_chunk_frames(400, limits),
+                limits);
+            *out = copy_out(audio.samples);
+            *out_samples = audio.samples.size();
+            *out_channels = audio.channels;
+        });
+}
+}

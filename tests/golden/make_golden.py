@@ -9,11 +9,15 @@ sources exist; the fixtures then travel with the repository.
     python tests/golden/make_golden.py --cases short
     python tests/golden/make_golden.py --cases cfg0_stereo_30s
     python tests/golden/make_golden.py --cases known
+    python tests/golden/make_golden.py --cases cfg4 --jobs 6
+    python tests/golden/make_golden.py --cases cfg3_mono_60s
 """
 from __future__ import annotations
 
 import argparse
+import concurrent.futures
 import ctypes
+import multiprocessing
 import hashlib
 import json
 import pathlib
@@ -56,6 +60,79 @@ KNOWN = {
     "known_1026_1_1": (1026, 1, 1, 2, 1),
     "known_mono_40_2_1": (40, 2, 1, 1, 9),
 }
+
+
+# cfg4 box batch: 30 s joint-stereo clips coded at q=12, batch 3, encode only
+# (stream bytes are the contract; decoding a byte-identical stream is checked
+# by its token CRC).  Seeds are bench.py's clip seeds rank*100000 + i: clips
+# 1..8 of rank 0 and clip 0 of ranks 1..7, so every rank of an 8-GPU bench
+# byte-checks at least one clip.
+CFG4_SEEDS = list(range(1, 9)) + [r * 100000 for r in range(1, 8)]
+CFG4_DIR = HERE / "cfg4"
+# cfg3 DAC-only decode: 60 s mono, 9 books, tokens uniform in [0, 1024) from
+# seed 3, packed as a fast (method 0) stream and decoded by the reference.
+CFG3 = {"seconds": 60.0, "books": 9, "token_seed": 3}
+
+
+def cfg3_tokens() -> np.ndarray:
+    frames = -(-int(round(CFG3["seconds"] * 44100)) // 512)
+    rng = np.random.default_rng(CFG3["token_seed"])
+    return rng.integers(0, 1024, size=frames * CFG3["books"]).astype(np.uint16)
+
+
+def run_cfg3(package: pathlib.Path) -> dict:
+    lib = ref_library()
+    tokens = cfg3_tokens()
+    frames = tokens.size // CFG3["books"]
+    out = ctypes.POINTER(ctypes.c_uint8)()
+    nbytes = ctypes.c_size_t()
+    ref_check(lib, lib.ref_pack_fast(1, 1, CFG3["books"], ctypes.c_size_t(frames),
+                                     tokens.ctypes.data_as(ctypes.c_void_p), ctypes.byref(out),
+                                     ctypes.byref(nbytes)))
+    stream = bytes(out[: nbytes.value])
+    lib.ref_free(out)
+    pcm_out = ctypes.POINTER(ctypes.c_float)()
+    ns, nc = ctypes.c_size_t(), ctypes.c_uint()
+    t0 = time.time()
+    ref_check(lib, lib.ref_decode(str(package).encode(), stream, ctypes.c_size_t(len(stream)),
+                                  ctypes.byref(pcm_out), ctypes.byref(ns), ctypes.byref(nc)))
+    decode_s = time.time() - t0
+    decoded = np.ctypeslib.as_array(pcm_out, shape=(ns.value,)).copy()
+    lib.ref_free(pcm_out)
+    record = {"case": "cfg3_mono_60s", "frames": frames, "books": CFG3["books"], "channels": 1,
+              "method": 0, "tokens": "numpy default_rng(3).integers(0, 1024, frames*books)",
+              "weights_seed": 0, "pack_id": tsac_cuda.SEEDED_PACK_ID,
+              "stream_bytes": len(stream), "stream_sha256": sha(stream),
+              "pcm_samples": int(decoded.size), "pcm_channels": nc.value,
+              "pcm_sha256": sha(decoded.astype("<f4").tobytes()),
+              "pcm_max_abs": float(np.abs(decoded).max()),
+              "pcm_head": decoded[: 4096].astype(float).tolist(),
+              "reference_decode_seconds": round(decode_s, 3)}
+    (HERE / "cfg3_mono_60s.tsac").write_bytes(stream)
+    (HERE / "cfg3_mono_60s.json").write_text(json.dumps(record, indent=1) + "\n")
+    return record
+
+
+def run_cfg4(seed: int) -> dict:
+    package = tsac_cuda.seeded_package(0)
+    lib = ref_library()
+    pcm = synthetic.music_like(seed, 30.0, 2)
+    out = ctypes.POINTER(ctypes.c_uint8)()
+    nbytes, bits = ctypes.c_size_t(), ctypes.c_size_t()
+    t0 = time.time()
+    ref_check(lib, lib.ref_encode(str(package).encode(), pcm.ctypes.data_as(ctypes.c_void_p),
+                                  ctypes.c_size_t(2), ctypes.c_size_t(pcm.shape[0]), 1, 12, 0, 3,
+                                  ctypes.byref(out), ctypes.byref(nbytes), ctypes.byref(bits)))
+    encode_s = time.time() - t0
+    stream = bytes(out[: nbytes.value])
+    lib.ref_free(out)
+    record = {"pcm_seed": seed, "seconds": 30.0, "channels": 2, "method": 1, "codebooks": 12,
+              "batch": 3, "weights_seed": 0, "pack_id": tsac_cuda.SEEDED_PACK_ID,
+              "stream_bytes": len(stream), "stream_sha256": sha(stream),
+              "symbol_bits": bits.value, "reference_encode_seconds": round(encode_s, 3)}
+    CFG4_DIR.mkdir(exist_ok=True)
+    (CFG4_DIR / f"seed_{seed}.json").write_text(json.dumps(record, indent=1) + "\n")
+    return record
 
 
 def known_tokens(frames, groups, books):
@@ -153,12 +230,27 @@ def run_case(name: str, package: pathlib.Path) -> dict:
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--cases", default="short",
-                        help="'short', 'all' or a comma-separated list of case names")
+                        help="'short', 'all', 'known', 'cfg4' or a comma-separated list of case names")
+    parser.add_argument("--jobs", type=int, default=1, help="worker processes for 'cfg4'")
     args = parser.parse_args()
+    if args.cases == "cfg4":
+        tsac_cuda.seeded_package(0)
+        todo = [s for s in CFG4_SEEDS if not (CFG4_DIR / f"seed_{s}.json").exists()]
+        ctx = multiprocessing.get_context("spawn")
+        with concurrent.futures.ProcessPoolExecutor(args.jobs, mp_context=ctx) as pool:
+            for r in pool.map(run_cfg4, todo):
+                print("cfg4 seed", r["pcm_seed"], r["stream_bytes"], r["stream_sha256"][:16],
+                      r["reference_encode_seconds"], flush=True)
+        return
     names = SHORT if args.cases == "short" else list(KNOWN) if args.cases == "known" \
         else list(CASES) + list(KNOWN) if args.cases == "all" else args.cases.split(",")
     package = tsac_cuda.seeded_package(0)
     for name in names:
+        if name == "cfg3_mono_60s":
+            r = run_cfg3(package)
+            print(name, r["stream_bytes"], r["pcm_sha256"][:16], r["reference_decode_seconds"],
+                  flush=True)
+            continue
         if name in KNOWN:
             r = run_known(name, package)
             print(name, r["stream_bytes"], r["stream_sha256"][:16], r["reference_seconds"],

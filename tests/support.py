@@ -41,6 +41,7 @@ def oracle() -> ctypes.CDLL:
     lib.oracle_exp.argtypes = [ctypes.c_float]
     lib.oracle_probability_sum.restype = ctypes.c_float
     lib.oracle_probability_sum.argtypes = [c_void_p, c_size_t]
+    lib.oracle_bisection_masses.argtypes = [c_void_p, c_size_t, c_void_p]
     lib.oracle_conditional_q15.restype = ctypes.c_uint16
     lib.oracle_conditional_q15.argtypes = [ctypes.c_float, ctypes.c_float]
     lib.oracle_gelu.restype = ctypes.c_uint16

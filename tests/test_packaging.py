@@ -74,6 +74,45 @@ def test_token_crc_changes_with_every_token():
         assert tsac_cuda.token_crc32(t) != base
 
 
+def _crc32_msb_first(tokens):
+    """The token CRC restated bit by bit: polynomial 0x04c11db7, MSB first,
+    initial ~0, no final xor, over each token's four little-endian bytes."""
+    reg = 0xFFFFFFFF
+    for t in tokens.tolist():
+        for byte in int(t).to_bytes(4, "little"):
+            reg ^= byte << 24
+            for _ in range(8):
+                reg = ((reg << 1) ^ 0x04C11DB7 if reg & 0x80000000 else reg << 1) & 0xFFFFFFFF
+    return reg
+
+
+@pytest.mark.parametrize("count", [0, 1, 3, 257, 1000])
+def test_token_crc_matches_bitwise_definition(count):
+    tokens = np.random.default_rng(count).integers(0, 1024, count).astype(np.uint16)
+    assert tsac_cuda.token_crc32(tokens) == _crc32_msb_first(tokens)
+
+
+@pytest.mark.parametrize("groups,books,frames", [(1, 1, 1), (1, 9, 7), (2, 12, 3), (3, 5, 11),
+                                                 (1, 12, 64), (5, 3, 2)])
+def test_fast_unpack_of_reference_packed_streams(groups, books, frames):
+    """Streams packed by the reference's pack_fast (every token count modulo
+    4, so every tail of the 40-bit words) unpack to the same tokens."""
+    import ctypes
+
+    from support import ptr, ref, ref_check
+
+    channels = 2 if books > 9 else 1
+    tokens = np.random.default_rng(groups * 100 + books * 10 + frames).integers(
+        0, 1024, frames * groups * books).astype(np.uint16)
+    out, size = ctypes.POINTER(ctypes.c_uint8)(), ctypes.c_size_t()
+    ref_check(ref().ref_pack_fast(channels, groups, books, ctypes.c_size_t(frames), ptr(tokens),
+                                  ctypes.byref(out), ctypes.byref(size)))
+    stream = bytes(out[: size.value])
+    ref().ref_free(out)
+    assert np.array_equal(tsac_cuda.unpack_fast(stream), tokens)
+    assert tsac_cuda.stream_info(stream)[2] == tokens.size
+
+
 @pytest.mark.slow
 def test_packer_matches_reference_packer(tmp_path):
     if not REF_PACKER.exists():

@@ -118,3 +118,34 @@ def test_host_coder_matches_reference_encode_categorical():
     ref().ref_free(out)
     assert encode(masses, symbols) == reference_stream
     assert np.array_equal(decode(reference_stream, masses), symbols)
+
+
+def test_long_stream_matches_reference_byte_for_byte():
+    """Thousands of symbols from very skewed and flat distributions: long runs
+    of 0xff bytes and carries into them occur many times, and the library's
+    coder (carry added into bytes already written) writes exactly the bytes
+    of the reference's encode_categorical (pending-byte carry handling)."""
+    from support import oracle, ptr, ref, ref_check
+
+    rng = np.random.default_rng(11)
+    count = 3000
+    probabilities = np.zeros((count, 1024), np.float32)
+    symbols = np.zeros(count, np.uint16)
+    for i in range(count):
+        p = rng.dirichlet(np.full(1024, rng.choice([0.005, 0.05, 1.0, 50.0])))
+        p = np.maximum(p, 1e-30).astype(np.float32)
+        probabilities[i] = p
+        # Mostly likely symbols, sometimes a very unlikely one (long codes).
+        symbols[i] = rng.integers(0, 1024) if rng.random() < 0.15 else int(np.argmax(p))
+    masses = np.zeros((count, 1023), np.float32)
+    oracle().oracle_bisection_masses(ptr(probabilities), ctypes.c_size_t(count), ptr(masses))
+    out, size = ctypes.c_void_p(), ctypes.c_size_t()
+    ref_check(ref().ref_encode_categorical(ptr(probabilities), ptr(symbols), ctypes.c_size_t(count),
+                                           ctypes.byref(out), ctypes.byref(size)))
+    reference_stream = ctypes.string_at(out, size.value)
+    ref().ref_free(out)
+    ours = encode(masses, symbols)
+    assert len(ours) == len(reference_stream) and ours == reference_stream
+    assert np.array_equal(decode(reference_stream, masses), symbols)
+    # The stream holds runs of 0xff bytes (the bytes a later carry can reach).
+    assert reference_stream.count(b"\xff\xff") > 0

@@ -193,7 +193,7 @@ int tsac_cuda_stream_info(const uint8_t* stream, size_t bytes, unsigned* channel
         [&]
         {
             tsacb::require(stream && channels && samples_per_channel, "null argument");
-            const auto h = tsacb::parse_header(tsacb::ByteView(stream, bytes));
+            const auto h = tsacb::read_header(tsacb::ByteView(stream, bytes));
             *channels = static_cast<unsigned>(h.channels());
             *samples_per_channel = h.samples_per_channel();
             if (symbols)
@@ -207,7 +207,7 @@ int tsac_cuda_stream_header_info(const uint8_t* stream, size_t bytes, tsac_cuda_
         [&]
         {
             tsacb::require(stream && out, "null argument");
-            const auto h = tsacb::parse_header(tsacb::ByteView(stream, bytes));
+            const auto h = tsacb::read_header(tsacb::ByteView(stream, bytes));
             out->method = h.method;
             out->model_channels = h.model_channels;
             out->groups = h.groups;
@@ -223,7 +223,7 @@ int tsac_cuda_unpack_fast(const uint8_t* stream, size_t bytes, uint16_t** tokens
         [&]
         {
             tsacb::require(stream && tokens && count, "null argument");
-            const auto values = tsacb::unpack_fast(tsacb::ByteView(stream, bytes));
+            const auto values = tsacb::fast_tokens(tsacb::ByteView(stream, bytes));
             *tokens = tsacb::malloc_copy(values.data(), values.size());
             *count = values.size();
         });
@@ -236,11 +236,11 @@ int tsac_cuda_range_encode_tree(const float* masses, const uint16_t* symbols, si
         [&]
         {
             tsacb::require(out && out_bytes && (count == 0 || (masses && symbols)), "null argument");
-            tsacb::RangeEncoder encoder;
+            tsacb::RangeWriter encoder;
             for (size_t i = 0; i < count; ++i)
             {
                 tsacb::require(symbols[i] < 1024, "symbol exceeds alphabet");
-                tsacb::encode_categorical_tree(encoder, masses + i * 1023, symbols[i]);
+                tsacb::write_symbol(encoder, masses + i * 1023, symbols[i]);
             }
             const auto bytes = encoder.finish();
             *out = tsacb::malloc_copy(bytes.data(), bytes.size());
@@ -255,9 +255,9 @@ int tsac_cuda_range_decode_tree(const uint8_t* bytes, size_t size, const float* 
         [&]
         {
             tsacb::require((bytes || size == 0) && (count == 0 || (masses && symbols)), "null argument");
-            tsacb::RangeDecoder decoder(tsacb::ByteView(bytes, size));
+            tsacb::RangeReader decoder(tsacb::ByteView(bytes, size));
             for (size_t i = 0; i < count; ++i)
-                symbols[i] = tsacb::decode_categorical_tree(decoder, masses + i * 1023);
+                symbols[i] = decoder.symbol(masses + i * 1023);
         });
 }
 
@@ -342,7 +342,7 @@ int tsac_cuda_transformer_probabilities(tsac_cuda_context* ctx, unsigned channel
             h.codebooks = static_cast<std::uint8_t>(books);
             h.frames = frames;
             h.batch = static_cast<std::uint16_t>(batch);
-            tsacb::validate_header(h);
+            tsacb::check_header(h);
             std::vector<std::uint16_t> q(h.symbol_count() * 10);
             ctx->impl.transformer(channels).predict_known(
                 h, std::span<const std::uint16_t>(tokens, h.symbol_count()), q.data(),

@@ -351,10 +351,10 @@ Bytes range_code(const Header& h, std::span<const std::uint16_t> tok, const std:
                  std::uint32_t* symbol_bits = nullptr)
 {
     require(limits.file_bytes >= 19, "normal framing exceeds file limit");
-    RangeEncoder encoder(limits.file_bytes - 18);
+    RangeWriter encoder(limits.file_bytes - 18);
     const bool observed = book_bits || symbol_bits;
     std::size_t index = 0;
-    visit_entropy_positions(h,
+    for_each_entropy_position(h,
                             [&](const EntropyPosition& p)
                             {
                                 // Bits of one symbol: the encoder's bit position
@@ -374,7 +374,7 @@ Bytes range_code(const Header& h, std::span<const std::uint16_t> tok, const std:
     if (bits)
         *bits = encoder.bit_position();
     const auto payload = encoder.finish();
-    return frame_normal(h, payload);
+    return normal_stream(h, payload);
 }
 } // namespace
 
@@ -400,7 +400,7 @@ Header audio_header(const PcmInput& pcm, const EncodeOptions& options, const Lim
     {
         header.batch = select_entropy_batch(header.frames, options.entropy_batch);
     }
-    validate_header(header, limits);
+    check_header(header, limits);
     require(checked_mul(header.samples_per_channel(), channels) <= limits.tensor_elements,
             "padded PCM exceeds element limit");
     return header;
@@ -424,7 +424,7 @@ Bytes pack_normal(Context& ctx, Header header, std::span<const std::uint16_t> to
 {
     ctx.bind();
     header.method = 1;
-    validate_header(header, ctx.limits());
+    check_header(header, ctx.limits());
     require(header.frames <= 0xffffffffu, "normal frame count exceeds uint32");
     require(tokens.size() == header.symbol_count(), "normal token count does not match header");
     header.token_crc = token_crc32(tokens);
@@ -483,7 +483,7 @@ std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
     {
         if (headers[i].method == 0)
         {
-            out[i] = pack_fast(headers[i], tokens[i], ctx.limits());
+            out[i] = fast_stream(headers[i], tokens[i], ctx.limits());
             continue;
         }
         headers[i].token_crc = token_crc32(tokens[i]);
@@ -517,9 +517,9 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
     std::vector<std::vector<std::uint16_t>> tokens(n);
     for (std::size_t i = 0; i < n; ++i)
     {
-        headers[i] = parse_header(streams[i], ctx.limits());
+        headers[i] = read_header(streams[i], ctx.limits());
         if (headers[i].method == 0)
-            tokens[i] = unpack_fast(streams[i], ctx.limits());
+            tokens[i] = fast_tokens(streams[i], ctx.limits());
         else
             tokens[i].assign(headers[i].symbol_count(), 0);
     }
@@ -538,7 +538,7 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
             continue;
         auto& engine = ctx.transformer(mc);
         engine.decode_begin(hs);
-        std::vector<RangeDecoder> decoders;
+        std::vector<RangeReader> decoders;
         std::size_t steps = 0, books = 0, lanes = 0;
         for (auto i : ids)
         {
@@ -579,7 +579,7 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
                     {
                         const auto r = static_cast<std::size_t>(rows[j].recording);
                         if (r % workers == w)
-                            decoded[j] = decode_categorical_tree(decoders[r], masses + j * 1023);
+                            decoded[j] = decoders[r].symbol(masses + j * 1023);
                     }
                 };
                 if (workers > 1)
@@ -592,8 +592,7 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
                     const auto& h = headers[ids[r]];
                     const std::size_t lane_b = static_cast<std::size_t>(rows[j].lane) / h.groups;
                     const std::size_t g = static_cast<std::size_t>(rows[j].lane) % h.groups;
-                    const std::size_t base = h.frames / h.batch, extra = h.frames % h.batch;
-                    const std::size_t frame = lane_b * base + std::min(lane_b, extra) + step;
+                    const std::size_t frame = LaneSchedule(h).first_frame(lane_b) + step;
                     tokens[ids[r]][(frame * h.groups + g) * h.codebooks + book] = decoded[j];
                 }
                 const auto t2 = clock::now();
@@ -607,7 +606,7 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
             std::fprintf(stderr, "tsac_cuda decode steps %zu: predict %.1f ms, range %.1f ms, commit %.1f ms\n",
                          steps * books, t_predict, t_range, t_commit);
         for (auto i : ids)
-            verify_token_crc(headers[i], tokens[i]);
+            check_token_crc(headers[i], tokens[i]);
     }
     profile.mark("transformer + range");
     // RVQ reconstruction + DAC synthesis over chunk windows

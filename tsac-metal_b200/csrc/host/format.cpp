@@ -1,362 +1,431 @@
 #include "format.hpp"
 
+#include "range_core.hpp"
+
 #include <algorithm>
 #include <array>
 
 namespace tsacb
 {
-void validate_header(const Header& header, const Limits& limits)
+namespace
 {
-    require(header.method <= 1, "unsupported method");
-    require(header.groups > 0 && header.groups <= 127, "invalid channel groups");
-    require(header.model_channels == 1 || header.model_channels == 2, "invalid model channels");
-    require(header.codebooks > 0 && header.codebooks <= (header.model_channels == 1 ? 9 : 12),
-            "invalid codebook count");
-    require(header.method == 0 || header.batch > 0, "zero entropy batch size");
-    require(header.symbol_count() <= limits.symbols, "symbol count exceeds limit");
-    require(header.pcm16_bytes() <= limits.pcm_bytes, "decoded PCM size exceeds limit");
+constexpr std::uint32_t stream_magic = 0x4642415au; // "FBAZ"
+constexpr unsigned token_field_bits = 10;
+
+// Big-endian field of `width` bytes at `at`; short input is "truncated input".
+std::uint32_t field(ByteView bytes, std::size_t at, unsigned width)
+{
+    require(at <= bytes.size() && bytes.size() - at >= width, "truncated input");
+    std::uint32_t value = 0;
+    for (unsigned i = 0; i < width; ++i)
+    {
+        value = (value << 8) | bytes[at + i];
+    }
+    return value;
 }
 
-Header parse_header(ByteView bytes, const Limits& limits)
+void append_field(Bytes& out, std::size_t value, unsigned width)
 {
-    require(bytes.size() <= limits.file_bytes, "input exceeds file size limit");
-    require(be32(bytes, 0) == 0x4642415a, "invalid FBAZ magic");
-    require(bytes.size() >= 8, "truncated input");
-    require(bytes[4] == 0, "unsupported TSAC version");
-    Header header;
-    header.method = bytes[5];
-    header.groups = bytes[6] & 127;
-    header.model_channels = static_cast<std::uint8_t>(1 + (bytes[6] >> 7));
-    header.codebooks = bytes[7];
-    require(header.method <= 1, "unsupported TSAC method");
-    require(header.groups && header.codebooks, "zero groups or codebooks");
-    if (header.method == 0)
+    for (unsigned i = width; i-- > 0;)
     {
-        header.payload_bytes = bytes.size() - 8;
-        const auto bits_per_frame = checked_mul(checked_mul(header.groups, header.codebooks), 10);
-        const auto bits = checked_mul(header.payload_bytes, 8);
-        header.frames = bits / bits_per_frame;
-        const auto padding = bits % bits_per_frame;
-        require(padding < 8, "incomplete fast frame or excess padding");
-        if (padding)
-        {
-            require((bytes.back() & ((1u << padding) - 1)) == 0, "nonzero fast padding");
-        }
+        out.push_back(static_cast<std::uint8_t>(value >> (8 * i)));
     }
-    else
-    {
-        require(bytes.size() >= 19, "truncated normal stream");
-        header.frames = be32(bytes, 8);
-        header.batch = static_cast<std::uint16_t>((std::uint16_t(bytes[12]) << 8) | bytes[13]);
-        header.payload_offset = 14;
-        header.payload_bytes = bytes.size() - 18;
-        header.token_crc = be32(bytes, bytes.size() - 4);
-    }
-    validate_header(header, limits);
-    return header;
 }
 
-std::vector<std::uint16_t> unpack_fast(ByteView bytes, const Limits& limits)
+std::uint8_t channel_byte(const Header& h)
 {
-    const auto header = parse_header(bytes, limits);
-    require(header.method == 0, "normal-mode unpacking requires the probability model");
-    std::vector<std::uint16_t> indices;
-    indices.reserve(header.symbol_count());
-    std::uint32_t buffer = 0;
-    unsigned bits = 0;
-    for (auto byte : bytes.subspan(8))
-    {
-        buffer = (buffer << 8) | byte;
-        bits += 8;
-        while (bits >= 10)
-        {
-            bits -= 10;
-            indices.push_back(static_cast<std::uint16_t>((buffer >> bits) & 1023));
-        }
-        buffer &= (1u << bits) - 1;
-    }
-    require(indices.size() == header.symbol_count(), "fast symbol count mismatch");
-    return indices;
+    return static_cast<std::uint8_t>(h.groups | ((h.model_channels - 1) << 7));
 }
 
-Bytes pack_fast(const Header& header, std::span<const std::uint16_t> indices, const Limits& limits)
+// The first eight bytes of every stream.
+Bytes stream_prefix(const Header& h, std::uint8_t method, std::size_t reserve)
 {
-    validate_header(header, limits);
-    require(header.method == 0, "pack_fast requires method 0");
-    require(indices.size() == header.symbol_count(), "symbol count does not match header");
-    const auto payload = checked_add(checked_mul(indices.size(), 10), 7) / 8;
-    require(checked_add(payload, 8) <= limits.file_bytes, "output exceeds file size limit");
-    Bytes bytes{'F', 'B', 'A', 'Z', 0, 0,
-                static_cast<std::uint8_t>(header.groups | ((header.model_channels - 1) << 7)),
-                header.codebooks};
-    bytes.reserve(payload + 8);
-    std::uint32_t buffer = 0;
-    unsigned bits = 0;
-    for (auto index : indices)
-    {
-        require(index < 1024, "index outside 10-bit alphabet");
-        buffer = (buffer << 10) | index;
-        bits += 10;
-        while (bits >= 8)
-        {
-            bits -= 8;
-            bytes.push_back(static_cast<std::uint8_t>(buffer >> bits));
-        }
-        buffer &= (1u << bits) - 1;
-    }
-    if (bits)
-    {
-        bytes.push_back(static_cast<std::uint8_t>(buffer << (8 - bits)));
-    }
-    return bytes;
+    Bytes out;
+    out.reserve(reserve);
+    append_field(out, stream_magic, 4);
+    out.push_back(0); // version
+    out.push_back(method);
+    out.push_back(channel_byte(h));
+    out.push_back(h.codebooks);
+    return out;
 }
 
-std::uint32_t token_crc32(std::span<const std::uint16_t> indices)
+// Fast streams carry no frame count: the payload holds whole frames of
+// groups x codebooks 10-bit fields and at most 7 zero bits of padding.
+void fast_geometry(Header& h, ByteView stream)
 {
-    // CRC-32 (poly 0x04c11db7, MSB first, init ~0, no final xor) over the four
-    // little-endian bytes of each token widened to 32 bits; table-driven.
-    static const auto table = []
+    h.payload_bytes = stream.size() - 8;
+    const auto frame_bits = checked_mul(checked_mul(h.groups, h.codebooks), token_field_bits);
+    const auto payload_bits = checked_mul(h.payload_bytes, 8);
+    h.frames = payload_bits / frame_bits;
+    const auto slack = static_cast<unsigned>(payload_bits % frame_bits);
+    require(slack < 8, "incomplete fast frame or excess padding");
+    require(slack == 0 || (stream.back() & ((1u << slack) - 1u)) == 0, "nonzero fast padding");
+}
+
+void normal_fields(Header& h, ByteView stream)
+{
+    require(stream.size() >= 19, "truncated normal stream");
+    h.frames = field(stream, 8, 4);
+    h.batch = static_cast<std::uint16_t>(field(stream, 12, 2));
+    h.payload_offset = 14;
+    h.payload_bytes = stream.size() - 18;
+    h.token_crc = field(stream, stream.size() - 4, 4);
+}
+
+// CRC-32 tables for four bytes at a time: table[k][b] is the register after
+// byte b followed by k zero bytes, starting from zero (MSB-first, 0x04c11db7).
+using CrcTables = std::array<std::array<std::uint32_t, 256>, 4>;
+const CrcTables& crc_tables()
+{
+    static const CrcTables tables = []
     {
-        std::array<std::uint32_t, 256> t{};
-        for (std::uint32_t i = 0; i < 256; ++i)
+        CrcTables t{};
+        for (std::uint32_t b = 0; b < 256; ++b)
         {
-            std::uint32_t c = i << 24;
-            for (int b = 0; b < 8; ++b)
+            std::uint32_t reg = b << 24;
+            for (int i = 0; i < 8; ++i)
             {
-                c = (c << 1) ^ ((c & 0x80000000u) ? 0x04c11db7u : 0u);
+                reg = (reg << 1) ^ ((0u - (reg >> 31)) & 0x04c11db7u);
             }
-            t[i] = c;
+            t[0][b] = reg;
+        }
+        for (int k = 1; k < 4; ++k)
+        {
+            for (std::uint32_t b = 0; b < 256; ++b)
+            {
+                const auto prev = t[k - 1][b];
+                t[k][b] = (prev << 8) ^ t[0][prev >> 24];
+            }
         }
         return t;
     }();
-    std::uint32_t crc = 0xffffffff;
-    for (auto index : indices)
+    return tables;
+}
+
+struct HostMath
+{
+    static std::uint16_t q15(float left, float mass)
     {
-        require(index < 1024, "index outside 10-bit alphabet");
-        const std::uint32_t v = index;
-        for (unsigned shift = 0; shift < 32; shift += 8)
+        return conditional_q15(left, mass);
+    }
+    static float sub(float a, float b)
+    {
+        return ftz_sub(a, b);
+    }
+};
+} // namespace
+
+// ------------------------------------------------------------- container --
+void check_header(const Header& h, const Limits& limits)
+{
+    const unsigned most_books = h.model_channels == 1 ? 9 : 12;
+    require(h.method <= 1, "unsupported method");
+    require(h.groups >= 1 && h.groups <= 127, "invalid channel groups");
+    require(h.model_channels == 1 || h.model_channels == 2, "invalid model channels");
+    require(h.codebooks >= 1 && h.codebooks <= most_books, "invalid codebook count");
+    require(h.method == 0 || h.batch != 0, "zero entropy batch size");
+    require(h.symbol_count() <= limits.symbols, "symbol count exceeds limit");
+    require(h.pcm16_bytes() <= limits.pcm_bytes, "decoded PCM size exceeds limit");
+}
+
+Header read_header(ByteView stream, const Limits& limits)
+{
+    require(stream.size() <= limits.file_bytes, "input exceeds file size limit");
+    require(field(stream, 0, 4) == stream_magic, "invalid FBAZ magic");
+    require(stream.size() >= 8, "truncated input");
+    require(stream[4] == 0, "unsupported TSAC version");
+    Header h;
+    h.method = stream[5];
+    h.groups = stream[6] & 0x7f;
+    h.model_channels = static_cast<std::uint8_t>((stream[6] >> 7) + 1);
+    h.codebooks = stream[7];
+    require(h.method <= 1, "unsupported TSAC method");
+    require(h.groups != 0 && h.codebooks != 0, "zero groups or codebooks");
+    if (h.method == 1)
+    {
+        normal_fields(h, stream);
+    }
+    else
+    {
+        fast_geometry(h, stream);
+    }
+    check_header(h, limits);
+    return h;
+}
+
+// Four 10-bit fields are exactly five bytes, so the payload is handled in
+// 40-bit words; a final partial word is zero-filled.
+std::vector<std::uint16_t> fast_tokens(ByteView stream, const Limits& limits)
+{
+    const auto h = read_header(stream, limits);
+    require(h.method == 0, "normal-mode unpacking requires the probability model");
+    const auto count = h.symbol_count();
+    require(checked_mul(h.payload_bytes, 8) / token_field_bits == count, "fast symbol count mismatch");
+    const auto payload = stream.subspan(8);
+    std::vector<std::uint16_t> tokens(count);
+    for (std::size_t first = 0; first < count; first += 4)
+    {
+        const std::size_t at = first / 4 * 5;
+        std::uint64_t word = 0;
+        for (std::size_t b = 0; b < 5; ++b)
         {
-            crc = (crc << 8) ^ table[((crc >> 24) ^ ((v >> shift) & 255u)) & 255u];
+            word = (word << 8) | (at + b < payload.size() ? payload[at + b] : 0u);
+        }
+        for (std::size_t j = 0; j < 4 && first + j < count; ++j)
+        {
+            tokens[first + j] = static_cast<std::uint16_t>((word >> (30 - 10 * j)) & 1023u);
         }
     }
-    return crc;
+    return tokens;
 }
 
-void verify_token_crc(const Header& header, std::span<const std::uint16_t> indices)
+Bytes fast_stream(const Header& header, std::span<const std::uint16_t> tokens, const Limits& limits)
 {
-    require(header.method == 1 && indices.size() == header.symbol_count(),
-            "CRC requires a normal header and complete indices");
-    require(token_crc32(indices) == header.token_crc, "invalid token CRC32");
+    check_header(header, limits);
+    require(header.method == 0, "pack_fast requires method 0");
+    require(tokens.size() == header.symbol_count(), "symbol count does not match header");
+    const auto payload = checked_add(checked_mul(tokens.size(), token_field_bits), 7) / 8;
+    require(checked_add(payload, 8) <= limits.file_bytes, "output exceeds file size limit");
+    require(std::all_of(tokens.begin(), tokens.end(), [](std::uint16_t t) { return t < 1024; }),
+            "index outside 10-bit alphabet");
+    Bytes out = stream_prefix(header, 0, payload + 8);
+    out.resize(payload + 8);
+    for (std::size_t first = 0; first < tokens.size(); first += 4)
+    {
+        std::uint64_t word = 0;
+        for (std::size_t j = 0; j < 4; ++j)
+        {
+            word = (word << 10) | (first + j < tokens.size() ? tokens[first + j] : 0u);
+        }
+        const std::size_t at = 8 + first / 4 * 5;
+        for (std::size_t b = 0; b < 5 && at + b < out.size(); ++b)
+        {
+            out[at + b] = static_cast<std::uint8_t>(word >> (32 - 8 * b));
+        }
+    }
+    return out;
 }
 
+Bytes normal_stream(const Header& header, ByteView payload)
+{
+    Bytes out = stream_prefix(header, 1, payload.size() + 18);
+    append_field(out, header.frames, 4);
+    append_field(out, header.batch, 2);
+    out.insert(out.end(), payload.begin(), payload.end());
+    append_field(out, header.token_crc, 4);
+    return out;
+}
+
+std::uint32_t token_crc32(std::span<const std::uint16_t> tokens)
+{
+    const auto& t = crc_tables();
+    std::uint32_t reg = 0xffffffffu;
+    for (const auto token : tokens)
+    {
+        require(token < 1024, "index outside 10-bit alphabet");
+        // The token's little-endian bytes, first byte in the top position.
+        const std::uint32_t x = reg ^ ((std::uint32_t(token & 255u) << 24) | (std::uint32_t(token >> 8) << 16));
+        reg = t[3][x >> 24] ^ t[2][(x >> 16) & 255u] ^ t[1][(x >> 8) & 255u] ^ t[0][x & 255u];
+    }
+    return reg;
+}
+
+void check_token_crc(const Header& header, std::span<const std::uint16_t> tokens)
+{
+    require(header.method == 1 && tokens.size() == header.symbol_count(),
+            "CRC requires a normal header and complete indices");
+    require(token_crc32(tokens) == header.token_crc, "invalid token CRC32");
+}
+
+// ---------------------------------------------------------- entropy order --
 std::uint16_t select_entropy_batch(std::size_t frames, int requested)
 {
     require(requested >= 0 && requested <= 65535, "invalid entropy batch size");
-    if (requested)
+    if (requested != 0)
     {
         return static_cast<std::uint16_t>(requested);
     }
-    auto batch = frames / 1024 + (frames % 1024 != 0);
-    if (batch > 8)
+    std::size_t lanes = frames / 1024 + (frames % 1024 != 0 ? 1 : 0);
+    if (lanes > 8)
     {
-        batch = checked_add(batch, 7) & ~std::size_t{7};
+        lanes = (lanes + 7) / 8 * 8;
     }
-    return static_cast<std::uint16_t>(std::clamp<std::size_t>(batch, 1, 128));
+    return static_cast<std::uint16_t>(std::clamp<std::size_t>(lanes, 1, 128));
 }
 
-void visit_entropy_positions(const Header& header,
-                             const std::function<void(const EntropyPosition&)>& visit,
-                             const Limits& limits)
+LaneSchedule::LaneSchedule(const Header& header)
 {
-    validate_header(header, limits);
+    require(header.batch != 0, "zero entropy batch size");
+    lanes = std::min<std::size_t>(header.batch, header.frames);
+    short_length = header.frames / header.batch;
+    long_lanes = header.frames % header.batch;
+    steps = short_length + (long_lanes != 0 ? 1 : 0);
+}
+
+void for_each_entropy_position(const Header& header,
+                               const std::function<void(const EntropyPosition&)>& symbol,
+                               const Limits& limits)
+{
+    check_header(header, limits);
     require(header.method == 1, "entropy traversal requires method 1");
-    const auto per_lane = header.frames / header.batch;
-    const auto extra = header.frames % header.batch;
-    const auto steps = per_lane + (extra != 0);
-    const auto lanes = std::min<std::size_t>(header.batch, header.frames);
-    for (std::size_t step = 0; step < steps; ++step)
+    const LaneSchedule lanes(header);
+    for (std::size_t step = 0; step < lanes.steps; ++step)
     {
         for (std::size_t book = 0; book < header.codebooks; ++book)
         {
-            for (std::size_t lane = 0; lane < lanes; ++lane)
+            for (std::size_t lane = 0; lane < lanes.lanes; ++lane)
             {
-                if (step >= per_lane + (lane < extra))
+                if (step >= lanes.length(lane))
                 {
                     continue;
                 }
-                const auto frame = lane * per_lane + std::min(lane, extra) + step;
+                const auto frame = lanes.first_frame(lane) + step;
                 for (std::size_t group = 0; group < header.groups; ++group)
                 {
-                    visit({frame, group, book, lane, step,
-                           (frame * header.groups + group) * header.codebooks + book});
+                    const auto offset = (frame * header.groups + group) * header.codebooks + book;
+                    symbol({frame, group, book, lane, step, offset});
                 }
             }
         }
     }
 }
 
-Bytes frame_normal(const Header& header, ByteView payload)
-{
-    Bytes bytes{'F', 'B', 'A', 'Z', 0, 1,
-                static_cast<std::uint8_t>(header.groups | ((header.model_channels - 1) << 7)),
-                header.codebooks};
-    const auto be = [&](std::size_t value, unsigned count)
-    {
-        for (unsigned i = count; i > 0; --i)
-        {
-            bytes.push_back(static_cast<std::uint8_t>(value >> ((i - 1) * 8)));
-        }
-    };
-    be(header.frames, 4);
-    be(header.batch, 2);
-    bytes.insert(bytes.end(), payload.begin(), payload.end());
-    be(header.token_crc, 4);
-    return bytes;
-}
-
 // ------------------------------------------------------------ range coder --
-namespace
+void RangeWriter::push_top_byte()
 {
-constexpr std::uint32_t minimum_range = 0xff01;
-
-std::uint32_t split(std::uint32_t range, std::uint16_t p0)
-{
-    require(p0 > 0 && p0 < 32768, "Q15 probability must be in [1,32767]");
-    require(range >= minimum_range, "unnormalized range state");
-    return static_cast<std::uint32_t>((std::uint64_t(range) * p0) >> 15);
-}
-} // namespace
-
-void RangeEncoder::emit(std::uint32_t value)
-{
-    require(bytes_.size() < max_bytes_, "range output exceeds limit");
-    bytes_.push_back(static_cast<std::uint8_t>(value));
-}
-
-void RangeEncoder::flush_pending(std::uint32_t value)
-{
-    const auto carry = (value >> 8) & 255;
-    if (pending_count_)
-    {
-        emit(std::uint32_t(pending_byte_) + carry);
-        while (pending_count_ > 1)
-        {
-            emit(carry - 1);
-            --pending_count_;
-        }
-    }
-    pending_byte_ = static_cast<std::uint8_t>(value);
-    pending_count_ = 1;
-}
-
-void RangeEncoder::shift()
-{
-    if ((low_ >> 16) == 0xff)
-    {
-        pending_count_ = checked_add(pending_count_, 1);
-        require(pending_count_ <= max_bytes_, "pending range output exceeds limit");
-    }
-    else
-    {
-        flush_pending(low_ >> 16);
-    }
-    low_ = (low_ & 0xffff) << 8;
+    require(out_.size() < max_bytes_, "range output exceeds limit");
+    out_.push_back(static_cast<std::uint8_t>(low_ >> 16));
+    low_ = (low_ & 0xffffu) << 8;
     range_ <<= 8;
 }
 
-void RangeEncoder::put(std::uint16_t probability_zero, bool bit)
+void RangeWriter::add_carry()
+{
+    // Bytes of 0xff wrap to 0x00 and pass the carry on to the byte before.
+    for (std::size_t i = out_.size(); i-- > 0;)
+    {
+        if (++out_[i] != 0)
+        {
+            return;
+        }
+    }
+    require(false, "range carry past the first byte");
+}
+
+void RangeWriter::put(std::uint16_t p0, bool bit)
 {
     require(!finished_, "range encoder already finished");
-    const auto range0 = split(range_, probability_zero);
+    require(p0 > 0 && p0 < 32768, "Q15 probability must be in [1,32767]");
+    const auto zero = range::zero_width(range_, p0);
     if (bit)
     {
-        low_ += range0;
-        range_ -= range0;
+        low_ += zero;
+        range_ -= zero;
+        if (low_ >> 24)
+        {
+            add_carry();
+            low_ &= 0xffffffu;
+        }
     }
     else
     {
-        range_ = range0;
+        range_ = zero;
     }
-    while (range_ < minimum_range)
+    while (range_ < range::renormalise_below)
     {
-        shift();
+        push_top_byte();
     }
 }
 
-std::size_t RangeEncoder::bit_position() const
+std::size_t RangeWriter::bit_position() const
 {
     require(!finished_, "range encoder already finished");
-    const auto whole = checked_add(pending_count_, bytes_.size());
-    return checked_add(checked_mul(whole, 8),
-                       static_cast<std::size_t>(24 - std::bit_width(range_)));
+    return checked_add(checked_mul(out_.size(), 8), static_cast<std::size_t>(24 - std::bit_width(range_)));
 }
 
-Bytes RangeEncoder::finish()
+Bytes RangeWriter::finish()
 {
     require(!finished_, "range encoder already finished");
-    if (range_ < 0x10000)
+    if (range_ < 0x10000u)
     {
-        shift();
+        push_top_byte();
     }
-    const auto n = std::bit_width(range_) - 1;
-    require(n >= 16 && n <= 23, "invalid final range");
-    const std::uint32_t unit = 1u << n;
-    const auto val = (low_ & (unit - 1)) == 0 ? low_ : (low_ + unit) & (0u - unit);
-    require(val >= low_ && val < low_ + range_, "invalid range termination");
-    if ((val >> 16) == 0xff)
+    // The shortest tail: the multiple of the largest power of two not above
+    // the range that lies in [low, low + range); its low 16 bits are zero, so
+    // only its top byte is written.
+    const int top = std::bit_width(range_) - 1;
+    require(top >= 16 && top <= 23, "invalid final range");
+    const std::uint32_t unit = 1u << top;
+    const std::uint32_t end = (low_ + unit - 1) & ~(unit - 1);
+    require(end >= low_ && end - low_ < range_, "invalid range termination");
+    if (end >> 24)
     {
-        pending_count_ = checked_add(pending_count_, 1);
-        require(pending_count_ <= max_bytes_, "pending range output exceeds limit");
+        add_carry();
     }
-    else
-    {
-        flush_pending(val >> 16);
-    }
-    if (pending_count_)
-    {
-        flush_pending(0);
-    }
+    require(out_.size() < max_bytes_, "range output exceeds limit");
+    out_.push_back(static_cast<std::uint8_t>(end >> 16));
     finished_ = true;
-    return std::move(bytes_);
+    return std::move(out_);
 }
 
-std::uint32_t RangeDecoder::read()
+RangeReader::RangeReader(ByteView payload) : payload_(payload)
 {
-    return offset_ < bytes_.size() ? bytes_[offset_++] : 0u;
-}
-
-RangeDecoder::RangeDecoder(ByteView bytes) : bytes_(bytes)
-{
-    code_ = read() << 16;
-    code_ |= read() << 8;
-    code_ |= read();
+    for (int i = 0; i < 3; ++i)
+    {
+        code_ = (code_ << 8) | next_byte();
+    }
+    range_ = range::initial_range;
     require(code_ < range_, "range code outside initial interval");
 }
 
-bool RangeDecoder::get(std::uint16_t probability_zero)
+bool RangeReader::get(std::uint16_t p0)
 {
-    const auto range0 = split(range_, probability_zero);
-    const bool bit = code_ >= range0;
-    if (bit)
-    {
-        code_ -= range0;
-        range_ -= range0;
-    }
-    else
-    {
-        range_ = range0;
-    }
-    while (range_ < minimum_range)
-    {
-        range_ <<= 8;
-        code_ = (code_ << 8) + read();
-    }
-    require(code_ < range_, "range code outside interval");
-    return bit;
+    require(p0 > 0 && p0 < 32768, "Q15 probability must be in [1,32767]");
+    range::DecodeWindow w{range_, code_};
+    const int bit = range::decide(w, p0, *this);
+    require(bit >= 0, "range code outside interval");
+    range_ = w.range;
+    code_ = w.code;
+    return bit != 0;
 }
 
+std::uint16_t RangeReader::symbol(const float* left_masses)
+{
+    struct Step
+    {
+        RangeReader& reader;
+        int node(std::uint32_t p0, int)
+        {
+            return reader.get(static_cast<std::uint16_t>(p0)) ? 1 : 0;
+        }
+    } step{*this};
+    return static_cast<std::uint16_t>(range::walk_bisection<HostMath>(left_masses, step));
+}
+
+void write_symbol(RangeWriter& writer, const float* left_masses, std::uint16_t symbol)
+{
+    require(symbol < 1024, "symbol outside the 1024-entry alphabet");
+    struct Step
+    {
+        RangeWriter& writer;
+        unsigned symbol;
+        int node(std::uint32_t p0, int bit_index)
+        {
+            const bool bit = (symbol >> bit_index) & 1u;
+            writer.put(static_cast<std::uint16_t>(p0), bit);
+            return bit ? 1 : 0;
+        }
+    } step{writer, symbol};
+    range::walk_bisection<HostMath>(left_masses, step);
+}
+
+// ------------------------------------------------------ probability model --
 std::uint16_t conditional_q15(float left_mass, float mass)
 {
+    // round(flush(flush(left * 32768) / mass)) to a 64-bit integer, its low
+    // 32 bits as a signed value clamped to [1, 32767]; nonfinite or
+    // unrepresentable ratios give 1 (src/format/categorical.cpp:76-89).
     const float value = ftz_div(ftz_mul(left_mass, 32768.0f), mass);
     if (!std::isfinite(value) || value >= 0x1p63f || value < -0x1p63f)
     {
@@ -367,66 +436,19 @@ std::uint16_t conditional_q15(float left_mass, float mass)
     return static_cast<std::uint16_t>(std::clamp(low, 1, 32767));
 }
 
-void encode_categorical_tree(RangeEncoder& encoder, const float* left_masses, std::uint16_t symbol)
-{
-    std::size_t node = 0, base = 0, count = 1024;
-    float mass = 1;
-    while (count > 1)
-    {
-        const auto half = count / 2;
-        const float left = left_masses[node];
-        const bool bit = symbol >= base + half;
-        encoder.put(conditional_q15(left, mass), bit);
-        if (bit)
-        {
-            base += half;
-            count -= half;
-            mass = ftz_sub(mass, left);
-            node = 2 * node + 2;
-        }
-        else
-        {
-            count = half;
-            mass = left;
-            node = 2 * node + 1;
-        }
-    }
-}
-
-std::uint16_t decode_categorical_tree(RangeDecoder& decoder, const float* left_masses)
-{
-    std::size_t node = 0, base = 0, count = 1024;
-    float mass = 1;
-    while (count > 1)
-    {
-        const auto half = count / 2;
-        const float left = left_masses[node];
-        if (decoder.get(conditional_q15(left, mass)))
-        {
-            base += half;
-            count -= half;
-            mass = ftz_sub(mass, left);
-            node = 2 * node + 2;
-        }
-        else
-        {
-            count = half;
-            mass = left;
-            node = 2 * node + 1;
-        }
-    }
-    return static_cast<std::uint16_t>(base);
-}
-
 float probability_sum(std::span<const float> values)
 {
-    const auto pair_sum = [](std::span<const float> input, std::size_t width)
+    // Each block of up to 64 values is summed as a pairwise tree over 64
+    // slots (8 slots for inputs of at most 8 values), zero-filled; block sums
+    // merge like a binary counter (the running sum of block k carries into
+    // the levels that its index's trailing zero bits clear), and the levels
+    // left at the end add from the lowest.
+    const auto tree = [](std::span<const float> input, std::size_t slots)
     {
         std::array<float, 64> v{};
         std::copy(input.begin(), input.end(), v.begin());
-        while (width > 1)
+        for (std::size_t width = slots / 2; width >= 1; width /= 2)
         {
-            width /= 2;
             for (std::size_t i = 0; i < width; ++i)
             {
                 v[i] = ftz_add(v[2 * i], v[2 * i + 1]);
@@ -436,29 +458,27 @@ float probability_sum(std::span<const float> values)
     };
     if (values.size() <= 8)
     {
-        return pair_sum(values, 8);
+        return tree(values, 8);
     }
-    std::array<float, 64> partial{};
+    std::array<float, 64> level{};
     std::size_t blocks = 0;
-    for (std::size_t offset = 0; offset < values.size();)
+    for (std::size_t at = 0; at < values.size(); at += 64)
     {
-        const auto count = std::min<std::size_t>(64, values.size() - offset);
-        float value = pair_sum(values.subspan(offset, count), 64);
+        float carry = tree(values.subspan(at, std::min<std::size_t>(64, values.size() - at)), 64);
         ++blocks;
-        const auto level = static_cast<std::size_t>(std::countr_zero(blocks));
-        for (std::size_t i = 0; i < level; ++i)
+        const auto depth = static_cast<std::size_t>(std::countr_zero(blocks));
+        for (std::size_t i = 0; i < depth; ++i)
         {
-            value = ftz_add(value, partial[i]);
-            partial[i] = 0;
+            carry = ftz_add(carry, level[i]);
+            level[i] = 0;
         }
-        partial[level] = value;
-        offset += count;
+        level[depth] = carry;
     }
-    float value = partial[0];
+    float total = level[0];
     for (std::size_t i = 1; i < static_cast<std::size_t>(std::bit_width(blocks)); ++i)
     {
-        value = ftz_add(value, partial[i]);
+        total = ftz_add(total, level[i]);
     }
-    return value;
+    return total;
 }
 } // namespace tsacb

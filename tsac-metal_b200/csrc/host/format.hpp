@@ -1,10 +1,13 @@
-// TSAC container format, entropy traversal order and the sequential range
-// coder, restated for this library's host side.
+// The .tsac stream on the host: container header and framing, the order in
+// which a normal stream's symbols are coded, and the sequential range coder
+// that writes and reads them.
 //
-//   Header / validate / parse / fast pack / CRC   src/format/container.cpp:9-190
-//   select_entropy_batch / visit_entropy_positions src/format/entropy.cpp:11-55
-//   RangeEncoder / RangeDecoder                     src/format/range.cpp:14-157
-//   conditional_q15 / bisection coding             src/format/categorical.cpp:76-142
+// What the stream fixes, and where the reference defines it:
+//   header bytes, fast 10-bit packing, token CRC-32   src/format/container.cpp:9-190
+//   entropy lanes and symbol order                    src/format/entropy.cpp:11-55
+//   binary range coder                                src/format/range.cpp:14-157
+//   bisection coding with conditional_q15             src/format/categorical.cpp:76-142
+// The arithmetic shared with the device decoder lives in range_core.hpp.
 #pragma once
 #include "common.hpp"
 
@@ -12,6 +15,10 @@
 
 namespace tsacb
 {
+// Decoded stream header.  Byte layout: "FBAZ", version 0, method, then
+// (groups | (model channels - 1) << 7), codebooks; a normal stream follows
+// with frames (BE32) and entropy batch (BE16), the range-coded payload and
+// the token CRC-32 (BE32); a fast stream with 10-bit token fields.
 struct Header
 {
     std::uint8_t method = 0;
@@ -40,9 +47,49 @@ struct Header
     {
         return checked_mul(checked_mul(samples_per_channel(), channels()), 2);
     }
-    std::size_t lanes() const // entropy lanes x groups
+    // Rows the probability model evaluates per step: entropy lanes x groups.
+    std::size_t lanes() const
     {
         return (batch < frames ? batch : frames) * groups;
+    }
+};
+
+// Rejects a header whose dimensions or policy limits are out of range.
+void check_header(const Header& header, const Limits& limits = {});
+// Decodes and checks the header of a whole stream.
+Header read_header(ByteView stream, const Limits& limits = {});
+// Tokens [frame][group][book] of a fast (method 0) stream.
+std::vector<std::uint16_t> fast_tokens(ByteView stream, const Limits& limits = {});
+// A fast stream of tokens [frame][group][book].
+Bytes fast_stream(const Header& header, std::span<const std::uint16_t> tokens,
+                  const Limits& limits = {});
+// A normal stream: header, the range coder's payload, header.token_crc.
+Bytes normal_stream(const Header& header, ByteView payload);
+// CRC-32 (polynomial 0x04c11db7, MSB first, initial ~0, no final xor) over
+// the four little-endian bytes of each token.
+std::uint32_t token_crc32(std::span<const std::uint16_t> tokens);
+void check_token_crc(const Header& header, std::span<const std::uint16_t> tokens);
+
+// Entropy batch for a recording of `frames` frames: `requested` if nonzero,
+// else one lane per started 1024 frames, rounded up to a multiple of 8 past
+// 8 lanes, within 1..128.
+std::uint16_t select_entropy_batch(std::size_t frames, int requested = 0);
+
+// The frames of a normal stream split into min(batch, frames) lanes of
+// consecutive frames; the first frames % batch lanes hold one frame more.
+// Step s of lane l is frame first_frame(l) + s.
+struct LaneSchedule
+{
+    std::size_t lanes = 0, steps = 0, short_length = 0, long_lanes = 0;
+
+    explicit LaneSchedule(const Header& header);
+    std::size_t length(std::size_t lane) const
+    {
+        return short_length + (lane < long_lanes ? 1 : 0);
+    }
+    std::size_t first_frame(std::size_t lane) const
+    {
+        return lane * short_length + (lane < long_lanes ? lane : long_lanes);
     }
 };
 
@@ -50,65 +97,58 @@ struct EntropyPosition
 {
     std::size_t frame, group, codebook, lane, step, token_offset;
 };
+// Calls `symbol` for every symbol of a normal stream in coding order: step,
+// then codebook, then lane, then group.
+void for_each_entropy_position(const Header& header,
+                               const std::function<void(const EntropyPosition&)>& symbol,
+                               const Limits& limits = {});
 
-void validate_header(const Header& header, const Limits& limits = {});
-Header parse_header(ByteView bytes, const Limits& limits = {});
-std::vector<std::uint16_t> unpack_fast(ByteView bytes, const Limits& limits = {});
-Bytes pack_fast(const Header& header, std::span<const std::uint16_t> indices,
-                const Limits& limits = {});
-std::uint32_t token_crc32(std::span<const std::uint16_t> indices);
-void verify_token_crc(const Header& header, std::span<const std::uint16_t> indices);
-std::uint16_t select_entropy_batch(std::size_t frames, int requested = 0);
-// Calls visit in stream order: step, then book, then lane, then group.
-void visit_entropy_positions(const Header& header,
-                             const std::function<void(const EntropyPosition&)>& visit,
-                             const Limits& limits = {});
-// Normal-stream framing around a range-coded payload.
-Bytes frame_normal(const Header& header, ByteView payload);
-
-class RangeEncoder
+// Writes binary decisions.  Output bytes are appended as soon as they leave
+// the 24-bit window; a carry out of the window is added into the bytes
+// already written.
+class RangeWriter
 {
 public:
-    explicit RangeEncoder(std::size_t max_bytes = std::size_t{64} * 1024 * 1024)
-        : max_bytes_(max_bytes)
-    {
-    }
-    void put(std::uint16_t probability_zero, bool bit);
+    explicit RangeWriter(std::size_t max_bytes = std::size_t{64} * 1024 * 1024) : max_bytes_(max_bytes) {}
+    void put(std::uint16_t p0, bool bit);
+    // Bits the stream holds so far (whole bytes written plus the settled
+    // high bits of the window).
     std::size_t bit_position() const;
     Bytes finish();
 
 private:
-    void emit(std::uint32_t value);
-    void flush_pending(std::uint32_t value);
-    void shift();
-    std::uint32_t range_ = 0xff0000, low_ = 0;
-    std::uint8_t pending_byte_ = 0xff;
-    std::size_t pending_count_ = 0, max_bytes_;
+    void add_carry();
+    void push_top_byte();
+    std::uint32_t low_ = 0, range_ = 0xff0000u;
+    std::size_t max_bytes_;
     bool finished_ = false;
-    Bytes bytes_;
+    Bytes out_;
 };
 
-class RangeDecoder
+class RangeReader
 {
 public:
-    explicit RangeDecoder(ByteView bytes);
-    bool get(std::uint16_t probability_zero);
+    explicit RangeReader(ByteView payload);
+    bool get(std::uint16_t p0);
+    // One symbol of 1024 from its 1023 left-child masses (heap order).
+    std::uint16_t symbol(const float* left_masses);
+
+    // The byte source of range::decide: the next payload byte, 0 past the end.
+    std::uint32_t next_byte()
+    {
+        return at_ < payload_.size() ? payload_[at_++] : 0u;
+    }
 
 private:
-    std::uint32_t read();
-    ByteView bytes_;
-    std::size_t offset_ = 0;
-    std::uint32_t range_ = 0xff0000, code_ = 0;
+    ByteView payload_;
+    std::size_t at_ = 0;
+    std::uint32_t range_ = 0, code_ = 0;
 };
 
 std::uint16_t conditional_q15(float left_mass, float mass);
-// Decodes one symbol of a 1024-entry alphabet from the left-child masses of
-// the 1023 internal bisection nodes (heap order: children 2i+1, 2i+2).
-std::uint16_t decode_categorical_tree(RangeDecoder& decoder, const float* left_masses);
-// The encoding counterpart (encode_categorical, src/format/categorical.cpp:91-117):
-// the 10 decisions of `symbol`'s path, each with conditional_q15 of the node's
-// left mass and the path mass.
-void encode_categorical_tree(RangeEncoder& encoder, const float* left_masses, std::uint16_t symbol);
-// Host probability_sum (64-value FTZ pair trees + binary carry).
+// Codes `symbol`'s 10 decisions with the node probabilities of its path.
+void write_symbol(RangeWriter& writer, const float* left_masses, std::uint16_t symbol);
+// Host probability_sum (64-value FTZ pair trees + binary carry,
+// src/format/categorical.cpp:44-74).
 float probability_sum(std::span<const float> values);
 } // namespace tsacb

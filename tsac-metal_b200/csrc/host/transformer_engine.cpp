@@ -217,7 +217,7 @@ void TransformerEngine::run_stack(Workspace& ws_, bool temporal, int rows, std::
 void TransformerEngine::predict_known(const Header& header, std::span<const std::uint16_t> tokens,
                                       std::uint16_t* q15, float* probabilities)
 {
-    validate_header(header);
+    check_header(header);
     require(header.method == 1, "Transformer predictor requires normal framing");
     require(header.model_channels == model_->channels && header.codebooks <= model_->books,
             "Transformer stream/model mismatch");
@@ -516,7 +516,7 @@ void TransformerEngine::decode_begin(const std::vector<Header>& headers)
     for (std::size_t r = 0; r < headers.size(); ++r)
     {
         const auto& h = headers[r];
-        validate_header(h);
+        check_header(h);
         require(h.method == 1 && h.model_channels == model_->channels &&
                     h.codebooks <= model_->books,
                 "Transformer stream/model mismatch");

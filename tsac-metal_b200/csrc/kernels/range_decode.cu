@@ -4,7 +4,10 @@
 //   decode_categorical (tree walk)    src/format/categorical.cpp:119-142,
 //                                     with the left-child masses the softmax
 //                                     kernel emits (heap order, right mass =
-//                                     path mass - left, never re-summed)
+//                                     path mass - left, never re-summed);
+//                                     the decision arithmetic and the walk
+//                                     are range_core.hpp's, shared with the
+//                                     host decoder
 //   the Metal serialized decoder      src/metal/probability/range.metal:12-77
 //
 // B200 mapping: a stream's symbols are one serial chain (each decision's
@@ -18,13 +21,12 @@
 #include "kernels/numeric.cuh"
 #include "kernels/range_decode.cuh"
 #include "kernels/row_ops.cuh"
+#include "range_core.hpp"
 
 namespace tsacb::dev
 {
 namespace
 {
-constexpr std::uint32_t MINIMUM_RANGE = 0xff01u, INITIAL_RANGE = 0xff0000u;
-
 __device__ __forceinline__ std::uint32_t payload_byte(const std::uint8_t* payload, std::uint64_t size,
                                                       RangeCursor& c)
 {
@@ -41,10 +43,9 @@ __global__ void range_start_kernel(const std::uint8_t* __restrict__ bytes,
         return;
     const std::uint8_t* payload = bytes + offsets[s];
     const std::uint64_t size = sizes[s];
-    RangeCursor c{INITIAL_RANGE, 0u, 0u, 0u};
-    c.code = payload_byte(payload, size, c) << 16;
-    c.code |= payload_byte(payload, size, c) << 8;
-    c.code |= payload_byte(payload, size, c);
+    RangeCursor c{range::initial_range, 0u, 0u, 0u};
+    for (int i = 0; i < 3; ++i)
+        c.code = (c.code << 8) | payload_byte(payload, size, c);
     if (c.code >= c.range)
     {
         c.status = 1;
@@ -54,50 +55,55 @@ __global__ void range_start_kernel(const std::uint8_t* __restrict__ bytes,
     cursors[s] = c;
 }
 
-// One symbol of 1024 from the left-child masses of its bisection heap.
-// Returns false (and leaves the cursor's status at 1) when the code leaves
-// its interval.
-__device__ bool decode_symbol(const std::uint8_t* payload, std::uint64_t size, RangeCursor& c,
-                              const float* left_masses, std::uint16_t& symbol)
+struct DeviceMath
 {
-    int node = 0, base = 0, count = 1024;
-    float mass = 1.0f;
-#pragma unroll 1
-    while (count > 1)
+    static __device__ __forceinline__ std::uint16_t q15(float left, float mass)
     {
-        const int half = count / 2;
-        const float left = left_masses[node];
-        const std::uint32_t p0 = conditional_q15(left, mass);
-        const auto range0 = static_cast<std::uint32_t>((static_cast<std::uint64_t>(c.range) * p0) >> 15);
-        if (c.code >= range0)
-        {
-            c.code -= range0;
-            c.range -= range0;
-            base += half;
-            count -= half;
-            mass = ftz_sub(mass, left);
-            node = 2 * node + 2;
-        }
-        else
-        {
-            c.range = range0;
-            count = half;
-            mass = left;
-            node = 2 * node + 1;
-        }
-#pragma unroll 1
-        while (c.range < MINIMUM_RANGE)
-        {
-            c.range <<= 8;
-            c.code = (c.code << 8) + payload_byte(payload, size, c);
-        }
-        if (c.code >= c.range)
-        {
-            c.status = 1;
-            return false;
-        }
+        return conditional_q15(left, mass);
     }
-    symbol = static_cast<std::uint16_t>(base);
+    static __device__ __forceinline__ float sub(float a, float b)
+    {
+        return ftz_sub(a, b);
+    }
+};
+
+// A stream's decoder inside one kernel: its window and payload cursor.
+struct StreamDecoder
+{
+    range::DecodeWindow w;
+    const std::uint8_t* payload;
+    std::uint64_t size;
+    std::uint64_t at;
+
+    __device__ __forceinline__ std::uint32_t next_byte()
+    {
+        return at < size ? static_cast<std::uint32_t>(payload[at++]) : 0u;
+    }
+    __device__ __forceinline__ int node(std::uint32_t p0, int)
+    {
+        return range::decide(w, p0, *this);
+    }
+};
+
+// One symbol of 1024 from the left-child masses of its bisection heap (the
+// walk and the decision arithmetic of range_core.hpp, as the host decoder).
+// Returns false (and sets the cursor's status to 1) when the code leaves its
+// interval.
+__device__ __forceinline__ bool decode_symbol(const std::uint8_t* payload, std::uint64_t size,
+                                              RangeCursor& c, const float* left_masses,
+                                              std::uint16_t& symbol)
+{
+    StreamDecoder d{{c.range, c.code}, payload, size, c.offset};
+    const int s = range::walk_bisection<DeviceMath>(left_masses, d);
+    c.range = d.w.range;
+    c.code = d.w.code;
+    c.offset = static_cast<std::uint32_t>(d.at);
+    if (s < 0)
+    {
+        c.status = 1;
+        return false;
+    }
+    symbol = static_cast<std::uint16_t>(s);
     return true;
 }
 

@@ -34,11 +34,12 @@ static __device__ __align__(256) unsigned char noalloc_scratch[activation_bytes 
 constexpr int max_devices = 64;
 std::mutex setup_mutex;
 void* scratch_address[max_devices] = {};
-bool kernels_ready = false;
 
 // Device address of the array on the current device.  The host-side symbol is
 // only a stand-in, so the first call on each device looks the address up with
-// that device current and keeps it.
+// that device current and keeps it.  The kept address belongs to the device's
+// primary context: a cudaDeviceReset destroys it, so this entry point must not
+// be used on a device after cudaDeviceReset in the same process.
 void* device_scratch()
 {
     int device = 0;
@@ -52,11 +53,9 @@ void* device_scratch()
                           "cudaGetSymbolAddress(no-allocation qlinear scratch)");
         scratch_address[device] = ptr;
     }
-    if (!kernels_ready)
-    {
-        tsacb::dev::qlinear_init();
-        kernels_ready = true;
-    }
+    // Kernel attributes are per device; qlinear_init keeps one bit per device
+    // and returns at once when this device is already set up.
+    tsacb::dev::qlinear_init();
     return scratch_address[device];
 }
 } // namespace
