@@ -51,11 +51,67 @@ def test_plus_sign_and_grouped_flags_accepted(tmp_path):
     assert "expects an integer" not in r.stderr and "unknown option" not in r.stderr
 
 
-def test_without_gpu_fails_loudly(tmp_path):
+def _wave(channels=2, rate=44100, bits=16, fmt_tag=1, frames=600, data_size=None, order=("fmt", "data"),
+          extra=b""):
+    import struct
+
+    import numpy as np
+    pcm = (np.arange(frames * channels, dtype=np.int64) * 37 % 65536 - 32768).astype("<i2").tobytes()
+    fmt = struct.pack("<HHIIHH", fmt_tag, channels, rate, rate * channels * 2, channels * 2, bits)
+    chunks = {"fmt": b"fmt " + struct.pack("<I", len(fmt)) + fmt,
+              "data": b"data" + struct.pack("<I", len(pcm) if data_size is None else data_size) + pcm}
+    body = b"WAVE" + extra + b"".join(chunks[c] for c in order)
+    return b"RIFF" + struct.pack("<I", len(body)) + body
+
+
+def _no_gpu():
     torch = pytest.importorskip("torch")
     if torch.cuda.is_available():
         pytest.skip("a GPU is present")
+
+
+def test_without_gpu_fails_loudly(tmp_path):
+    _no_gpu()
     import tsac_cuda
+    (tmp_path / "in.wav").write_bytes(_wave())
     r = run("--models", str(tsac_cuda.seeded_package(0)), "c", str(tmp_path / "in.wav"),
             str(tmp_path / "out.tsac"))
     assert r.returncode == 1 and "no CUDA device" in r.stderr
+
+
+@pytest.mark.parametrize("kwargs,message", [
+    (dict(rate=48000), "the sample rate must be 44100 Hz"),
+    (dict(channels=9), "unsupported number of channels"),
+    (dict(bits=24), "invalid wav file"),
+    (dict(fmt_tag=3), "invalid wav file"),
+    (dict(order=("data", "fmt")), "invalid wav file"),
+    (dict(order=("fmt",)), "invalid wav file"),
+])
+def test_wave_input_rejections(tmp_path, kwargs, message):
+    """The native WAVE reader's checks (wave_input, src/audio.cpp:39-73) run
+    before any device work."""
+    (tmp_path / "in.wav").write_bytes(_wave(**kwargs))
+    r = run("--models", str(tmp_path), "c", str(tmp_path / "in.wav"), str(tmp_path / "out.tsac"))
+    assert r.returncode == 1 and message in r.stderr, r.stderr
+
+
+@pytest.mark.parametrize("kwargs", [dict(data_size=0xFFFFFFF0), dict(extra=b"LIST\x04\x00\x00\x00abcd"),
+                                    dict(channels=8, frames=3)])
+def test_wave_input_accepted(tmp_path, kwargs):
+    """A data chunk is read to the end of the file whatever size it declares,
+    unknown chunks are skipped: parsing succeeds and the run stops only at the
+    missing device."""
+    _no_gpu()
+    import tsac_cuda
+    (tmp_path / "in.wav").write_bytes(_wave(**kwargs))
+    r = run("--models", str(tsac_cuda.seeded_package(0)), "c", str(tmp_path / "in.wav"),
+            str(tmp_path / "out.tsac"))
+    assert r.returncode == 1 and "no CUDA device" in r.stderr, r.stderr
+
+
+def test_truncated_riff_rejected(tmp_path):
+    data = _wave()
+    for size in (0, 4, 11, 12 + 6):
+        (tmp_path / "in.wav").write_bytes(data[:size])
+        r = run("--models", str(tmp_path), "c", str(tmp_path / "in.wav"), str(tmp_path / "out.tsac"))
+        assert r.returncode == 1 and "invalid wav file" in r.stderr, (size, r.stderr)

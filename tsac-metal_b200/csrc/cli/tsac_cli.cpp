@@ -18,6 +18,8 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <cfenv>
+#include <span>
 #include <filesystem>
 #include <fstream>
 #include <iomanip>
@@ -65,102 +67,142 @@ struct Options
     std::string input, output, models;
 };
 
-// The reference's parser (src/cli.cpp:6-126): short options group ("-vv"),
-// "+n" values, "--" ends options, exactly three positionals.
+// One command line option.  `letter` is its short spelling (0: none), `word`
+// its long one ("" for none).  Value options read the following argument; an
+// integer may carry a leading '+'.
+struct OptionSpec
+{
+    char letter;
+    std::string_view word;
+    enum Kind { set_flag, add_one, integer, text, refused } kind;
+    bool Options::* flag = nullptr;
+    int Options::* number = nullptr;
+};
+
+constexpr std::string_view letters = "hfsvTqc";
+
+const std::vector<OptionSpec>& option_table()
+{
+    static const std::vector<OptionSpec> table{
+        {'h', "--help", OptionSpec::set_flag, &Options::help},
+        {'f', "--fast", OptionSpec::set_flag, &Options::fast},
+        {'s', "--separate_channels", OptionSpec::set_flag, &Options::separate},
+        {'v', "", OptionSpec::add_one},
+        {'T', "", OptionSpec::integer, nullptr, &Options::threads},
+        {'q', "--n_codebooks", OptionSpec::integer, nullptr, &Options::quality},
+        {'c', "--channels", OptionSpec::integer, nullptr, &Options::channels},
+        {0, "--batch_size", OptionSpec::integer, nullptr, &Options::batch},
+        {0, "--metal", OptionSpec::refused},
+        {0, "--exact", OptionSpec::set_flag, &Options::exact},
+        {0, "--device", OptionSpec::integer, nullptr, &Options::device},
+        {0, "--models", OptionSpec::text},
+    };
+    return table;
+}
+
+const OptionSpec* find_option(std::string_view spelled)
+{
+    for (const auto& spec : option_table())
+        if ((spelled.size() == 2 && spec.letter && spelled[1] == spec.letter) ||
+            (!spec.word.empty() && spelled == spec.word))
+            return &spec;
+    return nullptr;
+}
+
+// Integer option values: the whole argument, optionally after a '+'.  A bad
+// value names the option by its long spelling where it has one.
+int integer_value(const OptionSpec& spec, std::string_view spelled, std::string_view text)
+{
+    const std::string_view digits = text.starts_with('+') ? text.substr(1) : text;
+    int number = 0;
+    const auto [end, ec] = std::from_chars(digits.data(), digits.data() + digits.size(), number);
+    if (digits.empty() || ec != std::errc{} || end != digits.data() + digits.size())
+    {
+        const bool use_word = spec.letter && !spec.word.empty() && spec.kind == OptionSpec::integer;
+        throw Error("option " + std::string(use_word ? spec.word : spelled) + " expects an integer");
+    }
+    return number;
+}
+
+// The reference command line rules (src/cli.cpp:7-130): short options may be
+// grouped ("-vv", "-fs"), every letter of a group is checked before any is
+// applied (so "-q1" is the unknown option '-1', not an attached value), "--"
+// ends the options, "-h" ends parsing, and anything but three positionals
+// (command, input, output) prints the help.
 Options parse_cli(const std::vector<std::string_view>& arguments)
 {
     Options options;
     std::vector<std::string_view> positional;
-    for (std::size_t i = 0; i < arguments.size(); ++i)
+    std::size_t next = 0;
+    const auto take_value = [&](std::string_view spelled) -> std::string_view
     {
-        const auto arg = arguments[i];
+        if (next >= arguments.size())
+            throw Error("option '" + std::string(spelled) + "' must have an argument");
+        return arguments[next++];
+    };
+    const auto apply = [&](const OptionSpec& spec, std::string_view spelled)
+    {
+        switch (spec.kind)
+        {
+        case OptionSpec::set_flag:
+            options.*spec.flag = true;
+            break;
+        case OptionSpec::add_one:
+            ++options.verbose;
+            break;
+        case OptionSpec::integer:
+            options.*spec.number = integer_value(spec, spelled, take_value(spelled));
+            break;
+        case OptionSpec::text:
+            options.models = std::string(take_value(spelled));
+            break;
+        case OptionSpec::refused:
+            throw Error("Metal execution is not available on this platform (this tool runs on CUDA)");
+        }
+    };
+    while (next < arguments.size() && !options.help)
+    {
+        const auto arg = arguments[next++];
         if (arg == "--")
         {
-            positional.insert(positional.end(), arguments.begin() + static_cast<std::ptrdiff_t>(i + 1),
+            positional.insert(positional.end(), arguments.begin() + static_cast<std::ptrdiff_t>(next),
                               arguments.end());
             break;
         }
-        if (arg.size() <= 1 || arg[0] != '-')
+        if (arg.size() < 2 || arg.front() != '-')
         {
             positional.push_back(arg);
-            continue;
         }
-        const auto text_value = [&](std::string_view name)
+        else if (arg.starts_with("--"))
         {
-            if (++i == arguments.size())
-                throw Error("option '" + std::string(name) + "' must have an argument");
-            return std::string(arguments[i]);
-        };
-        const auto value = [&](std::string_view name)
-        {
-            if (++i == arguments.size())
-                throw Error("option '" + std::string(name) + "' must have an argument");
-            auto text = arguments[i];
-            if (text.starts_with('+'))
-                text.remove_prefix(1);
-            int number = 0;
-            const auto parsed = std::from_chars(text.data(), text.data() + text.size(), number);
-            if (text.empty() || parsed.ec != std::errc{} || parsed.ptr != text.data() + text.size())
-            {
-                const auto canonical = name == "-q" ? "--n_codebooks" : name == "-c" ? "--channels" : name;
-                throw Error("option " + std::string(canonical) + " expects an integer");
-            }
-            return number;
-        };
-        const auto flag = [&](std::string_view name)
-        {
-            if (name == "-h" || name == "--help")
-                options.help = true;
-            else if (name == "-f" || name == "--fast")
-                options.fast = true;
-            else if (name == "-s" || name == "--separate_channels")
-                options.separate = true;
-            else if (name == "-v")
-                ++options.verbose;
-            else if (name == "-T")
-                options.threads = value(name);
-            else if (name == "-q" || name == "--n_codebooks")
-                options.quality = value(name);
-            else if (name == "-c" || name == "--channels")
-                options.channels = value(name);
-            else if (name == "--batch_size")
-                options.batch = value(name);
-            else if (name == "--metal")
-                throw Error("Metal execution is not available on this platform (this tool runs on CUDA)");
-            else if (name == "--exact")
-                options.exact = true;
-            else if (name == "--device")
-                options.device = value(name);
-            else if (name == "--models")
-                options.models = text_value(name);
-            else
-                throw Error("unknown option: '" + std::string(name) + "'");
-        };
-        if (arg.starts_with("--"))
-        {
-            flag(arg);
+            const auto* spec = find_option(arg);
+            if (!spec || spec->word.empty())
+                throw Error("unknown option: '" + std::string(arg) + "'");
+            apply(*spec, arg);
         }
         else
         {
-            // Validate the whole short-option group before consuming values:
-            // -q1 is an unknown -1 option, not an attached value.
-            for (const char character : arg.substr(1))
-                if (std::string_view("hfsvTqc").find(character) == std::string_view::npos)
-                    throw Error("unknown option: '-" + std::string(1, character) + "'");
-            for (std::size_t character = 1; character < arg.size(); ++character)
-                flag(std::string("-") + arg[character]);
+            const auto group = arg.substr(1);
+            if (const auto bad = group.find_first_not_of(letters); bad != std::string_view::npos)
+                throw Error("unknown option: '-" + std::string(1, group[bad]) + "'");
+            for (const char letter : group)
+            {
+                const std::string spelled{'-', letter};
+                apply(*find_option(spelled), spelled);
+            }
         }
-        if (options.help)
-            return options;
     }
+    if (options.help)
+        return options;
     if (positional.size() != 3)
     {
         options.help = true;
         return options;
     }
-    if (positional[0] != "c" && positional[0] != "d" && positional[0] != "t")
-        throw Error("unknown command: " + std::string(positional[0]));
-    options.command = positional[0][0];
+    const auto command = positional[0];
+    if (command.size() != 1 || std::string_view("cdt").find(command[0]) == std::string_view::npos)
+        throw Error("unknown command: " + std::string(command));
+    options.command = command[0];
     options.input = positional[1];
     options.output = positional[2];
     return options;
@@ -222,58 +264,65 @@ struct Audio
     std::vector<float> samples;
 };
 
-std::uint32_t le32(const Bytes& b, std::size_t at)
+// Little-endian unsigned field of `width` bytes; out of range is a bad file.
+std::uint32_t le_field(std::span<const std::uint8_t> bytes, std::size_t at, unsigned width)
 {
-    require(at + 4 <= b.size(), "invalid wav file");
-    return std::uint32_t(b[at]) | (std::uint32_t(b[at + 1]) << 8) | (std::uint32_t(b[at + 2]) << 16) |
-           (std::uint32_t(b[at + 3]) << 24);
+    require(at <= bytes.size() && bytes.size() - at >= width, "invalid wav file");
+    std::uint32_t value = 0;
+    for (unsigned i = width; i-- > 0;)
+        value = (value << 8) | bytes[at + i];
+    return value;
 }
 
-// Raw little-endian PCM16 (pcm16_input, src/audio.cpp:19-37): an incomplete
-// interleaved frame is discarded; value / 32768.
-Audio pcm16_input(const std::uint8_t* data, std::size_t bytes, unsigned channels)
+// Raw little-endian PCM16 (pcm16_input, src/audio.cpp:19-37): whole
+// interleaved frames only (a trailing partial frame is dropped), each sample
+// value / 32768, zero-padded to a multiple of 512 frames.
+Audio pcm16_input(std::span<const std::uint8_t> bytes, unsigned channels)
 {
     require(channels > 0 && channels <= 127, "unsupported number of channels");
-    const std::size_t frames = bytes / (2 * channels);
-    const std::size_t padded = (frames + 511) / 512 * 512;
-    Audio audio{channels, std::vector<float>(padded * channels, 0.0f)};
-    for (std::size_t i = 0; i < frames * channels; ++i)
+    const std::size_t frames = bytes.size() / (2 * std::size_t{channels});
+    const std::size_t samples = frames * channels;
+    Audio audio{channels, std::vector<float>((frames + 511) / 512 * 512 * channels, 0.0f)};
+    for (std::size_t i = 0; i < samples; ++i)
     {
-        const unsigned value = unsigned(data[2 * i]) | (unsigned(data[2 * i + 1]) << 8);
-        const int signed_value = value < 32768 ? static_cast<int>(value) : static_cast<int>(value) - 65536;
-        audio.samples[i] = static_cast<float>(signed_value) * (1.0f / 32768.0f);
+        const auto value = static_cast<std::int16_t>(static_cast<std::uint16_t>(le_field(bytes, 2 * i, 2)));
+        audio.samples[i] = static_cast<float>(value) * (1.0f / 32768.0f);
     }
     return audio;
 }
 
-// Native RIFF/WAVE reader (wave_input, src/audio.cpp:39-73): PCM16 at
-// 44.1 kHz, 1..8 channels, data read to the end of the file.
-Audio wave_input(const Bytes& bytes)
+// RIFF/WAVE input (wave_input, src/audio.cpp:39-73).  Chunks are walked from
+// byte 12 by their declared sizes (no pad byte); "fmt " must describe 16-bit
+// PCM at 44.1 kHz with 1..8 channels and precede "data", whose samples run to
+// the end of the file whatever its declared size.
+Audio wave_input(std::span<const std::uint8_t> bytes)
 {
-    const auto tag = [&](std::size_t at, const char* text)
-    { return at + 4 <= bytes.size() && std::memcmp(bytes.data() + at, text, 4) == 0; };
-    require(tag(0, "RIFF") && tag(8, "WAVE"), "invalid wav file");
+    const auto id_is = [&](std::size_t at, std::string_view id)
+    { return at <= bytes.size() && bytes.size() - at >= 4 && std::string_view(
+                 reinterpret_cast<const char*>(bytes.data() + at), 4) == id; };
+    require(id_is(0, "RIFF") && id_is(8, "WAVE"), "invalid wav file");
     unsigned channels = 0;
-    for (std::size_t offset = 12; offset < bytes.size();)
+    std::size_t chunk = 12;
+    while (chunk < bytes.size())
     {
-        const std::size_t length = le32(bytes, offset + 4);
-        const std::size_t payload = offset + 8;
-        if (tag(offset, "fmt "))
-        {
-            require(length >= 16 && payload + length <= bytes.size(), "invalid wav file");
-            const auto* fmt = bytes.data() + payload;
-            require(fmt[0] == 1 && fmt[1] == 0 && fmt[14] == 16 && fmt[15] == 0, "invalid wav file");
-            channels = unsigned(fmt[2]) | (unsigned(fmt[3]) << 8);
-            require(channels > 0 && channels <= 8, "unsupported number of channels");
-            require(le32(bytes, payload + 4) == 44100, "the sample rate must be 44100 Hz");
-        }
-        else if (tag(offset, "data"))
+        const std::size_t size = le_field(bytes, chunk + 4, 4);
+        const std::size_t body = chunk + 8;
+        if (id_is(chunk, "data"))
         {
             require(channels > 0, "invalid wav file");
-            return pcm16_input(bytes.data() + payload, bytes.size() - std::min(bytes.size(), payload), channels);
+            return pcm16_input(bytes.subspan(body), channels);
         }
-        require(payload + length <= bytes.size(), "invalid wav file");
-        offset = payload + length;
+        require(bytes.size() - body >= size, "invalid wav file");
+        const auto content = bytes.subspan(body, size);
+        if (id_is(chunk, "fmt "))
+        {
+            const bool pcm16 = size >= 16 && le_field(content, 0, 2) == 1 && le_field(content, 14, 2) == 16;
+            require(pcm16, "invalid wav file");
+            channels = le_field(content, 2, 2);
+            require(channels >= 1 && channels <= 8, "unsupported number of channels");
+            require(le_field(content, 4, 4) == 44100, "the sample rate must be 44100 Hz");
+        }
+        chunk = body + size;
     }
     throw Error("invalid wav file");
 }
@@ -286,8 +335,7 @@ Audio read_audio(const std::filesystem::path& path, int requested_channels)
     if (path.extension() == ".sw")
     {
         const auto bytes = read_file(path);
-        return pcm16_input(bytes.data(), bytes.size(),
-                           requested_channels ? static_cast<unsigned>(requested_channels) : 1);
+        return pcm16_input(bytes, requested_channels ? static_cast<unsigned>(requested_channels) : 1);
     }
     if (path.extension() == ".wav" && requested_channels == 0)
     {
@@ -336,44 +384,37 @@ Audio read_audio(const std::filesystem::path& path, int requested_channels)
     return audio;
 }
 
-// 16-bit WAVE writer (pcm16_wave, src/audio.cpp:198-246): samples scaled by
-// 32768, clipped, rounded to nearest with ties to even; all padded samples kept.
+// 16-bit WAVE output (pcm16_wave, src/audio.cpp:184-247): a 44-byte
+// canonical header, then every sample (padding included) as
+// clamp(x * 32768, -32768, 32767) rounded to nearest, ties to even.
 Bytes pcm16_wave(const std::vector<float>& samples, unsigned channels)
 {
     require(channels > 0 && samples.size() % channels == 0, "audio sample shape mismatch");
-    const std::size_t block = 2ull * channels, rate = block * 44100, bytes = samples.size() * 2;
-    require(block <= 0xffff && rate <= 0xffffffffull && bytes <= 0xffffffffull - 36,
+    const std::uint64_t block = 2ull * channels, data_bytes = 2ull * samples.size();
+    require(block <= 0xffffu && block * 44100 <= 0xffffffffull && data_bytes <= 0xffffffffull - 36,
             "audio exceeds RIFF/WAVE dimensions");
-    Bytes out;
-    out.reserve(bytes + 44);
-    const auto word = [&](std::size_t value, unsigned count)
+    require(std::all_of(samples.begin(), samples.end(), [](float x) { return std::isfinite(x); }),
+            "nonfinite audio sample");
+    struct Field
     {
-        for (unsigned i = 0; i < count; ++i)
-            out.push_back(static_cast<std::uint8_t>((value >> (8 * i)) & 255));
+        std::uint64_t value;
+        unsigned width;
     };
-    const auto tag = [&](const char* text) { out.insert(out.end(), text, text + 4); };
-    tag("RIFF");
-    word(bytes + 36, 4);
-    tag("WAVE");
-    tag("fmt ");
-    word(16, 4);
-    word(1, 2);
-    word(channels, 2);
-    word(44100, 4);
-    word(rate, 4);
-    word(block, 2);
-    word(16, 2);
-    tag("data");
-    word(bytes, 4);
+    const Field header[] = {{0x46464952u, 4}, {data_bytes + 36, 4}, {0x45564157u, 4}, {0x20746d66u, 4},
+                            {16, 4}, {1, 2}, {channels, 2}, {44100, 4}, {block * 44100, 4},
+                            {block, 2}, {16, 2}, {0x61746164u, 4}, {data_bytes, 4}};
+    Bytes out(44 + data_bytes);
+    std::size_t at = 0;
+    for (const auto& f : header)
+        for (unsigned i = 0; i < f.width; ++i)
+            out[at++] = static_cast<std::uint8_t>(f.value >> (8 * i));
     for (const float x : samples)
     {
-        require(std::isfinite(x), "nonfinite audio sample");
-        const double scaled = std::clamp(double(x) * 32768.0, -32768.0, 32767.0);
-        const double lower = std::floor(scaled);
-        const auto integer = static_cast<std::int32_t>(lower);
-        const double fraction = scaled - lower;
-        const auto rounded = integer + ((fraction > 0.5 || (fraction == 0.5 && integer % 2 != 0)) ? 1 : 0);
-        word(static_cast<std::uint16_t>(rounded), 2);
+        // Rounding in double under the default round-to-nearest-even mode.
+        const auto value = static_cast<std::int32_t>(std::nearbyint(std::clamp(double(x) * 32768.0, -32768.0, 32767.0)));
+        const auto word = static_cast<std::uint16_t>(value);
+        out[at++] = static_cast<std::uint8_t>(word);
+        out[at++] = static_cast<std::uint8_t>(word >> 8);
     }
     return out;
 }
@@ -424,9 +465,9 @@ struct Context
     }
 };
 
-Bytes compress(Context& c, const Options& options, std::size_t& frames, unsigned& channels)
+Bytes compress(Context& c, const Audio& audio, const Options& options, std::size_t& frames,
+               unsigned& channels)
 {
-    const auto audio = read_audio(options.input, options.channels);
     require(options.quality >= 0, "invalid number of codebooks");
     tsac_cuda_encode_options encode{};
     encode.method = options.fast ? 0 : 1;
@@ -486,6 +527,13 @@ int run(const Options& options)
     // constructed, before any file is read (src/apple-arm/audio_analyzer.cpp:93).
     if (options.threads > 256)
         throw Error("CPU thread count exceeds supported limit (256)");
+    // Input is read and checked before the device is touched.
+    Audio audio;
+    Bytes stream;
+    if (options.command == 'd')
+        stream = read_file(options.input);
+    else
+        audio = read_audio(options.input, options.channels);
     Context c;
     const auto models = options.models.empty() ? default_models() : std::filesystem::path(options.models);
     check(tsac_cuda_context_create(models.c_str(), options.device, &c.ctx));
@@ -500,7 +548,7 @@ int run(const Options& options)
     {
         std::size_t frames = 0;
         unsigned channels = 0;
-        output = compress(c, options, frames, channels);
+        output = compress(c, audio, options, frames, channels);
         if (options.verbose)
         {
             const double kbps = frames ? double(output.size()) * 8.0 * 44100.0 / (double(frames) * 512.0 * 1000.0) : 0.0;
@@ -512,7 +560,7 @@ int run(const Options& options)
     }
     else
     {
-        output = decompress(c, read_file(options.input), options);
+        output = decompress(c, stream, options);
     }
     write_file(options.output, output);
     return 0;
