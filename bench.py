@@ -22,6 +22,10 @@ Workloads
   frontend encoder front end only (padding, DAC analysis, RVQ) of B clips per
            GPU: the exact-order analysis convolutions in isolation, for
            profiling.
+  synthesis  DAC decoder only (RVQ reconstruction + tensor-core synthesis) of
+           --frames latent frames of one stereo window batch (profiling).
+  decode   Transformer decode steps + range decoding of B clips of S seconds
+           (encoded once, untimed), for profiling the decode loop.
 
 Multi-GPU: one process per GPU (torchrun); each rank codes its own clips
 (clips shard with no data-path collective: "scaling": "weak"); the timed region
@@ -164,6 +168,41 @@ def gather_streams(streams, world, rank, torch, dist):
     return out
 
 
+def golden_streams():
+    """sha256 of the reference's stream per PCM seed (30 s stereo, q=12, batch
+    3): the cfg0 golden (seed 0) and the cfg4 box-batch goldens, all made by
+    tests/golden/make_golden.py running the reference scalar path."""
+    out = {}
+    cfg0 = ROOT / "tests" / "golden" / "cfg0_stereo_30s.json"
+    if cfg0.exists():
+        out[0] = json.loads(cfg0.read_text())["stream_sha256"]
+    for path in sorted((ROOT / "tests" / "golden" / "cfg4").glob("seed_*.json")):
+        record = json.loads(path.read_text())
+        out[int(record["pcm_seed"])] = record["stream_sha256"]
+    return out
+
+
+def parity_counts(streams, seeds, goldens):
+    """(checked, matched): streams whose seed has a reference golden, and how
+    many of them are byte-identical to it."""
+    checked = matched = 0
+    for stream, seed in zip(streams, seeds):
+        if seed in goldens:
+            checked += 1
+            matched += hashlib.sha256(bytes(stream)).hexdigest() == goldens[seed]
+    return checked, matched
+
+
+def sum_over_ranks(values, world, torch, dist):
+    """Element-wise sum of small integer counters over ranks (every rank calls it)."""
+    if world == 1:
+        return list(values)
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor(list(values), device=device, dtype=torch.int64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return [int(x) for x in t.tolist()]
+
+
 def clip_seeds(rank, clips):
     """PCM seeds of one rank's clips: disjoint across ranks (clip sharding with
     no data-path exchange); rank 0's clip 0 is the cfg0 clip (seed 0)."""
@@ -209,6 +248,28 @@ def kernel_stats():
     return json.loads(text)
 
 
+def fp32_issue_peak(torch):
+    """FMUL+FADD issue rate of this GPU (the exact convolution's instruction
+    pair) from the library's probe kernel, with the SM clock sampled meanwhile."""
+    import tsac_cuda
+    lib = tsac_cuda.library()
+    rate, ms = ctypes.c_double(), ctypes.c_double()
+    clocks = ClockSampler(torch).start()
+    clocks.active = True
+    status = 0
+    for _ in range(3):
+        status |= lib.tsac_cuda_fp32_issue_rate(200000, ctypes.byref(rate), ctypes.byref(ms),
+                                                ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    clocks.active = False
+    clocks.stop()
+    if status != 0:
+        return None
+    info = clocks.summary()
+    return {"tops": round(rate.value / 1e12, 2), "launch_ms": round(ms.value, 2),
+            "sm_mhz": info.get("sm_mhz"),
+            "nominal_at_that_clock": round(SM_COUNT * 128 * (info.get("sm_mhz") or 1965.0) * 1e6 / 1e12, 2)}
+
+
 # -------------------------------------------------------------------- codec --
 def codec_workload(args, rank, world, torch, dist):
     import synthetic
@@ -236,11 +297,12 @@ def codec_workload(args, rank, world, torch, dist):
     clocks = ClockSampler(torch).start()
     for _ in range(args.warmup):
         streams = step()
-    # Parity spot check: clip 0 of rank 0 is cfg0 (seed 0); compare to the reference golden.
-    golden = ROOT / "tests" / "golden" / "cfg0_stereo_30s.json"
-    parity = None
-    if rank == 0 and golden.exists() and args.seconds == CLIP_SECONDS:
-        parity = hashlib.sha256(streams[0]).hexdigest() == json.loads(golden.read_text())["stream_sha256"]
+    # Parity: every clip of every rank whose seed has a reference golden
+    # (cfg0 = rank 0's clip 0, cfg4's box-batch goldens) is byte-compared.
+    seeds = clip_seeds(rank, clips)
+    goldens = golden_streams() if args.seconds == CLIP_SECONDS else {}
+    parity_checked, parity_matched = sum_over_ranks(parity_counts(streams, seeds, goldens), world,
+                                                    torch, dist)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -284,6 +346,11 @@ def codec_workload(args, rank, world, torch, dist):
     clocks.stop()
     e2e_ms = max_over_ranks(s2.elapsed_time(e2), world, torch, dist)
     e2e_value = whole_job_rate(clips * args.seconds * e2e_steps, world, e2e_ms)
+    # The streams rank 0 gathered (all ranks' clips, rank-major) against the goldens.
+    gathered_parity = None
+    if gathered is not None:
+        all_seeds = [s for r in range(world) for s in clip_seeds(r, clips)]
+        gathered_parity = dict(zip(("checked", "matched"), parity_counts(gathered, all_seeds, goldens)))
 
     # Roofline of the dominant kernel family, from the live CUDA-event timing.
     peaks = measured_peaks()
@@ -302,20 +369,28 @@ def codec_workload(args, rank, world, torch, dist):
                     "kernel": name, "peak_source": peaks["source"] + " bf16 / 6 (3xTF32)"}
     elif name.startswith("conv"):
         # Exact-order convolutions issue one FP32 multiply and one add per MAC
-        # on the CUDA cores: peak = 148 SMs x 128 lanes x SM clock ops/s.
+        # on the CUDA cores.  Peak: the FMUL+FADD issue rate measured on this
+        # GPU by the library's probe (tsac_cuda_fp32_issue_rate), beside the
+        # nominal 148 SMs x 128 lanes x median SM clock.
         # traffic: DRAM bytes per MAC of the committed ncu capture of this
-        # kernel (profile_cases.py analysis 4, a 128 -> 128 7-tap layer:
-        # 45.9 MB read + 9.5 MB written for 10.10 G MAC), scaled to the mean
-        # launch here by its MACs (streaming activations: bytes grow with MACs).
+        # kernel (bench.py --workload frontend --seconds 4, a 128 -> 128 7-tap
+        # layer: 45.9 MB read + 9.5 MB written for 10.10 G MAC), scaled to the
+        # mean launch here by its MACs (streaming activations: bytes grow with MACs).
         achieved = d["work"] / (d["ms"] / 1e3) / 1e12
-        peak = SM_COUNT * 128 * sm_mhz * 1e6 / 1e12
+        nominal = SM_COUNT * 128 * sm_mhz * 1e6 / 1e12
+        probe = fp32_issue_peak(torch)
+        peak = probe["tops"] if probe else nominal
         traffic = None
         if name == "conv_exact":
             traffic = round((45.9e6 + 9.5e6) / 10.10e9 * (d["work"] / 2) / d["launches"])
         roofline = {"bound": "fp32", "achieved": round(achieved, 2), "peak": round(peak, 2),
                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": traffic,
                     "traffic_source": "ncu capture of a smaller launch, scaled by MACs" if traffic else None,
-                    "kernel": name, "peak_source": f"nominal FP32 issue at median SM clock {sm_mhz} MHz",
+                    "kernel": name,
+                    "peak_source": ("measured FMUL+FADD issue rate (tsac_cuda_fp32_issue_rate)" if probe
+                                    else f"nominal FP32 issue at median SM clock {sm_mhz} MHz"),
+                    "fp32_probe": probe, "nominal_peak": round(nominal, 2),
+                    "frac_of_nominal": round(achieved / nominal, 4),
                     "work_per_launch": d["work"] / d["launches"],
                     "avg_launch_ms": d["ms"] / d["launches"]}
     else:
@@ -334,9 +409,12 @@ def codec_workload(args, rank, world, torch, dist):
                    "codebooks": 12, "entropy_batch": 3, "seconds_per_clip": args.seconds,
                    "l2": "working set (PCM, activations) far larger than L2 each step",
                    "host_threads_per_rank": threads or "auto",
-                   "parity_cfg0_stream_vs_reference": parity},
+                   "parity_streams_checked": parity_checked,
+                   "parity_streams_matched": parity_matched,
+                   "parity_gathered_streams": gathered_parity},
         "roofline": roofline,
         "kernel_time_shares": shares,
+        "qlinear": qlinear_summary(torch) if rank == 0 else None,
         "gpu_launches": launches,
         "launches_before_timed": launches_before,
         "clocks": clock_info,
@@ -346,53 +424,76 @@ def codec_workload(args, rank, world, torch, dist):
     }
 
 
-def _reference_clip(seed):
-    """One reference ScalarAnalyzer encode+decode of a short stereo clip (child process)."""
-    import synthetic
+# Reference scalar path (oracle/_ref: the reference's ScalarAnalyzer code
+# compiled from its own sources), timed on the host cores.  Each worker process
+# prepares the five models once (ref_session_create: exactly the models
+# ScalarAnalyzer::encode/decode build inside every call) before timing, so the
+# timed region holds coding only.
+_REF = {}
+
+
+def _reference_worker_init():
     import tsac_cuda
     lib = ctypes.CDLL(str(ROOT / "oracle" / "_ref" / "libtsac_ref.so"))
-    pcm = synthetic.music_like(seed, REFERENCE_SAMPLE_SECONDS, 2)
-    package = str(tsac_cuda.seeded_package(0)).encode()
+    lib.ref_last_error.restype = ctypes.c_char_p
+    handle = ctypes.c_void_p()
+    if lib.ref_session_create(str(tsac_cuda.seeded_package(0)).encode(), 2, 12, ctypes.byref(handle)) != 0:
+        raise RuntimeError(lib.ref_last_error().decode())
+    _REF["lib"], _REF["session"] = lib, handle
+
+
+def _reference_clip(job):
+    """One reference encode (q=12, batch 3) + decode of a stereo clip; returns
+    (status, seconds)."""
+    import synthetic
+    seed, seconds = job
+    lib, session = _REF["lib"], _REF["session"]
+    pcm = synthetic.music_like(seed, seconds, 2)
     out = ctypes.POINTER(ctypes.c_uint8)()
-    n, bits = ctypes.c_size_t(), ctypes.c_size_t()
+    n = ctypes.c_size_t()
     t0 = time.time()
-    rc = lib.ref_encode(package, pcm.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(2),
-                        ctypes.c_size_t(pcm.shape[0]), 1, 12, 0, 3, ctypes.byref(out),
-                        ctypes.byref(n), ctypes.byref(bits))
+    rc = lib.ref_session_encode(session, pcm.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(2),
+                                ctypes.c_size_t(pcm.shape[0]), 1, 3, ctypes.byref(out), ctypes.byref(n))
+    if rc != 0:
+        return rc, time.time() - t0
     stream = bytes(out[: n.value])
+    lib.ref_free(out)
     pcm_out = ctypes.POINTER(ctypes.c_float)()
     ns, nc = ctypes.c_size_t(), ctypes.c_uint()
-    rc |= lib.ref_decode(package, stream, ctypes.c_size_t(len(stream)), ctypes.byref(pcm_out),
-                         ctypes.byref(ns), ctypes.byref(nc))
+    rc = lib.ref_session_decode(session, stream, ctypes.c_size_t(len(stream)), ctypes.byref(pcm_out),
+                                ctypes.byref(ns), ctypes.byref(nc))
+    if rc == 0:
+        lib.ref_free(pcm_out)
     return rc, time.time() - t0
 
 
-REFERENCE_SAMPLE_SECONDS = 0.1
+# The reference codes ~0.006 s of audio per second per core, the same at
+# 0.1 s, 0.5 s, 1 s and 30 s clips (measured), so short clips sample its rate
+# faithfully; a 30 s clip would take ~80 min per core.
+REFERENCE_ARM_SECONDS = 0.5     # --impl reference: ~80 s per step
+BASELINE_SAMPLE_SECONDS = 0.1   # cpu_baseline inside our arm: ~16 s
 
 
-def codec_cpu(steps: int, warmup: int = 0):
-    """Reference scalar path (oracle/_ref ScalarAnalyzer) on all host cores: one
-    0.1 s stereo clip per core per step, as independent processes."""
-    # Each reference process expands the DAC weights in RAM (~0.5 GB): cap the pool.
+def codec_cpu(steps: int, seconds: float):
+    """Reference scalar path on all host cores: per step, one clip of `seconds`
+    per core, as independent processes (each with models prepared before timing)."""
     cores = min(os.cpu_count() or 1, 32)
     ctx = mp.get_context("spawn")
     walls = []
-    with ctx.Pool(cores) as pool:
-        pool.map(_reference_clip, range(min(cores, 1)))  # warm the package cache
-        for step in range(warmup + steps):
+    with ctx.Pool(cores, initializer=_reference_worker_init) as pool:
+        pool.map(_reference_clip, [(999, 0.02)] * cores)  # every worker prepared and warm
+        for step in range(steps):
             t0 = time.time()
-            results = pool.map(_reference_clip, [1000 + step * cores + i for i in range(cores)])
-            wall = time.time() - t0
+            results = pool.map(_reference_clip, [(1000 + step * cores + i, seconds) for i in range(cores)])
+            walls.append(time.time() - t0)
             if any(rc for rc, _ in results):
                 raise RuntimeError("reference encode/decode failed")
-            if step >= warmup:
-                walls.append(wall)
     wall = sum(walls)
-    value = cores * REFERENCE_SAMPLE_SECONDS * len(walls) / wall
+    value = cores * seconds * len(walls) / wall
     return {"value": round(value, 5), "unit": "x realtime", "cores": cores, "kind": "reference",
             "sample": f"{len(walls)} step(s) x {cores} processes, each the reference ScalarAnalyzer "
-                      f"encode+decode of one {REFERENCE_SAMPLE_SECONDS} s stereo clip (q=12, batch 3); "
-                      f"{wall:.1f} s wall"}
+                      f"path encode+decode of one {seconds} s stereo clip (q=12, batch 3), models "
+                      f"prepared before timing; {wall:.1f} s wall"}
 
 
 def frontend_workload(args, rank, world, torch, dist):
@@ -442,6 +543,56 @@ def frontend_workload(args, rank, world, torch, dist):
     }
 
 
+def profile_workload(args, rank, world, torch, dist):
+    """Small single-family workloads for ncu captures: the timed steps sit in
+    the NVTX range "timed"; the line reports per-family kernel time."""
+    import synthetic
+    import tsac_cuda
+
+    analyzer = tsac_cuda.CudaAnalyzer(tsac_cuda.seeded_package(0), torch.cuda.current_device())
+    if args.workload == "synthesis":
+        tokens = np.random.default_rng(1).integers(0, 1024, (args.frames, 12)).astype(np.uint16)
+        latent = analyzer.rvq_decode(2, 12, tokens)
+        audio_seconds = args.frames * 512 / 44100
+
+        def step():
+            analyzer.dac_synthesis(2, latent)
+    else:
+        opts = tsac_cuda.EncodeOptions(method="normal", codebooks=12, entropy_batch=3)
+        pcms = [synthetic.music_like(rank * 100000 + i, args.seconds, 2) for i in range(args.clips)]
+        streams = analyzer.encode_batch(pcms, opts)
+        audio_seconds = args.clips * args.seconds
+
+        def step():
+            analyzer.decode_batch(streams)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    tsac_cuda.library().tsac_cuda_kernel_timing(1)
+    launches_before = launch_count()
+    start, end = event_pair(torch)
+    torch.cuda.nvtx.range_push("timed")
+    start.record()
+    for _ in range(args.steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    elapsed_ms = start.elapsed_time(end)
+    stats = kernel_stats()
+    tsac_cuda.library().tsac_cuda_kernel_timing(0)
+    analyzer.close()
+    total = sum(v["ms"] for v in stats.values()) or 1.0
+    return {"metric": f"x-realtime ({args.workload} only; profiling workload)",
+            "value": round(audio_seconds * args.steps / (elapsed_ms / 1e3), 2), "unit": "x realtime",
+            "ms_per_step": round(elapsed_ms / args.steps, 3), "dtype": "f32+int8",
+            "config": {"workload": args.workload, "frames": args.frames, "clips": args.clips,
+                       "seconds": args.seconds},
+            "kernel_ms": {k: round(v["ms"], 3) for k, v in stats.items()},
+            "kernel_time_shares": {k: round(v["ms"] / total, 4) for k, v in stats.items()},
+            "gpu_launches": launch_count() - launches_before, "e2e": None}
+
+
 # ------------------------------------------------------------------ qlinear --
 def qlinear_bytes(k, n, m):
     """Algorithmic bytes of one call (cfg1 formula)."""
@@ -454,89 +605,86 @@ def _bf16(x):
 
 
 def qlinear_workload(args, rank, world, torch, dist):
+    """cfg1: for each weight shape, a pool of distinct weight matrices larger
+    than 2x L2 is cycled through (every call reads its weights from HBM); for
+    each M the pool's calls are captured in one CUDA graph, and the timed
+    replay gives the per-call time.  GB/s = algorithmic bytes per call / time.
+    A step replays all 15 (shape, M) graphs once."""
     import tsac_cuda
 
     dev = torch.device("cuda", torch.cuda.current_device())
     rng = np.random.default_rng(1 + rank)
-    per_slot = sum(n * k for k, n in QLINEAR_SHAPES) * len(QLINEAR_MS)
-    slots = max(2, -(-2 * L2_BYTES // per_slot))
-    cases = []
-    for _ in range(slots):
-        row = []
-        for k, n in QLINEAR_SHAPES:
-            for m in QLINEAR_MS:
-                w = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev)
-                s = (torch.rand((k // 256, n), device=dev) * 1.5 + 0.5) / 127
-                b = torch.zeros(n, device=dev)
-                x = torch.from_numpy(_bf16(rng.standard_normal((m, k)).astype(np.float32))
-                                     .view(np.int16)).to(dev)
-                y = torch.empty((m, n), dtype=torch.int16, device=dev)
-                row.append((k, n, m, w, s, b, x, y))
-        cases.append(row)
     scratch = torch.empty(tsac_cuda.qlinear_scratch_bytes(256, 4096), dtype=torch.uint8, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
-    # One CUDA graph per pool slot: the step's 15 calls replay without host gaps.
-    graphs = []
-    for row in cases:
-        for (k, n, m, w, s, b, x, y) in row:  # warm (lazy init) before capture
-            tsac_cuda.qlinear(w, s, b, x, y, scratch, error_word=err)
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            for (k, n, m, w, s, b, x, y) in row:
-                tsac_cuda.qlinear(w, s, b, x, y, scratch, error_word=err)
-        graphs.append(g)
-    per_case = {}
-    for row in cases[:1]:
-        for (k, n, m, w, s, b, x, y) in row:
+    graphs, calls, pool_bytes = {}, {}, 0
+    for k, n in QLINEAR_SHAPES:
+        pool = max(2, -(-2 * L2_BYTES // (n * k)))
+        weights = [(torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev),
+                    (torch.rand((k // 256, n), device=dev) * 1.5 + 0.5) / 127) for _ in range(pool)]
+        pool_bytes += pool * (n * k + 4 * n * k // 256)
+        bias = torch.zeros(n, device=dev)
+        for m in QLINEAR_MS:
+            x = torch.from_numpy(_bf16(rng.standard_normal((m, k)).astype(np.float32)).view(np.int16)).to(dev)
+            y = torch.empty((m, n), dtype=torch.int16, device=dev)
+            tsac_cuda.qlinear(weights[0][0], weights[0][1], bias, x, y, scratch, error_word=err)  # lazy init
+            torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                for _ in range(20):
-                    tsac_cuda.qlinear(w, s, b, x, y, scratch, error_word=err)
-            g.replay()
-            e0, e1 = event_pair(torch)
-            e0.record()
-            g.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            per_case[(k, n, m)] = e0.elapsed_time(e1) / 20
+                for w, ws in weights:
+                    tsac_cuda.qlinear(w, ws, bias, x, y, scratch, error_word=err)
+            graphs[(k, n, m)] = g
+            calls[(k, n, m)] = pool
+        del weights
     clocks = ClockSampler(torch).start()
-    for i in range(args.warmup):
-        graphs[i % slots].replay()
+    for _ in range(args.warmup):
+        for g in graphs.values():
+            g.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    start, end = event_pair(torch)
+    per_case = {key: 0.0 for key in graphs}
+    marks = []
     clocks.active = True
+    start, end = event_pair(torch)
     start.record(stream)
-    for i in range(args.steps):
-        graphs[(args.warmup + i) % slots].replay()
+    for _ in range(args.steps):
+        for key, g in graphs.items():
+            e0, e1 = event_pair(torch)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+            marks.append((key, e0, e1))
     end.record(stream)
     torch.cuda.synchronize()
     clocks.active = False
     clocks.stop()
+    for key, e0, e1 in marks:
+        per_case[key] += e0.elapsed_time(e1)
     elapsed_ms = max_over_ranks(start.elapsed_time(end), world, torch, dist)
     assert int(err.item()) == 0
-    step_bytes = sum(qlinear_bytes(k, n, m) for k, n in QLINEAR_SHAPES for m in QLINEAR_MS)
+    step_bytes = sum(qlinear_bytes(k, n, m) * calls[(k, n, m)] for (k, n, m) in graphs)
     value = step_bytes * args.steps * world / (elapsed_ms / 1e3) / 1e9
-    sweep = {f"K{k}_N{n}_M{m}": round(qlinear_bytes(k, n, m) / (ms / 1e3) / 1e9, 1)
-             for (k, n, m), ms in per_case.items()}
-    dom = per_case[(1024, 4096, 3)]
-    dom_gbs = qlinear_bytes(1024, 4096, 3) / (dom / 1e3) / 1e9
+    sweep = {f"K{k}_N{n}_M{m}": round(qlinear_bytes(k, n, m) * calls[(k, n, m)] * args.steps
+                                      / (per_case[(k, n, m)] / 1e3) / 1e9, 1)
+             for (k, n, m) in graphs}
+    dom_key = (1024, 4096, 3)
+    dom_ms = per_case[dom_key] / (args.steps * calls[dom_key])
+    dom_gbs = qlinear_bytes(*dom_key) / (dom_ms / 1e3) / 1e9
     peaks = measured_peaks()
     return {
         "metric": "qlinear HBM GB/s (cfg1 aggregate)", "value": round(value, 1), "unit": "GB/s",
         "ms_per_step": round(elapsed_ms / args.steps, 4), "dtype": "int8",
         "config": {"workload": "cfg1 quantized-linear microbench", "shapes": QLINEAR_SHAPES,
-                   "M": QLINEAR_MS, "weights_pool_bytes": per_slot * slots,
-                   "l2": "weights cycle through a pool > 2x L2 (HBM-resident)"},
+                   "M": QLINEAR_MS, "weights_pool_bytes": pool_bytes,
+                   "calls_per_step": sum(calls.values()),
+                   "l2": "each shape cycles through > 2x L2 of distinct weights (HBM-resident)"},
         "sweep_gbs": sweep,
         "roofline": {"bound": "hbm", "achieved": round(dom_gbs, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(dom_gbs / peaks["hbm_gbs"], 4), "traffic": None,
-                     "kernel": "qlinear K=1024 N=4096 M=3 (graph-replayed)",
-                     "peak_source": peaks["source"]},
-        "gpu_launches": 2 * len(QLINEAR_SHAPES) * len(QLINEAR_MS) * args.steps,
+                     "kernel": "qlinear K=1024 N=4096 M=3 (quantize + matmul, graph-replayed)",
+                     "avg_call_ms": round(dom_ms, 5), "peak_source": peaks["source"]},
+        "gpu_launches": 2 * sum(calls.values()) * args.steps,
         "clocks": clocks.summary(),
         "e2e": None,
     }
@@ -549,7 +697,9 @@ def main():
     parser.add_argument("--steps", type=int, default=2)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--workload", choices=["codec", "qlinear", "frontend"], default="codec")
+    parser.add_argument("--workload", choices=["codec", "qlinear", "frontend", "synthesis", "decode"],
+                        default="codec")
+    parser.add_argument("--frames", type=int, default=172, help="latent frames (synthesis workload)")
     parser.add_argument("--clips", type=int, default=64, help="clips per GPU per step (8 x 64 = cfg4's 512)")
     parser.add_argument("--seconds", type=float, default=CLIP_SECONDS,
                         help="clip length (30 s is the benchmark; shorter for profiling runs)")
@@ -564,14 +714,17 @@ def main():
               "data": "synthetic (seeded music-like PCM; seeded random-init weights)"}
     if args.impl == "reference":
         if rank == 0:
-            cpu = codec_cpu(max(1, min(args.steps, 2)), warmup=0)
+            steps_run = max(1, min(args.steps, 2))
+            cpu = codec_cpu(steps_run, REFERENCE_ARM_SECONDS)
             line = {"impl": "reference",
                     "metric": "x-realtime encode+decode (30 s 44.1 kHz joint stereo, q=12, batch 3)",
                     "value": cpu["value"], "unit": "x realtime", **common,
+                    "steps": steps_run, "steps_requested": args.steps, "warmup": 0,
                     "dtype": "f32+int8 (exact reference arithmetic)",
-                    "config": {"workload": "cfg0/cfg4: encode+decode of 30 s stereo clips",
+                    "config": {"workload": "cfg0/cfg4: encode+decode of stereo clips (q=12, batch 3)",
                                "codebooks": 12, "entropy_batch": 3,
-                               "reference_sample": "0.1 s clips (bounded CPU sample)"},
+                               "reference_sample": f"{REFERENCE_ARM_SECONDS} s clips, one per host core "
+                                                   "per step (a 30 s clip takes ~80 min per core)"},
                     "cpu_baseline": cpu,
                     "e2e": {"value": cpu["value"], "unit": "x realtime", "h2d_bytes_per_step": 0,
                             "d2h_bytes_per_step": 0}}
@@ -593,11 +746,14 @@ def main():
         result = codec_workload(args, rank, world, torch, dist)
     elif args.workload == "frontend":
         result = frontend_workload(args, rank, world, torch, dist)
+    elif args.workload in ("synthesis", "decode"):
+        result = profile_workload(args, rank, world, torch, dist)
     else:
         result = qlinear_workload(args, rank, world, torch, dist)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
-            result["cpu_baseline"] = (codec_cpu(1) if args.workload == "codec" else None)
+            result["cpu_baseline"] = (codec_cpu(1, BASELINE_SAMPLE_SECONDS)
+                                      if args.workload == "codec" else None)
         line = {"metric": result.pop("metric"), "value": result.pop("value"),
                 "unit": result.pop("unit"), **common, **result}
         line["config"]["parallelism"] = (f"clip sharding over {world} GPU(s); no collective in the "

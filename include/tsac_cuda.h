@@ -283,6 +283,34 @@ int tsac_cuda_qlinear_noalloc(const int8_t* weights, const float* weight_scales,
                               const uint16_t* residual, uint16_t* y, unsigned* error_word,
                               void* stream);
 
+/* Measurement helper (no reference counterpart): the FP32 issue rate of the
+ * current device for the exact convolution's instruction pair, a separately
+ * rounded multiply then an add, as operations (multiplies + adds) per second.
+ * Runs 16 independent recurrences per thread on 8 x 256-thread CTAs per SM
+ * for `iterations` steps, timed with CUDA events on `stream` after one
+ * warm-up launch; *milliseconds (nullable) receives the timed launch's
+ * duration.  Allocates a small sink buffer.  Synchronous. */
+int tsac_cuda_fp32_issue_rate(int iterations, double* ops_per_second, double* milliseconds, void* stream);
+
+/* Causal attention of the probability model, 4 heads x 128 over bf16 keys
+ * and values: scalar::Attention / attention_bf16_into
+ * (src/scalar/attention.cpp:12-131), per head 64-key blocks merged in order,
+ * value sums bf16-rounded when `round` is set (the reference's
+ * `time > 64 || prefill`, :128).
+ *   query      device bf16 [rows][512]
+ *   rows_meta  device int32 [rows][5]: (slot, base, time, rotary, round);
+ *              row r attends to keys/values [base, base + time) (slot and
+ *              rotary are unused here)
+ *   keys, values device bf16 [positions][512]; out device bf16 [rows][512]
+ *   max_time   >= every row's time (at most 4,194,240)
+ *   scratch    device, >= tsac_cuda_attention_scratch_bytes(rows, max_time)
+ *              (may be NULL when max_time <= 64)
+ * Asynchronous on `stream`. */
+size_t tsac_cuda_attention_scratch_bytes(size_t rows, size_t max_time);
+int tsac_cuda_attention(const uint16_t* query, const int* rows_meta, const uint16_t* keys,
+                        const uint16_t* values, size_t rows, size_t max_time, uint16_t* out,
+                        void* scratch, size_t scratch_bytes, void* stream);
+
 /* Scratch bytes tsac_cuda_conv1d needs (its per-launch tile table). */
 size_t tsac_cuda_conv1d_scratch_bytes(size_t out_frames, int stride, int transposed);
 

@@ -5,6 +5,7 @@
 #include "kernels/dac.cuh"
 #include "kernels/qlinear.cuh"
 #include "kernels/range_decode.cuh"
+#include "kernels/transformer_ops.cuh"
 
 #include <vector>
 
@@ -62,6 +63,37 @@ int tsac_cuda_qlinear(const int8_t* weights, const float* weight_scales, const f
             a.k = static_cast<int>(k);
             dev::qlinear_matmul(a, s);
             cuda_check(cudaGetLastError(), "qlinear launch");
+        });
+}
+
+size_t tsac_cuda_attention_scratch_bytes(size_t rows, size_t max_time)
+{
+    return tsacb::dev::attention_partials_bytes(static_cast<int>(rows), static_cast<int>(max_time));
+}
+
+int tsac_cuda_attention(const uint16_t* query, const int* rows_meta, const uint16_t* keys,
+                        const uint16_t* values, size_t rows, size_t max_time, uint16_t* out,
+                        void* scratch, size_t scratch_bytes, void* stream)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            using namespace tsacb;
+            require_device();
+            require(query && rows_meta && keys && values && out, "null argument");
+            require(rows > 0 && rows <= (1u << 20), "attention row count out of range");
+            require(max_time > 0 && max_time <= 65535u * 64u, "attention history length out of range");
+            require(rows * 4 <= 0x7fffffffu, "attention grid too large");
+            require(max_time <= 64 ||
+                        (scratch && scratch_bytes >= dev::attention_partials_bytes(static_cast<int>(rows),
+                                                                                   static_cast<int>(max_time))),
+                    "attention scratch too small");
+            require(aligned16(query) && aligned16(keys) && aligned16(values) && aligned16(out),
+                    "attention buffers must be 16-byte aligned");
+            dev::attention(query, reinterpret_cast<const dev::RowMeta*>(rows_meta), keys, values,
+                           static_cast<int>(rows), static_cast<int>(max_time), static_cast<float*>(scratch), out,
+                           static_cast<cudaStream_t>(stream));
+            cuda_check(cudaGetLastError(), "attention launch");
         });
 }
 
