@@ -690,6 +690,21 @@ def qlinear_workload(args, rank, world, torch, dist):
     }
 
 
+def qlinear_summary(torch, steps=20):
+    """cfg1 (the metric's "qlinear HBM GB/s") measured beside the codec step,
+    as --workload qlinear measures it: aggregate and per-shape GB/s of
+    algorithmic bytes with every call's weights read from HBM."""
+    class Args:
+        pass
+    a = Args()
+    a.steps, a.warmup = steps, 3
+    r = qlinear_workload(a, 0, 1, torch, None)
+    return {"aggregate_gbs": r["value"], "unit": "GB/s",
+            "frac_of_hbm": round(r["value"] / measured_peaks()["hbm_gbs"], 4),
+            "per_shape_gbs": r["sweep_gbs"], "roofline": r["roofline"], "ms_per_step": r["ms_per_step"],
+            "steps": steps, "clocks": r["clocks"], "config": r["config"]}
+
+
 # --------------------------------------------------------------------- main --
 def main():
     parser = argparse.ArgumentParser()
