@@ -618,6 +618,7 @@ def qlinear_workload(args, rank, world, torch, dist):
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
     graphs, calls, pool_bytes = {}, {}, 0
+    keep = []  # every tensor a captured graph reads stays alive while the graphs do
     for k, n in QLINEAR_SHAPES:
         pool = max(2, -(-2 * L2_BYTES // (n * k)))
         weights = [(torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev),
@@ -635,7 +636,8 @@ def qlinear_workload(args, rank, world, torch, dist):
                     tsac_cuda.qlinear(w, ws, bias, x, y, scratch, error_word=err)
             graphs[(k, n, m)] = g
             calls[(k, n, m)] = pool
-        del weights
+            keep += [x, y]
+        keep += [weights, bias]
     clocks = ClockSampler(torch).start()
     for _ in range(args.warmup):
         for g in graphs.values():
@@ -707,6 +709,8 @@ def qlinear_summary(torch, steps=20):
 
 # --------------------------------------------------------------------- main --
 def main():
+    import faulthandler
+    faulthandler.enable()  # a crash in native code still prints the Python stack
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=2)

@@ -231,27 +231,45 @@ def test_host_thread_budget(analyzer):
         analyzer.set_host_threads(0)
 
 
-def test_fused_codebook_step_decodes_identically(tmp_path):
-    """The opt-in fused codebook-step kernel (one cluster launch per step)
-    produces the same PCM as the default separate kernels."""
-    import os
-    import subprocess
-    import sys
-    stream = (GOLDEN / "stereo_q12_b3_1s.tsac").read_bytes()
-    (tmp_path / "in.tsac").write_bytes(stream)
-    script = (
-        "import sys, numpy as np; sys.path.insert(0, %r)\n"
-        "import tsac_cuda\n"
-        "a = tsac_cuda.CudaAnalyzer(tsac_cuda.seeded_package(0), 0)\n"
-        "a.set_exact_synthesis(True)\n"
-        "d = a.decode(open(%r, 'rb').read())\n"
-        "np.save(%r, d.samples)\n"
-    ) % (str(pathlib.Path(tsac_cuda.__file__).parent), str(tmp_path / "in.tsac"), str(tmp_path / "out.npy"))
-    env = dict(os.environ, TSAC_CUDA_FUSED_CODEBOOK="1")
-    subprocess.run([sys.executable, "-c", script], env=env, check=True, timeout=600)
-    fused = np.load(tmp_path / "out.npy")
-    a = tsac_cuda.CudaAnalyzer(tsac_cuda.seeded_package(0), 0)
-    a.set_exact_synthesis(True)
-    default = a.decode(stream).samples
-    a.close()
-    assert np.array_equal(fused.view(np.uint32), default.view(np.uint32))
+@pytest.mark.parametrize("case", ["known_17_8_16", "known_101_3_1", "known_35_3_2", "known_17_1_1",
+                                  "known_3_8_2", "known_1026_1_1", "known_mono_40_2_1"])
+def test_decode_known_token_streams(analyzer, case):
+    """The reference's own streams of known tokens decode on the GPU-resident
+    loop: 16 channel groups, batches 1..8, mono, and 1026 frames at batch 1,
+    which replays the last 256 frames after 1024 (a different row shape for
+    that step).  The decoder checks the stream's token CRC-32, so a wrong
+    token anywhere fails the call."""
+    g = _golden(case)
+    stream = (GOLDEN / f"{case}.tsac").read_bytes()
+    assert hashlib.sha256(stream).hexdigest() == g["stream_sha256"]
+    decoded = analyzer.decode(stream)
+    assert decoded.samples.shape == (g["frames"] * 512, g["channels"] * g["groups"])
+
+
+def test_decode_batch_mixed_shapes_equals_single(analyzer):
+    """One decode batch holding recordings of different lengths, codebook
+    counts, channel groups and entropy batches (lanes end at different steps
+    and books, so the loop runs several row shapes) decodes each exactly as
+    alone."""
+    names = ["stereo_q12_b3_1s", "separate_q5_b2_0p5s", "stereo_q1_b7_0p3s", "stereo_q4_b8_0p05s",
+             "known_35_3_2", "stereo_q12_auto_0p1s"]
+    streams = [(GOLDEN / f"{n}.tsac").read_bytes() for n in names]
+    singles = [analyzer.decode(s).samples for s in streams]
+    for got, want in zip(analyzer.decode_batch(streams), singles):
+        assert np.array_equal(got.samples.view(np.uint32), want.view(np.uint32))
+
+
+def test_corrupt_payload_is_an_error_and_analyzer_is_reusable(analyzer):
+    """Flipped payload bytes make the device range decoder leave its interval
+    or decode wrong tokens: the call fails (range error or token CRC) and the
+    next call on the same analyzer succeeds."""
+    stream = bytearray((GOLDEN / "stereo_q12_b3_1s.tsac").read_bytes())
+    for at in (14, 15, 40, len(stream) // 2):
+        bad = bytearray(stream)
+        bad[at] ^= 0xFF
+        with pytest.raises(tsac_cuda.TsacError, match="range code|CRC"):
+            analyzer.decode(bytes(bad))
+    truncated = bytes(stream[:40]) + bytes(stream[-4:])
+    with pytest.raises(tsac_cuda.TsacError):
+        analyzer.decode(truncated)
+    assert analyzer.decode(bytes(stream)).samples.shape[1] == 2

@@ -72,81 +72,6 @@ template <class F> void parallel_for(std::size_t n, std::size_t max_workers, F&&
         j.get();
 }
 
-// Persistent workers for the decode loop's per-step range decoding.  A step
-// is a few microseconds of host work between two GPU predictions, too short
-// for thread creation, so the workers live for the whole loop and wait for
-// the next step by spinning on a generation counter (yielding after a short
-// spin).  run(f) calls f(w) for every worker w, w = 0 on the caller, and
-// returns when all have finished; the first exception is rethrown.
-class StepPool
-{
-public:
-    explicit StepPool(std::size_t workers) : errors_(std::max<std::size_t>(workers, 1))
-    {
-        for (std::size_t w = 1; w < errors_.size(); ++w)
-            threads_.emplace_back([this, w] { work(w); });
-    }
-    ~StepPool()
-    {
-        stop_.store(true, std::memory_order_release);
-        generation_.fetch_add(1, std::memory_order_acq_rel);
-        for (auto& t : threads_)
-            t.join();
-    }
-    StepPool(const StepPool&) = delete;
-    StepPool& operator=(const StepPool&) = delete;
-
-    std::size_t size() const { return errors_.size(); }
-
-    template <class F> void run(F&& f)
-    {
-        job_ = std::function<void(std::size_t)>(std::forward<F>(f));
-        pending_.store(threads_.size(), std::memory_order_relaxed);
-        generation_.fetch_add(1, std::memory_order_acq_rel);
-        call(0);
-        for (unsigned spin = 0; pending_.load(std::memory_order_acquire) != 0; ++spin)
-            if (spin > 4096)
-                std::this_thread::yield();
-        for (auto& e : errors_)
-            if (e)
-                std::rethrow_exception(std::exchange(e, nullptr));
-    }
-
-private:
-    void call(std::size_t w)
-    {
-        try
-        {
-            job_(w);
-        }
-        catch (...)
-        {
-            errors_[w] = std::current_exception();
-        }
-    }
-    void work(std::size_t w)
-    {
-        std::uint64_t seen = 0;
-        for (;;)
-        {
-            std::uint64_t g;
-            for (unsigned spin = 0; (g = generation_.load(std::memory_order_acquire)) == seen; ++spin)
-                if (spin > 4096)
-                    std::this_thread::yield();
-            seen = g;
-            if (stop_.load(std::memory_order_acquire))
-                return;
-            call(w);
-            pending_.fetch_sub(1, std::memory_order_acq_rel);
-        }
-    }
-    std::vector<std::exception_ptr> errors_;
-    std::vector<std::thread> threads_;
-    std::function<void(std::size_t)> job_;
-    std::atomic<std::uint64_t> generation_{0};
-    std::atomic<std::size_t> pending_{0};
-    std::atomic<bool> stop_{false};
-};
 
 // Stage timing (TSAC_CUDA_PROFILE=1): synchronises the stream at each mark.
 class Profile
@@ -523,90 +448,29 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
         else
             tokens[i].assign(headers[i].symbol_count(), 0);
     }
-    // Normal streams: GPU predictor + host range decoders, one variant at a time.
+    // Normal streams: the whole token loop (probability model, bisection
+    // masses, range decoders) runs on the GPU, one model variant at a time.
     for (unsigned mc : {1u, 2u})
     {
         std::vector<std::size_t> ids;
         std::vector<Header> hs;
+        std::vector<ByteView> payloads;
         for (std::size_t i = 0; i < n; ++i)
             if (headers[i].method == 1 && headers[i].model_channels == mc)
             {
                 ids.push_back(i);
                 hs.push_back(headers[i]);
+                payloads.push_back(streams[i].subspan(headers[i].payload_offset, headers[i].payload_bytes));
             }
         if (ids.empty())
             continue;
-        auto& engine = ctx.transformer(mc);
-        engine.decode_begin(hs);
-        std::vector<RangeReader> decoders;
-        std::size_t steps = 0, books = 0, lanes = 0;
-        for (auto i : ids)
+        std::vector<std::vector<std::uint16_t>> decoded;
+        ctx.transformer(mc).decode_streams(hs, payloads, decoded);
+        for (std::size_t j = 0; j < ids.size(); ++j)
         {
-            const auto& h = headers[i];
-            decoders.emplace_back(streams[i].subspan(h.payload_offset, h.payload_bytes));
-            steps = std::max(steps, h.frames / h.batch + (h.frames % h.batch != 0));
-            books = std::max<std::size_t>(books, h.codebooks);
-            lanes += h.lanes();
+            check_token_crc(headers[ids[j]], decoded[j]);
+            tokens[ids[j]] = std::move(decoded[j]);
         }
-        (void)lanes;
-        // Recordings are independent streams: worker w range-decodes the rows
-        // of recordings r with r % workers == w, each in stream order.  The
-        // caller is worker 0; automatically up to 8 (a step is a few
-        // microseconds of work, spread thinner it costs more than it saves).
-        const std::size_t budget = ctx.host_threads() ? ctx.host_threads()
-                                                      : std::min<std::size_t>(8, host_workers(ctx));
-        StepPool pool(std::min<std::size_t>(ids.size(), budget));
-        // Host-side split of the step loop (TSAC_CUDA_PROFILE): time in
-        // decode_predict (input staging, graph launch, waiting for the masses),
-        // in the range decoders, and in commit.
-        double t_predict = 0, t_range = 0, t_commit = 0;
-        using clock = std::chrono::steady_clock;
-        for (std::size_t step = 0; step < steps; ++step)
-            for (std::size_t book = 0; book < books; ++book)
-            {
-                const float* masses = nullptr;
-                const auto t0 = clock::now();
-                const auto rows = engine.decode_predict(step, book, &masses);
-                const auto t1 = clock::now();
-                std::vector<std::uint16_t> decoded(rows.size());
-                // Rows are in stream order per recording (lane, then group); each
-                // recording's decoder consumes its rows in that order (~0.2 us
-                // per symbol).
-                const std::size_t workers = pool.size();
-                auto walk = [&](std::size_t w)
-                {
-                    for (std::size_t j = 0; j < rows.size(); ++j)
-                    {
-                        const auto r = static_cast<std::size_t>(rows[j].recording);
-                        if (r % workers == w)
-                            decoded[j] = decoders[r].symbol(masses + j * 1023);
-                    }
-                };
-                if (workers > 1)
-                    pool.run(walk);
-                else
-                    walk(0);
-                for (std::size_t j = 0; j < rows.size(); ++j)
-                {
-                    const auto r = static_cast<std::size_t>(rows[j].recording);
-                    const auto& h = headers[ids[r]];
-                    const std::size_t lane_b = static_cast<std::size_t>(rows[j].lane) / h.groups;
-                    const std::size_t g = static_cast<std::size_t>(rows[j].lane) % h.groups;
-                    const std::size_t frame = LaneSchedule(h).first_frame(lane_b) + step;
-                    tokens[ids[r]][(frame * h.groups + g) * h.codebooks + book] = decoded[j];
-                }
-                const auto t2 = clock::now();
-                engine.decode_commit(decoded);
-                const auto t3 = clock::now();
-                t_predict += std::chrono::duration<double, std::milli>(t1 - t0).count();
-                t_range += std::chrono::duration<double, std::milli>(t2 - t1).count();
-                t_commit += std::chrono::duration<double, std::milli>(t3 - t2).count();
-            }
-        if (const char* e = std::getenv("TSAC_CUDA_PROFILE"); e && *e && *e != '0')
-            std::fprintf(stderr, "tsac_cuda decode steps %zu: predict %.1f ms, range %.1f ms, commit %.1f ms\n",
-                         steps * books, t_predict, t_range, t_commit);
-        for (auto i : ids)
-            check_token_crc(headers[i], tokens[i]);
     }
     profile.mark("transformer + range");
     // RVQ reconstruction + DAC synthesis over chunk windows

@@ -2,7 +2,9 @@
 
 #include "kernel_timer.hpp"
 
-#include "kernels/codebook_step.cuh"
+#include "kernels/decode_loop.cuh"
+#include "kernels/error_bits.hpp"
+#include "kernels/range_decode.cuh"
 #include "kernels/launch_count.hpp"
 #include "kernels/qlinear.cuh"
 #include "kernels/transformer_ops.cuh"
@@ -411,40 +413,12 @@ void TransformerEngine::predict_known(const Header& header, std::span<const std:
 // ------------------------------------------------------------------ decode --
 namespace
 {
-// Page-locked host staging (graph memcpy nodes need fixed host addresses).
-class PinnedBuffer
+// Device row buffers of one decode step (decode_setup writes them), laid out
+// in one allocation for `rows` codebook rows and `temporal` temporal rows.
+struct StepRowsLayout
 {
-public:
-    explicit PinnedBuffer(std::size_t bytes) : bytes_(bytes)
-    {
-        cuda_ok(cudaHostAlloc(&ptr_, bytes ? bytes : 1, cudaHostAllocDefault), "cudaHostAlloc");
-    }
-    ~PinnedBuffer()
-    {
-        if (ptr_)
-            cudaFreeHost(ptr_);
-    }
-    PinnedBuffer(const PinnedBuffer&) = delete;
-    PinnedBuffer& operator=(const PinnedBuffer&) = delete;
-    template <class T> T* as() const
-    {
-        return static_cast<T*>(ptr_);
-    }
-    std::size_t bytes() const
-    {
-        return bytes_;
-    }
-
-private:
-    void* ptr_ = nullptr;
-    std::size_t bytes_;
-};
-
-// Packed per-step inputs: struct-of-arrays for up to `rows` rows and 12 books.
-struct StepBlock
-{
-    std::size_t meta, lane_rows, books, offsets, counts, tokens, bytes;
-    explicit StepBlock(std::size_t rows)
+    std::size_t tmeta, toffsets, tcounts, csource, clane, cmeta, clanes, cbooks, coffsets, ccounts, dest, bytes;
+    StepRowsLayout(std::size_t rows, std::size_t temporal)
     {
         std::size_t at = 0;
         const auto take = [&](std::size_t n)
@@ -453,436 +427,361 @@ struct StepBlock
             at = align_up(at + n, 256);
             return here;
         };
-        meta = take(rows * sizeof(RowMeta));
-        lane_rows = take(rows * 4);
-        books = take(rows * 4);
-        offsets = take(rows * 4);
-        counts = take(rows * 4);
-        tokens = take(rows * 12 * 2);
+        tmeta = take(temporal * sizeof(RowMeta));
+        toffsets = take(temporal * 4);
+        tcounts = take(temporal * 4);
+        csource = take(rows * 4);
+        clane = take(rows * 4);
+        cmeta = take(rows * sizeof(RowMeta));
+        clanes = take(rows * 4);
+        cbooks = take(rows * 4);
+        coffsets = take(rows * 4);
+        ccounts = take(rows * 4);
+        dest = take(rows * 4);
         bytes = at;
+    }
+    dev::DecodeStepRows at(char* base) const
+    {
+        return {reinterpret_cast<RowMeta*>(base + tmeta), reinterpret_cast<int*>(base + toffsets),
+                reinterpret_cast<int*>(base + tcounts),   reinterpret_cast<int*>(base + csource),
+                reinterpret_cast<int*>(base + clane),     reinterpret_cast<RowMeta*>(base + cmeta),
+                reinterpret_cast<int*>(base + clanes),    reinterpret_cast<int*>(base + cbooks),
+                reinterpret_cast<int*>(base + coffsets),  reinterpret_cast<int*>(base + ccounts),
+                reinterpret_cast<int*>(base + dest)};
     }
 };
 } // namespace
 
 struct TransformerEngine::DecodeState
 {
-    struct Lane
-    {
-        int recording = 0, lane_b = 0, group = 0;
-        int start = 0, length = 0, used = 0;
-        std::vector<std::uint16_t> current;
-        std::deque<std::vector<std::uint16_t>> history;
-        int tslot = 0; // first temporal cache slot (1024 per lane)
-        int cslot = 0; // first codebook cache slot (books per lane)
-    };
     std::vector<Header> headers;
-    std::vector<Lane> lanes;
-    int max_rows = 0, replay_rows = 0;
-    std::size_t tstride = 0, cstride = 0;
-    Workspace ws; // sized once per session: graph-captured pointers stay valid
-    std::uint16_t *tck = nullptr, *tcv = nullptr, *cck = nullptr, *ccv = nullptr,
-                  *cond = nullptr;
-    // Temporal and codebook inputs, staged together with one copy.
-    std::unique_ptr<StepBlock> temporal_block, codebook_block;
-    std::unique_ptr<PinnedBuffer> host_in, host_masses, host_error;
-    char* dev_in = nullptr;
-    int* identity = nullptr;
-    struct StepGraph
+    std::vector<dev::DecodeLane> lanes;
+    std::vector<int> lengths;        // frames per lane
+    std::vector<int> step_position;  // per step: temporal position, -1 = context replay
+    std::vector<std::size_t> token_base;
+    std::size_t tstride = 0, cstride = 0, total_tokens = 0;
+    int max_books = 0;
+    Workspace ws; // sized once per call: graph-captured pointers stay valid
+    std::uint16_t *tck = nullptr, *tcv = nullptr, *cck = nullptr, *ccv = nullptr, *cond = nullptr;
+    std::uint16_t* tokens = nullptr; // batch token array + 12 zero tokens
+    int zero_row = 0;
+    std::uint8_t* payload = nullptr;
+    std::uint64_t *offsets = nullptr, *sizes = nullptr;
+    dev::RangeCursor* cursors = nullptr;
+    dev::DecodeLane* d_lanes = nullptr;
+    dev::DecodeClock* clock = nullptr;
+    int* d_step_position = nullptr;
+    dev::DecodeStepRows rows{};
+    struct Shape
     {
-        cudaGraphExec_t exec;
-        unsigned long long kernels; // kernel nodes, for the launch tally
+        DeviceBuffer row_lane, row_begin;
+        int rows = 0;
+        cudaGraphExec_t exec = nullptr;
+        unsigned long long kernels = 0; // kernel nodes, for the launch tally
     };
-    std::map<std::tuple<int, int, int>, StepGraph> graphs; // (temporal, book, rows)
-    std::vector<LaneRef> last;
-    std::vector<int> last_lanes;
-    std::size_t last_book = 0;
+    // (book, active lanes, temporal rows per lane): the lanes active at a
+    // step are those longer than it, so the count names the set.
+    std::map<std::tuple<int, int, int>, Shape> shapes;
 
     ~DecodeState()
     {
-        for (auto& [key, graph] : graphs)
-            cudaGraphExecDestroy(graph.exec);
+        for (auto& [key, shape] : shapes)
+            if (shape.exec)
+                cudaGraphExecDestroy(shape.exec);
     }
 };
 
 TransformerEngine::~TransformerEngine() = default;
 
-void TransformerEngine::decode_begin(const std::vector<Header>& headers)
+void TransformerEngine::decode_streams(const std::vector<Header>& headers, const std::vector<ByteView>& payloads,
+                                       std::vector<std::vector<std::uint16_t>>& tokens)
 {
-    decode_.reset();
-    auto state = std::make_unique<DecodeState>();
-    state->headers = headers;
+    require(headers.size() == payloads.size(), "decode: one payload per header");
+    tokens.assign(headers.size(), {});
+    if (headers.empty())
+        return;
+    decode_ = std::make_unique<DecodeState>();
+    auto& st = *decode_;
+    auto s = stream_;
+    st.headers = headers;
     int tslots = 0, cslots = 0;
-    bool replay = false;
+    std::size_t payload_bytes = 0;
     for (std::size_t r = 0; r < headers.size(); ++r)
     {
         const auto& h = headers[r];
         check_header(h);
-        require(h.method == 1 && h.model_channels == model_->channels &&
-                    h.codebooks <= model_->books,
+        require(h.method == 1 && h.model_channels == model_->channels && h.codebooks <= model_->books,
                 "Transformer stream/model mismatch");
-        const int F = static_cast<int>(h.frames), B = h.batch, G = h.groups;
-        const int lanes_b = std::min(B, F), base = F / B, extra = F % B;
-        for (int lane = 0; lane < lanes_b; ++lane)
-        {
-            for (int g = 0; g < G; ++g)
+        require(payloads[r].size() == h.payload_bytes, "decode: payload size does not match header");
+        st.token_base.push_back(st.total_tokens);
+        st.total_tokens = checked_add(st.total_tokens, h.symbol_count());
+        payload_bytes = checked_add(payload_bytes, align_up(h.payload_bytes, 16));
+        st.max_books = std::max<int>(st.max_books, h.codebooks);
+        const LaneSchedule schedule(h);
+        for (std::size_t lane = 0; lane < schedule.lanes; ++lane)
+            for (int g = 0; g < h.groups; ++g)
             {
-                DecodeState::Lane l;
-                l.recording = static_cast<int>(r);
-                l.lane_b = lane;
-                l.group = g;
-                l.length = base + (lane < extra);
-                l.start = lane * base + std::min(lane, extra);
-                l.current.assign(h.codebooks, 0);
-                l.tslot = tslots;
-                l.cslot = cslots;
+                require(st.token_base[r] <= 0x7fffffffu, "decode batch exceeds 2^31 tokens");
+                st.lanes.push_back({static_cast<int>(r), g, h.groups, h.codebooks,
+                                    static_cast<int>(schedule.first_frame(lane)), tslots, cslots,
+                                    static_cast<int>(st.token_base[r])});
+                st.lengths.push_back(static_cast<int>(schedule.length(lane)));
                 tslots += context;
                 cslots += h.codebooks;
-                replay = replay || l.length > context;
-                state->lanes.push_back(std::move(l));
             }
-        }
     }
-    auto& st = *state;
-    st.max_rows = static_cast<int>(st.lanes.size());
-    st.replay_rows = st.max_rows * (replay ? replay_frames : 1);
-    const auto cap = static_cast<std::size_t>(std::max(st.replay_rows, 1));
-    st.tstride = static_cast<std::size_t>(tslots) * 512;
-    st.cstride = static_cast<std::size_t>(cslots) * 512;
-    st.tck = st.ws.get<std::uint16_t>("tck", st.tstride * 12);
-    st.tcv = st.ws.get<std::uint16_t>("tcv", st.tstride * 12);
-    st.cck = st.ws.get<std::uint16_t>("cck", st.cstride * 3);
-    st.ccv = st.ws.get<std::uint16_t>("ccv", st.cstride * 3);
-    st.cond = st.ws.get<std::uint16_t>("cond", cap * 512);
-    // Every scratch name at its session maximum, so no pointer moves later.
-    st.ws.get<std::int8_t>("xq", cap * 2048);
-    st.ws.get<float>("xs", cap * 8);
-    st.ws.get<std::uint16_t>("qkv", cap * 1536);
-    st.ws.get<std::uint16_t>("query", cap * 512);
-    st.ws.get<std::uint16_t>("att", cap * 512);
-    st.ws.get<std::uint16_t>("mlp", cap * 2048);
-    st.ws.get<float>("partials", dev::attention_partials_bytes(static_cast<int>(cap), context) / 4);
-    for (const char* name : {"emb", "pemb"})
-        st.ws.get<std::uint16_t>(name, cap * 1024);
-    for (const char* name : {"eq", "pq"})
-        st.ws.get<std::int8_t>(name, cap * 1024);
-    for (const char* name : {"es", "ps"})
-        st.ws.get<float>(name, cap * 4);
-    for (const char* name : {"th", "tout", "ch"})
-        st.ws.get<std::uint16_t>(name, cap * 512);
-    st.ws.get<std::int8_t>("fq", cap * 512);
-    st.ws.get<float>("fs", cap * 2);
-    st.ws.get<std::uint16_t>("logits", cap * 1024);
-    st.ws.get<float>("tree", cap * 1023);
-    st.temporal_block = std::make_unique<StepBlock>(cap);
-    st.codebook_block = std::make_unique<StepBlock>(cap);
-    const auto in_bytes = st.temporal_block->bytes + st.codebook_block->bytes;
-    st.dev_in = st.ws.get<char>("in", in_bytes);
-    st.host_in = std::make_unique<PinnedBuffer>(in_bytes);
-    st.host_masses = std::make_unique<PinnedBuffer>(cap * 1023 * 4);
-    st.host_error = std::make_unique<PinnedBuffer>(4);
-    std::vector<int> ident(cap);
-    for (std::size_t i = 0; i < cap; ++i)
-        ident[i] = static_cast<int>(i);
-    st.identity = st.ws.get<int>("identity", cap);
-    cuda_ok(cudaMemcpyAsync(st.identity, ident.data(), cap * 4, cudaMemcpyHostToDevice, stream_),
-            "H2D");
-    cuda_ok(cudaStreamSynchronize(stream_), "decode session");
-    decode_ = std::move(state);
-}
-
-std::vector<TransformerEngine::LaneRef>
-TransformerEngine::decode_predict(std::size_t step, std::size_t book, const float** masses)
-{
-    require(decode_ != nullptr, "decode session not started");
-    auto& st = *decode_;
-    auto s = stream_;
-    std::vector<int> active;
-    for (int i = 0; i < static_cast<int>(st.lanes.size()); ++i)
-    {
-        const auto& l = st.lanes[static_cast<std::size_t>(i)];
-        if (static_cast<int>(step) < l.length && book < l.current.size())
-            active.push_back(i);
-    }
-    st.last.clear();
-    st.last_lanes = active;
-    st.last_book = book;
-    if (active.empty())
-        return {};
-    const int n = static_cast<int>(active.size());
-    char* host = st.host_in->as<char>();
-    const auto& tb = *st.temporal_block;
-    const auto& cb = *st.codebook_block;
-    char* host_c = host + tb.bytes;
-    char* dev_t = st.dev_in;
-    char* dev_c = st.dev_in + tb.bytes;
-
-    // ---- temporal inputs (book 0): one row per lane, or a 256-row replay.
-    int temporal_rows = 0;
+    require(st.total_tokens + 16 <= 0x7fffffffu, "decode batch exceeds 2^31 tokens");
+    const int steps = *std::max_element(st.lengths.begin(), st.lengths.end());
+    // Temporal positions: TransformerPredictor's context use, the same for
+    // every lane (all lanes start at step 0): positions 0..1023, then a
+    // replay of the last 256 frames at positions 0..255, and so on.
     bool replay = false;
-    if (book == 0)
+    for (int step = 0, used = 0; step < steps; ++step)
     {
-        auto* meta = reinterpret_cast<RowMeta*>(host + tb.meta);
-        auto* lane_rows = reinterpret_cast<int*>(host + tb.lane_rows);
-        auto* offsets = reinterpret_cast<int*>(host + tb.offsets);
-        auto* counts = reinterpret_cast<int*>(host + tb.counts);
-        auto* tokens = reinterpret_cast<std::uint16_t*>(host + tb.tokens);
-        int tok = 0;
-        for (std::size_t j = 0; j < active.size(); ++j)
+        if (used == context)
         {
-            const int i = active[j];
-            auto& l = st.lanes[static_cast<std::size_t>(i)];
-            const int Q = static_cast<int>(l.current.size());
-            const auto add = [&](const std::vector<std::uint16_t>& fb, bool is_replay)
-            {
-                const int position = l.used++;
-                meta[temporal_rows] = {l.tslot + position, l.tslot, position + 1, position,
-                                       (position + 1 > 64 || is_replay) ? 1 : 0};
-                offsets[temporal_rows] = tok;
-                counts[temporal_rows] = Q;
-                std::copy(fb.begin(), fb.end(), tokens + tok);
-                tok += 12;
-                ++temporal_rows;
-            };
-            std::fill(l.current.begin(), l.current.end(), 0);
-            if (l.used == context)
-            {
-                require(static_cast<int>(l.history.size()) == replay_frames,
-                        "incomplete Transformer replay history");
-                l.used = 0;
-                replay = true;
-                for (const auto& fb : l.history)
-                    add(fb, true);
-            }
-            else
-            {
-                add(l.history.empty() ? l.current : l.history.back(), false);
-            }
-            // The lane's conditioning is its last temporal row: entry j of the
-            // scatter maps row (temporal_rows - 1) to lane i.
-            lane_rows[j] = i;
-            reinterpret_cast<int*>(host + tb.books)[j] = temporal_rows - 1;
-        }
-    }
-    // ---- codebook inputs: one row per active lane.
-    {
-        auto* meta = reinterpret_cast<RowMeta*>(host_c + cb.meta);
-        auto* lane_rows = reinterpret_cast<int*>(host_c + cb.lane_rows);
-        auto* books = reinterpret_cast<int*>(host_c + cb.books);
-        auto* offsets = reinterpret_cast<int*>(host_c + cb.offsets);
-        auto* counts = reinterpret_cast<int*>(host_c + cb.counts);
-        auto* tokens = reinterpret_cast<std::uint16_t*>(host_c + cb.tokens);
-        for (int j = 0; j < n; ++j)
-        {
-            const auto& l = st.lanes[static_cast<std::size_t>(active[static_cast<std::size_t>(j)])];
-            meta[j] = {l.cslot + static_cast<int>(book), l.cslot, static_cast<int>(book) + 1, -1, 0};
-            lane_rows[j] = active[static_cast<std::size_t>(j)];
-            books[j] = static_cast<int>(book);
-            offsets[j] = j * 12;
-            counts[j] = static_cast<int>(book);
-            std::copy_n(l.current.begin(), book, tokens + j * 12);
-            st.last.push_back({l.recording,
-                               l.lane_b * st.headers[static_cast<std::size_t>(l.recording)].groups + l.group});
-        }
-    }
-
-    // TSAC_CUDA_FUSED_CODEBOOK=1 runs each codebook step as one cluster
-    // launch (codebook_step.cu).  Bit-identical, but measured slower on B200
-    // (about 178 us against 150 us per step at 48 lanes: each cluster's
-    // phases are serial dependent chains on a few SMs, while the separate
-    // kernels spread every phase over 100+ CTAs), so it is off by default.
-    static const bool fused_codebook_step = []
-    {
-        const char* e = std::getenv("TSAC_CUDA_FUSED_CODEBOOK");
-        return e && e[0] == '1';
-    }();
-    const auto enqueue = [&](int trows)
-    {
-        cuda_ok(cudaMemcpyAsync(st.dev_in, host, tb.bytes + cb.bytes, cudaMemcpyHostToDevice, s), "H2D");
-        auto& ws = st.ws;
-        if (trows > 0)
-        {
-            const auto* d_meta = reinterpret_cast<const RowMeta*>(dev_t + tb.meta);
-            auto* emb = ws.get<std::uint16_t>("emb", static_cast<std::size_t>(trows) * 1024);
-            dev::embed_sum(model_->embeddings.as<std::uint16_t>(),
-                           reinterpret_cast<const std::uint16_t*>(dev_t + tb.tokens),
-                           reinterpret_cast<const int*>(dev_t + tb.offsets),
-                           reinterpret_cast<const int*>(dev_t + tb.counts), trows, emb, s);
-            auto* eq = ws.get<std::int8_t>("eq", static_cast<std::size_t>(trows) * 1024);
-            auto* es = ws.get<float>("es", static_cast<std::size_t>(trows) * 4);
-            auto* th = ws.get<std::uint16_t>("th", static_cast<std::size_t>(trows) * 512);
-            run_linear_bf16(60, emb, trows, th, nullptr, false, eq, es);
-            auto* tout = ws.get<std::uint16_t>("tout", static_cast<std::size_t>(trows) * 512);
-            run_stack(ws, true, trows, th, d_meta, context, st.tck, st.tcv, st.tstride, tout,
-                      nullptr, nullptr);
-            // Conditioning: each active lane's last temporal row.
-            dev::scatter_rows(tout, reinterpret_cast<const int*>(dev_t + tb.books),
-                              reinterpret_cast<const int*>(dev_t + tb.lane_rows), n, st.cond, s);
-        }
-        const auto* d_meta = reinterpret_cast<const RowMeta*>(dev_c + cb.meta);
-        const auto* d_books = reinterpret_cast<const int*>(dev_c + cb.books);
-        auto* tree = ws.get<float>("tree", static_cast<std::size_t>(n) * 1023);
-        if (fused_codebook_step)
-        {
-            // The whole codebook step in one cluster launch (codebook_step.cu).
-            dev::CodebookStepArgs a{};
-            a.rows = n;
-            a.book = static_cast<int>(book);
-            a.cond = st.cond;
-            a.lane_rows = reinterpret_cast<const int*>(dev_c + cb.lane_rows);
-            a.embeddings = model_->embeddings.as<std::uint16_t>();
-            a.tokens = reinterpret_cast<const std::uint16_t*>(dev_c + cb.tokens);
-            a.offsets = reinterpret_cast<const int*>(dev_c + cb.offsets);
-            a.counts = reinterpret_cast<const int*>(dev_c + cb.counts);
-            const auto linear = [&](int p)
-            {
-                const auto& l = model_->projections[static_cast<std::size_t>(p)];
-                return dev::CodebookLinear{l.weights.as<std::int8_t>(), l.scales.as<float>(),
-                                           l.bias.as<float>()};
-            };
-            a.proj61 = linear(61);
-            a.positions = model_->positions.as<std::uint16_t>();
-            a.books = d_books;
-            for (int l = 0; l < 3; ++l)
-            {
-                for (int op = 0; op < 4; ++op)
-                    a.layer[l][op] = linear(projection_index(false, l, op));
-                for (int second = 0; second < 2; ++second)
-                {
-                    const int nrm = norm_index(false, l, second != 0);
-                    a.norm_gain[2 * l + second] = model_->norm_gain[static_cast<std::size_t>(nrm)].as<std::uint16_t>();
-                    a.norm_bias[2 * l + second] = model_->norm_bias[static_cast<std::size_t>(nrm)].as<std::uint16_t>();
-                }
-            }
-            a.norm_gain[6] = model_->norm_gain[static_cast<std::size_t>(final_norm(false))].as<std::uint16_t>();
-            a.norm_bias[6] = model_->norm_bias[static_cast<std::size_t>(final_norm(false))].as<std::uint16_t>();
-            a.proj62 = linear(62);
-            a.gelu = model_->gelu.as<std::uint16_t>();
-            a.meta = d_meta;
-            a.cache_k = st.cck;
-            a.cache_v = st.ccv;
-            a.cache_stride = st.cstride;
-            a.tree = tree;
-            a.error_word = error_word();
-            KernelTimer::Scope timing("codebook_step", s, 0.0);
-            dev::codebook_step(a, s);
+            st.step_position.push_back(-1);
+            used = replay_frames;
+            replay = true;
         }
         else
         {
-            auto* ch = ws.get<std::uint16_t>("ch", static_cast<std::size_t>(n) * 512);
-            if (book == 0)
-            {
-                dev::add_positions(st.cond, reinterpret_cast<const int*>(dev_c + cb.lane_rows), d_books,
-                                   model_->positions.as<std::uint16_t>(), n, ch, s);
-            }
-            else
-            {
-                // Prefix embedding sum (BF8L-quantized in the same kernel),
-                // cb_proj, and the book's position row added as a residual
-                // broadcast to every row: all rows of a step share `book`, and
-                // bf16(pos + y) is add_positions' bf16(y + pos).
-                auto* pemb = ws.get<std::uint16_t>("pemb", static_cast<std::size_t>(n) * 1024);
-                auto* pq = ws.get<std::int8_t>("pq", static_cast<std::size_t>(n) * 1024);
-                auto* ps = ws.get<float>("ps", static_cast<std::size_t>(n) * 4);
-                dev::embed_sum(model_->embeddings.as<std::uint16_t>(),
-                               reinterpret_cast<const std::uint16_t*>(dev_c + cb.tokens),
-                               reinterpret_cast<const int*>(dev_c + cb.offsets),
-                               reinterpret_cast<const int*>(dev_c + cb.counts), n, pemb, s, pq, ps,
-                               error_word());
-                run_linear(61, pq, ps, n, ch, model_->positions.as<std::uint16_t>() + book * 512, false, 0);
-            }
-            auto* fq = ws.get<std::int8_t>("fq", static_cast<std::size_t>(n) * 512);
-            auto* fs = ws.get<float>("fs", static_cast<std::size_t>(n) * 2);
-            run_stack(ws, false, n, ch, d_meta, 12, st.cck, st.ccv, st.cstride, nullptr, fq, fs);
-            auto* logits = ws.get<std::uint16_t>("logits", static_cast<std::size_t>(n) * 1024);
-            run_linear(62, fq, fs, n, logits, nullptr, false);
-            KernelTimer::Scope timing("softmax_tree", s, 0.0);
-            dev::softmax_tree(logits, n, nullptr, nullptr, tree, error_word(), s);
+            st.step_position.push_back(used++);
         }
-        cuda_ok(cudaMemcpyAsync(st.host_masses->as<void>(), tree, static_cast<std::size_t>(n) * 1023 * 4,
-                                cudaMemcpyDeviceToHost, s),
-                "D2H");
-        cuda_ok(cudaMemcpyAsync(st.host_error->as<void>(), error_word(), 4, cudaMemcpyDeviceToHost, s),
-                "D2H");
-    };
+    }
+    const int lane_count = static_cast<int>(st.lanes.size());
+    const int temporal_cap = lane_count * (replay ? replay_frames : 1);
+    const auto cap = static_cast<std::size_t>(temporal_cap);
+    st.tstride = static_cast<std::size_t>(tslots) * 512;
+    st.cstride = static_cast<std::size_t>(cslots) * 512;
+    auto& ws = st.ws;
+    st.tck = ws.get<std::uint16_t>("tck", st.tstride * 12);
+    st.tcv = ws.get<std::uint16_t>("tcv", st.tstride * 12);
+    st.cck = ws.get<std::uint16_t>("cck", st.cstride * 3);
+    st.ccv = ws.get<std::uint16_t>("ccv", st.cstride * 3);
+    st.cond = ws.get<std::uint16_t>("cond", static_cast<std::size_t>(lane_count) * 512);
+    // Every scratch name at its call maximum, so no pointer moves later.
+    ws.get<std::int8_t>("xq", cap * 2048);
+    ws.get<float>("xs", cap * 8);
+    ws.get<std::uint16_t>("qkv", cap * 1536);
+    ws.get<std::uint16_t>("query", cap * 512);
+    ws.get<std::uint16_t>("att", cap * 512);
+    ws.get<std::uint16_t>("mlp", cap * 2048);
+    ws.get<float>("partials", dev::attention_partials_bytes(static_cast<int>(cap), context) / 4);
+    for (const char* name : {"emb", "pemb"})
+        ws.get<std::uint16_t>(name, cap * 1024);
+    for (const char* name : {"eq", "pq"})
+        ws.get<std::int8_t>(name, cap * 1024);
+    for (const char* name : {"es", "ps"})
+        ws.get<float>(name, cap * 4);
+    for (const char* name : {"th", "tout", "ch"})
+        ws.get<std::uint16_t>(name, cap * 512);
+    ws.get<std::int8_t>("fq", cap * 512);
+    ws.get<float>("fs", cap * 2);
+    ws.get<std::uint16_t>("logits", cap * 1024);
+    ws.get<float>("tree", cap * 1023);
+    const StepRowsLayout layout(static_cast<std::size_t>(lane_count), cap);
+    st.rows = layout.at(ws.get<char>("step_rows", layout.bytes));
+    // Batch token array (+ 16 zero tokens: the feedback before frame 0).
+    st.zero_row = static_cast<int>(st.total_tokens);
+    st.tokens = ws.get<std::uint16_t>("tokens", st.total_tokens + 16);
+    cuda_ok(cudaMemsetAsync(st.tokens, 0, (st.total_tokens + 16) * 2, s), "memset");
+    // Range decoders: payloads, cursors.
+    std::vector<std::uint8_t> packed(payload_bytes);
+    std::vector<std::uint64_t> offs, sizes;
+    for (std::size_t r = 0, at = 0; r < headers.size(); ++r)
+    {
+        std::copy(payloads[r].begin(), payloads[r].end(), packed.begin() + static_cast<std::ptrdiff_t>(at));
+        offs.push_back(at);
+        sizes.push_back(payloads[r].size());
+        at += align_up(payloads[r].size(), 16);
+    }
+    st.payload = ws.get<std::uint8_t>("payload", packed.size() + 16);
+    st.offsets = ws.get<std::uint64_t>("payload_offsets", offs.size());
+    st.sizes = ws.get<std::uint64_t>("payload_sizes", sizes.size());
+    st.cursors = ws.get<dev::RangeCursor>("cursors", headers.size());
+    st.d_lanes = ws.get<dev::DecodeLane>("lanes", st.lanes.size());
+    st.clock = ws.get<dev::DecodeClock>("clock", 1);
+    st.d_step_position = ws.get<int>("step_position", st.step_position.size());
+    cuda_ok(cudaMemcpyAsync(st.payload, packed.data(), packed.size(), cudaMemcpyHostToDevice, s), "H2D");
+    cuda_ok(cudaMemcpyAsync(st.offsets, offs.data(), offs.size() * 8, cudaMemcpyHostToDevice, s), "H2D");
+    cuda_ok(cudaMemcpyAsync(st.sizes, sizes.data(), sizes.size() * 8, cudaMemcpyHostToDevice, s), "H2D");
+    cuda_ok(cudaMemcpyAsync(st.d_lanes, st.lanes.data(), st.lanes.size() * sizeof(dev::DecodeLane),
+                            cudaMemcpyHostToDevice, s),
+            "H2D");
+    cuda_ok(cudaMemcpyAsync(st.d_step_position, st.step_position.data(), st.step_position.size() * 4,
+                            cudaMemcpyHostToDevice, s),
+            "H2D");
+    cuda_ok(cudaMemsetAsync(st.clock, 0, sizeof(dev::DecodeClock), s), "memset");
+    dev::range_start(st.payload, st.offsets, st.sizes, st.cursors, static_cast<int>(headers.size()),
+                     error_word(), s);
+    cuda_ok(cudaStreamSynchronize(s), "decode setup"); // host staging vectors go out of scope
 
+    // TSAC_CUDA_DECODE_GRAPHS=0 runs every step's kernels directly (each
+    // kernel family then shows in the kernel timing).
+    static const bool graphs_enabled = []
+    {
+        const char* e = std::getenv("TSAC_CUDA_DECODE_GRAPHS");
+        return !(e && e[0] == '0');
+    }();
     // Algorithmic bytes of one step: the int8 weights it streams.
     const auto weights = [&](int p)
     {
         const auto& l = model_->projections[static_cast<std::size_t>(p)];
         return static_cast<double>(l.input) * l.output;
     };
-    double weight_bytes = weights(61) + weights(62);
+    double codebook_bytes = weights(61) + weights(62), temporal_bytes = weights(60);
     for (int p = 48; p < 60; ++p)
-        weight_bytes += weights(p);
+        codebook_bytes += weights(p);
+    for (int p = 0; p < 48; ++p)
+        temporal_bytes += weights(p);
+
+    for (int step = 0; step < steps; ++step)
+    {
+        int active = 0;
+        for (const int length : st.lengths)
+            active += length > step;
+        const int per_lane = st.step_position[static_cast<std::size_t>(step)] < 0 ? replay_frames : 1;
+        for (int book = 0; book < st.max_books; ++book)
+        {
+            const auto key = std::make_tuple(book, active, book == 0 ? per_lane : 1);
+            auto found = st.shapes.find(key);
+            if (found == st.shapes.end())
+            {
+                // Rows of this shape: lanes longer than `step` whose recording
+                // has book `book`, in stream order; each recording's rows are
+                // consecutive.
+                DecodeState::Shape shape;
+                std::vector<int> row_lane;
+                std::vector<int> row_begin(headers.size() + 1, 0);
+                for (int i = 0; i < lane_count; ++i)
+                {
+                    const auto& lane = st.lanes[static_cast<std::size_t>(i)];
+                    if (st.lengths[static_cast<std::size_t>(i)] > step && book < lane.books)
+                    {
+                        row_lane.push_back(i);
+                        ++row_begin[static_cast<std::size_t>(lane.recording) + 1];
+                    }
+                }
+                for (std::size_t r = 0; r < headers.size(); ++r)
+                    row_begin[r + 1] += row_begin[r];
+                shape.rows = static_cast<int>(row_lane.size());
+                shape.row_lane.resize(std::max<std::size_t>(row_lane.size(), 1) * 4);
+                shape.row_begin.resize(row_begin.size() * 4);
+                cuda_ok(cudaMemcpy(shape.row_lane.as<void>(), row_lane.data(), row_lane.size() * 4,
+                                   cudaMemcpyHostToDevice),
+                        "H2D");
+                cuda_ok(cudaMemcpy(shape.row_begin.as<void>(), row_begin.data(), row_begin.size() * 4,
+                                   cudaMemcpyHostToDevice),
+                        "H2D");
+                found = st.shapes.emplace(key, std::move(shape)).first;
+                auto& sh = found->second;
+                if (graphs_enabled && sh.rows > 0)
+                {
+                    cudaGraph_t graph = nullptr;
+                    {
+                        dev::CaptureTally tally;
+                        cuda_ok(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "capture");
+                        enqueue_decode_step(sh.row_lane.as<int>(), sh.row_begin.as<int>(), sh.rows, book,
+                                            book == 0 ? per_lane : 1);
+                        cuda_ok(cudaStreamEndCapture(s, &graph), "capture");
+                        sh.kernels = tally.kernels();
+                    }
+                    const auto status = cudaGraphInstantiate(&sh.exec, graph, 0);
+                    cudaGraphDestroy(graph);
+                    cuda_ok(status, "cudaGraphInstantiate");
+                }
+            }
+            auto& sh = found->second;
+            if (sh.rows == 0)
+                continue;
+            KernelTimer::Scope timing("decode_step", s, codebook_bytes + (book == 0 ? temporal_bytes : 0.0));
+            if (sh.exec)
+            {
+                cuda_ok(cudaGraphLaunch(sh.exec, s), "cudaGraphLaunch");
+                dev::note_launch(sh.kernels);
+            }
+            else
+            {
+                enqueue_decode_step(sh.row_lane.as<int>(), sh.row_begin.as<int>(), sh.rows, book,
+                                    book == 0 ? per_lane : 1);
+            }
+        }
+    }
+    unsigned word = 0;
+    cuda_ok(cudaMemcpyAsync(&word, error_word(), 4, cudaMemcpyDeviceToHost, s), "D2H");
+    for (std::size_t r = 0; r < headers.size(); ++r)
+    {
+        tokens[r].resize(headers[r].symbol_count());
+        cuda_ok(cudaMemcpyAsync(tokens[r].data(), st.tokens + st.token_base[r], tokens[r].size() * 2,
+                                cudaMemcpyDeviceToHost, s),
+                "D2H");
+    }
+    cuda_ok(cudaStreamSynchronize(s), "decode loop");
+    if (word)
+    {
+        cuda_ok(cudaMemset(error_word(), 0, 4), "memset");
+        if (word & dev::error_nonfinite)
+            throw NumericError("Transformer activations must be finite");
+        throw Error("range code outside interval");
+    }
+}
+
+void TransformerEngine::enqueue_decode_step(const int* row_lane, const int* row_begin, int n, int book,
+                                            int per_lane)
+{
+    auto& st = *decode_;
+    auto& ws = st.ws;
+    auto s = stream_;
+    const auto& r = st.rows;
+    dev::decode_setup(st.d_lanes, row_lane, n, book, per_lane, st.d_step_position, st.clock, st.zero_row, r, s);
     if (book == 0)
     {
-        weight_bytes += weights(60);
-        for (int p = 0; p < 48; ++p)
-            weight_bytes += weights(p);
+        const int trows = n * per_lane;
+        auto* emb = ws.get<std::uint16_t>("emb", static_cast<std::size_t>(trows) * 1024);
+        dev::embed_sum(model_->embeddings.as<std::uint16_t>(), st.tokens, r.temporal_offsets, r.temporal_counts,
+                       trows, emb, s);
+        auto* eq = ws.get<std::int8_t>("eq", static_cast<std::size_t>(trows) * 1024);
+        auto* es = ws.get<float>("es", static_cast<std::size_t>(trows) * 4);
+        auto* th = ws.get<std::uint16_t>("th", static_cast<std::size_t>(trows) * 512);
+        run_linear_bf16(60, emb, trows, th, nullptr, false, eq, es);
+        auto* tout = ws.get<std::uint16_t>("tout", static_cast<std::size_t>(trows) * 512);
+        run_stack(ws, true, trows, th, r.temporal_meta, context, st.tck, st.tcv, st.tstride, tout, nullptr,
+                  nullptr);
+        // Conditioning: each active lane's last temporal row.
+        dev::scatter_rows(tout, r.cond_source, r.cond_lane, n, st.cond, s);
     }
-    // TSAC_CUDA_DECODE_GRAPHS=0 runs every step's kernels directly (each
-    // kernel family then shows in the kernel timing); replay steps (once per
-    // 768 frames of a lane) always run directly.
-    static const bool graphs_enabled = []
+    auto* ch = ws.get<std::uint16_t>("ch", static_cast<std::size_t>(n) * 512);
+    if (book == 0)
     {
-        const char* e = std::getenv("TSAC_CUDA_DECODE_GRAPHS");
-        return !(e && e[0] == '0');
-    }();
-    if (replay || !graphs_enabled)
-    {
-        enqueue(temporal_rows);
+        dev::add_positions(st.cond, r.codebook_lane, r.codebook_book, model_->positions.as<std::uint16_t>(), n, ch,
+                           s);
     }
     else
     {
-        const auto key = std::make_tuple(book == 0 ? 1 : 0, static_cast<int>(book), n);
-        auto found = st.graphs.find(key);
-        if (found == st.graphs.end())
-        {
-            cudaGraph_t graph = nullptr;
-            unsigned long long kernels = 0;
-            {
-                dev::CaptureTally tally;
-                cuda_ok(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "capture");
-                enqueue(temporal_rows);
-                cuda_ok(cudaStreamEndCapture(s, &graph), "capture");
-                kernels = tally.kernels();
-            }
-            cudaGraphExec_t exec = nullptr;
-            const auto status = cudaGraphInstantiate(&exec, graph, 0);
-            cudaGraphDestroy(graph);
-            cuda_ok(status, "cudaGraphInstantiate");
-            found = st.graphs.emplace(key, DecodeState::StepGraph{exec, kernels}).first;
-        }
-        KernelTimer::Scope timing("decode_step", s, weight_bytes);
-        cuda_ok(cudaGraphLaunch(found->second.exec, s), "cudaGraphLaunch");
-        dev::note_launch(found->second.kernels);
+        // Prefix embedding sum (BF8L-quantized in the same kernel), cb_proj,
+        // and the book's position row added as a residual broadcast to every
+        // row: all rows of a step share `book`, and bf16(pos + y) is
+        // add_positions' bf16(y + pos).
+        auto* pemb = ws.get<std::uint16_t>("pemb", static_cast<std::size_t>(n) * 1024);
+        auto* pq = ws.get<std::int8_t>("pq", static_cast<std::size_t>(n) * 1024);
+        auto* ps = ws.get<float>("ps", static_cast<std::size_t>(n) * 4);
+        dev::embed_sum(model_->embeddings.as<std::uint16_t>(), st.tokens, r.codebook_offsets, r.codebook_counts, n,
+                       pemb, s, pq, ps, error_word());
+        run_linear(61, pq, ps, n, ch, model_->positions.as<std::uint16_t>() + book * 512, false, 0);
     }
-    cuda_ok(cudaStreamSynchronize(s), "decode step");
-    if (*st.host_error->as<unsigned>())
+    auto* fq = ws.get<std::int8_t>("fq", static_cast<std::size_t>(n) * 512);
+    auto* fs = ws.get<float>("fs", static_cast<std::size_t>(n) * 2);
+    run_stack(ws, false, n, ch, r.codebook_meta, 12, st.cck, st.ccv, st.cstride, nullptr, fq, fs);
+    auto* logits = ws.get<std::uint16_t>("logits", static_cast<std::size_t>(n) * 1024);
+    run_linear(62, fq, fs, n, logits, nullptr, false);
+    auto* tree = ws.get<float>("tree", static_cast<std::size_t>(n) * 1023);
     {
-        cuda_ok(cudaMemset(error_word(), 0, 4), "memset");
-        throw NumericError("Transformer activations must be finite");
+        KernelTimer::Scope timing("softmax_tree", s, 0.0);
+        dev::softmax_tree(logits, n, nullptr, nullptr, tree, error_word(), s);
     }
-    *masses = st.host_masses->as<float>();
-    return st.last;
-}
-
-void TransformerEngine::decode_commit(std::span<const std::uint16_t> tokens)
-{
-    require(decode_ != nullptr, "decode session not started");
-    auto& st = *decode_;
-    require(tokens.size() == st.last_lanes.size(), "decode commit does not match prediction");
-    for (std::size_t j = 0; j < tokens.size(); ++j)
-    {
-        require(tokens[j] < 1024, "Transformer feedback token exceeds alphabet");
-        auto& l = st.lanes[static_cast<std::size_t>(st.last_lanes[j])];
-        l.current[st.last_book] = tokens[j];
-        if (st.last_book + 1 == l.current.size())
-        {
-            l.history.push_back(l.current);
-            if (static_cast<int>(l.history.size()) > replay_frames)
-                l.history.pop_front();
-        }
-    }
+    KernelTimer::Scope timing("range_decode", s, 0.0);
+    dev::range_decode_rows(st.payload, st.offsets, st.sizes, st.cursors, static_cast<int>(st.headers.size()),
+                           row_begin, tree, r.destination, st.tokens, error_word(), s);
 }
 } // namespace tsacb

@@ -13,10 +13,11 @@
 // Q15 probabilities of the bisection nodes on the path to its token.
 //
 // Decode: one (step, book) at a time for all lanes of all recordings in the
-// batch; emits the left-child subtree masses the host range decoder walks.
-// Each step is a CUDA graph (captured once per (stack, book, rows), replayed
-// with its inputs staged through one pinned block), so a step costs one
-// launch and one synchronisation on the host.
+// batch, entirely on the device: each step's rows are set up from a device
+// step clock, the model emits each row's bisection masses, and the device
+// range decoders write the symbols into the batch token array that the next
+// step's embeddings read.  Each step shape is a CUDA graph captured once, so
+// the host only enqueues graph launches and synchronises once per batch.
 #pragma once
 #include "device.hpp"
 #include "kernels/row_meta.hpp"
@@ -58,19 +59,13 @@ public:
     void predict_known(const Header& header, std::span<const std::uint16_t> tokens,
                        std::uint16_t* q15, float* probabilities);
 
-    // --- decode stepping for a batch of recordings (same model) -------------
-    void decode_begin(const std::vector<Header>& headers);
-    struct LaneRef
-    {
-        int recording, lane;
-    };
-    // Computes the distributions of book `book` at `step` for every lane of
-    // every recording that has that step; returns the rows' lanes in stream
-    // order and a pointer to their left-child masses [row][1023] (pinned host
-    // memory, valid until the next call).
-    std::vector<LaneRef> decode_predict(std::size_t step, std::size_t book, const float** masses);
-    // Commits the decoded tokens of the rows returned by the last decode_predict.
-    void decode_commit(std::span<const std::uint16_t> tokens);
+    // --- decode: the whole token loop of a batch of normal streams on the GPU
+    // payloads[r]: recording r's range-coded payload (headers[r].payload_bytes);
+    // tokens[r] receives its tokens [frame][group][book].  Runs every (step,
+    // book) of every lane as device work (the probability model, the bisection
+    // masses and the range decoders), with one host synchronisation at the end.
+    void decode_streams(const std::vector<Header>& headers, const std::vector<ByteView>& payloads,
+                        std::vector<std::vector<std::uint16_t>>& tokens);
 
     unsigned* error_word() const
     {
@@ -93,6 +88,8 @@ private:
                  const dev::RowMeta* meta, std::uint16_t* query, std::uint16_t* cache_k,
                  std::uint16_t* cache_v, std::uint16_t* qkv);
     void quantize(const std::uint16_t* x, int rows, int k, std::int8_t* xq, float* xs);
+    // One (step, book) of the decode loop for the rows of one shape.
+    void enqueue_decode_step(const int* row_lane, const int* row_begin, int rows, int book, int per_lane);
     void run_stack(Workspace& ws, bool temporal, int rows, std::uint16_t* h,
                    const void* meta_device, int max_time, std::uint16_t* cache_k,
                    std::uint16_t* cache_v, std::size_t cache_layer_stride,

@@ -19,6 +19,7 @@
 #include "kernels/error_bits.hpp"
 #include "kernels/launch_count.hpp"
 #include "kernels/numeric.cuh"
+#include "kernels/pdl.cuh"
 #include "kernels/range_decode.cuh"
 #include "kernels/row_ops.cuh"
 #include "range_core.hpp"
@@ -145,6 +146,57 @@ __global__ void __launch_bounds__(128)
             atomicOr(error_word, error_range);
     }
 }
+// The decode loop's range decoding: one warp per stream (recording), whose
+// rows of this step are rows [row_begin[s], row_begin[s + 1]) in stream
+// order.  For each row the warp stages the 1023 left-child masses in shared
+// memory with coalesced loads, then lane 0 walks the bisection heap from
+// there; the symbol goes to tokens[destination[row]], where the next step's
+// embeddings read it.
+constexpr int rows_warps = 4;
+
+__global__ void __launch_bounds__(rows_warps * 32)
+    range_decode_rows_kernel(const std::uint8_t* __restrict__ bytes, const std::uint64_t* __restrict__ offsets,
+                             const std::uint64_t* __restrict__ sizes, RangeCursor* cursors, int streams,
+                             const int* __restrict__ row_begin, const float* __restrict__ masses,
+                             const int* __restrict__ destination, std::uint16_t* __restrict__ tokens,
+                             unsigned* error_word)
+{
+    pdl_prologue();
+    __shared__ float staged[rows_warps][1024];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int s = blockIdx.x * rows_warps + warp;
+    if (s >= streams)
+        return;
+    const int first = row_begin[s], last = row_begin[s + 1];
+    if (first == last)
+        return;
+    const std::uint8_t* payload = bytes + offsets[s];
+    const std::uint64_t size = sizes[s];
+    RangeCursor c = cursors[s];
+    const bool was_running = c.status == 0;
+    float* heap = staged[warp];
+    for (int row = first; row < last; ++row)
+    {
+        const float* m = masses + static_cast<size_t>(row) * 1023;
+        for (int i = lane; i < 1023; i += 32)
+            heap[i] = m[i];
+        __syncwarp();
+        if (lane == 0)
+        {
+            std::uint16_t symbol = 0;
+            if (c.status == 0)
+                decode_symbol(payload, size, c, heap, symbol);
+            tokens[destination[row]] = c.status == 0 ? symbol : 0;
+        }
+        __syncwarp();
+    }
+    if (lane == 0)
+    {
+        cursors[s] = c;
+        if (was_running && c.status != 0 && error_word)
+            atomicOr(error_word, error_range);
+    }
+}
 } // namespace
 
 void range_start(const std::uint8_t* bytes, const std::uint64_t* offsets, const std::uint64_t* sizes,
@@ -165,6 +217,17 @@ void range_decode(const std::uint8_t* bytes, const std::uint64_t* offsets, const
         return;
     range_decode_kernel<<<(streams + 3) / 4, 128, 0, stream>>>(bytes, offsets, sizes, cursors, streams, rows,
                                                               count, masses, symbols, error_word);
+    note_launch();
+}
+void range_decode_rows(const std::uint8_t* bytes, const std::uint64_t* offsets, const std::uint64_t* sizes,
+                       RangeCursor* cursors, int streams, const int* row_begin, const float* masses,
+                       const int* destination, std::uint16_t* tokens, unsigned* error_word, cudaStream_t stream)
+{
+    if (streams <= 0)
+        return;
+    launch_pdl(range_decode_rows_kernel, dim3((streams + rows_warps - 1) / rows_warps), dim3(rows_warps * 32), 0,
+               stream, bytes, offsets, sizes, cursors, streams, row_begin, masses, destination, tokens,
+               error_word);
     note_launch();
 }
 } // namespace tsacb::dev

@@ -29,4 +29,10 @@ void range_start(const std::uint8_t* bytes, const std::uint64_t* offsets, const 
 void range_decode(const std::uint8_t* bytes, const std::uint64_t* offsets, const std::uint64_t* sizes,
                   RangeCursor* cursors, int streams, const int* rows, int count, const float* masses,
                   std::uint16_t* symbols, unsigned* error_word, cudaStream_t stream);
+// The decode loop's form: stream s decodes rows [row_begin[s], row_begin[s+1])
+// in order (row_begin has streams + 1 entries), and row r's symbol is stored
+// to tokens[destination[r]].  Launched with programmatic dependent launch.
+void range_decode_rows(const std::uint8_t* bytes, const std::uint64_t* offsets, const std::uint64_t* sizes,
+                       RangeCursor* cursors, int streams, const int* row_begin, const float* masses,
+                       const int* destination, std::uint16_t* tokens, unsigned* error_word, cudaStream_t stream);
 } // namespace tsacb::dev

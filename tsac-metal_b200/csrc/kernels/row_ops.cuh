@@ -1,6 +1,6 @@
-// Per-row device routines of the Transformer, shared by the standalone
-// kernels (transformer_ops.cu, attention.cu, qlinear.cu) and the fused
-// codebook-step kernel (codebook_step.cu), so every path runs the same
+// Per-row device routines of the Transformer, shared by its kernels
+// (transformer_ops.cu, attention.cu, qlinear.cu) and the device range
+// decoder (range_decode.cu: conditional_q15), so every path runs the same
 // operations in the same order.
 //
 // Reference arithmetic restated (reference project paths):
