@@ -79,6 +79,17 @@ typedef struct tsac_cuda_encode_options
 int tsac_cuda_context_create(const char* package_directory, int device, tsac_cuda_context** out);
 void tsac_cuda_context_destroy(tsac_cuda_context* context);
 
+/* Policy limits (tsac::Limits, include/tsac/types.hpp:20-31), checked
+ * before any allocation exactly where the reference checks them: input and
+ * padded PCM elements, symbols, decoded PCM bytes and elements, stream size.
+ * A new context uses the reference's defaults. */
+typedef struct tsac_cuda_limits
+{
+    size_t file_bytes, symbols, pcm_bytes, cache_bytes, tensor_elements, tensors, metadata_bytes,
+        name_bytes;
+} tsac_cuda_limits;
+int tsac_cuda_set_limits(tsac_cuda_context* context, const tsac_cuda_limits* limits);
+
 /* Decoder synthesis arithmetic of a context.  0 (the default): the wide DAC
  * decoder convolutions run on the tensor cores in 3xTF32 (decoded PCM within
  * 1e-4 * (1 + max(|a|, |b|)) of the reference, the reference's own pipeline
@@ -89,10 +100,10 @@ int tsac_cuda_set_exact_synthesis(tsac_cuda_context* context, int exact);
 
 /* Host worker budget of a context (the reference CLI's -T, src/cli.cpp:66-68,
  * passed to AppleArmAnalyzer, src/codec.cpp:117-120, which accepts 1-256,
- * src/apple-arm/audio_analyzer.cpp:93): range encoding of a batch's recordings
- * and each decode step's range decoding use at most `threads` host threads.
- * 0 (the default): automatic (all hardware threads for encoding, up to 8 for
- * the per-step decoding).  More than 256 is TSAC_CUDA_ERROR. */
+ * src/apple-arm/audio_analyzer.cpp:93): range encoding of a batch's
+ * recordings uses at most `threads` host threads (decoding runs its range
+ * decoders on the GPU).  0 (the default): all hardware threads.  More than
+ * 256 is TSAC_CUDA_ERROR. */
 int tsac_cuda_set_host_threads(tsac_cuda_context* context, unsigned threads);
 
 /* AudioAnalyzer::encode (include/tsac/audio_analyzer.hpp:33-34) for a host

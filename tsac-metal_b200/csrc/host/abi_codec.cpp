@@ -407,6 +407,18 @@ int tsac_cuda_set_exact_synthesis(tsac_cuda_context* ctx, int exact)
         });
 }
 
+int tsac_cuda_set_limits(tsac_cuda_context* ctx, const tsac_cuda_limits* limits)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            tsacb::require(ctx && limits, "null argument");
+            ctx->impl.set_limits({limits->file_bytes, limits->symbols, limits->pcm_bytes, limits->cache_bytes,
+                                  limits->tensor_elements, limits->tensors, limits->metadata_bytes,
+                                  limits->name_bytes});
+        });
+}
+
 int tsac_cuda_set_host_threads(tsac_cuda_context* ctx, unsigned threads)
 {
     return tsacb::guarded(

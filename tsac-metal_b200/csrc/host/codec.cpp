@@ -443,6 +443,10 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
     for (std::size_t i = 0; i < n; ++i)
     {
         headers[i] = read_header(streams[i], ctx.limits());
+        // allocate_pcm's limit (src/common/audio_analyzer.cpp), checked
+        // before any device work rather than after the token loop.
+        require(checked_mul(headers[i].channels(), headers[i].samples_per_channel()) <= ctx.limits().tensor_elements,
+                "output audio exceeds element limit");
         if (headers[i].method == 0)
             tokens[i] = fast_tokens(streams[i], ctx.limits());
         else

@@ -26,6 +26,10 @@ public:
     {
         return limits_;
     }
+    void set_limits(const Limits& limits)
+    {
+        limits_ = limits;
+    }
     cudaStream_t stream() const
     {
         return stream_;
