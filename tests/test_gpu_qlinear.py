@@ -73,7 +73,22 @@ def test_cfg1_shapes_bit_exact(k, n, m):
     assert np.array_equal(_run_gpu(w, ws, b, x), _run_oracle(w, ws, b, x))
 
 
-@pytest.mark.parametrize("m", [3, 40])
+@pytest.mark.parametrize("k,n", MODEL_SHAPES)
+@pytest.mark.parametrize("m", [256, 257, 383, 1000])
+def test_gemm_model_shapes_bit_exact(k, n, m):
+    """From 256 rows the tcgen05 int8 GEMM runs (qlinear_tc.cu): full and
+    partial 128-row tiles, every model projection shape, edge-value rows."""
+    w, ws, b, x = _case(k, n, m, seed=k * 3 + n + m, special=True)
+    assert np.array_equal(_run_gpu(w, ws, b, x), _run_oracle(w, ws, b, x))
+
+
+@pytest.mark.parametrize("k,n", [(1024, 1024), (1024, 4096), (4096, 1024)])
+def test_gemm_cfg1_shapes_bit_exact(k, n):
+    w, ws, b, x = _case(k, n, 512, seed=k + n)
+    assert np.array_equal(_run_gpu(w, ws, b, x), _run_oracle(w, ws, b, x))
+
+
+@pytest.mark.parametrize("m", [3, 40, 300])
 def test_residual_epilogue(m):
     w, ws, b, x = _case(512, 512, m, seed=99)
     rng = np.random.default_rng(5)

@@ -96,8 +96,9 @@ double linear_work(int rows, double n, double k)
 {
     const double m = rows;
     // GEMV-shaped launches are weight-streaming (bytes); GEMM launches count int8 ops.
-    return rows <= 256 ? n * k + 4 * n * k / 256 + 4 * n + m * k + 4 * m * k / 256 + 2 * m * n
-                       : 2.0 * m * n * k;
+    return dev::qlinear_uses_gemm(rows, static_cast<int>(n), static_cast<int>(k))
+               ? 2.0 * m * n * k
+               : n * k + 4 * n * k / 256 + 4 * n + m * k + 4 * m * k / 256 + 2 * m * n;
 }
 } // namespace
 
@@ -119,7 +120,9 @@ void TransformerEngine::run_linear(int projection, const std::int8_t* xq, const 
     a.n = l.output;
     a.k = l.input;
     a.residual_stride = residual_stride;
-    KernelTimer::Scope timing(rows <= 256 ? "qlinear_small" : "qlinear_gemm", stream_,
+    a.error_word = error_word();
+    KernelTimer::Scope timing(dev::qlinear_uses_gemm(rows, l.output, l.input) ? "qlinear_gemm" : "qlinear_small",
+                              stream_,
                               linear_work(rows, l.output, l.input));
     dev::qlinear_matmul(a, stream_);
 }

@@ -20,6 +20,8 @@
 #include "kernels/numeric.cuh"
 #include "kernels/row_ops.cuh"
 #include "kernels/pdl.cuh"
+#include "kernels/qlinear_epilogue.cuh"
+#include "kernels/qlinear_tc.cuh"
 
 #include <atomic>
 
@@ -56,131 +58,7 @@ __global__ void quantize_bf8l_kernel(const std::uint16_t* __restrict__ x, int k,
     }
 }
 
-struct Epilogue
-{
-    const float* bias;
-    const std::uint16_t* residual; // [M][residual_stride] or null
-    const std::uint16_t* lut;      // 65536-entry bf16 map or null
-    int residual_stride;           // 0: one residual row for every column
-};
-
-__device__ __forceinline__ std::uint16_t finish(float sum, int m, int n, const Epilogue& e)
-{
-    std::uint16_t y = to_bf16(__fadd_rn(sum, e.bias[n]));
-    if (e.residual)
-    {
-        y = to_bf16(__fadd_rn(from_bf16(e.residual[static_cast<size_t>(m) * e.residual_stride + n]),
-                              from_bf16(y)));
-    }
-    if (e.lut)
-    {
-        y = e.lut[y];
-    }
-    return y;
-}
-
-// Tiled GEMM for large M: 64x64 output tile, one 256-deep K block per step,
-// 256 threads each owning a 4x4 sub-tile; dp4a keeps the block dot exact.
-constexpr int BM = 64, BN = 64, BK = 256;
-
-__global__ void __launch_bounds__(256)
-    qlinear_gemm_kernel(const std::int8_t* __restrict__ w, const float* __restrict__ wscale,
-                        const std::int8_t* __restrict__ xq, const float* __restrict__ xscale,
-                        int m_rows, int n_cols, int k, Epilogue e, std::uint16_t* __restrict__ y)
-{
-    pdl_prologue();
-    __shared__ __align__(16) int As[BK / 4][BM];
-    __shared__ __align__(16) int Bs[BK / 4][BN];
-    const int tid = threadIdx.x;
-    const int tx = tid & 15, ty = tid >> 4;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-    const int blocks = k / 256;
-    float sum[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            sum[i][j] = 0.0f;
-    for (int b = 0; b < blocks; ++b)
-    {
-        // Stage the 64x256 A and B tiles, transposed to [k/4][row] words.
-#pragma unroll
-        for (int it = 0; it < 4; ++it)
-        {
-            const int row = tid & 63, chunk = (tid >> 6) + 4 * it; // 16-byte chunk 0..15
-            uint4 a = make_uint4(0, 0, 0, 0), bw;
-            if (m0 + row < m_rows)
-            {
-                a = *reinterpret_cast<const uint4*>(xq + static_cast<size_t>(m0 + row) * k +
-                                                    b * 256 + chunk * 16);
-            }
-            bw = *reinterpret_cast<const uint4*>(w + static_cast<size_t>(n0 + row) * k + b * 256 +
-                                                 chunk * 16);
-            As[chunk * 4 + 0][row] = a.x;
-            As[chunk * 4 + 1][row] = a.y;
-            As[chunk * 4 + 2][row] = a.z;
-            As[chunk * 4 + 3][row] = a.w;
-            Bs[chunk * 4 + 0][row] = bw.x;
-            Bs[chunk * 4 + 1][row] = bw.y;
-            Bs[chunk * 4 + 2][row] = bw.z;
-            Bs[chunk * 4 + 3][row] = bw.w;
-        }
-        __syncthreads();
-        int acc[4][4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                acc[i][j] = 0;
-#pragma unroll 8
-        for (int k4 = 0; k4 < BK / 4; ++k4)
-        {
-            const int4 a = *reinterpret_cast<const int4*>(&As[k4][ty * 4]);
-            const int4 bb = *reinterpret_cast<const int4*>(&Bs[k4][tx * 4]);
-            const int av[4] = {a.x, a.y, a.z, a.w};
-            const int bv[4] = {bb.x, bb.y, bb.z, bb.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    acc[i][j] = __dp4a(av[i], bv[j], acc[i][j]);
-        }
-        // Ordered block fold: sum = fma(dot, w_scale * a_scale, sum).
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-        {
-            const int m = m0 + ty * 4 + i;
-            const float as = m < m_rows ? xscale[m * blocks + b] : 0.0f;
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-            {
-                const int n = n0 + tx * 4 + j;
-                const float scale = __fmul_rn(wscale[b * n_cols + n], as);
-                sum[i][j] = __fmaf_rn(static_cast<float>(acc[i][j]), scale, sum[i][j]);
-            }
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-    {
-        const int m = m0 + ty * 4 + i;
-        if (m >= m_rows)
-        {
-            continue;
-        }
-        std::uint16_t out[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-        {
-            out[j] = finish(sum[i][j], m, n0 + tx * 4 + j, e);
-        }
-        *reinterpret_cast<uint2*>(y + static_cast<size_t>(m) * n_cols + n0 + tx * 4) =
-            make_uint2(out[0] | (unsigned(out[1]) << 16), out[2] | (unsigned(out[3]) << 16));
-    }
-}
-
-// Decode-shaped launch (m <= 256 columns).  A CTA owns 16 output features x
+// Decode-shaped launch (fewer than GEMM_MIN_M columns).  A CTA owns 16 output features x
 // 32 columns (four 8-column m-tiles).  Its 8 warps split K into 64-byte chunks
 // (warp w takes quarter w % 4 of the 256-blocks b = w / 4, w / 4 + 2, ...) and
 // form int8 dots on the tensor cores with mma.sync m16n8k32 (s8 x s8 -> s32:
@@ -190,7 +68,10 @@ __global__ void __launch_bounds__(256)
 // byte-to-k assignment, so every byte pair meets exactly once.  Quarter dots
 // meet in shared memory (integer atomics, exact), and 256 threads then fold
 // the blocks in order, two outputs each: sum = fma(dot, w_scale * x_scale, sum).
-constexpr int SMALL_MAX_M = 1 << 20;
+// Row count from which the tcgen05 GEMM (qlinear_tc.cu) takes over: below it
+// the weights are read once per 32 rows here, which costs less than a GEMM
+// tile pass over them.
+constexpr int GEMM_MIN_M = 256;
 constexpr int MMA_MT = 4; // 8-column m-tiles per CTA
 
 __device__ __forceinline__ void mma_s8(int (&d)[4], unsigned a0, unsigned a1, unsigned a2,
@@ -388,22 +269,22 @@ void qlinear_quantize(const std::uint16_t* x, int m, int k, std::int8_t* xq, flo
     note_launch();
 }
 
+bool qlinear_uses_gemm(int m, int n, int k)
+{
+    return m >= GEMM_MIN_M && qlinear_tc_supported(m, n, k);
+}
+
 bool qlinear_qkv_fusable(int m, int n)
 {
-    return m >= 1 && m <= SMALL_MAX_M && n == 1536;
+    return m >= 1 && n == 1536 && !qlinear_uses_gemm(m, n, 512);
 }
 
 void qlinear_matmul(const QLinearArgs& a, cudaStream_t stream)
 {
     const Epilogue e{a.bias, a.residual, a.lut, a.residual_stride < 0 ? a.n : a.residual_stride};
-    if (a.m <= SMALL_MAX_M && a.n % 16 == 0)
-        launch_small(a, e, stream);
+    if (!a.qkv.meta && qlinear_uses_gemm(a.m, a.n, a.k))
+        qlinear_tc(a.weights, a.weight_scales, a.xq, a.xscale, a.m, a.n, a.k, e, a.y, a.error_word, stream);
     else
-    {
-        const dim3 grid(a.n / BN, (a.m + BM - 1) / BM);
-        launch_pdl(qlinear_gemm_kernel, grid, dim3(256), 0, stream, a.weights, a.weight_scales,
-                   a.xq, a.xscale, a.m, a.n, a.k, e, a.y);
-        note_launch();
-    }
+        launch_small(a, e, stream);
 }
 } // namespace tsacb::dev

@@ -32,6 +32,7 @@ struct QLinearArgs
     int m = 0, n = 0, k = 0;
     int residual_stride = -1;                 // elements per residual row; -1: n, 0: one row for all
     QkvScatter qkv;                           // only where qlinear_qkv_fusable
+    unsigned* error_word = nullptr;           // the GEMM's bounded waits report here
 };
 
 // True when the decode-shaped kernel can apply the fused QKV epilogue.
@@ -42,8 +43,9 @@ size_t qlinear_scratch_bytes(size_t m, size_t k);
 // BF8L quantization of bf16 activations [m][k] into int8 + per-block scales.
 void qlinear_quantize(const std::uint16_t* x, int m, int k, std::int8_t* xq, float* xscale,
                       unsigned* error_word, cudaStream_t stream);
-// Exact int8 block dots + ordered FP32 epilogue (int8 tensor-core split-K tiles for
-// m <= 256, tiled dp4a GEMM above).
+// Exact int8 block dots + ordered FP32 epilogue: int8 mma.sync split-K tiles
+// for decode-sized m, the tcgen05 GEMM (qlinear_tc.cu) from 256 rows.
+bool qlinear_uses_gemm(int m, int n, int k);
 void qlinear_matmul(const QLinearArgs& args, cudaStream_t stream);
 // One-time kernel attribute setup (dynamic shared memory limits).
 void qlinear_init();

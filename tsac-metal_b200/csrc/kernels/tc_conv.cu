@@ -24,9 +24,7 @@
 #include "kernels/launch_count.hpp"
 #include "kernels/numeric.cuh"
 #include "kernels/tc_conv.cuh"
-
-#include <cuda.h>
-#include <cudaTypedefs.h>
+#include "kernels/tc_common.cuh"
 
 #include <mutex>
 
@@ -34,11 +32,12 @@ namespace tsacb::dev
 {
 namespace
 {
+using namespace tc;
+
 constexpr int BM = 128;        // rows per tile (TMEM lanes)
 constexpr int TC_THREADS = 320; // producer warp, MMA warp, 8 epilogue warps
 constexpr int BK = 32;         // fp32 per k-block row: one 128-byte swizzle row
 constexpr int A_BYTES = BM * BK * 4;
-constexpr unsigned long long WAIT_NS = 1000000000ull;
 
 // Four TMEM accumulators per tile (BN columns each): the hi*hi products of
 // k-step j go to accumulator j mod 3 and the hi*lo + lo*hi corrections to the
@@ -68,97 +67,6 @@ template <int BN> __host__ __device__ constexpr int smem_bytes()
 static_assert(smem_bytes<128>() <= 227 * 1024 && smem_bytes<96>() <= 227 * 1024,
               "stage ring exceeds the per-CTA shared memory limit");
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p)
-{
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ unsigned long long global_ns()
-{
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-__device__ __forceinline__ void bar_init(uint32_t bar, uint32_t count)
-{
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-
-__device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity)
-{
-    uint32_t ok;
-    asm volatile("{\n\t.reg .pred p;\n\t"
-                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-                 "selp.u32 %0, 1, 0, p;\n\t}"
-                 : "=r"(ok)
-                 : "r"(bar), "r"(parity)
-                 : "memory");
-    return ok != 0;
-}
-
-// Bounded wait for the phase of `parity` to complete.  Returns false after
-// about WAIT_NS of global time, or early when another role has aborted.
-__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag)
-{
-    if (bar_try(bar, parity))
-        return true;
-    const unsigned long long start = global_ns();
-    for (unsigned iter = 1;; ++iter)
-    {
-        if (bar_try(bar, parity))
-            return true;
-        if ((iter & 63u) == 0)
-        {
-            if (*abort_flag)
-                return false;
-            if (global_ns() - start > WAIT_NS)
-                return false;
-        }
-    }
-}
-
-__device__ __forceinline__ void bar_expect_tx(uint32_t bar, uint32_t bytes)
-{
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void bar_arrive(uint32_t bar)
-{
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
-                                       uint32_t bar)
-{
-    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-                 "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
-                 : "memory");
-}
-
-__device__ __forceinline__ void tma_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
-                                       uint32_t bar)
-{
-    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
-                 "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
-                 : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
-// 128 bytes in 8-row (1024-byte) atoms stacked along M/N.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr)
-{
-    uint64_t d = static_cast<uint64_t>((saddr & 0x3ffffu) >> 4);
-    d |= static_cast<uint64_t>(1) << 16;           // leading byte offset (unused here)
-    d |= static_cast<uint64_t>(1024 >> 4) << 32;   // stride byte offset: 8 rows x 128 B
-    d |= static_cast<uint64_t>(1) << 46;           // descriptor version
-    d |= static_cast<uint64_t>(2) << 61;           // 128-byte swizzle
-    return d;
-}
-
 // Instruction descriptor: D f32, A and B tf32, both K-major, M = 128, N = BN.
 template <int BN> __device__ __forceinline__ uint32_t tf32_idesc()
 {
@@ -173,39 +81,6 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b
                  "setp.ne.b32 p, %4, 0;\n\t"
                  "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
                  "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
-}
-
-__device__ __forceinline__ void mma_commit(uint32_t bar)
-{
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     bar)
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before()
-{
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after()
-{
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-// 16 consecutive TMEM columns of this thread's lane; the values are valid
-// after tmem_wait_loads().
-__device__ __forceinline__ void tmem_load16(uint32_t taddr, uint32_t (&r)[16])
-{
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32"
-                 " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
-                   "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
-                   "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-                 : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_wait_loads()
-{
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 // Nearest TF32 value (ties away from zero) of a finite fp32; the truncated
@@ -573,23 +448,6 @@ __global__ void pad_split_rows_kernel(const float* __restrict__ src, long long r
 }
 
 // ------------------------------------------------------------ host side --
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
-{
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once,
-                   []
-                   {
-                       void* p = nullptr;
-                       cudaDriverEntryPointQueryResult q{};
-                       if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
-                                                            cudaEnableDefault, &q) == cudaSuccess &&
-                           q == cudaDriverEntryPointSuccess)
-                           fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-                   });
-    return fn;
-}
-
 bool make_map(CUtensorMap* map, const float* base, int rank, const cuuint64_t* dims,
               const cuuint64_t* strides, const cuuint32_t* box)
 {
@@ -600,14 +458,6 @@ bool make_map(CUtensorMap* map, const float* base, int rank, const cuuint64_t* d
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<float*>(base), dims, strides,
               box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-int sm_count()
-{
-    int device = 0, count = 148;
-    if (cudaGetDevice(&device) == cudaSuccess)
-        cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device);
-    return count;
 }
 
 template <int BN>

@@ -103,6 +103,7 @@ int tsac_cuda_qlinear_noalloc(const int8_t* weights, const float* weight_scales,
             a.m = static_cast<int>(m);
             a.n = static_cast<int>(n);
             a.k = static_cast<int>(k);
+            a.error_word = error_word;
             dev::qlinear_matmul(a, s);
             cuda_check(cudaGetLastError(), "qlinear launch");
         });
