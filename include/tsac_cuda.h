@@ -98,6 +98,24 @@ int tsac_cuda_set_limits(tsac_cuda_context* context, const tsac_cuda_limits* lim
  * unaffected either way. */
 int tsac_cuda_set_exact_synthesis(tsac_cuda_context* context, int exact);
 
+/* Certified fast analysis (the encoder's DAC analysis; streams stay
+ * byte-identical to the reference's).  margin 0 (the default): the exact
+ * analysis, the reference's serial arithmetic (analysis.tpp:169-214 with
+ * scalar::Conv1d, src/scalar/dsp.cpp:11-51).  margin > 0: the analysis
+ * convolutions use fused multiply-adds (one rounding per term), every RVQ
+ * decision reports by how much the winning similarity leads the runner-up
+ * (similarities lie in [-1, 1]), and every frame with a decision whose lead
+ * is below `margin` is recomputed exactly on the 17-frame sub-window its
+ * latent depends on, so its tokens are the reference's; the margin must
+ * exceed the fast path's largest similarity error (see DESIGN).  Also makes
+ * tsac_cuda_dac_analysis return the fast latents.  margin in [0, 2]. */
+int tsac_cuda_set_fast_analysis(tsac_cuda_context* context, float margin);
+/* Cumulative counts since the context was created: central frames the fast
+ * analysis coded, frames it flagged as uncertain, and frames the exact
+ * recomputation evaluated (sub-windows included). */
+int tsac_cuda_fast_analysis_stats(tsac_cuda_context* context, uint64_t* frames, uint64_t* uncertain,
+                                  uint64_t* recomputed_frames);
+
 /* Host worker budget of a context (the reference CLI's -T, src/cli.cpp:66-68,
  * passed to AppleArmAnalyzer, src/codec.cpp:117-120, which accepts 1-256,
  * src/apple-arm/audio_analyzer.cpp:93): range encoding of a batch's

@@ -389,7 +389,8 @@ int tsac_cuda_dac_analysis(tsac_cuda_context* ctx, unsigned channels, const floa
             auto d_pcm = to_device(pcm, pcm_frames * channels, s);
             const auto frames = pcm_frames / 512;
             tsacb::DeviceBuffer d_lat(frames * 1024 * 4);
-            dac.analyze(d_pcm.as<float>(), {0}, {static_cast<int>(frames)}, d_lat.as<float>());
+            dac.analyze(d_pcm.as<float>(), {0}, {static_cast<int>(frames)}, d_lat.as<float>(),
+                        ctx->impl.fast_analysis_margin() > 0.0f);
             tsacb::cuda_ok(cudaMemcpyAsync(latent, d_lat.as<void>(), frames * 1024 * 4,
                                            cudaMemcpyDeviceToHost, s),
                            "D2H");
@@ -416,6 +417,31 @@ int tsac_cuda_set_limits(tsac_cuda_context* ctx, const tsac_cuda_limits* limits)
             ctx->impl.set_limits({limits->file_bytes, limits->symbols, limits->pcm_bytes, limits->cache_bytes,
                                   limits->tensor_elements, limits->tensors, limits->metadata_bytes,
                                   limits->name_bytes});
+        });
+}
+
+int tsac_cuda_set_fast_analysis(tsac_cuda_context* ctx, float margin)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            tsacb::require(ctx != nullptr, "null argument");
+            ctx->impl.set_fast_analysis(margin);
+        });
+}
+
+int tsac_cuda_fast_analysis_stats(tsac_cuda_context* ctx, uint64_t* frames, uint64_t* uncertain,
+                                  uint64_t* recomputed_frames)
+{
+    return tsacb::guarded(
+        [&]
+        {
+            tsacb::require(ctx && frames && uncertain && recomputed_frames, "null argument");
+            std::uint64_t f = 0, u = 0, r = 0;
+            ctx->impl.fast_analysis_stats(&f, &u, &r);
+            *frames = f;
+            *uncertain = u;
+            *recomputed_frames = r;
         });
 }
 

@@ -183,6 +183,97 @@ float* padded_device(Context& ctx, const std::vector<PcmInput>& pcm,
     return out;
 }
 
+// Receptive-field half-width of one latent frame in the analysis, in frames:
+// every intermediate value a latent frame depends on lies within 4,026 PCM
+// samples of it (the entry convolution, the three residual units and the
+// strided convolution of each stage, and the exit convolution), under 8
+// frames of 512 samples.  This is also the chunk context of analysis windows
+// (8 frames before, 9 after: src/common/audio_pipeline.hpp:46).
+constexpr std::size_t analysis_reach = 8;
+
+// Exact recomputation for the certified fast analysis.  Frame f of a window
+// [left, right) whose RVQ margin was too small is recomputed with the exact
+// kernels on the sub-window [max(left, f - 8), min(right, f + 9)): each
+// output of the exact convolution depends only on its own inputs, the
+// sub-window shares the window's edges where it reaches them, and elsewhere
+// the padding it introduces reaches at most 8 frames inwards, so f's latent
+// is bit-identical to the window's exact latent; the exact RVQ of it gives
+// the reference's tokens.  Overlapping sub-windows of a window are merged.
+void fast_analysis_recompute(Context& ctx, const float* padded, const std::vector<long long>& base,
+                             const std::vector<Header>& headers, const std::vector<Window>& windows,
+                             std::size_t w0, std::size_t wn, const std::vector<unsigned char>& uncertain,
+                             int books, std::vector<std::uint16_t>& host_tok)
+{
+    struct Run
+    {
+        std::size_t window, left, right; // frames [left, right) of the recording
+        std::vector<std::size_t> frames; // uncertain frames inside, ascending
+    };
+    std::vector<Run> runs;
+    std::vector<std::size_t> token_rows; // central index of each recomputed frame
+    std::size_t cen = 0, flagged = 0;
+    for (std::size_t i = 0; i < wn; ++i)
+    {
+        const auto& c = windows[w0 + i].chunk;
+        for (std::size_t k = 0; k < c.count; ++k)
+        {
+            if (!uncertain[cen + k])
+                continue;
+            ++flagged;
+            const std::size_t f = c.begin + k;
+            const std::size_t lo = std::max(c.left, f >= analysis_reach ? f - analysis_reach : 0);
+            const std::size_t hi = std::min(c.right, f + analysis_reach + 1);
+            if (!runs.empty() && runs.back().window == i && lo <= runs.back().right)
+                runs.back().right = std::max(runs.back().right, hi);
+            else
+                runs.push_back({i, lo, hi, {}});
+            runs.back().frames.push_back(f);
+            token_rows.push_back(cen + k);
+        }
+        cen += c.count;
+    }
+    ctx.note_fast_analysis(cen, flagged, 0);
+    if (runs.empty())
+        return;
+    std::vector<int> frames;
+    std::vector<long long> offsets;
+    std::size_t total = 0;
+    for (const auto& r : runs)
+    {
+        const auto& w = windows[w0 + r.window];
+        const auto& h = headers[w.recording];
+        frames.push_back(static_cast<int>(r.right - r.left));
+        offsets.push_back(base[w.recording] +
+                          static_cast<long long>(w.group * h.samples_per_channel() + r.left * 512));
+        total += r.right - r.left;
+    }
+    ctx.note_fast_analysis(0, 0, total);
+    auto s = ctx.stream();
+    auto& dac = ctx.analysis(headers[0].model_channels);
+    auto& rvq = ctx.rvq(headers[0].model_channels);
+    auto& ws = ctx.workspace();
+    float* d_latent = ws.get<float>("fix_latent", total * 1024);
+    float* d_frames = ws.get<float>("fix_frames", token_rows.size() * 1024);
+    auto* d_tok = ws.get<std::uint16_t>("fix_tokens", token_rows.size() * static_cast<std::size_t>(books));
+    dac.analyze(padded, offsets, frames, d_latent, false);
+    std::size_t at = 0, row = 0;
+    for (const auto& r : runs)
+    {
+        for (const auto f : r.frames)
+            cuda_ok(cudaMemcpyAsync(d_frames + (row++) * 1024, d_latent + (at + f - r.left) * 1024, 1024 * 4,
+                                    cudaMemcpyDeviceToDevice, s),
+                    "D2D");
+        at += r.right - r.left;
+    }
+    rvq.encode(d_frames, static_cast<int>(token_rows.size()), books, d_tok, books);
+    std::vector<std::uint16_t> fixed(token_rows.size() * static_cast<std::size_t>(books));
+    cuda_ok(cudaMemcpyAsync(fixed.data(), d_tok, fixed.size() * 2, cudaMemcpyDeviceToHost, s), "D2H");
+    check_word(s, dac.error_word(), "nonfinite DSP value");
+    check_word(s, rvq.error_word(), "nonfinite RVQ residual");
+    for (std::size_t j = 0; j < token_rows.size(); ++j)
+        std::copy_n(fixed.data() + j * books, books, host_tok.data() + token_rows[j] * books);
+}
+
 // DAC analysis + RVQ for every recording of one model variant.
 void analyze_recordings(Context& ctx, const std::vector<PcmInput>& pcm,
                         const std::vector<Header>& headers,
@@ -211,6 +302,7 @@ void analyze_recordings(Context& ctx, const std::vector<PcmInput>& pcm,
                 b += c.count;
             }
     }
+    const float margin = ctx.fast_analysis_margin();
     for (std::size_t w0 = 0; w0 < windows.size(); w0 += window_group)
     {
         const auto wn = std::min(window_group, windows.size() - w0);
@@ -231,33 +323,66 @@ void analyze_recordings(Context& ctx, const std::vector<PcmInput>& pcm,
         auto& ws = ctx.workspace();
         float* d_latent = ws.get<float>("enc_latent", latent_frames * 1024);
         float* d_central = ws.get<float>("enc_central", central * 1024);
-        dac.analyze(padded, offsets, frames, d_latent);
-        // Keep each window's central latents (src/common/audio_pipeline.hpp:49-56).
-        std::size_t lat = 0, cen = 0;
-        for (std::size_t i = 0; i < wn; ++i)
-        {
-            const auto& c = windows[w0 + i].chunk;
-            cuda_ok(cudaMemcpyAsync(d_central + cen * 1024,
-                                    d_latent + (lat + c.begin - c.left) * 1024,
-                                    c.count * 1024 * 4, cudaMemcpyDeviceToDevice, s),
-                    "D2D");
-            lat += c.right - c.left;
-            cen += c.count;
-        }
-        profile.mark("dac analysis");
         const int books = headers[0].codebooks;
         auto* d_tok = ws.get<std::uint16_t>("enc_tokens", central * static_cast<std::size_t>(books));
-        rvq.encode(d_central, static_cast<int>(central), books,
-                   d_tok, books);
         std::vector<std::uint16_t> host_tok(central * static_cast<std::size_t>(books));
-        cuda_ok(cudaMemcpyAsync(host_tok.data(), d_tok, host_tok.size() * 2,
-                                cudaMemcpyDeviceToHost, s),
-                "D2H");
-        check_word(s, dac.error_word(), "nonfinite DSP value");
-        check_word(s, rvq.error_word(), "nonfinite RVQ residual");
+        // Exact analysis (the reference's arithmetic), or the certified fast
+        // analysis: fused multiply-add convolutions, RVQ with the winning
+        // margin of every decision, and exact recomputation of every frame
+        // whose margin is below `margin` (fast_analysis_recompute).
+        bool fast = margin > 0.0f;
+        for (int attempt = 0; attempt < 2; ++attempt)
+        {
+            dac.analyze(padded, offsets, frames, d_latent, fast);
+            // Keep each window's central latents (src/common/audio_pipeline.hpp:49-56).
+            std::size_t lat = 0, cen = 0;
+            for (std::size_t i = 0; i < wn; ++i)
+            {
+                const auto& c = windows[w0 + i].chunk;
+                cuda_ok(cudaMemcpyAsync(d_central + cen * 1024, d_latent + (lat + c.begin - c.left) * 1024,
+                                        c.count * 1024 * 4, cudaMemcpyDeviceToDevice, s),
+                        "D2D");
+                lat += c.right - c.left;
+                cen += c.count;
+            }
+            profile.mark(fast ? "dac analysis (fast)" : "dac analysis");
+            std::vector<unsigned char> uncertain;
+            if (fast)
+            {
+                auto* d_flags = ws.get<unsigned char>("enc_uncertain", central);
+                rvq.encode_margins(d_central, static_cast<int>(central), books, d_tok, books, margin, d_flags);
+                uncertain.resize(central);
+                cuda_ok(cudaMemcpyAsync(uncertain.data(), d_flags, central, cudaMemcpyDeviceToHost, s), "D2H");
+            }
+            else
+            {
+                rvq.encode(d_central, static_cast<int>(central), books, d_tok, books);
+            }
+            cuda_ok(cudaMemcpyAsync(host_tok.data(), d_tok, host_tok.size() * 2, cudaMemcpyDeviceToHost, s),
+                    "D2H");
+            unsigned words[2] = {0, 0};
+            cuda_ok(cudaMemcpyAsync(&words[0], dac.error_word(), 4, cudaMemcpyDeviceToHost, s), "D2H");
+            cuda_ok(cudaMemcpyAsync(&words[1], rvq.error_word(), 4, cudaMemcpyDeviceToHost, s), "D2H");
+            cuda_ok(cudaStreamSynchronize(s), "analysis");
+            if (fast && (words[0] || words[1]))
+            {
+                // A nonfinite value on the fast path: redo the group exactly, so
+                // that the outcome (a stream or the reference's error) is the
+                // exact path's.
+                cuda_ok(cudaMemsetAsync(dac.error_word(), 0, 4, s), "memset");
+                cuda_ok(cudaMemsetAsync(rvq.error_word(), 0, 4, s), "memset");
+                fast = false;
+                continue;
+            }
+            check_word(s, dac.error_word(), "nonfinite DSP value");
+            check_word(s, rvq.error_word(), "nonfinite RVQ residual");
+            if (fast)
+                fast_analysis_recompute(ctx, padded, base, headers, windows, w0, wn, uncertain, books, host_tok);
+            break;
+        }
         profile.mark("rvq encode");
         // store_tokens (src/common/audio_analyzer.cpp:164-172).
-        cen = 0;
+        std::size_t cen = 0;
         for (std::size_t i = 0; i < wn; ++i)
         {
             const auto& w = windows[w0 + i];

@@ -101,6 +101,12 @@ void Context::set_host_threads(unsigned threads)
     host_threads_ = threads;
 }
 
+void Context::set_fast_analysis(float margin)
+{
+    require(margin >= 0.0f && margin <= 2.0f, "fast analysis margin must be in [0, 2]");
+    fast_margin_ = margin;
+}
+
 RvqEngine& Context::rvq(unsigned channels)
 {
     require(channels == 1 || channels == 2, "invalid model variant");

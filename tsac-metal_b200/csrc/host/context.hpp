@@ -45,6 +45,28 @@ public:
     // reference CLI, AppleArmAnalyzer's 1-256 bound,
     // src/apple-arm/audio_analyzer.cpp:93); 0: automatic.
     void set_host_threads(unsigned threads);
+    // Certified fast analysis: 0 (default) runs the exact analysis; a positive
+    // margin runs fused multiply-add convolutions and recomputes exactly every
+    // frame whose RVQ decision margin is below it.
+    void set_fast_analysis(float margin);
+    float fast_analysis_margin() const
+    {
+        return fast_margin_;
+    }
+    // Cumulative counts of the fast analysis: central frames analysed,
+    // frames flagged uncertain, frames the exact recomputation evaluated.
+    void note_fast_analysis(std::uint64_t frames, std::uint64_t flagged, std::uint64_t recomputed)
+    {
+        fast_frames_ += frames;
+        fast_flagged_ += flagged;
+        fast_recomputed_ += recomputed;
+    }
+    void fast_analysis_stats(std::uint64_t* frames, std::uint64_t* flagged, std::uint64_t* recomputed) const
+    {
+        *frames = fast_frames_;
+        *flagged = fast_flagged_;
+        *recomputed = fast_recomputed_;
+    }
     unsigned host_threads() const
     {
         return host_threads_;
@@ -66,6 +88,8 @@ private:
     Package package_;
     int device_;
     unsigned host_threads_ = 0;
+    float fast_margin_ = 0.0f;
+    std::uint64_t fast_frames_ = 0, fast_flagged_ = 0, fast_recomputed_ = 0;
     Limits limits_;
     cudaStream_t stream_ = nullptr;
     std::shared_ptr<DeviceTransformer> transformers_[2];

@@ -196,7 +196,10 @@ void DacEngine::conv(int index, const float* x, float* y, const float* residual,
     double macs = 0;
     for (int of : out_frames)
         macs += static_cast<double>(of) * shape.cout * shape.cin * (sp.transposed ? 2 : shape.kernel);
-    KernelTimer::Scope timing(shape.cout < 16 ? "conv_narrow" : sp.transposed ? "conv_transposed" : "conv_exact",
+    KernelTimer::Scope timing(shape.cout < 16        ? "conv_narrow"
+                              : sp.transposed        ? "conv_transposed"
+                              : fast_analysis_       ? "conv_fast"
+                                                     : "conv_exact",
                               stream_, 2.0 * macs);
     if (shape.cout < 16)
     {
@@ -212,6 +215,7 @@ void DacEngine::conv(int index, const float* x, float* y, const float* residual,
             "H2D");
     dev::ConvLaunch l{error_word(), x, c.weights.as<float>(), c.bias.as<float>(), residual, y,
                       d_seq, d_tiles, static_cast<int>(tiles.size()), shape};
+    l.fast = fast_analysis_;
     if (act)
     {
         l.alpha = alphas_[static_cast<std::size_t>(alpha)].as<float>();
@@ -221,9 +225,21 @@ void DacEngine::conv(int index, const float* x, float* y, const float* residual,
 }
 
 void DacEngine::analyze(const float* pcm, const std::vector<long long>& offsets,
-                        const std::vector<int>& frames, float* latent)
+                        const std::vector<int>& frames, float* latent, bool fast)
 {
     require(!synthesis_, "analysis on a synthesis model");
+    struct Mode
+    {
+        bool& flag;
+        Mode(bool& f, bool value) : flag(f)
+        {
+            flag = value;
+        }
+        ~Mode()
+        {
+            flag = false;
+        }
+    } mode(fast_analysis_, fast);
     require(offsets.size() == frames.size(), "analysis window table mismatch");
     std::vector<int> f0(frames.size()), f1;
     long long total = 0;
@@ -457,6 +473,15 @@ void RvqEngine::encode(const float* latent, int frames, int books, std::uint16_t
     require(books > 0 && books <= books_, "stream and prepared RVQ codebooks do not match");
     dev::rvq_encode(latent, frames, table_.as<dev::RvqBookDevice>(), books, tokens, stride,
                     error_word(), stream_);
+}
+
+void RvqEngine::encode_margins(const float* latent, int frames, int books, std::uint16_t* tokens, int stride,
+                               float margin, unsigned char* uncertain)
+{
+    KernelTimer::Scope timing("rvq_encode", stream_, static_cast<double>(frames) * books * 2.0 * (8192 + 8192 + 8192));
+    require(books > 0 && books <= books_, "stream and prepared RVQ codebooks do not match");
+    dev::rvq_encode_margins(latent, frames, table_.as<dev::RvqBookDevice>(), books, tokens, stride, margin,
+                            uncertain, error_word(), stream_);
 }
 
 void RvqEngine::decode(const std::uint16_t* tokens, int stride, int frames, int books, float* latent)

@@ -34,8 +34,10 @@ public:
     }
     // Analysis: window w reads frames[w]*512 PCM rows [C] starting at row
     // offsets[w] of `pcm` -> latent [sum of frames][1024] (windows in order).
+    // fast: fused multiply-add convolutions (the certified fast analysis;
+    // latents differ from the reference's in the last bits).
     void analyze(const float* pcm, const std::vector<long long>& offsets,
-                 const std::vector<int>& frames, float* latent);
+                 const std::vector<int>& frames, float* latent, bool fast = false);
     // Synthesis: latent windows [sum of frames][1024] -> pcm [sum frames*512][C].
     // Tensor-core mode (the default) runs the wide convolutions as 3xTF32
     // tcgen05 GEMMs (PCM within tolerance of the reference); exact mode keeps
@@ -71,6 +73,7 @@ private:
 
     bool synthesis_;
     bool exact_synthesis_ = false;
+    bool fast_analysis_ = false; // set for the duration of a fast analyze()
     bool tensor_ready_ = true; // every wide synthesis convolution has tensor operands
     long long tc_valid_latent_ = 0;
     unsigned channels_;
@@ -88,6 +91,10 @@ public:
     RvqEngine(const std::vector<PreparedRvqBook>& books, cudaStream_t stream);
     // latent [frames][1024] (consumed as residual) -> tokens [frames][stride], books 0..count-1.
     void encode(const float* latent, int frames, int books, std::uint16_t* tokens, int stride);
+    // encode, flagging uncertain[f] = 1 for frames where any book's winning
+    // similarity leads the runner-up by less than `margin`.
+    void encode_margins(const float* latent, int frames, int books, std::uint16_t* tokens, int stride,
+                        float margin, unsigned char* uncertain);
     void decode(const std::uint16_t* tokens, int stride, int frames, int books, float* latent);
     unsigned* error_word() const
     {

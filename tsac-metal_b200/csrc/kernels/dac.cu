@@ -107,7 +107,20 @@ template <int TO> constexpr size_t conv_smem_bytes()
 // Per output the order is the reference's: taps ascending, channels
 // ascending, sum = sum + x * w with the product and the sum each rounded; a
 // row skips taps whose input frame lies outside its window.
-template <int TO, int THREADS>
+// One multiply-accumulate term of a chain.  Exact (the reference's order):
+// the product and the sum are each rounded.  FAST (the certified fast
+// analysis only): one fused multiply-add, a single rounding per term and half
+// the issued instructions; its results differ from the reference's in the
+// last bits, so the caller checks every decision that depends on them.
+template <bool FAST> __device__ __forceinline__ float accumulate(float sum, float x, float w)
+{
+    if constexpr (FAST)
+        return __fmaf_rn(x, w, sum);
+    else
+        return __fadd_rn(sum, __fmul_rn(x, w));
+}
+
+template <int TO, int THREADS, bool FAST>
 __global__ void __launch_bounds__(THREADS, 512 / THREADS)
     conv1d_kernel(ConvLaunch l)
 {
@@ -250,7 +263,7 @@ __global__ void __launch_bounds__(THREADS, 512 / THREADS)
                 for (int i = 0; i < TR; ++i)
 #pragma unroll
                     for (int j = 0; j < 8; ++j)
-                        sum[i][j] = __fadd_rn(sum[i][j], __fmul_rn(xa[i], wa[j]));
+                        sum[i][j] = accumulate<FAST>(sum[i][j], xa[i], wa[j]);
             }
         }
         else
@@ -275,7 +288,7 @@ __global__ void __launch_bounds__(THREADS, 512 / THREADS)
 #pragma unroll
                     for (int j = 0; j < 8; ++j)
                     {
-                        const float n = __fadd_rn(sum[i][j], __fmul_rn(xv, wa[j]));
+                        const float n = accumulate<FAST>(sum[i][j], xv, wa[j]);
                         sum[i][j] = take ? n : sum[i][j];
                     }
                 }
@@ -373,16 +386,41 @@ __device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b)
     return (a.value < b.value || (a.value == b.value && b.index < a.index)) ? b : a;
 }
 
+// The runner-up similarity of a search (MARGIN variant): the largest value
+// among the candidates other than the selected one (equal maxima count, so an
+// exact tie leaves a zero margin).
+struct TopTwo
+{
+    ArgMax best;
+    float second;
+};
+
+__device__ __forceinline__ TopTwo merge(TopTwo a, const TopTwo& b)
+{
+    const ArgMax winner = better(a.best, b.best);
+    const float loser = (winner.index == a.best.index && winner.value == a.best.value) ? b.best.value
+                                                                                       : a.best.value;
+    a.second = fmaxf(fmaxf(a.second, b.second), loser);
+    a.best = winner;
+    return a;
+}
+
+// MARGIN: also flags the frame in uncertain[frame] when, for any book, the
+// winning similarity beats the runner-up by less than `margin` (or is not
+// finite); the certified fast analysis recomputes such frames exactly.
+template <bool MARGIN>
 __global__ void __launch_bounds__(256)
     rvq_encode_kernel(const float* __restrict__ latent, const RvqBookDevice* __restrict__ books,
                       int book_count, std::uint16_t* __restrict__ tokens, int token_stride,
-                      unsigned* error_word)
+                      unsigned* error_word, float margin, unsigned char* __restrict__ uncertain)
 {
     __shared__ float residual[1024];
     __shared__ float projected[8];
     __shared__ float query[8];
     __shared__ ArgMax warp_best[8];
+    __shared__ float warp_second[8];
     __shared__ int selected;
+    bool doubtful = false;
     const int frame = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
     for (int i = t; i < 1024; i += 256)
         residual[i] = latent[static_cast<size_t>(frame) * 1024 + i];
@@ -419,7 +457,7 @@ __global__ void __launch_bounds__(256)
                 query[i] = __fmul_rn(__fmul_rn(projected[i], inverse_rms), inverse_width);
         }
         __syncthreads();
-        ArgMax best{-INFINITY, 1 << 20};
+        TopTwo top{{-INFINITY, 1 << 20}, -INFINITY};
         for (int index = t; index < 1024; index += 256)
         {
             const float* v = book.search + index * 8;
@@ -429,27 +467,38 @@ __global__ void __launch_bounds__(256)
                 similarity = __fmaf_rn(v[i], query[i], similarity);
             // Candidates that never exceed -inf (NaN) are never selected, as in the reference.
             if (similarity > -INFINITY || index == 0)
-                best = better(best, ArgMax{similarity > -INFINITY ? similarity : -INFINITY, index});
+            {
+                const TopTwo one{{similarity > -INFINITY ? similarity : -INFINITY, index}, -INFINITY};
+                top = MARGIN ? merge(top, one) : TopTwo{better(top.best, one.best), -INFINITY};
+            }
         }
 #pragma unroll
         for (int offset = 16; offset > 0; offset >>= 1)
         {
-            ArgMax other{__shfl_xor_sync(0xffffffffu, best.value, offset),
-                         __shfl_xor_sync(0xffffffffu, best.index, offset)};
-            best = better(best, other);
+            const TopTwo other{{__shfl_xor_sync(0xffffffffu, top.best.value, offset),
+                                __shfl_xor_sync(0xffffffffu, top.best.index, offset)},
+                               __shfl_xor_sync(0xffffffffu, top.second, offset)};
+            top = MARGIN ? merge(top, other) : TopTwo{better(top.best, other.best), -INFINITY};
         }
         if (lane == 0)
-            warp_best[warp] = best;
+        {
+            warp_best[warp] = top.best;
+            warp_second[warp] = top.second;
+        }
         __syncthreads();
         if (t == 0)
         {
-            ArgMax all = warp_best[0];
+            TopTwo all{warp_best[0], warp_second[0]};
             for (int i = 1; i < 8; ++i)
-                all = better(all, warp_best[i]);
+                all = MARGIN ? merge(all, TopTwo{warp_best[i], warp_second[i]})
+                             : TopTwo{better(all.best, warp_best[i]), -INFINITY};
             // A reference search that never passes -inf keeps index 0.
-            selected = all.value > -INFINITY ? all.index : 0;
+            selected = all.best.value > -INFINITY ? all.best.index : 0;
             tokens[static_cast<size_t>(frame) * token_stride + b] =
                 static_cast<std::uint16_t>(selected);
+            if (MARGIN)
+                doubtful = doubtful || !(__fsub_rn(all.best.value, all.second) >= margin) ||
+                           !isfinite(all.best.value);
         }
         __syncthreads();
         const float* cb = book.codebook + selected * 8;
@@ -468,6 +517,8 @@ __global__ void __launch_bounds__(256)
     }
     if (!__syncthreads_and(ok) && t == 0 && error_word)
         atomicOr(error_word, error_nonfinite);
+    if (MARGIN && t == 0)
+        uncertain[frame] = doubtful ? 1 : 0;
 }
 
 __global__ void rvq_decode_kernel(const std::uint16_t* __restrict__ tokens, int token_stride,
@@ -524,7 +575,7 @@ int conv_tile_frames(const ConvShape&)
     return TF;
 }
 
-template <int TO, int THREADS> void launch_conv(const ConvLaunch& l, cudaStream_t stream)
+template <int TO, int THREADS, bool FAST> void launch_conv(const ConvLaunch& l, cudaStream_t stream)
 {
     constexpr size_t smem = conv_smem_bytes<TO>();
     static std::once_flag attr_once[64];
@@ -534,12 +585,12 @@ template <int TO, int THREADS> void launch_conv(const ConvLaunch& l, cudaStream_
         std::call_once(attr_once[device],
                        []
                        {
-                           cudaFuncSetAttribute(conv1d_kernel<TO, THREADS>,
+                           cudaFuncSetAttribute(conv1d_kernel<TO, THREADS, FAST>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 static_cast<int>(smem));
                        });
     const dim3 grid(l.tile_count, (l.shape.cout + TO - 1) / TO);
-    conv1d_kernel<TO, THREADS><<<grid, THREADS, smem, stream>>>(l);
+    conv1d_kernel<TO, THREADS, FAST><<<grid, THREADS, smem, stream>>>(l);
     note_launch();
 }
 
@@ -552,9 +603,9 @@ void conv1d(const ConvLaunch& l, cudaStream_t stream)
     // for the 64-channel layers.  (The 256-thread tile at two CTAs per SM on
     // the wide layers measured 0.59 of FP32 issue against 0.63.)
     if (l.shape.cout >= 128)
-        launch_conv<128, 512>(l, stream);
+        l.fast ? launch_conv<128, 512, true>(l, stream) : launch_conv<128, 512, false>(l, stream);
     else
-        launch_conv<64, 256>(l, stream);
+        l.fast ? launch_conv<64, 256, true>(l, stream) : launch_conv<64, 256, false>(l, stream);
 }
 
 void conv1d_narrow(const float* x, const float* w, const float* bias, float* y,
@@ -573,8 +624,20 @@ void rvq_encode(const float* latent, int frames, const RvqBookDevice* books, int
 {
     if (frames > 0)
     {
-        rvq_encode_kernel<<<frames, 256, 0, stream>>>(latent, books, book_count, tokens,
-                                                      token_stride, error_word);
+        rvq_encode_kernel<false><<<frames, 256, 0, stream>>>(latent, books, book_count, tokens, token_stride,
+                                                             error_word, 0.0f, nullptr);
+        note_launch();
+    }
+}
+
+void rvq_encode_margins(const float* latent, int frames, const RvqBookDevice* books, int book_count,
+                        std::uint16_t* tokens, int token_stride, float margin, unsigned char* uncertain,
+                        unsigned* error_word, cudaStream_t stream)
+{
+    if (frames > 0)
+    {
+        rvq_encode_kernel<true><<<frames, 256, 0, stream>>>(latent, books, book_count, tokens, token_stride,
+                                                            error_word, margin, uncertain);
         note_launch();
     }
 }

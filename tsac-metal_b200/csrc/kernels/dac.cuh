@@ -46,6 +46,9 @@ struct ConvLaunch
     ConvShape shape;
     const float* alpha = nullptr; // next layer's Snake alpha [cout], with act
     float* act = nullptr;         // Snake(result) (same shape as y), or null
+    // Fused multiply-add chains instead of the exact separately rounded ones
+    // (the certified fast analysis; its RVQ decisions are checked).
+    bool fast = false;
 };
 void conv1d(const ConvLaunch& launch, cudaStream_t stream);
 // Output channels < 16 (DAC exit to PCM): one thread per output.
@@ -69,6 +72,11 @@ struct RvqBookDevice
 void rvq_encode(const float* latent, int frames, const RvqBookDevice* books, int book_count,
                 std::uint16_t* tokens, int token_stride, unsigned* error_word,
                 cudaStream_t stream);
+// rvq_encode that also sets uncertain[frame] = 1 when any book's winning
+// similarity leads the runner-up by less than `margin` (0 otherwise).
+void rvq_encode_margins(const float* latent, int frames, const RvqBookDevice* books, int book_count,
+                        std::uint16_t* tokens, int token_stride, float margin, unsigned char* uncertain,
+                        unsigned* error_word, cudaStream_t stream);
 // RVQ decode: tokens [frames][books] (row stride token_stride) -> latent [frames][1024].
 void rvq_decode(const std::uint16_t* tokens, int token_stride, int frames,
                 const RvqBookDevice* books, int book_count, float* latent, cudaStream_t stream);

@@ -200,6 +200,19 @@ class CudaAnalyzer:
             raise TsacError("invalid thread count")
         check(library().tsac_cuda_set_host_threads(self._ctx, ctypes.c_uint(threads)))
 
+    def set_fast_analysis(self, margin: float) -> None:
+        """Certified fast analysis: 0 = exact analysis; margin > 0 = fused
+        multiply-add analysis with every frame whose RVQ decision lead is below
+        `margin` recomputed exactly (streams stay the reference's)."""
+        check(library().tsac_cuda_set_fast_analysis(self._ctx, ctypes.c_float(margin)))
+
+    def fast_analysis_stats(self):
+        """(central frames coded, frames flagged uncertain, frames recomputed exactly)."""
+        f, u, r = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+        check(library().tsac_cuda_fast_analysis_stats(self._ctx, ctypes.byref(f), ctypes.byref(u),
+                                                      ctypes.byref(r)))
+        return f.value, u.value, r.value
+
     def close(self):
         if self._ctx:
             library().tsac_cuda_context_destroy(self._ctx)
