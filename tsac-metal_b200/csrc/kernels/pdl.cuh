@@ -22,6 +22,21 @@ __device__ __forceinline__ void pdl_prologue()
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Split form for kernels that first read inputs no predecessor writes (model
+// weights, scales, biases): pdl_release() lets the next kernel begin its own
+// launch, the constant loads follow, and pdl_wait() then blocks until the
+// predecessor grid has completed and its memory is visible, before anything
+// it produced is read.
+__device__ __forceinline__ void pdl_release()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void pdl_wait()
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 template <class... Params, class... Args>
 void launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
                 cudaStream_t stream, Args&&... args)

@@ -101,10 +101,14 @@ __host__ __device__ constexpr size_t mma_smem_bytes(int k)
     return static_cast<size_t>(k / 256) * MMA_MT * 128 * sizeof(int);
 }
 
+// Weight chunks (per warp) and fold scales (per thread) loaded before the
+// programmatic-dependency wait: the model's K <= 2048 layers fit entirely.
+constexpr int MMA_PRE_CHUNKS = 4, MMA_PRE_BLOCKS = 8;
+
 template <bool QKV_OUT>
 __global__ void __launch_bounds__(256) qlinear_mma_kernel(MmaArgs a)
 {
-    pdl_prologue();
+    pdl_release();
     extern __shared__ __align__(16) unsigned char mma_smem[];
     int* dots = reinterpret_cast<int*>(mma_smem); // [block][m-tile][lane][4]
     const int k = a.k, m_rows = a.m_rows, n_cols = a.n_cols;
@@ -114,14 +118,39 @@ __global__ void __launch_bounds__(256) qlinear_mma_kernel(MmaArgs a)
     const int blocks = k / 256;
     for (int i = threadIdx.x; i < blocks * MMA_MT * 128; i += 256)
         dots[i] = 0;
-    __syncthreads();
     const int quarter = warp & 3;
     const std::int8_t* wa = a.w + static_cast<size_t>(n0 + g) * k + quarter * 64 + t * 16;
     const std::int8_t* wb = wa + static_cast<size_t>(8) * k;
-    for (int b = warp >> 2; b < blocks; b += 2)
+    // Model constants first (no predecessor writes them): this warp's weight
+    // chunks, and each thread's fold scales and biases for its two outputs.
+    uint4 pre_lo[MMA_PRE_CHUNKS], pre_hi[MMA_PRE_CHUNKS];
+#pragma unroll
+    for (int it = 0; it < MMA_PRE_CHUNKS; ++it)
     {
-        const uint4 a_lo = __ldg(reinterpret_cast<const uint4*>(wa + b * 256));
-        const uint4 a_hi = __ldg(reinterpret_cast<const uint4*>(wb + b * 256));
+        const int b = (warp >> 2) + 2 * it;
+        if (b < blocks)
+        {
+            pre_lo[it] = __ldg(reinterpret_cast<const uint4*>(wa + b * 256));
+            pre_hi[it] = __ldg(reinterpret_cast<const uint4*>(wb + b * 256));
+        }
+    }
+    float pre_scale[2][MMA_PRE_BLOCKS], pre_bias[2];
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
+    {
+        const int n = n0 + ((threadIdx.x + half * 256) & 15);
+        pre_bias[half] = __ldg(a.e.bias + n);
+#pragma unroll
+        for (int b = 0; b < MMA_PRE_BLOCKS; ++b)
+            pre_scale[half][b] = b < blocks ? __ldg(a.wscale + b * n_cols + n) : 0.0f;
+    }
+    pdl_wait();
+    __syncthreads();
+    // One 64-byte chunk of every 256-block b this warp owns (b = warp / 4,
+    // warp / 4 + 2, ...): int8 MMAs of the 16 weight rows with the CTA's four
+    // 8-column m-tiles, quarter dots merged in shared memory.
+    const auto chunk = [&](int b, const uint4& a_lo, const uint4& a_hi)
+    {
         uint4 x[MMA_MT];
 #pragma unroll
         for (int mt = 0; mt < MMA_MT; ++mt)
@@ -142,7 +171,17 @@ __global__ void __launch_bounds__(256) qlinear_mma_kernel(MmaArgs a)
             for (int c = 0; c < 4; ++c)
                 atomicAdd(slot + c, d[c]);
         }
+    };
+#pragma unroll
+    for (int it = 0; it < MMA_PRE_CHUNKS; ++it)
+    {
+        const int b = (warp >> 2) + 2 * it;
+        if (b < blocks)
+            chunk(b, pre_lo[it], pre_hi[it]);
     }
+    for (int b = (warp >> 2) + 2 * MMA_PRE_CHUNKS; b < blocks; b += 2)
+        chunk(b, __ldg(reinterpret_cast<const uint4*>(wa + b * 256)),
+              __ldg(reinterpret_cast<const uint4*>(wb + b * 256)));
     __syncthreads();
     // Fold: output (nl, ml), nl = 0..15, ml = 0..31; fragment element c of
     // lane (g, t) holds (n = g + 8 (c / 2), m = 2 t + c % 2) of its m-tile.
@@ -160,15 +199,24 @@ __global__ void __launch_bounds__(256) qlinear_mma_kernel(MmaArgs a)
             const int frag_lane = (nl & 7) * 4 + (col >> 1);
             const int c = (nl >> 3) * 2 + (col & 1);
             float sum = 0.0f;
-#pragma unroll 4
-            for (int b = 0; b < blocks; ++b)
+#pragma unroll
+            for (int b = 0; b < MMA_PRE_BLOCKS; ++b)
+            {
+                if (b < blocks)
+                {
+                    const float scale = __fmul_rn(pre_scale[half][b], __ldg(a.xscale + m * blocks + b));
+                    const int dot = dots[((b * MMA_MT + mt) * 32 + frag_lane) * 4 + c];
+                    sum = __fmaf_rn(static_cast<float>(dot), scale, sum);
+                }
+            }
+            for (int b = MMA_PRE_BLOCKS; b < blocks; ++b)
             {
                 const float scale = __fmul_rn(__ldg(a.wscale + b * n_cols + n),
                                               __ldg(a.xscale + m * blocks + b));
                 const int dot = dots[((b * MMA_MT + mt) * 32 + frag_lane) * 4 + c];
                 sum = __fmaf_rn(static_cast<float>(dot), scale, sum);
             }
-            out = finish(sum, m, n, a.e);
+            out = finish_with_bias(sum, pre_bias[half], m, n, a.e);
         }
         if constexpr (QKV_OUT)
         {

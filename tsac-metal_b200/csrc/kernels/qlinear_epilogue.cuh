@@ -17,6 +17,22 @@ struct Epilogue
     int residual_stride;           // 0: one residual row for every column
 };
 
+// finish() with the bias value already loaded.
+__device__ __forceinline__ std::uint16_t finish_with_bias(float sum, float bias, int m, int n, const Epilogue& e)
+{
+    std::uint16_t y = to_bf16(__fadd_rn(sum, bias));
+    if (e.residual)
+    {
+        y = to_bf16(__fadd_rn(from_bf16(e.residual[static_cast<size_t>(m) * e.residual_stride + n]),
+                              from_bf16(y)));
+    }
+    if (e.lut)
+    {
+        y = e.lut[y];
+    }
+    return y;
+}
+
 __device__ __forceinline__ std::uint16_t finish(float sum, int m, int n, const Epilogue& e)
 {
     std::uint16_t y = to_bf16(__fadd_rn(sum, e.bias[n]));

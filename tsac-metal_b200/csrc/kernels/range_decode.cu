@@ -148,11 +148,34 @@ __global__ void __launch_bounds__(128)
 }
 // The decode loop's range decoding: one warp per stream (recording), whose
 // rows of this step are rows [row_begin[s], row_begin[s + 1]) in stream
-// order.  For each row the warp stages the 1023 left-child masses in shared
-// memory with coalesced loads, then lane 0 walks the bisection heap from
-// there; the symbol goes to tokens[destination[row]], where the next step's
-// embeddings read it.
-constexpr int rows_warps = 4;
+// order.  The warp first stages, with coalesced loads, the next 128 payload
+// bytes from its cursor (a step consumes a few bytes per row) and the
+// left-child masses of up to four rows; lane 0 then walks the rows' bisection
+// heaps from shared memory, reading payload bytes from the staged window
+// (global memory only past it).  Each symbol goes to tokens[destination[row]],
+// where the next step's embeddings read it.
+constexpr int rows_warps = 2, staged_rows = 4, window_bytes = 128;
+
+struct WindowedDecoder
+{
+    range::DecodeWindow w;
+    const std::uint8_t* payload;
+    const std::uint8_t* window; // payload bytes [window_start, window_start + window_bytes)
+    std::uint64_t size, window_start, at;
+
+    __device__ __forceinline__ std::uint32_t next_byte()
+    {
+        std::uint32_t byte = 0;
+        if (at < size)
+            byte = at - window_start < window_bytes ? window[at - window_start] : payload[at];
+        ++at;
+        return byte;
+    }
+    __device__ __forceinline__ int node(std::uint32_t p0, int)
+    {
+        return range::decide(w, p0, *this);
+    }
+};
 
 __global__ void __launch_bounds__(rows_warps * 32)
     range_decode_rows_kernel(const std::uint8_t* __restrict__ bytes, const std::uint64_t* __restrict__ offsets,
@@ -162,7 +185,8 @@ __global__ void __launch_bounds__(rows_warps * 32)
                              unsigned* error_word)
 {
     pdl_prologue();
-    __shared__ float staged[rows_warps][1024];
+    __shared__ float staged[rows_warps][staged_rows * 1023 + 1];
+    __shared__ std::uint8_t window[rows_warps][window_bytes];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int s = blockIdx.x * rows_warps + warp;
     if (s >= streams)
@@ -174,24 +198,40 @@ __global__ void __launch_bounds__(rows_warps * 32)
     const std::uint64_t size = sizes[s];
     RangeCursor c = cursors[s];
     const bool was_running = c.status == 0;
-    float* heap = staged[warp];
-    for (int row = first; row < last; ++row)
+    for (int i = lane; i < window_bytes; i += 32)
+        window[warp][i] = c.offset + i < size ? payload[c.offset + i] : 0;
+    WindowedDecoder d{{c.range, c.code}, payload, window[warp], size, c.offset, c.offset};
+    for (int r0 = first; r0 < last; r0 += staged_rows)
     {
-        const float* m = masses + static_cast<size_t>(row) * 1023;
-        for (int i = lane; i < 1023; i += 32)
-            heap[i] = m[i];
+        const int n = last - r0 < staged_rows ? last - r0 : staged_rows;
+        const float* m = masses + static_cast<size_t>(r0) * 1023;
+        for (int i = lane; i < n * 1023; i += 32)
+            staged[warp][i] = m[i];
         __syncwarp();
         if (lane == 0)
         {
-            std::uint16_t symbol = 0;
-            if (c.status == 0)
-                decode_symbol(payload, size, c, heap, symbol);
-            tokens[destination[row]] = c.status == 0 ? symbol : 0;
+            for (int j = 0; j < n; ++j)
+            {
+                int symbol = 0;
+                if (c.status == 0)
+                {
+                    symbol = range::walk_bisection<DeviceMath>(staged[warp] + j * 1023, d);
+                    if (symbol < 0)
+                    {
+                        c.status = 1;
+                        symbol = 0;
+                    }
+                }
+                tokens[destination[r0 + j]] = static_cast<std::uint16_t>(symbol);
+            }
         }
         __syncwarp();
     }
     if (lane == 0)
     {
+        c.range = d.w.range;
+        c.code = d.w.code;
+        c.offset = static_cast<std::uint32_t>(d.at);
         cursors[s] = c;
         if (was_running && c.status != 0 && error_word)
             atomicOr(error_word, error_range);
