@@ -99,7 +99,11 @@ __device__ __forceinline__ void tma_3d(uint32_t dst, const CUtensorMap* map, int
 }
 
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
-// 128 bytes in 8-row (1024-byte) atoms stacked along M/N.
+// 128 bytes in 8-row (1024-byte) atoms stacked along M/N.  The swizzle follows
+// the shared-memory address bits, as the TMA writes it, so an operand may start
+// at any 128-byte row of a 1024-byte-aligned tile or window (base offset 0;
+// measured: setting the descriptor's base-offset field to the row phase gave
+// wrong products).
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr)
 {
     uint64_t d = static_cast<uint64_t>((saddr & 0x3ffffu) >> 4);

@@ -37,7 +37,6 @@ using namespace tc;
 constexpr int BM = 128;        // rows per tile (TMEM lanes)
 constexpr int TC_THREADS = 320; // producer warp, MMA warp, 8 epilogue warps
 constexpr int BK = 32;         // fp32 per k-block row: one 128-byte swizzle row
-constexpr int A_BYTES = BM * BK * 4;
 
 // Four TMEM accumulators per tile (BN columns each): the hi*hi products of
 // k-step j go to accumulator j mod 3 and the hi*lo + lo*hi corrections to the
@@ -46,26 +45,35 @@ constexpr int A_BYTES = BM * BK * 4;
 // chains and a correction chain 2^11 times smaller in magnitude, summed with
 // round-to-nearest adds in the epilogue, keep the error near fp32 rounding.
 constexpr int ACCS = 4;
+// Input windows: per (tile, 32-channel chunk) one TMA load of the rows every
+// tap of the tile reads, BM + span rows with span = (taps - 1) |tap_step| <=
+// MAX_SPAN; each tap's A operand starts at its own row of the window.
+constexpr int MAX_SPAN = 64;
+constexpr int WIN_ROWS = BM + MAX_SPAN;
+constexpr int WIN_BYTES = WIN_ROWS * BK * 4; // one head or tail window (1024-byte multiple)
+constexpr int A_STAGES = 2;
 template <int BN> struct Config;
 template <> struct Config<128>
 {
-    static constexpr int stages = 3, tmem_cols = 512;
+    static constexpr int stages = 4, tmem_cols = 512; // weight (B) stages
 };
 template <> struct Config<96>
 {
-    static constexpr int stages = 3, tmem_cols = 512;
+    static constexpr int stages = 4, tmem_cols = 512;
 };
 
 template <int BN> __host__ __device__ constexpr int stage_bytes()
 {
-    return 2 * A_BYTES + 2 * BN * BK * 4;
+    return 2 * BN * BK * 4; // weight head + tail of one (tap, chunk)
 }
 template <int BN> __host__ __device__ constexpr int smem_bytes()
 {
-    return Config<BN>::stages * stage_bytes<BN>() + 1024 /* alignment */ + 256 /* barriers */;
+    return A_STAGES * 2 * WIN_BYTES + Config<BN>::stages * stage_bytes<BN>() + 1024 /* alignment */ +
+           256 /* barriers */;
 }
 static_assert(smem_bytes<128>() <= 227 * 1024 && smem_bytes<96>() <= 227 * 1024,
-              "stage ring exceeds the per-CTA shared memory limit");
+              "stage rings exceed the per-CTA shared memory limit");
+static_assert(WIN_BYTES % 1024 == 0, "windows keep the 1024-byte swizzle alignment");
 
 // Instruction descriptor: D f32, A and B tf32, both K-major, M = 128, N = BN.
 template <int BN> __device__ __forceinline__ uint32_t tf32_idesc()
@@ -134,20 +142,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
-    // bars: full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+    unsigned char* windows = smem;                            // [A_STAGES][head, tail][WIN_BYTES]
+    unsigned char* weights = smem + A_STAGES * 2 * WIN_BYTES; // [STAGES][head, tail][B_BYTES]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(weights + STAGES * STAGE);
+    // bars: full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain,
+    // win_full[A_STAGES], win_empty[A_STAGES]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5 + 2 * A_STAGES);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
     const uint32_t acc_full0 = smem_u32(bars + 2 * STAGES), acc_empty0 = acc_full0 + 16;
     const uint32_t drain = acc_full0 + 32;
+    const uint32_t win_full0 = drain + 8, win_empty0 = win_full0 + 8 * A_STAGES;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long m_tiles = (g.rows + BM - 1) / BM;
     const int n_tiles = g.cout / BN;
     const long long tiles = m_tiles * n_tiles * g.phases;
-    const int kb_per_tap = g.cin / BK;
-    const int kblocks = g.taps * kb_per_tap;
+    const int chunks = g.cin / BK;
+    // Window geometry: the window starts `low` rows from the tile's first
+    // input row; tap t's operand starts at window row t * tap_step - low.
+    const int low = g.tap_step < 0 ? (g.taps - 1) * g.tap_step : 0;
+    const int win_rows = BM + (g.taps - 1) * (g.tap_step < 0 ? -g.tap_step : g.tap_step);
 
     if (threadIdx.x == 0)
     {
@@ -160,6 +175,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         {
             bar_init(acc_full0 + 8 * a, 1);
             bar_init(acc_empty0 + 8 * a, TC_THREADS - 64);
+        }
+        for (int w = 0; w < A_STAGES; ++w)
+        {
+            bar_init(win_full0 + 8 * w, 1);
+            bar_init(win_empty0 + 8 * w, 1);
         }
         bar_init(drain, 1);
         *abort_flag = 0;
@@ -182,36 +202,53 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (lane == 0)
         {
             // ---------------------------------------------------- producer --
-            int stage = 0;
-            uint32_t phase = 0;
-            long long issued = 0;
+            int stage = 0, wstage = 0;
+            uint32_t phase = 0, wphase = 0;
+            long long issued = 0, win_issued = 0;
             bool ok = true;
             for (long long tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
             {
                 const TileCoord t = tile_coord(tile, m_tiles, n_tiles);
-                const long long row0 = t.m * BM + g.row_shift[t.phase];
-                for (int kb = 0; kb < kblocks; ++kb)
+                const int win_row = static_cast<int>(t.m * BM + g.row_shift[t.phase] + low);
+                for (int cb = 0; cb < chunks && ok; ++cb)
                 {
-                    if (!bar_wait(empty0 + 8 * stage, phase ^ 1u, abort_flag))
+                    if (!bar_wait(win_empty0 + 8 * wstage, wphase ^ 1u, abort_flag))
                     {
                         ok = false;
                         break;
                     }
-                    const int tap = kb / kb_per_tap, cb = kb - tap * kb_per_tap;
-                    const int row = static_cast<int>(row0 + static_cast<long long>(tap) * g.tap_step);
-                    const int slice = t.phase * g.taps + tap;
-                    const uint32_t base = smem_u32(smem + stage * STAGE);
-                    const uint32_t bar = full0 + 8 * stage;
-                    bar_expect_tx(bar, STAGE);
-                    tma_2d(base, &map_xhi, cb * BK, row, bar);
-                    tma_2d(base + A_BYTES, &map_xlo, cb * BK, row, bar);
-                    tma_3d(base + 2 * A_BYTES, &map_whi, cb * BK, t.n * BN, slice, bar);
-                    tma_3d(base + 2 * A_BYTES + B_BYTES, &map_wlo, cb * BK, t.n * BN, slice, bar);
-                    ++issued;
-                    if (++stage == STAGES)
                     {
-                        stage = 0;
-                        phase ^= 1u;
+                        const uint32_t base = smem_u32(windows + wstage * 2 * WIN_BYTES);
+                        const uint32_t bar = win_full0 + 8 * wstage;
+                        bar_expect_tx(bar, 2u * static_cast<uint32_t>(win_rows) * BK * 4);
+                        tma_2d(base, &map_xhi, cb * BK, win_row, bar);
+                        tma_2d(base + WIN_BYTES, &map_xlo, cb * BK, win_row, bar);
+                        ++win_issued;
+                        if (++wstage == A_STAGES)
+                        {
+                            wstage = 0;
+                            wphase ^= 1u;
+                        }
+                    }
+                    for (int tap = 0; tap < g.taps; ++tap)
+                    {
+                        if (!bar_wait(empty0 + 8 * stage, phase ^ 1u, abort_flag))
+                        {
+                            ok = false;
+                            break;
+                        }
+                        const int slice = t.phase * g.taps + tap;
+                        const uint32_t base = smem_u32(weights + stage * STAGE);
+                        const uint32_t bar = full0 + 8 * stage;
+                        bar_expect_tx(bar, STAGE);
+                        tma_3d(base, &map_whi, cb * BK, t.n * BN, slice, bar);
+                        tma_3d(base + B_BYTES, &map_wlo, cb * BK, t.n * BN, slice, bar);
+                        ++issued;
+                        if (++stage == STAGES)
+                        {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
                     }
                 }
             }
@@ -220,16 +257,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 *abort_flag = 1;
                 if (e.error_word)
                     atomicOr(e.error_word, error_timeout);
-                // Loads in flight land in the last (up to) STAGES stages issued;
-                // wait for them (bounded) before the CTA may exit.
-                const long long pending = issued < STAGES ? issued : STAGES;
+                // Loads in flight land in the last (up to) STAGES weight stages
+                // and A_STAGES windows issued; wait for them (bounded) before
+                // the CTA may exit.
                 volatile int never = 0;
+                const long long pending = issued < STAGES ? issued : STAGES;
                 for (long long k = 1; k <= pending; ++k)
                 {
                     const long long n = issued - k;
-                    const int s = static_cast<int>(n % STAGES);
-                    const uint32_t par = static_cast<uint32_t>((n / STAGES) & 1);
-                    bar_wait(full0 + 8 * s, par, &never);
+                    bar_wait(full0 + 8 * static_cast<int>(n % STAGES), static_cast<uint32_t>((n / STAGES) & 1),
+                             &never);
+                }
+                const long long win_pending = win_issued < A_STAGES ? win_issued : A_STAGES;
+                for (long long k = 1; k <= win_pending; ++k)
+                {
+                    const long long n = win_issued - k;
+                    bar_wait(win_full0 + 8 * static_cast<int>(n % A_STAGES),
+                             static_cast<uint32_t>((n / A_STAGES) & 1), &never);
                 }
             }
         }
@@ -240,8 +284,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         {
             // --------------------------------------------------------- MMA --
             const uint32_t idesc = tf32_idesc<BN>();
-            int stage = 0;
-            uint32_t phase = 0;
+            int stage = 0, wstage = 0;
+            uint32_t phase = 0, wphase = 0;
             int local = 0;
             bool ok = true, any = false;
             for (long long tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++local)
@@ -256,33 +300,52 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 tc_fence_after();
                 const uint32_t corr = tmem + static_cast<uint32_t>(3 * BN);
                 int step = 0; // k-step within the tile
-                for (int kb = 0; kb < kblocks; ++kb)
+                for (int cb = 0; cb < chunks && ok; ++cb)
                 {
-                    if (!bar_wait(full0 + 8 * stage, phase, abort_flag))
+                    if (!bar_wait(win_full0 + 8 * wstage, wphase, abort_flag))
                     {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t base = smem_u32(smem + stage * STAGE);
+                    const uint32_t win = smem_u32(windows + wstage * 2 * WIN_BYTES);
+                    for (int tap = 0; tap < g.taps; ++tap)
+                    {
+                        if (!bar_wait(full0 + 8 * stage, phase, abort_flag))
+                        {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a_row = static_cast<uint32_t>(tap * g.tap_step - low) * (BK * 4);
+                        const uint32_t base = smem_u32(weights + stage * STAGE);
 #pragma unroll
-                    for (int k = 0; k < BK / 8; ++k, ++step)
-                    {
-                        const uint64_t ahi = sw128_desc(base + k * 32);
-                        const uint64_t alo = sw128_desc(base + A_BYTES + k * 32);
-                        const uint64_t bhi = sw128_desc(base + 2 * A_BYTES + k * 32);
-                        const uint64_t blo = sw128_desc(base + 2 * A_BYTES + B_BYTES + k * 32);
-                        const uint32_t main = tmem + static_cast<uint32_t>((step % 3) * BN);
-                        mma_tf32(main, ahi, bhi, idesc, step >= 3 ? 1u : 0u);
-                        mma_tf32(corr, ahi, blo, idesc, step > 0 ? 1u : 0u);
-                        mma_tf32(corr, alo, bhi, idesc, 1u);
+                        for (int k = 0; k < BK / 8; ++k, ++step)
+                        {
+                            const uint64_t ahi = sw128_desc(win + a_row + k * 32);
+                            const uint64_t alo = sw128_desc(win + WIN_BYTES + a_row + k * 32);
+                            const uint64_t bhi = sw128_desc(base + k * 32);
+                            const uint64_t blo = sw128_desc(base + B_BYTES + k * 32);
+                            const uint32_t main = tmem + static_cast<uint32_t>((step % 3) * BN);
+                            mma_tf32(main, ahi, bhi, idesc, step >= 3 ? 1u : 0u);
+                            mma_tf32(corr, ahi, blo, idesc, step > 0 ? 1u : 0u);
+                            mma_tf32(corr, alo, bhi, idesc, 1u);
+                        }
+                        any = true;
+                        mma_commit(empty0 + 8 * stage);
+                        if (++stage == STAGES)
+                        {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
                     }
-                    any = true;
-                    mma_commit(empty0 + 8 * stage);
-                    if (++stage == STAGES)
+                    if (!ok)
+                        break;
+                    mma_commit(win_empty0 + 8 * wstage);
+                    if (++wstage == A_STAGES)
                     {
-                        stage = 0;
-                        phase ^= 1u;
+                        wstage = 0;
+                        wphase ^= 1u;
                     }
                 }
                 if (!ok)
@@ -467,7 +530,8 @@ cudaError_t launch(const TcConvOperands& op, const TcConvGeometry& g, const TcCo
     CUtensorMap xhi, xlo, whi, wlo;
     const cuuint64_t xdims[2] = {static_cast<cuuint64_t>(g.cin), static_cast<cuuint64_t>(g.in_rows)};
     const cuuint64_t xstrides[1] = {static_cast<cuuint64_t>(g.cin) * 4};
-    const cuuint32_t xbox[2] = {BK, BM};
+    const int span = (g.taps - 1) * (g.tap_step < 0 ? -g.tap_step : g.tap_step);
+    const cuuint32_t xbox[2] = {BK, static_cast<cuuint32_t>(BM + span)};
     const int slices = g.taps * g.phases;
     const cuuint64_t wdims[3] = {static_cast<cuuint64_t>(g.cin), static_cast<cuuint64_t>(g.cout),
                                  static_cast<cuuint64_t>(slices)};
@@ -507,7 +571,8 @@ cudaError_t tc_conv(const TcConvOperands& op, const TcConvGeometry& g, const TcC
                     cudaStream_t stream)
 {
     if (!tc_conv_supported(g.cin, g.cout) || g.rows <= 0 || g.phases < 1 || g.phases > 8 ||
-        g.taps < 1 || g.taps * g.phases > 16 || g.out_scale < 1 || g.in_rows >= (1ll << 31))
+        g.taps < 1 || g.taps * g.phases > 16 || g.out_scale < 1 || g.in_rows >= (1ll << 31) ||
+        (g.taps - 1) * (g.tap_step < 0 ? -g.tap_step : g.tap_step) > MAX_SPAN)
         return cudaErrorInvalidValue;
     if (g.cout % 128 == 0)
         return launch<128>(op, g, e, stream);
