@@ -95,15 +95,33 @@ struct MmaArgs
     QkvScatter qkv; // QKV_OUT destinations
 };
 
-// Shared memory of the decode-shaped kernel: the block dots.
-__host__ __device__ constexpr size_t mma_smem_bytes(int k)
+// Shared memory of the decode-shaped kernel: the block dots, then the fold
+// operands (activation scales of the CTA's rows, weight scales, biases).
+__host__ __device__ constexpr size_t mma_dots_bytes(int k)
 {
     return static_cast<size_t>(k / 256) * MMA_MT * 128 * sizeof(int);
 }
 
-// Weight chunks (per warp) and fold scales (per thread) loaded before the
-// programmatic-dependency wait: the model's K <= 2048 layers fit entirely.
-constexpr int MMA_PRE_CHUNKS = 4, MMA_PRE_BLOCKS = 8;
+__host__ __device__ constexpr size_t mma_smem_bytes(int k)
+{
+    return mma_dots_bytes(k) + static_cast<size_t>(k / 256) * (8 * MMA_MT + 16) * sizeof(float) + 16 * sizeof(float);
+}
+
+// 4-byte asynchronous global -> shared copy (completion: cp_async_wait_all).
+__device__ __forceinline__ void cp_async_4(void* smem, const void* gmem)
+{
+    const unsigned address = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(address), "l"(gmem) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all()
+{
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// Weight chunks (per warp) loaded before the programmatic-dependency wait:
+// the model's K <= 2048 layers fit entirely.
+constexpr int MMA_PRE_CHUNKS = 4;
 
 template <bool QKV_OUT>
 __global__ void __launch_bounds__(256) qlinear_mma_kernel(MmaArgs a)
@@ -122,7 +140,7 @@ __global__ void __launch_bounds__(256) qlinear_mma_kernel(MmaArgs a)
     const std::int8_t* wa = a.w + static_cast<size_t>(n0 + g) * k + quarter * 64 + t * 16;
     const std::int8_t* wb = wa + static_cast<size_t>(8) * k;
     // Model constants first (no predecessor writes them): this warp's weight
-    // chunks, and each thread's fold scales and biases for its two outputs.
+    // chunks in registers; the fold's weight scales and biases below.
     uint4 pre_lo[MMA_PRE_CHUNKS], pre_hi[MMA_PRE_CHUNKS];
 #pragma unroll
     for (int it = 0; it < MMA_PRE_CHUNKS; ++it)
@@ -134,18 +152,41 @@ __global__ void __launch_bounds__(256) qlinear_mma_kernel(MmaArgs a)
             pre_hi[it] = __ldg(reinterpret_cast<const uint4*>(wb + b * 256));
         }
     }
-    float pre_scale[2][MMA_PRE_BLOCKS], pre_bias[2];
+    // The fold's weight scales [block][16 outputs] and biases: asynchronous
+    // copies into shared memory, which hold no registers.
+    float* xs_tile = reinterpret_cast<float*>(mma_smem + mma_dots_bytes(k)); // [32 rows][blocks]
+    float* ws_tile = xs_tile + 8 * MMA_MT * blocks;                          // [blocks][16]
+    float* bias_tile = ws_tile + 16 * blocks;                                // [16]
+    for (int i = threadIdx.x; i < 16 * blocks; i += 256)
+        cp_async_4(ws_tile + i, a.wscale + static_cast<size_t>(i >> 4) * n_cols + n0 + (i & 15));
+    if (threadIdx.x < 16)
+        cp_async_4(bias_tile + threadIdx.x, a.e.bias + n0 + threadIdx.x);
+    pdl_wait();
+    __syncthreads();
+    // Predecessor outputs the fold reads, requested now so their latency
+    // overlaps the activation loads and the MMAs instead of following them:
+    // the CTA's activation scales (asynchronous copies into shared memory),
+    // and per thread its residual values and QKV row slots.
+    for (int i = threadIdx.x; i < 8 * MMA_MT * blocks; i += 256)
+        if (m0 + i / blocks < m_rows)
+            cp_async_4(xs_tile + i, a.xscale + static_cast<size_t>(m0) * blocks + i);
+    std::uint16_t pre_res[2] = {0, 0};
+    int pre_slot[2] = {0, 0}, pre_rotary[2] = {-1, -1};
 #pragma unroll
     for (int half = 0; half < 2; ++half)
     {
-        const int n = n0 + ((threadIdx.x + half * 256) & 15);
-        pre_bias[half] = __ldg(a.e.bias + n);
-#pragma unroll
-        for (int b = 0; b < MMA_PRE_BLOCKS; ++b)
-            pre_scale[half][b] = b < blocks ? __ldg(a.wscale + b * n_cols + n) : 0.0f;
+        const int id = threadIdx.x + half * 256;
+        const int n = n0 + (id & 15), m = m0 + (id >> 4);
+        if (m >= m_rows)
+            continue;
+        if (a.e.residual)
+            pre_res[half] = a.e.residual[static_cast<size_t>(m) * a.e.residual_stride + n];
+        if constexpr (QKV_OUT)
+        {
+            pre_slot[half] = a.qkv.meta[m].slot;
+            pre_rotary[half] = a.qkv.meta[m].rotary;
+        }
     }
-    pdl_wait();
-    __syncthreads();
     // One 64-byte chunk of every 256-block b this warp owns (b = warp / 4,
     // warp / 4 + 2, ...): int8 MMAs of the 16 weight rows with the CTA's four
     // 8-column m-tiles, quarter dots merged in shared memory.
@@ -182,6 +223,7 @@ __global__ void __launch_bounds__(256) qlinear_mma_kernel(MmaArgs a)
     for (int b = (warp >> 2) + 2 * MMA_PRE_CHUNKS; b < blocks; b += 2)
         chunk(b, __ldg(reinterpret_cast<const uint4*>(wa + b * 256)),
               __ldg(reinterpret_cast<const uint4*>(wb + b * 256)));
+    cp_async_wait_all();
     __syncthreads();
     // Fold: output (nl, ml), nl = 0..15, ml = 0..31; fragment element c of
     // lane (g, t) holds (n = g + 8 (c / 2), m = 2 t + c % 2) of its m-tile.
@@ -199,24 +241,13 @@ __global__ void __launch_bounds__(256) qlinear_mma_kernel(MmaArgs a)
             const int frag_lane = (nl & 7) * 4 + (col >> 1);
             const int c = (nl >> 3) * 2 + (col & 1);
             float sum = 0.0f;
-#pragma unroll
-            for (int b = 0; b < MMA_PRE_BLOCKS; ++b)
+            for (int b = 0; b < blocks; ++b)
             {
-                if (b < blocks)
-                {
-                    const float scale = __fmul_rn(pre_scale[half][b], __ldg(a.xscale + m * blocks + b));
-                    const int dot = dots[((b * MMA_MT + mt) * 32 + frag_lane) * 4 + c];
-                    sum = __fmaf_rn(static_cast<float>(dot), scale, sum);
-                }
-            }
-            for (int b = MMA_PRE_BLOCKS; b < blocks; ++b)
-            {
-                const float scale = __fmul_rn(__ldg(a.wscale + b * n_cols + n),
-                                              __ldg(a.xscale + m * blocks + b));
+                const float scale = __fmul_rn(ws_tile[b * 16 + nl], xs_tile[ml * blocks + b]);
                 const int dot = dots[((b * MMA_MT + mt) * 32 + frag_lane) * 4 + c];
                 sum = __fmaf_rn(static_cast<float>(dot), scale, sum);
             }
-            out = finish_with_bias(sum, pre_bias[half], m, n, a.e);
+            out = finish_loaded(sum, bias_tile[nl], a.e.residual != nullptr, pre_res[half], a.e.lut);
         }
         if constexpr (QKV_OUT)
         {
@@ -226,15 +257,15 @@ __global__ void __launch_bounds__(256) qlinear_mma_kernel(MmaArgs a)
             const unsigned other = __shfl_xor_sync(0xffffffffu, static_cast<unsigned>(out), 1);
             if (!valid)
                 continue;
-            const RowMeta rm = a.qkv.meta[m];
+            const int slot = pre_slot[half], rotary = pre_rotary[half];
             if (n < 1024)
             {
                 const bool even = (n & 1) == 0;
                 std::uint16_t result = out;
-                if (rm.rotary >= 0)
+                if (rotary >= 0)
                 {
                     const int pair = (n & 511) >> 1;
-                    const unsigned cs = reinterpret_cast<const unsigned*>(a.qkv.rotations + rm.rotary * 128)[pair & 63];
+                    const unsigned cs = reinterpret_cast<const unsigned*>(a.qkv.rotations + rotary * 128)[pair & 63];
                     const float cosine = from_bf16(cs & 0xffffu), sine = from_bf16(cs >> 16);
                     const float real = from_bf16(even ? out : static_cast<std::uint16_t>(other));
                     const float imaginary = from_bf16(even ? static_cast<std::uint16_t>(other) : out);
@@ -246,11 +277,11 @@ __global__ void __launch_bounds__(256) qlinear_mma_kernel(MmaArgs a)
                 if (n < 512)
                     a.qkv.query[static_cast<size_t>(m) * 512 + n] = result;
                 else
-                    a.qkv.cache_k[static_cast<size_t>(rm.slot) * 512 + (n - 512)] = result;
+                    a.qkv.cache_k[static_cast<size_t>(slot) * 512 + (n - 512)] = result;
             }
             else
             {
-                a.qkv.cache_v[static_cast<size_t>(rm.slot) * 512 + (n - 1024)] = out;
+                a.qkv.cache_v[static_cast<size_t>(slot) * 512 + (n - 1024)] = out;
             }
         }
         else
@@ -285,8 +316,8 @@ void launch_small(const QLinearArgs& a, const Epilogue& e, cudaStream_t stream)
 
 void qlinear_init()
 {
-    // The decode-shaped kernel keeps its block dots in shared memory (64 KB
-    // at k = 8192).  The attribute belongs to each device's context, so it is
+    // The decode-shaped kernel keeps its block dots and fold operands in
+    // shared memory (70 KB at k = 8192).  The attribute belongs to each device's context, so it is
     // set once per device (a bit per ordinal; setting it twice from racing
     // threads is harmless).
     static std::atomic<unsigned long long> ready{0};

@@ -17,6 +17,18 @@ struct Epilogue
     int residual_stride;           // 0: one residual row for every column
 };
 
+// finish() with the bias and the residual value already loaded.
+__device__ __forceinline__ std::uint16_t finish_loaded(float sum, float bias, bool has_residual,
+                                                       std::uint16_t residual, const std::uint16_t* lut)
+{
+    std::uint16_t y = to_bf16(__fadd_rn(sum, bias));
+    if (has_residual)
+        y = to_bf16(__fadd_rn(from_bf16(residual), from_bf16(y)));
+    if (lut)
+        y = lut[y];
+    return y;
+}
+
 // finish() with the bias value already loaded.
 __device__ __forceinline__ std::uint16_t finish_with_bias(float sum, float bias, int m, int n, const Epilogue& e)
 {

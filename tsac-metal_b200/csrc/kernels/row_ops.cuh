@@ -54,8 +54,28 @@ __device__ __forceinline__ float warp_sum512(const float* v)
 // LayerNorm of one bf16 row by one warp: bf16 output to y (nullable) and/or
 // its BF8L quantization to yq / yscale[2] (nullable).  Returns whether every
 // output was finite (all lanes agree).
-__device__ __forceinline__ bool layer_norm_row(const std::uint16_t* x, const std::uint16_t* gain,
-                                               const std::uint16_t* bias, std::uint16_t* y,
+// Gain and bias values of one lane (columns 16 lane .. 16 lane + 15), loaded
+// ahead of the row so their latency overlaps the predecessor's completion.
+struct NormLane
+{
+    std::uint16_t gain[16], bias[16];
+};
+
+__device__ __forceinline__ NormLane load_norm_lane(const std::uint16_t* gain, const std::uint16_t* bias)
+{
+    const int lane = threadIdx.x & 31;
+    NormLane c;
+    *reinterpret_cast<uint4*>(c.gain) = __ldg(reinterpret_cast<const uint4*>(gain + lane * 16));
+    *reinterpret_cast<uint4*>(c.gain + 8) = __ldg(reinterpret_cast<const uint4*>(gain + lane * 16 + 8));
+    *reinterpret_cast<uint4*>(c.bias) = __ldg(reinterpret_cast<const uint4*>(bias + lane * 16));
+    *reinterpret_cast<uint4*>(c.bias + 8) = __ldg(reinterpret_cast<const uint4*>(bias + lane * 16 + 8));
+    return c;
+}
+
+__device__ __forceinline__ bool layer_norm_values(const std::uint16_t (&h)[16], const NormLane& c,
+                                                  std::uint16_t* y, std::int8_t* yq, float* yscale);
+
+__device__ __forceinline__ bool layer_norm_row(const std::uint16_t* x, const NormLane& c, std::uint16_t* y,
                                                std::int8_t* yq, float* yscale)
 {
     const int lane = threadIdx.x & 31;
@@ -63,6 +83,21 @@ __device__ __forceinline__ bool layer_norm_row(const std::uint16_t* x, const std
     std::uint16_t h[16];
     *reinterpret_cast<uint4*>(h) = *reinterpret_cast<const uint4*>(src);
     *reinterpret_cast<uint4*>(h + 8) = *reinterpret_cast<const uint4*>(src + 8);
+    return layer_norm_values(h, c, y, yq, yscale);
+}
+
+__device__ __forceinline__ bool layer_norm_row(const std::uint16_t* x, const std::uint16_t* gain,
+                                               const std::uint16_t* bias, std::uint16_t* y,
+                                               std::int8_t* yq, float* yscale)
+{
+    return layer_norm_row(x, load_norm_lane(gain, bias), y, yq, yscale);
+}
+
+// The row's 16 values of this lane already in registers.
+__device__ __forceinline__ bool layer_norm_values(const std::uint16_t (&h)[16], const NormLane& c,
+                                                  std::uint16_t* y, std::int8_t* yq, float* yscale)
+{
+    const int lane = threadIdx.x & 31;
     float v[16], sq[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i)
@@ -83,9 +118,8 @@ __device__ __forceinline__ bool layer_norm_row(const std::uint16_t* x, const std
 #pragma unroll
     for (int i = 0; i < 16; ++i)
     {
-        const int c = lane * 16 + i;
         const float normalized = __fmaf_rn(v[i], inverse, offset);
-        out[i] = to_bf16(__fmaf_rn(normalized, from_bf16(gain[c]), from_bf16(bias[c])));
+        out[i] = to_bf16(__fmaf_rn(normalized, from_bf16(c.gain[i]), from_bf16(c.bias[i])));
         const float o = from_bf16(out[i]);
         finite = finite && isfinite(o);
         m = fmaxf(m, fabsf(flush(o)));

@@ -76,12 +76,14 @@ __global__ void layer_norm_kernel(const std::uint16_t* __restrict__ x,
                                   std::uint16_t* __restrict__ y, std::int8_t* __restrict__ yq,
                                   float* __restrict__ yscale, unsigned* error_word)
 {
-    pdl_prologue();
+    pdl_release();
+    const NormLane consts = load_norm_lane(gain, bias); // model constants: before the wait
+    pdl_wait();
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= rows)
         return;
-    const bool finite = layer_norm_row(x + static_cast<size_t>(row) * 512, gain, bias,
+    const bool finite = layer_norm_row(x + static_cast<size_t>(row) * 512, consts,
                                        y ? y + static_cast<size_t>(row) * 512 : nullptr,
                                        yq ? yq + static_cast<size_t>(row) * 512 : nullptr,
                                        yq ? yscale + row * 2 : nullptr);
