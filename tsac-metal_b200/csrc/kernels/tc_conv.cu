@@ -49,31 +49,33 @@ constexpr int ACCS = 4;
 // tap of the tile reads, BM + span rows with span = (taps - 1) |tap_step| <=
 // MAX_SPAN; each tap's A operand starts at its own row of the window.
 constexpr int MAX_SPAN = 64;
-constexpr int WIN_ROWS = BM + MAX_SPAN;
-constexpr int WIN_BYTES = WIN_ROWS * BK * 4; // one head or tail window (1024-byte multiple)
 constexpr int A_STAGES = 2;
-template <int BN> struct Config;
-template <> struct Config<128>
+constexpr int TMEM_COLS = 512;
+// Shared memory: the windows of a launch (sized by its span, 1024-byte
+// aligned for the 128-byte swizzle), then as many weight (B) stages as the
+// rest of the 227 KB holds.
+constexpr int SMEM_BYTES = 227 * 1024;
+constexpr int SMEM_RESERVED = 1024 /* alignment */ + 256 /* barriers */;
+constexpr int MAX_B_STAGES = 8;
+
+__host__ __device__ constexpr int window_bytes(int span)
 {
-    static constexpr int stages = 4, tmem_cols = 512; // weight (B) stages
-};
-template <> struct Config<96>
-{
-    static constexpr int stages = 4, tmem_cols = 512;
-};
+    return ((BM + span) * BK * 4 + 1023) & ~1023; // one head or tail window
+}
 
 template <int BN> __host__ __device__ constexpr int stage_bytes()
 {
     return 2 * BN * BK * 4; // weight head + tail of one (tap, chunk)
 }
-template <int BN> __host__ __device__ constexpr int smem_bytes()
+
+template <int BN> __host__ __device__ constexpr int weight_stages(int span)
 {
-    return A_STAGES * 2 * WIN_BYTES + Config<BN>::stages * stage_bytes<BN>() + 1024 /* alignment */ +
-           256 /* barriers */;
+    const int s = (SMEM_BYTES - SMEM_RESERVED - A_STAGES * 2 * window_bytes(span)) / stage_bytes<BN>();
+    return s < MAX_B_STAGES ? s : MAX_B_STAGES;
 }
-static_assert(smem_bytes<128>() <= 227 * 1024 && smem_bytes<96>() <= 227 * 1024,
-              "stage rings exceed the per-CTA shared memory limit");
-static_assert(WIN_BYTES % 1024 == 0, "windows keep the 1024-byte swizzle alignment");
+static_assert(weight_stages<128>(MAX_SPAN) >= 4 && weight_stages<96>(MAX_SPAN) >= 4,
+              "the weight ring keeps at least four stages at the largest span");
+static_assert((2 * MAX_B_STAGES + 5 + 2 * A_STAGES) * 8 + 8 <= 256, "barrier block exceeds its reservation");
 
 // Instruction descriptor: D f32, A and B tf32, both K-major, M = 128, N = BN.
 template <int BN> __device__ __forceinline__ uint32_t tf32_idesc()
@@ -133,11 +135,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                    const __grid_constant__ CUtensorMap map_wlo, const TcConvGeometry g,
                    const TcConvEpilogue e)
 {
-    constexpr int STAGES = Config<BN>::stages;
-    constexpr int TMEM_COLS = Config<BN>::tmem_cols;
     static_assert(ACCS * BN <= TMEM_COLS, "accumulators exceed the TMEM allocation");
     static_assert((BN / 2) % 16 == 0, "each epilogue warp takes whole 16-column chunks");
     constexpr int STAGE = stage_bytes<BN>();
+    const int span = (g.taps - 1) * (g.tap_step < 0 ? -g.tap_step : g.tap_step);
+    const int WIN_BYTES = window_bytes(span);
+    const int STAGES = weight_stages<BN>(span);
     constexpr int B_BYTES = BN * BK * 4;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -425,7 +428,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const float* v = sum + 16 * c;
                 const int col = t.n * BN + c0;
                 const size_t at = static_cast<size_t>(o) * g.cout + col;
-                float raw[16], act[16];
+                float raw[16], act[16], res[16];
+                // The residual row segment in four 16-byte loads (it may be
+                // the raw output itself: each element is read before this
+                // thread writes it).
+#pragma unroll
+                for (int j = 0; j < 16; j += 4)
+                {
+                    const float4 r4 = valid && e.residual ? *reinterpret_cast<const float4*>(e.residual + at + j)
+                                                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    res[j] = r4.x;
+                    res[j + 1] = r4.y;
+                    res[j + 2] = r4.z;
+                    res[j + 3] = r4.w;
+                }
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
                 {
@@ -434,7 +450,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     {
                         r = __fadd_rn(v[j], __ldg(e.bias + col + j));
                         if (e.residual)
-                            r = __fadd_rn(e.residual[at + j], r);
+                            r = __fadd_rn(res[j], r);
                     }
                     raw[j] = r;
                     act[j] = (valid && e.alpha) ? snake_value(r, __ldg(e.alpha + col + j)) : r;
@@ -543,7 +559,7 @@ cudaError_t launch(const TcConvOperands& op, const TcConvGeometry& g, const TcCo
         !make_map(&whi, op.w_hi, 3, wdims, wstrides, wbox) ||
         !make_map(&wlo, op.w_lo, 3, wdims, wstrides, wbox))
         return cudaErrorInvalidValue;
-    constexpr int smem = smem_bytes<BN>();
+    constexpr int smem = SMEM_BYTES;
     static std::once_flag attr_once[64];
     int device = 0;
     cudaGetDevice(&device);
