@@ -16,6 +16,7 @@
 // source plane), w_scale f32 [K/256][N], bias f32 [N], activations bf16 [M][K].
 // Quantized activations: int8 [M][K] + f32 scale [M][K/256] in caller scratch.
 #include "kernels/qlinear.cuh"
+#include "kernels/async_copy.cuh"
 #include "kernels/launch_count.hpp"
 #include "kernels/numeric.cuh"
 #include "kernels/row_ops.cuh"
@@ -107,17 +108,6 @@ __host__ __device__ constexpr size_t mma_smem_bytes(int k)
     return mma_dots_bytes(k) + static_cast<size_t>(k / 256) * (8 * MMA_MT + 16) * sizeof(float) + 16 * sizeof(float);
 }
 
-// 4-byte asynchronous global -> shared copy (completion: cp_async_wait_all).
-__device__ __forceinline__ void cp_async_4(void* smem, const void* gmem)
-{
-    const unsigned address = static_cast<unsigned>(__cvta_generic_to_shared(smem));
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(address), "l"(gmem) : "memory");
-}
-
-__device__ __forceinline__ void cp_async_wait_all()
-{
-    asm volatile("cp.async.wait_all;" ::: "memory");
-}
 
 // Weight chunks (per warp) loaded before the programmatic-dependency wait:
 // the model's K <= 2048 layers fit entirely.

@@ -16,6 +16,7 @@
 // finds its rows with ballots over the row list, in row order, and lane 0
 // walks them.  Every loop is bounded: 10 decisions per symbol and at most
 // three renormalising shifts per decision (range >= 1 after any split).
+#include "kernels/async_copy.cuh"
 #include "kernels/error_bits.hpp"
 #include "kernels/launch_count.hpp"
 #include "kernels/numeric.cuh"
@@ -184,29 +185,42 @@ __global__ void __launch_bounds__(rows_warps * 32)
                              const int* __restrict__ destination, std::uint16_t* __restrict__ tokens,
                              unsigned* error_word)
 {
-    pdl_prologue();
     __shared__ float staged[rows_warps][staged_rows * 1023 + 1];
     __shared__ std::uint8_t window[rows_warps][window_bytes];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int s = blockIdx.x * rows_warps + warp;
-    if (s >= streams)
+    // Before the dependency wait: the stream's cursor and payload window.
+    // The cursor was last written by the previous step's decoding, many
+    // launches back; every kernel of the chain completes only after its
+    // predecessor has, and this kernel starts only once its predecessor has
+    // passed its own wait, so that write is complete here.
+    const bool active = s < streams && row_begin[s] != row_begin[s + 1];
+    RangeCursor c{};
+    const std::uint8_t* payload = nullptr;
+    std::uint64_t size = 0;
+    if (active)
+    {
+        payload = bytes + offsets[s];
+        size = sizes[s];
+        c = cursors[s];
+#pragma unroll
+        for (int i = lane; i < window_bytes; i += 32)
+            window[warp][i] = c.offset + i < size ? payload[c.offset + i] : 0;
+    }
+    pdl_prologue();
+    if (!active)
         return;
     const int first = row_begin[s], last = row_begin[s + 1];
-    if (first == last)
-        return;
-    const std::uint8_t* payload = bytes + offsets[s];
-    const std::uint64_t size = sizes[s];
-    RangeCursor c = cursors[s];
     const bool was_running = c.status == 0;
-    for (int i = lane; i < window_bytes; i += 32)
-        window[warp][i] = c.offset + i < size ? payload[c.offset + i] : 0;
     WindowedDecoder d{{c.range, c.code}, payload, window[warp], size, c.offset, c.offset};
     for (int r0 = first; r0 < last; r0 += staged_rows)
     {
         const int n = last - r0 < staged_rows ? last - r0 : staged_rows;
         const float* m = masses + static_cast<size_t>(r0) * 1023;
+        // Every lane's copies in flight together, then one wait.
         for (int i = lane; i < n * 1023; i += 32)
-            staged[warp][i] = m[i];
+            cp_async_4(&staged[warp][i], m + i);
+        cp_async_wait_all();
         __syncwarp();
         if (lane == 0)
         {
