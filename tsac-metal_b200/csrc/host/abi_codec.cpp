@@ -129,6 +129,43 @@ int tsac_cuda_encode_symbol_bits(tsac_cuda_context* ctx, const float* pcm, size_
         });
 }
 
+namespace
+{
+// Host-result decoding: each recording's buffer is allocated (malloc, for
+// tsac_cuda_free) once its header has passed the context's limits, and the
+// decoder copies the PCM from the device straight into it.
+void decode_to_host(tsac_cuda_context& ctx, size_t count, const uint8_t* const* streams, const size_t* bytes,
+                    float** out, size_t* samples, unsigned* channels)
+{
+    std::vector<tsacb::ByteView> views;
+    std::vector<float*> buffers(count, nullptr);
+    try
+    {
+        for (size_t i = 0; i < count; ++i)
+        {
+            views.emplace_back(streams[i], bytes[i]);
+            const auto h = tsacb::read_header(views.back(), ctx.impl.limits());
+            const auto n = tsacb::checked_mul(h.channels(), h.samples_per_channel());
+            tsacb::require(n <= ctx.impl.limits().tensor_elements, "output audio exceeds element limit");
+            buffers[i] = static_cast<float*>(std::malloc(n * sizeof(float) + 1));
+            if (!buffers[i])
+                throw tsacb::Error("out of host memory");
+            samples[i] = n;
+            channels[i] = static_cast<unsigned>(h.channels());
+        }
+        tsacb::decode_batch(ctx.impl, views, nullptr, buffers.data());
+    }
+    catch (...)
+    {
+        for (auto* b : buffers)
+            std::free(b);
+        throw;
+    }
+    for (size_t i = 0; i < count; ++i)
+        out[i] = buffers[i];
+}
+} // namespace
+
 int tsac_cuda_decode(tsac_cuda_context* ctx, const uint8_t* stream, size_t bytes, float** out,
                      size_t* samples, unsigned* channels)
 {
@@ -136,10 +173,8 @@ int tsac_cuda_decode(tsac_cuda_context* ctx, const uint8_t* stream, size_t bytes
         [&]
         {
             tsacb::require(ctx && stream && out && samples && channels, "null argument");
-            auto r = tsacb::decode_batch(ctx->impl, {tsacb::ByteView(stream, bytes)});
-            *out = tsacb::malloc_copy(r[0].samples.data(), r[0].samples.size());
-            *samples = r[0].samples.size();
-            *channels = r[0].channels;
+            const uint8_t* const streams[1] = {stream};
+            decode_to_host(*ctx, 1, streams, &bytes, out, samples, channels);
         });
 }
 
@@ -173,16 +208,7 @@ int tsac_cuda_decode_batch(tsac_cuda_context* ctx, size_t count, const uint8_t* 
         [&]
         {
             tsacb::require(ctx && streams && bytes && out && samples && channels, "null argument");
-            std::vector<tsacb::ByteView> views;
-            for (size_t i = 0; i < count; ++i)
-                views.emplace_back(streams[i], bytes[i]);
-            auto r = tsacb::decode_batch(ctx->impl, views);
-            for (size_t i = 0; i < count; ++i)
-            {
-                out[i] = tsacb::malloc_copy(r[i].samples.data(), r[i].samples.size());
-                samples[i] = r[i].samples.size();
-                channels[i] = r[i].channels;
-            }
+            decode_to_host(*ctx, count, streams, bytes, out, samples, channels);
         });
 }
 

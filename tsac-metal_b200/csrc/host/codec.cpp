@@ -558,7 +558,7 @@ std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
 }
 
 std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>& streams,
-                                       float* const* device_out)
+                                       float* const* device_out, float* const* host_out)
 {
     ctx.bind();
     Profile profile(ctx.stream(), "decode");
@@ -605,22 +605,29 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
     // RVQ reconstruction + DAC synthesis over chunk windows
     // (src/common/audio_pipeline.hpp:63-83, context 11/11).
     std::vector<DecodedAudio> out(n);
-    std::vector<DeviceBuffer> owned(n);
     std::vector<float*> dst(n);
+    std::size_t host_floats = 0;
     for (std::size_t i = 0; i < n; ++i)
     {
         out[i].channels = static_cast<unsigned>(headers[i].channels());
         out[i].frames = headers[i].samples_per_channel();
         const auto count = headers[i].channels() * headers[i].samples_per_channel();
         require(count <= ctx.limits().tensor_elements, "output audio exceeds element limit");
+        host_floats = checked_add(host_floats, align_up(count, 64));
+    }
+    // Host results are assembled in one device buffer of the context (kept
+    // between calls), then copied out.
+    float* assembled = device_out ? nullptr : ctx.workspace().get<float>("pcm_out", host_floats);
+    for (std::size_t i = 0, at = 0; i < n; ++i)
+    {
         if (device_out)
         {
             dst[i] = device_out[i];
         }
         else
         {
-            owned[i].resize(count * 4 + 4);
-            dst[i] = owned[i].as<float>();
+            dst[i] = assembled + at;
+            at += align_up(headers[i].channels() * headers[i].samples_per_channel(), 64);
         }
     }
     auto s = ctx.stream();
@@ -716,10 +723,14 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
     {
         for (std::size_t i = 0; i < n; ++i)
         {
-            out[i].samples.resize(headers[i].channels() * headers[i].samples_per_channel());
-            cuda_ok(cudaMemcpyAsync(out[i].samples.data(), dst[i], out[i].samples.size() * 4,
-                                    cudaMemcpyDeviceToHost, s),
-                    "D2H");
+            const auto count = headers[i].channels() * headers[i].samples_per_channel();
+            float* target = host_out ? host_out[i] : nullptr;
+            if (!target)
+            {
+                out[i].samples.resize(count);
+                target = out[i].samples.data();
+            }
+            cuda_ok(cudaMemcpyAsync(target, dst[i], count * 4, cudaMemcpyDeviceToHost, s), "D2H");
         }
         cuda_ok(cudaStreamSynchronize(s), "decode");
         profile.mark("pcm download");

@@ -50,8 +50,11 @@ std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
                                 std::vector<std::vector<std::uint32_t>>* symbol_bits = nullptr);
 // With device_out, recording i is written to device_out[i] (interleaved,
 // channels x padded samples floats) and DecodedAudio::samples stays empty.
+// With host_out, recording i is copied from the device straight into the
+// caller's host buffer host_out[i] (channels x samples floats) and
+// DecodedAudio::samples stays empty.
 std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>& streams,
-                                       float* const* device_out = nullptr);
+                                       float* const* device_out = nullptr, float* const* host_out = nullptr);
 
 // pack_normal (src/format/entropy.cpp:57-123) for known tokens with the GPU
 // predictor: header.method must be 1; returns the framed normal stream.

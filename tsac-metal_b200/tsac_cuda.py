@@ -14,6 +14,7 @@ import os
 import pathlib
 import shutil
 import threading
+import weakref
 
 import numpy as np
 
@@ -166,6 +167,20 @@ class PcmAudio:
     channels: int
 
 
+def _adopt(ptr, count, dtype):
+    """A numpy view of a library-allocated buffer that frees it (tsac_cuda_free)
+    when the last array using it is collected: large results (decoded PCM) are
+    not copied a second time."""
+    lib = library()
+    if not count:
+        lib.tsac_cuda_free(ptr)
+        return np.zeros(0, dtype)
+    address = ptr.value if isinstance(ptr, ctypes.c_void_p) else int(ptr)
+    storage = (np.ctypeslib.as_ctypes_type(dtype) * count).from_address(address)
+    weakref.finalize(storage, lib.tsac_cuda_free, ctypes.c_void_p(address))
+    return np.frombuffer(storage, dtype)
+
+
 def _take(ptr, count, dtype):
     """Copy a library-allocated buffer into numpy and free it."""
     lib = library()
@@ -266,7 +281,7 @@ class CudaAnalyzer:
         check(library().tsac_cuda_decode(self._ctx, stream, ctypes.c_size_t(len(stream)),
                                          ctypes.byref(out), ctypes.byref(samples),
                                          ctypes.byref(channels)))
-        data = _take(out, samples.value, np.float32)
+        data = _adopt(out, samples.value, np.float32)
         return PcmAudio(data.reshape(-1, channels.value), channels.value)
 
     def encode_batch(self, pcms, options: EncodeOptions | None = None):
@@ -292,7 +307,7 @@ class CudaAnalyzer:
         chans = (ctypes.c_uint * n)()
         check(library().tsac_cuda_decode_batch(self._ctx, ctypes.c_size_t(n), ptrs, sizes, outs,
                                                samples, chans))
-        return [PcmAudio(_take(ctypes.c_void_p(outs[i]), samples[i], np.float32)
+        return [PcmAudio(_adopt(ctypes.c_void_p(outs[i]), samples[i], np.float32)
                          .reshape(-1, chans[i]), chans[i]) for i in range(n)]
 
     # ---- pipeline stages (parity tests) ---------------------------------
