@@ -8,6 +8,7 @@
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <exception>
 #include <functional>
 #include <future>
@@ -119,6 +120,76 @@ void check_word(cudaStream_t s, unsigned* word, const char* message)
     }
 }
 
+// Host PCM -> device in 32 MiB pieces through the context's pinned double
+// buffer: the host workers copy piece p into one half while piece p - 1 goes
+// by DMA from the other (pageable copies ran at about 8 GB/s).  Returns once
+// every piece has reached the device.
+void upload_pcm(Context& ctx, const std::vector<const float*>& src, const std::vector<float*>& dst,
+                const std::vector<std::size_t>& count)
+{
+    constexpr std::size_t piece = std::size_t{8} << 20; // floats (32 MiB)
+    auto s = ctx.stream();
+    struct Piece
+    {
+        std::size_t job, offset, count;
+    };
+    std::vector<Piece> pieces;
+    std::size_t total = 0;
+    for (std::size_t j = 0; j < src.size(); ++j)
+    {
+        total += count[j];
+        for (std::size_t at = 0; at < count[j]; at += piece)
+            pieces.push_back({j, at, std::min(piece, count[j] - at)});
+    }
+    if (pieces.empty())
+        return;
+    if (total < piece / 4)
+    {
+        for (std::size_t j = 0; j < src.size(); ++j)
+            if (count[j])
+                cuda_ok(cudaMemcpyAsync(dst[j], src[j], count[j] * 4, cudaMemcpyHostToDevice, s), "H2D");
+        cuda_ok(cudaStreamSynchronize(s), "PCM upload");
+        return;
+    }
+    float* staging = ctx.pinned_staging(piece);
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    for (auto& e : done)
+        cuda_ok(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+    const std::size_t workers = host_workers(ctx);
+    try
+    {
+        for (std::size_t p = 0; p < pieces.size(); ++p)
+        {
+            // This half last carried piece p - 2: its DMA must be finished.
+            if (p >= 2)
+                cuda_ok(cudaEventSynchronize(done[p & 1]), "H2D");
+            const auto& q = pieces[p];
+            const float* from = src[q.job] + q.offset;
+            float* half = staging + (p & 1) * piece;
+            const std::size_t slice = (q.count + workers - 1) / workers;
+            parallel_for(workers, workers,
+                         [&](std::size_t w)
+                         {
+                             const std::size_t b = w * slice;
+                             if (b < q.count)
+                                 std::memcpy(half + b, from + b, std::min(slice, q.count - b) * sizeof(float));
+                         });
+            cuda_ok(cudaMemcpyAsync(dst[q.job] + q.offset, half, q.count * 4, cudaMemcpyHostToDevice, s), "H2D");
+            cuda_ok(cudaEventRecord(done[p & 1], s), "cudaEventRecord");
+        }
+        cuda_ok(cudaStreamSynchronize(s), "PCM upload");
+    }
+    catch (...)
+    {
+        cudaStreamSynchronize(s);
+        for (auto e : done)
+            cudaEventDestroy(e);
+        throw;
+    }
+    for (auto e : done)
+        cudaEventDestroy(e);
+}
+
 // padded_audio on the device for every recording of one variant, laid end to
 // end: recording r, group g starts at PCM row base[r] + g * padded_samples.
 float* padded_device(Context& ctx, const std::vector<PcmInput>& pcm,
@@ -136,24 +207,29 @@ float* padded_device(Context& ctx, const std::vector<PcmInput>& pcm,
     const unsigned mc = headers.empty() ? 1 : headers[0].model_channels;
     float* out = ctx.workspace().get<float>("pcm_padded", static_cast<std::size_t>(rows) * mc + 1);
     // Host views are copied into one staging area (interleaved, contiguous),
-    // all copies queued back to back, then regrouped on the device.
+    // then regrouped on the device.
     std::size_t staged_floats = 0;
     for (const auto& p : pcm)
         if (!p.device)
             staged_floats += p.samples * p.channels;
     float* staging = staged_floats ? ctx.workspace().get<float>("pcm_staging", staged_floats) : nullptr;
     std::vector<std::vector<float>> packed(pcm.size());
+    std::vector<const float*> up_src;
+    std::vector<float*> up_dst;
+    std::vector<std::size_t> up_count;
+    std::vector<const float*> src(pcm.size());
+    std::vector<long long> cstride(pcm.size()), sstride(pcm.size());
     std::size_t at = 0;
     for (std::size_t r = 0; r < pcm.size(); ++r)
     {
         const auto& p = pcm[r];
-        const auto& h = headers[r];
-        const float* src = p.data;
-        long long cs = p.channel_stride, ss = p.sample_stride;
+        src[r] = p.data;
+        cstride[r] = p.channel_stride;
+        sstride[r] = p.sample_stride;
         if (!p.device && p.samples)
         {
             const float* host = p.data;
-            if (!(cs == 1 && ss == static_cast<long long>(p.channels)))
+            if (!(p.channel_stride == 1 && p.sample_stride == static_cast<long long>(p.channels)))
             {
                 packed[r].resize(p.samples * p.channels);
                 for (std::size_t f = 0; f < p.samples; ++f)
@@ -163,22 +239,22 @@ float* padded_device(Context& ctx, const std::vector<PcmInput>& pcm,
                                    static_cast<std::ptrdiff_t>(f) * p.sample_stride];
                 host = packed[r].data();
             }
-            cuda_ok(cudaMemcpyAsync(staging + at, host, p.samples * p.channels * 4,
-                                    cudaMemcpyHostToDevice, s),
-                    "H2D");
-            src = staging + at;
+            up_src.push_back(host);
+            up_dst.push_back(staging + at);
+            up_count.push_back(p.samples * p.channels);
+            src[r] = staging + at;
             at += p.samples * p.channels;
-            cs = 1;
-            ss = static_cast<long long>(p.channels);
+            cstride[r] = 1;
+            sstride[r] = static_cast<long long>(p.channels);
         }
-        dev::pcm_regroup(src, static_cast<long long>(p.samples), cs, ss, h.groups, mc,
-                         static_cast<long long>(h.samples_per_channel()),
-                         out + base[r] * mc, error_word, s);
     }
-    if (staged_floats)
+    upload_pcm(ctx, up_src, up_dst, up_count);
+    for (std::size_t r = 0; r < pcm.size(); ++r)
     {
-        // Host copies of strided views must outlive their asynchronous upload.
-        cuda_ok(cudaStreamSynchronize(s), "PCM upload");
+        const auto& p = pcm[r];
+        const auto& h = headers[r];
+        dev::pcm_regroup(src[r], static_cast<long long>(p.samples), cstride[r], sstride[r], h.groups, mc,
+                         static_cast<long long>(h.samples_per_channel()), out + base[r] * mc, error_word, s);
     }
     return out;
 }
@@ -557,6 +633,86 @@ std::vector<Bytes> encode_batch(Context& ctx, const std::vector<PcmInput>& pcm,
     return out;
 }
 
+namespace
+{
+// Decoded PCM, device -> host.  Pageable copies into fresh host buffers run
+// on one driver thread that also takes every first-touch page fault (about
+// 2 GB/s measured); here 32 MiB pieces go by DMA into one half of a pinned
+// double buffer while the host workers move the previous piece into place.
+void download_pcm(Context& ctx, const std::vector<Header>& headers, const std::vector<float*>& src,
+                  const std::vector<float*>& dst)
+{
+    constexpr std::size_t piece = std::size_t{8} << 20; // floats (32 MiB)
+    auto s = ctx.stream();
+    struct Piece
+    {
+        std::size_t recording, offset, count;
+    };
+    std::vector<Piece> pieces;
+    std::size_t total = 0;
+    for (std::size_t i = 0; i < headers.size(); ++i)
+    {
+        const auto count = headers[i].channels() * headers[i].samples_per_channel();
+        total += count;
+        for (std::size_t at = 0; at < count; at += piece)
+            pieces.push_back({i, at, std::min(piece, count - at)});
+    }
+    if (total < piece / 4)
+    {
+        for (std::size_t i = 0; i < headers.size(); ++i)
+            cuda_ok(cudaMemcpyAsync(dst[i], src[i], headers[i].channels() * headers[i].samples_per_channel() * 4,
+                                    cudaMemcpyDeviceToHost, s),
+                    "D2H");
+        cuda_ok(cudaStreamSynchronize(s), "decode");
+        return;
+    }
+    float* staging = ctx.pinned_staging(piece);
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    for (auto& e : done)
+        cuda_ok(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+    const auto issue = [&](std::size_t p)
+    {
+        const auto& q = pieces[p];
+        cuda_ok(cudaMemcpyAsync(staging + (p & 1) * piece, src[q.recording] + q.offset, q.count * 4,
+                                cudaMemcpyDeviceToHost, s),
+                "D2H");
+        cuda_ok(cudaEventRecord(done[p & 1], s), "cudaEventRecord");
+    };
+    const std::size_t workers = host_workers(ctx);
+    try
+    {
+        issue(0);
+        for (std::size_t p = 0; p < pieces.size(); ++p)
+        {
+            // The other half held piece p - 1, already moved into place.
+            if (p + 1 < pieces.size())
+                issue(p + 1);
+            cuda_ok(cudaEventSynchronize(done[p & 1]), "D2H");
+            const auto& q = pieces[p];
+            const float* from = staging + (p & 1) * piece;
+            float* to = dst[q.recording] + q.offset;
+            const std::size_t slice = (q.count + workers - 1) / workers;
+            parallel_for(workers, workers,
+                         [&](std::size_t w)
+                         {
+                             const std::size_t b = w * slice;
+                             if (b < q.count)
+                                 std::memcpy(to + b, from + b, std::min(slice, q.count - b) * sizeof(float));
+                         });
+        }
+    }
+    catch (...)
+    {
+        cudaStreamSynchronize(s);
+        for (auto e : done)
+            cudaEventDestroy(e);
+        throw;
+    }
+    for (auto e : done)
+        cudaEventDestroy(e);
+}
+} // namespace
+
 std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>& streams,
                                        float* const* device_out, float* const* host_out)
 {
@@ -721,18 +877,17 @@ std::vector<DecodedAudio> decode_batch(Context& ctx, const std::vector<ByteView>
     }
     if (!device_out)
     {
+        std::vector<float*> targets(n);
         for (std::size_t i = 0; i < n; ++i)
         {
-            const auto count = headers[i].channels() * headers[i].samples_per_channel();
-            float* target = host_out ? host_out[i] : nullptr;
-            if (!target)
+            targets[i] = host_out ? host_out[i] : nullptr;
+            if (!targets[i])
             {
-                out[i].samples.resize(count);
-                target = out[i].samples.data();
+                out[i].samples.resize(headers[i].channels() * headers[i].samples_per_channel());
+                targets[i] = out[i].samples.data();
             }
-            cuda_ok(cudaMemcpyAsync(target, dst[i], count * 4, cudaMemcpyDeviceToHost, s), "D2H");
         }
-        cuda_ok(cudaStreamSynchronize(s), "decode");
+        download_pcm(ctx, headers, dst, targets);
         profile.mark("pcm download");
     }
     return out;

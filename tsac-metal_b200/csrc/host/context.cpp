@@ -45,6 +45,8 @@ Context::~Context()
         cudaStreamSynchronize(stream_);
         cudaStreamDestroy(stream_);
     }
+    if (pinned_)
+        cudaFreeHost(pinned_);
 }
 
 void Context::bind() const
@@ -93,6 +95,25 @@ void Context::set_exact_synthesis(bool exact)
     for (auto& e : synthesis_)
         if (e)
             e->set_exact_synthesis(exact);
+}
+
+float* Context::pinned_staging(std::size_t floats_per_half)
+{
+    if (pinned_floats_ < 2 * floats_per_half)
+    {
+        if (pinned_)
+        {
+            cuda_ok(cudaStreamSynchronize(stream_), "pinned staging");
+            cudaFreeHost(pinned_);
+            pinned_ = nullptr;
+            pinned_floats_ = 0;
+        }
+        void* p = nullptr;
+        cuda_ok(cudaMallocHost(&p, 2 * floats_per_half * sizeof(float)), "cudaMallocHost");
+        pinned_ = static_cast<float*>(p);
+        pinned_floats_ = 2 * floats_per_half;
+    }
+    return pinned_;
 }
 
 void Context::set_host_threads(unsigned threads)

@@ -83,6 +83,9 @@ public:
     {
         return workspace_;
     }
+    // Pinned host staging for large device -> host results: two halves of
+    // `floats_per_half` floats each, allocated on first use and kept.
+    float* pinned_staging(std::size_t floats_per_half);
 
 private:
     Package package_;
@@ -98,5 +101,7 @@ private:
     bool exact_synthesis_ = false;
     std::unique_ptr<RvqEngine> rvq_[2];
     Workspace workspace_;
+    float* pinned_ = nullptr;
+    std::size_t pinned_floats_ = 0;
 };
 } // namespace tsacb
