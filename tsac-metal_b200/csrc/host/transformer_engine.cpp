@@ -171,7 +171,7 @@ void TransformerEngine::run_stack(Workspace& ws_, bool temporal, int rows, std::
                                   const void* meta_device,
                                   int max_time, std::uint16_t* cache_k, std::uint16_t* cache_v,
                                   std::size_t cache_layer_stride, std::uint16_t* final_out,
-                                  std::int8_t* final_q, float* final_s)
+                                  std::int8_t* final_q, float* final_s, bool sequence_rows)
 {
     const auto* meta = static_cast<const RowMeta*>(meta_device);
     const int layers = temporal ? 12 : 3;
@@ -198,7 +198,7 @@ void TransformerEngine::run_stack(Workspace& ws_, bool temporal, int rows, std::
         {
             KernelTimer::Scope timing("attention", stream_, 0.0);
             quantized = dev::attention(query, meta, ck, cv, rows, max_time, partials, att, stream_, xq, xs,
-                                       error_word());
+                                       error_word(), sequence_rows);
         }
         if (quantized)
             run_linear(projection_index(temporal, l, 1), xq, xs, rows, h, h, false);
@@ -312,7 +312,7 @@ void TransformerEngine::predict_known(const Header& header, std::span<const std:
     auto* tck = ws_.get<std::uint16_t>("tck", tstride * 12);
     auto* tcv = ws_.get<std::uint16_t>("tcv", tstride * 12);
     auto* cond = ws_.get<std::uint16_t>("cond", static_cast<std::size_t>(trows) * 512);
-    run_stack(ws_, true, trows, th, d_tmeta, max_time, tck, tcv, tstride, cond, nullptr, nullptr);
+    run_stack(ws_, true, trows, th, d_tmeta, max_time, tck, tcv, tstride, cond, nullptr, nullptr, true);
 
     // ---- codebook stack, chunked by (frame, group) sequences of Q rows
     // (2048 sequences per launch group bound the per-chunk scratch).
@@ -750,7 +750,7 @@ void TransformerEngine::enqueue_decode_step(const int* row_lane, const int* row_
         run_linear_bf16(60, emb, trows, th, nullptr, false, eq, es);
         auto* tout = ws.get<std::uint16_t>("tout", static_cast<std::size_t>(trows) * 512);
         run_stack(ws, true, trows, th, r.temporal_meta, context, st.tck, st.tcv, st.tstride, tout, nullptr,
-                  nullptr);
+                  nullptr, per_lane > 1);
         // Conditioning: each active lane's last temporal row.
         dev::scatter_rows(tout, r.cond_source, r.cond_lane, n, st.cond, s);
     }

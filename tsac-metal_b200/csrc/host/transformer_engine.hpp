@@ -93,7 +93,8 @@ private:
     void run_stack(Workspace& ws, bool temporal, int rows, std::uint16_t* h,
                    const void* meta_device, int max_time, std::uint16_t* cache_k,
                    std::uint16_t* cache_v, std::size_t cache_layer_stride,
-                   std::uint16_t* final_out, std::int8_t* final_q, float* final_s);
+                   std::uint16_t* final_out, std::int8_t* final_q, float* final_s,
+                   bool sequence_rows = false);
 
     std::shared_ptr<const DeviceTransformer> model_;
     cudaStream_t stream_;

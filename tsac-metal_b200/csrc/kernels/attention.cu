@@ -69,6 +69,58 @@ __global__ void __launch_bounds__(128)
     }
 }
 
+// Prefill rows: consecutive rows of one sequence read the same key blocks.
+// One CTA per (TILE consecutive rows, head, 64-key block) stages the block once
+// for the rows that share a sequence base (a row of another base restages)
+// and runs each row's block arithmetic (attention_block_compute, unchanged)
+// in turn, writing the same partials as attention_block_kernel<false>.
+constexpr int TILE = 8;
+
+__global__ void __launch_bounds__(128)
+    attention_tile_kernel(const std::uint16_t* __restrict__ query, const RowMeta* __restrict__ meta,
+                          const std::uint16_t* __restrict__ cache_k, const std::uint16_t* __restrict__ cache_v,
+                          int rows, int max_blocks, float* __restrict__ partials)
+{
+    pdl_prologue();
+    __shared__ AttentionShared sh;
+    const int block = blockIdx.y;
+    const int group = blockIdx.x / HEADS, head = blockIdx.x % HEADS;
+    const int r0 = group * TILE, r1 = r0 + TILE < rows ? r0 + TILE : rows;
+    const int start = block * BLOCK;
+    const int t = threadIdx.x;
+    int staged_base = -1, staged_count = 0;
+    for (int row = r0; row < r1; ++row)
+    {
+        const RowMeta m = meta[row];
+        if (start >= m.time)
+            continue;
+        const int count = m.time - start < BLOCK ? m.time - start : BLOCK;
+        if (m.base != staged_base || count > staged_count)
+        {
+            // The most keys any remaining row of this base reads from the block.
+            int need = count;
+            for (int k = row + 1; k < r1; ++k)
+            {
+                const RowMeta n = meta[k];
+                if (n.base == m.base && n.time > start)
+                    need = max(need, n.time - start < BLOCK ? n.time - start : BLOCK);
+            }
+            attention_stage(m.base, head, cache_k, cache_v, start, need, sh, t);
+            staged_base = m.base;
+            staged_count = need;
+        }
+        const AttentionBlock b = attention_block_compute(query + static_cast<size_t>(row) * WIDTH + head * HW, m,
+                                                         count, sh, 0, t);
+        float* out = partials + (static_cast<size_t>(row * HEADS + head) * max_blocks + block) * PSTRIDE;
+        out[2 + t] = b.sum;
+        if (t == 0)
+        {
+            out[0] = b.maximum;
+            out[1] = b.block_sum;
+        }
+    }
+}
+
 // One-block histories with the output BF8L-quantized for the next
 // projection: one CTA per (row, head pair), i.e. per 256-value quantization
 // block.  Two 128-thread groups (named barriers 1 and 2) each run one head's
@@ -160,7 +212,7 @@ size_t attention_partials_bytes(int rows, int max_time)
 bool attention(const std::uint16_t* query, const RowMeta* meta, const std::uint16_t* cache_k,
                const std::uint16_t* cache_v, int rows, int max_time, float* partials,
                std::uint16_t* out, cudaStream_t stream, std::int8_t* yq, float* yscale,
-               unsigned* error_word)
+               unsigned* error_word, bool sequence_rows)
 {
     if (rows <= 0)
         return false;
@@ -191,8 +243,12 @@ bool attention(const std::uint16_t* query, const RowMeta* meta, const std::uint1
         note_launch();
         return false;
     }
-    launch_pdl(attention_block_kernel<false>, dim3(rows * HEADS, blocks), dim3(128), 0, stream, query,
-               meta, cache_k, cache_v, blocks, partials, static_cast<std::uint16_t*>(nullptr));
+    if (sequence_rows)
+        launch_pdl(attention_tile_kernel, dim3((rows + TILE - 1) / TILE * HEADS, blocks), dim3(128), 0, stream,
+                   query, meta, cache_k, cache_v, rows, blocks, partials);
+    else
+        launch_pdl(attention_block_kernel<false>, dim3(rows * HEADS, blocks), dim3(128), 0, stream, query,
+                   meta, cache_k, cache_v, blocks, partials, static_cast<std::uint16_t*>(nullptr));
     note_launch();
     launch_pdl(attention_combine_kernel, dim3(rows * HEADS), dim3(128), 0, stream, meta,
                static_cast<const float*>(partials), blocks, out);

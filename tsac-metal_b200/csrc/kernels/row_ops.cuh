@@ -14,6 +14,7 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "kernels/async_copy.cuh"
 #include "kernels/numeric.cuh"
 #include "kernels/row_meta.hpp"
 
@@ -248,26 +249,34 @@ struct AttentionBlock
     float maximum, block_sum, sum; // sum: this thread's coordinate
 };
 
-// One 64-key block [start, start + count) of one (row, head) by a group of
-// 128 threads (thread t = coordinate t): staged K/V, serial score chains,
-// block max, original_exp weights, pair-tree block sum, serial value sums
-// (bf16-rounded when m.round).  `query` is the head's 128 bf16 values.
-// `Shared` is AttentionShared or a smaller struct with the same members for
-// blocks of at most as many keys as its arrays hold.
+// Stages keys and values [start, start + count) of `head` for the sequence
+// whose position 0 is cache slot `base` (asynchronous copies, all in flight,
+// then this thread's wait; the group's next barrier publishes them).
 template <class Shared>
-__device__ __forceinline__ AttentionBlock attention_block_core(const std::uint16_t* query, const RowMeta& m,
-                                                               int head, const std::uint16_t* cache_k,
-                                                               const std::uint16_t* cache_v, int start,
-                                                               int count, Shared& sh, int bar, int t)
+__device__ __forceinline__ void attention_stage(int base, int head, const std::uint16_t* cache_k,
+                                                const std::uint16_t* cache_v, int start, int count, Shared& sh,
+                                                int t)
 {
-    sh.q[t] = from_bf16(query[t]);
     for (int i = t; i < count * 64; i += 128)
     {
         const int r = i >> 6, w = i & 63;
-        const size_t slot = static_cast<size_t>(m.base + start + r) * ATT_WIDTH + head * ATT_HW;
-        sh.ks[r][w] = reinterpret_cast<const unsigned*>(cache_k + slot)[w];
-        sh.vs[r][w] = reinterpret_cast<const unsigned*>(cache_v + slot)[w];
+        const size_t slot = static_cast<size_t>(base + start + r) * ATT_WIDTH + head * ATT_HW;
+        cp_async_4(&sh.ks[r][w], reinterpret_cast<const unsigned*>(cache_k + slot) + w);
+        cp_async_4(&sh.vs[r][w], reinterpret_cast<const unsigned*>(cache_v + slot) + w);
     }
+    cp_async_wait_all();
+}
+
+// The block arithmetic of one (row, head) over staged keys and values: serial
+// score chains, block max, original_exp weights, pair-tree block sum, serial
+// value sums (bf16-rounded when m.round), by a group of 128 threads (thread
+// t = coordinate t).  `query` is the head's 128 bf16 values.  The staged
+// block may hold more keys than `count`; only the first `count` are used.
+template <class Shared>
+__device__ __forceinline__ AttentionBlock attention_block_compute(const std::uint16_t* query, const RowMeta& m,
+                                                                  int count, Shared& sh, int bar, int t)
+{
+    sh.q[t] = from_bf16(query[t]);
     group_sync(bar);
     AttArgMax best{-INFINITY, ATT_BLOCK};
     if (t < count)
@@ -326,6 +335,19 @@ __device__ __forceinline__ AttentionBlock attention_block_core(const std::uint16
         sum = from_bf16(to_bf16(sum));
     group_sync(bar);
     return AttentionBlock{maximum, sh.block_sum, sum};
+}
+
+// One 64-key block [start, start + count) of one (row, head): staging, then
+// attention_block_compute.  `Shared` is AttentionShared or a smaller struct
+// with the same members for blocks of at most as many keys as its arrays hold.
+template <class Shared>
+__device__ __forceinline__ AttentionBlock attention_block_core(const std::uint16_t* query, const RowMeta& m,
+                                                               int head, const std::uint16_t* cache_k,
+                                                               const std::uint16_t* cache_v, int start,
+                                                               int count, Shared& sh, int bar, int t)
+{
+    attention_stage(m.base, head, cache_k, cache_v, start, count, sh, t);
+    return attention_block_compute(query, m, count, sh, bar, t);
 }
 
 // The streaming merge's first (and, for one block, only) step from

@@ -38,11 +38,13 @@ void rotary_scatter(const std::uint16_t* qkv, const RowMeta* meta, const std::ui
 // output goes BF8L-quantized to yq [rows][512] and yscale [rows][2] instead
 // of bf16 to `out` (qlinear_quantize's result; nonfinite values flagged in
 // error_word), and the call returns true; otherwise it writes `out` and
-// returns false.
+// returns false.  sequence_rows: rows come in runs of consecutive positions
+// of one sequence (a causal prefill, a context replay), so several rows can
+// share each staged key block.
 bool attention(const std::uint16_t* query, const RowMeta* meta, const std::uint16_t* cache_k,
                const std::uint16_t* cache_v, int rows, int max_time, float* partials,
                std::uint16_t* out, cudaStream_t stream, std::int8_t* yq = nullptr,
-               float* yscale = nullptr, unsigned* error_word = nullptr);
+               float* yscale = nullptr, unsigned* error_word = nullptr, bool sequence_rows = false);
 size_t attention_partials_bytes(int rows, int max_time);
 
 // out[r] = bf16(src[source_row[r]] + positions[book[r]]) (512 wide).
