@@ -158,7 +158,10 @@ def test_conv1d_tensor_cores_residual_and_snake():
     act = _conv_tensor(x, w, b, cin, cout, 7, 1, 3, 1, 0, residual=res, alpha=a)
     expected = np.zeros_like(raw)
     oracle().oracle_snake(ptr(np.ascontiguousarray(raw)), cout, 300, ptr(a), ptr(expected))
-    assert np.array_equal(act.view(np.uint32), expected.view(np.uint32))
+    # The tensor path multiplies sin^2 by a precomputed 1 / (alpha + eps)
+    # instead of dividing: one extra rounding of a quotient <= 2 (alpha >= 0.5),
+    # then the same final add.
+    assert (np.abs(act.astype(np.float64) - expected) <= 2.0 ** -21 * (1.0 + np.abs(expected))).all()
 
 
 def test_conv1d_residual_epilogue():

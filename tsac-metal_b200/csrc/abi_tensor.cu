@@ -4,6 +4,7 @@
 // this entry point builds that layout for one sequence around the caller's
 // tensors (it allocates and frees device memory, so it is not for hot loops).
 #include "cuda_util.cuh"
+#include "host/snake_inverse.hpp"
 #include "host/tf32_split.hpp"
 #include "kernels/tc_conv.cuh"
 
@@ -130,8 +131,19 @@ int tsac_cuda_conv1d_tensor(const float* x, size_t frames, const float* weights,
                 cuda_check(cudaMemcpyAsync(res.as<float>() + first, residual, count * 4,
                                            cudaMemcpyDeviceToDevice, s),
                            "D2D");
+            DeviceBlock d_inverse(alpha ? cout * 4 : 0);
+            if (alpha)
+            {
+                std::vector<float> a(cout);
+                cuda_check(cudaMemcpyAsync(a.data(), alpha, cout * 4, cudaMemcpyDeviceToHost, s), "D2H");
+                cuda_check(cudaStreamSynchronize(s), "alpha");
+                const auto inverse = tsacb::snake_inverse(a);
+                cuda_check(cudaMemcpyAsync(d_inverse.p, inverse.data(), cout * 4, cudaMemcpyHostToDevice, s),
+                           "H2D");
+            }
             const dev::TcConvEpilogue e{bias, residual ? res.as<float>() : nullptr,
                                         alpha ? nullptr : out.as<float>(), alpha,
+                                        alpha ? d_inverse.as<float>() : nullptr,
                                         alpha ? out.as<float>() : nullptr, nullptr,
                                         d_valid.as<unsigned char>(), error_word};
             const dev::TcConvOperands op{xhi.as<float>(), xlo.as<float>(), d_whi.as<float>(),

@@ -1,6 +1,7 @@
 #include "dac_engine.hpp"
 
 #include "kernel_timer.hpp"
+#include "snake_inverse.hpp"
 #include "tf32_split.hpp"
 #include "kernels/error_bits.hpp"
 #include "kernels/tc_conv.cuh"
@@ -122,6 +123,10 @@ DacEngine::DacEngine(const PreparedDac& dac, cudaStream_t stream)
     {
         alphas_.push_back(upload(a, stream));
         alpha_width_.push_back(static_cast<int>(a.size()));
+        // The tensor-core epilogue's Snake (a stated tolerance, not
+        // bit-exactness) multiplies by these instead of dividing.
+        if (synthesis_)
+            alpha_inverses_.push_back(upload(snake_inverse(a), stream));
     }
     cuda_ok(cudaMemsetAsync(error_.as<void>(), 0, sizeof(unsigned), stream), "memset");
     cuda_ok(cudaStreamSynchronize(stream), "DAC weight upload");
@@ -307,6 +312,8 @@ void DacEngine::tc_conv(int index, const float* x_hi, const float* x_lo, long lo
     g.out_scale = in_scale * c.tc_phases;
     const dev::TcConvEpilogue e{c.bias.as<float>(), residual, raw,
                                 alpha >= 0 ? alphas_[static_cast<std::size_t>(alpha)].as<float>() : nullptr,
+                                alpha >= 0 ? alpha_inverses_[static_cast<std::size_t>(alpha)].as<float>()
+                                           : nullptr,
                                 hi, lo, valid, error_word()};
     const dev::TcConvOperands op{x_hi, x_lo, c.tc_hi.as<float>(), c.tc_lo.as<float>()};
     // Useful MACs: valid output rows x cout x cin x taps per output.

@@ -79,6 +79,7 @@ private:
     unsigned channels_;
     std::vector<DeviceConv> convs_;
     std::vector<DeviceBuffer> alphas_;
+    std::vector<DeviceBuffer> alpha_inverses_; // synthesis: 1 / (alpha + eps) per Snake
     std::vector<int> alpha_width_;
     cudaStream_t stream_;
     Workspace ws_;

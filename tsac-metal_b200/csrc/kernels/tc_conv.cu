@@ -110,6 +110,14 @@ __device__ __forceinline__ void tf32_split(float x, float& hi, float& lo)
     lo = tf32_round(__fsub_rn(x, hi));
 }
 
+// Snake with the division by (alpha + eps) as a product with its precomputed
+// reciprocal: within one rounding of snake_value's quotient, inside the tensor
+// path's stated tolerance, and a short fixed sequence instead of a divide.
+__device__ __forceinline__ float snake_scaled(float v, float alpha, float inverse)
+{
+    return __fadd_rn(v, __fmul_rn(sine_squared(__fmul_rn(alpha, v)), inverse));
+}
+
 struct TileCoord
 {
     int phase;
@@ -453,7 +461,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             r = __fadd_rn(res[j], r);
                     }
                     raw[j] = r;
-                    act[j] = (valid && e.alpha) ? snake_value(r, __ldg(e.alpha + col + j)) : r;
+                    act[j] = (valid && e.alpha)
+                                 ? snake_scaled(r, __ldg(e.alpha + col + j), __ldg(e.alpha_inverse + col + j))
+                                 : r;
                     finite = finite && isfinite(act[j]) && isfinite(r);
                 }
                 if (e.raw)

@@ -48,6 +48,7 @@ struct TcConvEpilogue
     const float* residual;      // [out_rows][cout] or null (may alias raw)
     float* raw;                 // [out_rows][cout] or null: bias + sum (+ residual)
     const float* alpha;         // next Snake's alpha [cout], or null (no Snake)
+    const float* alpha_inverse; // 1 / (alpha + eps) [cout] (with alpha)
     float* hi;                  // [out_rows][cout] or null: Snake(raw) head (or full value)
     float* lo;                  // [out_rows][cout] or null: Snake(raw) tail; null = no split
     const unsigned char* valid; // [padded latent rows]
