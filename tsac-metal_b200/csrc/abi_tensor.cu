@@ -131,6 +131,11 @@ int tsac_cuda_conv1d_tensor(const float* x, size_t frames, const float* weights,
                 cuda_check(cudaMemcpyAsync(res.as<float>() + first, residual, count * 4,
                                            cudaMemcpyDeviceToDevice, s),
                            "D2D");
+            // The kernel reads bias / alpha in 16-byte loads: aligned copies.
+            DeviceBlock d_bias(cout * 4), d_alpha(alpha ? cout * 4 : 0);
+            cuda_check(cudaMemcpyAsync(d_bias.p, bias, cout * 4, cudaMemcpyDeviceToDevice, s), "D2D");
+            if (alpha)
+                cuda_check(cudaMemcpyAsync(d_alpha.p, alpha, cout * 4, cudaMemcpyDeviceToDevice, s), "D2D");
             DeviceBlock d_inverse(alpha ? cout * 4 : 0);
             if (alpha)
             {
@@ -141,8 +146,8 @@ int tsac_cuda_conv1d_tensor(const float* x, size_t frames, const float* weights,
                 cuda_check(cudaMemcpyAsync(d_inverse.p, inverse.data(), cout * 4, cudaMemcpyHostToDevice, s),
                            "H2D");
             }
-            const dev::TcConvEpilogue e{bias, residual ? res.as<float>() : nullptr,
-                                        alpha ? nullptr : out.as<float>(), alpha,
+            const dev::TcConvEpilogue e{d_bias.as<float>(), residual ? res.as<float>() : nullptr,
+                                        alpha ? nullptr : out.as<float>(), alpha ? d_alpha.as<float>() : nullptr,
                                         alpha ? d_inverse.as<float>() : nullptr,
                                         alpha ? out.as<float>() : nullptr, nullptr,
                                         d_valid.as<unsigned char>(), error_word};

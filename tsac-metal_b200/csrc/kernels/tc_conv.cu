@@ -450,21 +450,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     res[j + 2] = r4.z;
                     res[j + 3] = r4.w;
                 }
+                // Per-channel constants in 16-byte loads (16-byte aligned:
+                // col is a multiple of 16).
+                float bias[16], alpha[16], inverse[16];
+#pragma unroll
+                for (int j = 0; j < 16; j += 4)
+                {
+                    const float4 b4 = __ldg(reinterpret_cast<const float4*>(e.bias + col + j));
+                    bias[j] = b4.x;
+                    bias[j + 1] = b4.y;
+                    bias[j + 2] = b4.z;
+                    bias[j + 3] = b4.w;
+                    const float4 a4 = e.alpha ? __ldg(reinterpret_cast<const float4*>(e.alpha + col + j))
+                                              : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    alpha[j] = a4.x;
+                    alpha[j + 1] = a4.y;
+                    alpha[j + 2] = a4.z;
+                    alpha[j + 3] = a4.w;
+                    const float4 i4 = e.alpha ? __ldg(reinterpret_cast<const float4*>(e.alpha_inverse + col + j))
+                                              : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    inverse[j] = i4.x;
+                    inverse[j + 1] = i4.y;
+                    inverse[j + 2] = i4.z;
+                    inverse[j + 3] = i4.w;
+                }
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
                 {
                     float r = 0.0f;
                     if (valid)
                     {
-                        r = __fadd_rn(v[j], __ldg(e.bias + col + j));
+                        r = __fadd_rn(v[j], bias[j]);
                         if (e.residual)
                             r = __fadd_rn(res[j], r);
                     }
                     raw[j] = r;
-                    act[j] = (valid && e.alpha)
-                                 ? snake_scaled(r, __ldg(e.alpha + col + j), __ldg(e.alpha_inverse + col + j))
-                                 : r;
-                    finite = finite && isfinite(act[j]) && isfinite(r);
+                    act[j] = (valid && e.alpha) ? snake_scaled(r, alpha[j], inverse[j]) : r;
+                    // Snake adds a finite amount, so act is finite iff raw is.
+                    finite = finite && isfinite(act[j]);
                 }
                 if (e.raw)
                 {

@@ -44,7 +44,7 @@ struct TcConvGeometry
 
 struct TcConvEpilogue
 {
-    const float* bias;          // [cout]
+    const float* bias;          // [cout] (this and the alpha arrays 16-byte aligned)
     const float* residual;      // [out_rows][cout] or null (may alias raw)
     float* raw;                 // [out_rows][cout] or null: bias + sum (+ residual)
     const float* alpha;         // next Snake's alpha [cout], or null (no Snake)
