@@ -7,18 +7,16 @@
 
 namespace tsacb::dev
 {
-__device__ __forceinline__ float sine_squared(float phase)
+// sin^2 of `phase` given its quadrant (the nearest integer to phase * 2/pi)
+// and that quadrant's parity: two-constant reduction, then the odd or even
+// polynomial, squared.
+__device__ __forceinline__ float sine_squared_reduced(float phase, float quadrant, bool odd)
 {
-    const float reduced = __fmul_rn(phase, __uint_as_float(0x3f22f983u));
-    const float quadrant = rintf(reduced); // ties to even
-    const int q = (quadrant >= -2147483648.0f && quadrant < 2147483648.0f)
-                      ? static_cast<int>(quadrant)
-                      : INT_MIN;
     float x = __fmaf_rn(quadrant, __uint_as_float(0xbfc90000u), phase);
     x = __fmaf_rn(quadrant, __uint_as_float(0xb9fdaa22u), x);
     const float x2 = __fmul_rn(x, x);
     float value;
-    if ((q & 1) == 0)
+    if (!odd)
     {
         float p = __fmaf_rn(__uint_as_float(0xb94ca1f9u), x2, __uint_as_float(0x3c08839eu));
         p = __fmaf_rn(p, x2, __uint_as_float(0xbe2aaaa3u));
@@ -33,6 +31,16 @@ __device__ __forceinline__ float sine_squared(float phase)
         value = __fmaf_rn(p, x2, 1.0f);
     }
     return __fmul_rn(value, value);
+}
+
+__device__ __forceinline__ float sine_squared(float phase)
+{
+    const float reduced = __fmul_rn(phase, __uint_as_float(0x3f22f983u));
+    const float quadrant = rintf(reduced); // ties to even
+    const int q = (quadrant >= -2147483648.0f && quadrant < 2147483648.0f)
+                      ? static_cast<int>(quadrant)
+                      : INT_MIN;
+    return sine_squared_reduced(phase, quadrant, (q & 1) != 0);
 }
 
 // Snake: v + sin^2(alpha v) / (alpha + eps), each operation rounded.

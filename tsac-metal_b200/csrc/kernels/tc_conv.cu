@@ -97,9 +97,11 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b
 // value where rounding would overflow to infinity.
 __device__ __forceinline__ float tf32_round(float x)
 {
+    // Magnitudes from 0x7f7ff000 up would round to infinity (or are
+    // infinity / NaN already): those are truncated.
     const unsigned bits = __float_as_uint(x);
-    const float r = __uint_as_float((bits + 0x1000u) & 0xffffe000u);
-    return isinf(r) && !isinf(x) ? __uint_as_float(bits & 0xffffe000u) : r;
+    return __uint_as_float((bits & 0x7fffffffu) >= 0x7f7ff000u ? (bits & 0xffffe000u)
+                                                               : ((bits + 0x1000u) & 0xffffe000u));
 }
 
 // Head/tail split: hi = nearest TF32 of x, lo = nearest TF32 of the exact
@@ -115,7 +117,16 @@ __device__ __forceinline__ void tf32_split(float x, float& hi, float& lo)
 // path's stated tolerance, and a short fixed sequence instead of a divide.
 __device__ __forceinline__ float snake_scaled(float v, float alpha, float inverse)
 {
-    return __fadd_rn(v, __fmul_rn(sine_squared(__fmul_rn(alpha, v)), inverse));
+    // The quadrant is rounded, and its parity read, by adding 1.5 * 2^23: the
+    // same quadrant as rintf for |phase * 2/pi| < 2^22, without a float ->
+    // int conversion.  Beyond that the parity may select the other
+    // polynomial, whose square is a value in [0, 1] all the same, so the added
+    // term stays within [0, inverse].
+    const float phase = __fmul_rn(alpha, v);
+    const float shifted = __fadd_rn(__fmul_rn(phase, __uint_as_float(0x3f22f983u)), 12582912.0f);
+    const float quadrant = __fsub_rn(shifted, 12582912.0f);
+    const bool odd = (__float_as_uint(shifted) & 1u) != 0;
+    return __fadd_rn(v, __fmul_rn(sine_squared_reduced(phase, quadrant, odd), inverse));
 }
 
 struct TileCoord
