@@ -109,7 +109,9 @@ __device__ __forceinline__ float tf32_round(float x)
 __device__ __forceinline__ void tf32_split(float x, float& hi, float& lo)
 {
     hi = tf32_round(x);
-    lo = tf32_round(__fsub_rn(x, hi));
+    // The remainder is at most 2^-11 |x|, far from overflow: no guard needed
+    // (a nonfinite x leaves hi nonfinite, and the caller reports it).
+    lo = __uint_as_float((__float_as_uint(__fsub_rn(x, hi)) + 0x1000u) & 0xffffe000u);
 }
 
 // Snake with the division by (alpha + eps) as a product with its precomputed
