@@ -208,9 +208,12 @@ void DacEngine::conv(int index, const float* x, float* y, const float* residual,
                               stream_, 2.0 * macs);
     if (shape.cout < 16)
     {
+        long long narrow_tiles = 0;
+        for (int of : out_frames)
+            narrow_tiles += (of + 127) / 128;
         dev::conv1d_narrow(x, c.weights.as<float>(), c.bias.as<float>(), y, d_seq,
                            static_cast<int>(seqs.size()), shape,
-                           static_cast<long long>(out_off) * shape.cout, error_word(), stream_);
+                           static_cast<long long>(out_off) * shape.cout, error_word(), stream_, narrow_tiles);
         require(residual == nullptr && act == nullptr, "narrow convolution has no residual or Snake output");
         return;
     }

@@ -373,6 +373,87 @@ __global__ void conv1d_narrow_kernel(const float* __restrict__ x, const float* _
     y[static_cast<size_t>(seq.out_offset + f) * s.cout + o] = v;
 }
 
+// The same per-output chains from shared memory.  A CTA owns NARROW_TILE
+// consecutive output frames of one sequence: it stages the input rows they
+// read ([row][channel] in global memory, loaded coalesced) transposed to
+// [channel][row] (consecutive threads then read consecutive words) and the
+// weights, and each thread runs its frame's chains (taps ascending, channels
+// ascending, out-of-window taps skipped) exactly as conv1d_narrow_kernel.
+constexpr int NARROW_TILE = 128;
+
+__host__ __device__ constexpr int narrow_span(int stride, int kernel, int dilation)
+{
+    return (NARROW_TILE - 1) * stride + (kernel - 1) * dilation + 1;
+}
+
+__global__ void __launch_bounds__(NARROW_TILE)
+    conv1d_narrow_tile_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                              const float* __restrict__ bias, float* __restrict__ y,
+                              const Sequence* __restrict__ sequences, int sequence_count, ConvShape s,
+                              unsigned* error_word)
+{
+    extern __shared__ float narrow_smem[];
+    const int span = narrow_span(s.stride, s.kernel, s.dilation);
+    const int pitch = span + 1;
+    float* xs = narrow_smem;             // [cin][pitch]
+    float* ws = xs + s.cin * pitch;      // [tap][cin][cout]
+    const int t = threadIdx.x;
+    int tile = blockIdx.x, q = 0;
+    for (; q < sequence_count; ++q)
+    {
+        const int n = (sequences[q].out_frames + NARROW_TILE - 1) / NARROW_TILE;
+        if (tile < n)
+            break;
+        tile -= n;
+    }
+    if (q == sequence_count)
+        return; // uniform: the grid holds exactly the tiles
+    const Sequence seq = sequences[q];
+    const int f0 = tile * NARROW_TILE;
+    const int r0 = f0 * s.stride - s.padding; // input row of window row 0
+    const int weights = s.kernel * s.cin * s.cout;
+    for (int i = t; i < weights; i += NARROW_TILE)
+        ws[i] = __ldg(w + i);
+    // Window rows in memory order: element i is (row i / cin, channel i % cin).
+    int row = t / s.cin, c = t % s.cin;
+    for (int i = t; i < span * s.cin; i += NARROW_TILE)
+    {
+        const int src = r0 + row;
+        xs[c * pitch + row] =
+            src >= 0 && src < seq.in_frames ? __ldg(x + static_cast<size_t>(seq.in_offset + src) * s.cin + c) : 0.0f;
+        c += NARROW_TILE;
+        while (c >= s.cin)
+        {
+            c -= s.cin;
+            ++row;
+        }
+    }
+    __syncthreads();
+    const int f = f0 + t;
+    if (f >= seq.out_frames)
+        return;
+    bool finite = true;
+    for (int o = 0; o < s.cout; ++o)
+    {
+        float sum = 0.0f;
+        for (int tap = 0; tap < s.kernel; ++tap)
+        {
+            const int src = f * s.stride + tap * s.dilation - s.padding;
+            if (src < 0 || src >= seq.in_frames)
+                continue;
+            const float* xr = xs + (src - r0);
+            const float* wr = ws + tap * s.cin * s.cout + o;
+            for (int ch = 0; ch < s.cin; ++ch)
+                sum = __fadd_rn(sum, __fmul_rn(xr[ch * pitch], wr[ch * s.cout]));
+        }
+        const float v = __fadd_rn(sum, __ldg(bias + o));
+        finite = finite && isfinite(v);
+        y[static_cast<size_t>(seq.out_offset + f) * s.cout + o] = v;
+    }
+    if (!finite && error_word)
+        atomicOr(error_word, error_nonfinite);
+}
+
 // ---------------------------------------------------------------- RVQ ----
 struct ArgMax
 {
@@ -610,10 +691,34 @@ void conv1d(const ConvLaunch& l, cudaStream_t stream)
 
 void conv1d_narrow(const float* x, const float* w, const float* bias, float* y,
                    const Sequence* sequences, int sequence_count, const ConvShape& s,
-                   long long total_outputs, unsigned* error_word, cudaStream_t stream)
+                   long long total_outputs, unsigned* error_word, cudaStream_t stream,
+                   long long tiles)
 {
     if (total_outputs <= 0)
         return;
+    // Staged form where the window and weights fit in shared memory.
+    constexpr size_t smem_limit = 200 * 1024;
+    const size_t smem = (static_cast<size_t>(s.cin) * (narrow_span(s.stride, s.kernel, s.dilation) + 1) +
+                         static_cast<size_t>(s.kernel) * s.cin * s.cout) *
+                        sizeof(float);
+    if (!s.transposed && tiles > 0 && tiles < (1ll << 31) && smem <= smem_limit)
+    {
+        static std::once_flag attr_once[64];
+        int device = 0;
+        cudaGetDevice(&device);
+        if (device >= 0 && device < 64)
+            std::call_once(attr_once[device],
+                           []
+                           {
+                               cudaFuncSetAttribute(conv1d_narrow_tile_kernel,
+                                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    static_cast<int>(smem_limit));
+                           });
+        conv1d_narrow_tile_kernel<<<static_cast<int>(tiles), NARROW_TILE, smem, stream>>>(
+            x, w, bias, y, sequences, sequence_count, s, error_word);
+        note_launch();
+        return;
+    }
     conv1d_narrow_kernel<<<static_cast<int>((total_outputs + 127) / 128), 128, 0, stream>>>(
         x, w, bias, y, sequences, sequence_count, s, total_outputs, error_word);
     note_launch();

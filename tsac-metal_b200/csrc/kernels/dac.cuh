@@ -51,10 +51,14 @@ struct ConvLaunch
     bool fast = false;
 };
 void conv1d(const ConvLaunch& launch, cudaStream_t stream);
-// Output channels < 16 (DAC exit to PCM): one thread per output.
+// Output channels < 16 (DAC exit to PCM): one serial chain per output.
+// `tiles` = sum over sequences of ceil(out_frames / 128): with it (and the
+// input window within shared memory) a CTA stages 128 frames' inputs and
+// weights once; 0 runs one thread per output reading global memory.
 void conv1d_narrow(const float* x, const float* w, const float* bias, float* y,
                    const Sequence* sequences, int sequence_count, const ConvShape& shape,
-                   long long total_outputs, unsigned* error_word, cudaStream_t stream);
+                   long long total_outputs, unsigned* error_word, cudaStream_t stream,
+                   long long tiles = 0);
 // Frames per output tile along time (the tile table granularity).
 int conv_tile_frames(const ConvShape& shape);
 
