@@ -386,6 +386,7 @@ __host__ __device__ constexpr int narrow_span(int stride, int kernel, int dilati
     return (NARROW_TILE - 1) * stride + (kernel - 1) * dilation + 1;
 }
 
+template <int COUT> // 1 or 2 output channels, or 0: any (run one after another)
 __global__ void __launch_bounds__(NARROW_TILE)
     conv1d_narrow_tile_kernel(const float* __restrict__ x, const float* __restrict__ w,
                               const float* __restrict__ bias, float* __restrict__ y,
@@ -433,25 +434,81 @@ __global__ void __launch_bounds__(NARROW_TILE)
     if (f >= seq.out_frames)
         return;
     bool finite = true;
-    for (int o = 0; o < s.cout; ++o)
+    if constexpr (COUT > 0)
     {
-        float sum = 0.0f;
+        // The COUT chains advance together (one input load feeds them), each
+        // in its own order.
+        float sum[COUT];
+#pragma unroll
+        for (int o = 0; o < COUT; ++o)
+            sum[o] = 0.0f;
         for (int tap = 0; tap < s.kernel; ++tap)
         {
             const int src = f * s.stride + tap * s.dilation - s.padding;
             if (src < 0 || src >= seq.in_frames)
                 continue;
             const float* xr = xs + (src - r0);
-            const float* wr = ws + tap * s.cin * s.cout + o;
+            const float* wr = ws + tap * s.cin * COUT;
+#pragma unroll 8
             for (int ch = 0; ch < s.cin; ++ch)
-                sum = __fadd_rn(sum, __fmul_rn(xr[ch * pitch], wr[ch * s.cout]));
+            {
+                const float xv = xr[ch * pitch];
+#pragma unroll
+                for (int o = 0; o < COUT; ++o)
+                    sum[o] = __fadd_rn(sum[o], __fmul_rn(xv, wr[ch * COUT + o]));
+            }
         }
-        const float v = __fadd_rn(sum, __ldg(bias + o));
-        finite = finite && isfinite(v);
-        y[static_cast<size_t>(seq.out_offset + f) * s.cout + o] = v;
+#pragma unroll
+        for (int o = 0; o < COUT; ++o)
+        {
+            const float v = __fadd_rn(sum[o], __ldg(bias + o));
+            finite = finite && isfinite(v);
+            y[static_cast<size_t>(seq.out_offset + f) * COUT + o] = v;
+        }
+    }
+    else
+    {
+        for (int o = 0; o < s.cout; ++o)
+        {
+            float sum = 0.0f;
+            for (int tap = 0; tap < s.kernel; ++tap)
+            {
+                const int src = f * s.stride + tap * s.dilation - s.padding;
+                if (src < 0 || src >= seq.in_frames)
+                    continue;
+                const float* xr = xs + (src - r0);
+                const float* wr = ws + tap * s.cin * s.cout + o;
+#pragma unroll 8
+                for (int ch = 0; ch < s.cin; ++ch)
+                    sum = __fadd_rn(sum, __fmul_rn(xr[ch * pitch], wr[ch * s.cout]));
+            }
+            const float v = __fadd_rn(sum, __ldg(bias + o));
+            finite = finite && isfinite(v);
+            y[static_cast<size_t>(seq.out_offset + f) * s.cout + o] = v;
+        }
     }
     if (!finite && error_word)
         atomicOr(error_word, error_nonfinite);
+}
+
+template <int COUT>
+void launch_narrow_tiles(const float* x, const float* w, const float* bias, float* y, const Sequence* sequences,
+                         int sequence_count, const ConvShape& s, unsigned* error_word, cudaStream_t stream,
+                         long long tiles, size_t smem, size_t smem_limit)
+{
+    static std::once_flag attr_once[64];
+    int device = 0;
+    cudaGetDevice(&device);
+    if (device >= 0 && device < 64)
+        std::call_once(attr_once[device],
+                       [smem_limit]
+                       {
+                           cudaFuncSetAttribute(conv1d_narrow_tile_kernel<COUT>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(smem_limit));
+                       });
+    conv1d_narrow_tile_kernel<COUT><<<static_cast<int>(tiles), NARROW_TILE, smem, stream>>>(
+        x, w, bias, y, sequences, sequence_count, s, error_word);
 }
 
 // ---------------------------------------------------------------- RVQ ----
@@ -703,19 +760,15 @@ void conv1d_narrow(const float* x, const float* w, const float* bias, float* y,
                         sizeof(float);
     if (!s.transposed && tiles > 0 && tiles < (1ll << 31) && smem <= smem_limit)
     {
-        static std::once_flag attr_once[64];
-        int device = 0;
-        cudaGetDevice(&device);
-        if (device >= 0 && device < 64)
-            std::call_once(attr_once[device],
-                           []
-                           {
-                               cudaFuncSetAttribute(conv1d_narrow_tile_kernel,
-                                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                    static_cast<int>(smem_limit));
-                           });
-        conv1d_narrow_tile_kernel<<<static_cast<int>(tiles), NARROW_TILE, smem, stream>>>(
-            x, w, bias, y, sequences, sequence_count, s, error_word);
+        if (s.cout == 1)
+            launch_narrow_tiles<1>(x, w, bias, y, sequences, sequence_count, s, error_word, stream, tiles, smem,
+                                   smem_limit);
+        else if (s.cout == 2)
+            launch_narrow_tiles<2>(x, w, bias, y, sequences, sequence_count, s, error_word, stream, tiles, smem,
+                                   smem_limit);
+        else
+            launch_narrow_tiles<0>(x, w, bias, y, sequences, sequence_count, s, error_word, stream, tiles, smem,
+                                   smem_limit);
         note_launch();
         return;
     }
