@@ -72,3 +72,36 @@ def test_context_setters_reject_null_context():
     assert lib.tsac_cuda_set_host_threads(None, ctypes.c_uint(4)) == 1  # TSAC_CUDA_ERROR
     assert b"null" in lib.tsac_cuda_last_error()
     assert lib.tsac_cuda_set_exact_synthesis(None, 1) == 1
+
+
+def test_adopted_buffer_lives_as_long_as_its_arrays():
+    """Decoded PCM comes back in a malloc'd buffer that the binding wraps
+    without copying: the array and its views read it, and the buffer is
+    released (tsac_cuda_free) once the last of them is collected."""
+    import gc
+    import weakref
+
+    import numpy as np
+
+    libc = ctypes.CDLL(None)
+    libc.malloc.restype = ctypes.c_void_p
+    libc.malloc.argtypes = [ctypes.c_size_t]
+    count = 1000
+    raw = libc.malloc(count * 4)
+    assert raw
+    source = np.arange(count, dtype=np.float32)
+    ctypes.memmove(raw, source.ctypes.data, count * 4)
+    freed = []
+    arr = tsac_cuda._adopt(ctypes.c_void_p(raw), count, np.float32)
+    assert arr.dtype == np.float32 and arr.shape == (count,) and arr.ctypes.data == raw
+    assert np.array_equal(arr, source)
+    # The finaliser the binding registered fires once the storage goes away.
+    storage = arr.base
+    weakref.finalize(storage, freed.append, True)
+    view = arr.reshape(-1, 2)
+    del arr, storage
+    gc.collect()
+    assert not freed and view[499, 1] == 999.0
+    del view
+    gc.collect()
+    assert freed == [True]
