@@ -374,15 +374,16 @@ def codec_workload(args, rank, world, torch, dist):
         # nominal 148 SMs x 128 lanes x median SM clock.
         # traffic: DRAM bytes per MAC of the committed ncu capture of this
         # kernel (bench.py --workload frontend --seconds 4, a 128 -> 128 7-tap
-        # layer: 45.9 MB read + 9.5 MB written for 10.10 G MAC), scaled to the
-        # mean launch here by its MACs (streaming activations: bytes grow with MACs).
+        # layer: 45.8 MB read + 2.5 MB written for 10.10 G MAC; the rest of the
+        # output was still in L2 when the launch ended), scaled to the mean
+        # launch here by its MACs (streaming activations: bytes grow with MACs).
         achieved = d["work"] / (d["ms"] / 1e3) / 1e12
         nominal = SM_COUNT * 128 * sm_mhz * 1e6 / 1e12
         probe = fp32_issue_peak(torch)
         peak = probe["tops"] if probe else nominal
         traffic = None
         if name == "conv_exact":
-            traffic = round((45.9e6 + 9.5e6) / 10.10e9 * (d["work"] / 2) / d["launches"])
+            traffic = round((45.8e6 + 2.5e6) / 10.10e9 * (d["work"] / 2) / d["launches"])
         roofline = {"bound": "fp32", "achieved": round(achieved, 2), "peak": round(peak, 2),
                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": traffic,
                     "traffic_source": "ncu capture of a smaller launch, scaled by MACs" if traffic else None,
