@@ -479,18 +479,25 @@ struct TransformerEngine::DecodeState
     {
         DeviceBuffer row_lane, row_begin;
         int rows = 0;
-        cudaGraphExec_t exec = nullptr;
-        unsigned long long kernels = 0; // kernel nodes, for the launch tally
     };
     // (book, active lanes, temporal rows per lane): the lanes active at a
     // step are those longer than it, so the count names the set.
     std::map<std::tuple<int, int, int>, Shape> shapes;
+    // One graph per step shape (active lanes, temporal rows per lane) holding
+    // every book of the step, so consecutive books' kernels overlap through
+    // programmatic dependent launch instead of meeting at graph boundaries.
+    struct StepGraph
+    {
+        cudaGraphExec_t exec = nullptr;
+        unsigned long long kernels = 0; // kernel nodes, for the launch tally
+    };
+    std::map<std::pair<int, int>, StepGraph> step_graphs;
 
     ~DecodeState()
     {
-        for (auto& [key, shape] : shapes)
-            if (shape.exec)
-                cudaGraphExecDestroy(shape.exec);
+        for (auto& [key, graph] : step_graphs)
+            if (graph.exec)
+                cudaGraphExecDestroy(graph.exec);
     }
 };
 
@@ -639,77 +646,91 @@ void TransformerEngine::decode_streams(const std::vector<Header>& headers, const
     for (int p = 0; p < 48; ++p)
         temporal_bytes += weights(p);
 
+    // Row data of (book, active lanes, temporal rows per lane): lanes longer
+    // than the step whose recording has the book, in stream order; each
+    // recording's rows are consecutive.
+    const auto shape_of = [&](int step, int book, int active, int per_lane) -> DecodeState::Shape&
+    {
+        const auto key = std::make_tuple(book, active, book == 0 ? per_lane : 1);
+        auto found = st.shapes.find(key);
+        if (found != st.shapes.end())
+            return found->second;
+        DecodeState::Shape shape;
+        std::vector<int> row_lane;
+        std::vector<int> row_begin(headers.size() + 1, 0);
+        for (int i = 0; i < lane_count; ++i)
+        {
+            const auto& lane = st.lanes[static_cast<std::size_t>(i)];
+            if (st.lengths[static_cast<std::size_t>(i)] > step && book < lane.books)
+            {
+                row_lane.push_back(i);
+                ++row_begin[static_cast<std::size_t>(lane.recording) + 1];
+            }
+        }
+        for (std::size_t r = 0; r < headers.size(); ++r)
+            row_begin[r + 1] += row_begin[r];
+        shape.rows = static_cast<int>(row_lane.size());
+        shape.row_lane.resize(std::max<std::size_t>(row_lane.size(), 1) * 4);
+        shape.row_begin.resize(row_begin.size() * 4);
+        cuda_ok(cudaMemcpy(shape.row_lane.as<void>(), row_lane.data(), row_lane.size() * 4, cudaMemcpyHostToDevice),
+                "H2D");
+        cuda_ok(cudaMemcpy(shape.row_begin.as<void>(), row_begin.data(), row_begin.size() * 4,
+                           cudaMemcpyHostToDevice),
+                "H2D");
+        return st.shapes.emplace(key, std::move(shape)).first->second;
+    };
+
     for (int step = 0; step < steps; ++step)
     {
         int active = 0;
         for (const int length : st.lengths)
             active += length > step;
         const int per_lane = st.step_position[static_cast<std::size_t>(step)] < 0 ? replay_frames : 1;
+        std::vector<DecodeState::Shape*> books;
+        double step_bytes = 0.0;
         for (int book = 0; book < st.max_books; ++book)
         {
-            const auto key = std::make_tuple(book, active, book == 0 ? per_lane : 1);
-            auto found = st.shapes.find(key);
-            if (found == st.shapes.end())
-            {
-                // Rows of this shape: lanes longer than `step` whose recording
-                // has book `book`, in stream order; each recording's rows are
-                // consecutive.
-                DecodeState::Shape shape;
-                std::vector<int> row_lane;
-                std::vector<int> row_begin(headers.size() + 1, 0);
-                for (int i = 0; i < lane_count; ++i)
-                {
-                    const auto& lane = st.lanes[static_cast<std::size_t>(i)];
-                    if (st.lengths[static_cast<std::size_t>(i)] > step && book < lane.books)
-                    {
-                        row_lane.push_back(i);
-                        ++row_begin[static_cast<std::size_t>(lane.recording) + 1];
-                    }
-                }
-                for (std::size_t r = 0; r < headers.size(); ++r)
-                    row_begin[r + 1] += row_begin[r];
-                shape.rows = static_cast<int>(row_lane.size());
-                shape.row_lane.resize(std::max<std::size_t>(row_lane.size(), 1) * 4);
-                shape.row_begin.resize(row_begin.size() * 4);
-                cuda_ok(cudaMemcpy(shape.row_lane.as<void>(), row_lane.data(), row_lane.size() * 4,
-                                   cudaMemcpyHostToDevice),
-                        "H2D");
-                cuda_ok(cudaMemcpy(shape.row_begin.as<void>(), row_begin.data(), row_begin.size() * 4,
-                                   cudaMemcpyHostToDevice),
-                        "H2D");
-                found = st.shapes.emplace(key, std::move(shape)).first;
-                auto& sh = found->second;
-                if (graphs_enabled && sh.rows > 0)
-                {
-                    cudaGraph_t graph = nullptr;
-                    {
-                        dev::CaptureTally tally;
-                        cuda_ok(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "capture");
-                        enqueue_decode_step(sh.row_lane.as<int>(), sh.row_begin.as<int>(), sh.rows, book,
-                                            book == 0 ? per_lane : 1);
-                        cuda_ok(cudaStreamEndCapture(s, &graph), "capture");
-                        sh.kernels = tally.kernels();
-                    }
-                    const auto status = cudaGraphInstantiate(&sh.exec, graph, 0);
-                    cudaGraphDestroy(graph);
-                    cuda_ok(status, "cudaGraphInstantiate");
-                }
-            }
-            auto& sh = found->second;
-            if (sh.rows == 0)
-                continue;
-            KernelTimer::Scope timing("decode_step", s, codebook_bytes + (book == 0 ? temporal_bytes : 0.0));
-            if (sh.exec)
-            {
-                cuda_ok(cudaGraphLaunch(sh.exec, s), "cudaGraphLaunch");
-                dev::note_launch(sh.kernels);
-            }
-            else
-            {
-                enqueue_decode_step(sh.row_lane.as<int>(), sh.row_begin.as<int>(), sh.rows, book,
-                                    book == 0 ? per_lane : 1);
-            }
+            auto& sh = shape_of(step, book, active, per_lane);
+            books.push_back(&sh);
+            if (sh.rows > 0)
+                step_bytes += codebook_bytes + (book == 0 ? temporal_bytes : 0.0);
         }
+        const auto enqueue_books = [&]
+        {
+            for (int book = 0; book < st.max_books; ++book)
+            {
+                const auto& sh = *books[static_cast<std::size_t>(book)];
+                if (sh.rows > 0)
+                    enqueue_decode_step(sh.row_lane.as<int>(), sh.row_begin.as<int>(), sh.rows, book,
+                                        book == 0 ? per_lane : 1);
+            }
+        };
+        if (!graphs_enabled)
+        {
+            KernelTimer::Scope timing("decode_step", s, step_bytes);
+            enqueue_books();
+            continue;
+        }
+        auto& graph = st.step_graphs[std::make_pair(active, per_lane)];
+        if (!graph.exec)
+        {
+            cudaGraph_t captured = nullptr;
+            {
+                dev::CaptureTally tally;
+                cuda_ok(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "capture");
+                enqueue_books();
+                cuda_ok(cudaStreamEndCapture(s, &captured), "capture");
+                graph.kernels = tally.kernels();
+            }
+            const auto status = cudaGraphInstantiate(&graph.exec, captured, 0);
+            cudaGraphDestroy(captured);
+            cuda_ok(status, "cudaGraphInstantiate");
+        }
+        if (graph.kernels == 0)
+            continue;
+        KernelTimer::Scope timing("decode_step", s, step_bytes);
+        cuda_ok(cudaGraphLaunch(graph.exec, s), "cudaGraphLaunch");
+        dev::note_launch(graph.kernels);
     }
     unsigned word = 0;
     cuda_ok(cudaMemcpyAsync(&word, error_word(), 4, cudaMemcpyDeviceToHost, s), "D2H");
