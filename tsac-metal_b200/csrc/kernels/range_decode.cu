@@ -190,10 +190,11 @@ __global__ void __launch_bounds__(rows_warps * 32)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int s = blockIdx.x * rows_warps + warp;
     // Before the dependency wait: the stream's cursor and payload window.
-    // The cursor was last written by the previous step's decoding, many
-    // launches back; every kernel of the chain completes only after its
-    // predecessor has, and this kernel starts only once its predecessor has
-    // passed its own wait, so that write is complete here.
+    // The cursor was last written by this stream's previous decoding (the
+    // previous book of the step, or an earlier step), many launches back.
+    // Every kernel completes only after its predecessor has, and this
+    // kernel's predecessor (softmax_tree_kernel) lets it launch only after
+    // passing its own wait, so that write is complete here.
     const bool active = s < streams && row_begin[s] != row_begin[s + 1];
     RangeCursor c{};
     const std::uint8_t* payload = nullptr;

@@ -155,6 +155,8 @@ __global__ void softmax_tree_kernel(const std::uint16_t* __restrict__ logits,
                                     float* __restrict__ probs_f32, float* __restrict__ tree,
                                     unsigned* error_word)
 {
+    // Wait, then let the next kernel launch: the range decoder that follows
+    // reads its cursor before its own wait and relies on this order.
     pdl_prologue();
     __shared__ SoftmaxShared sh;
     const size_t row = blockIdx.x;
