@@ -7,29 +7,38 @@
 
 namespace tsacb::dev
 {
-// sin^2 of `phase` given its quadrant (the nearest integer to phase * 2/pi)
-// and that quadrant's parity: two-constant reduction, then the odd or even
-// polynomial, squared.
+// Two-constant reduction of `phase` by its quadrant (the nearest integer to
+// phase * 2/pi): x = phase - quadrant * pi/2, |x| <= pi/4.
+__device__ __forceinline__ float reduce_quadrant(float phase, float quadrant)
+{
+    const float x = __fmaf_rn(quadrant, __uint_as_float(0xbfc90000u), phase);
+    return __fmaf_rn(quadrant, __uint_as_float(0xb9fdaa22u), x);
+}
+
+// sin(x) and cos(x) on the reduced interval (x2 = x * x).
+__device__ __forceinline__ float sine_reduced(float x, float x2)
+{
+    float p = __fmaf_rn(__uint_as_float(0xb94ca1f9u), x2, __uint_as_float(0x3c08839eu));
+    p = __fmaf_rn(p, x2, __uint_as_float(0xbe2aaaa3u));
+    const float cube = __fmul_rn(x, x2);
+    return __fmaf_rn(cube, p, x);
+}
+
+__device__ __forceinline__ float cosine_reduced(float x2)
+{
+    float p = __fmaf_rn(__uint_as_float(0x37ccf5ceu), x2, __uint_as_float(0xbab6061au));
+    p = __fmaf_rn(p, x2, __uint_as_float(0x3d2aaaa5u));
+    p = __fmaf_rn(p, x2, __uint_as_float(0xbf000000u));
+    return __fmaf_rn(p, x2, 1.0f);
+}
+
+// sin^2 of `phase` given its quadrant and that quadrant's parity: the odd or
+// even polynomial of the reduced argument, squared.
 __device__ __forceinline__ float sine_squared_reduced(float phase, float quadrant, bool odd)
 {
-    float x = __fmaf_rn(quadrant, __uint_as_float(0xbfc90000u), phase);
-    x = __fmaf_rn(quadrant, __uint_as_float(0xb9fdaa22u), x);
+    const float x = reduce_quadrant(phase, quadrant);
     const float x2 = __fmul_rn(x, x);
-    float value;
-    if (!odd)
-    {
-        float p = __fmaf_rn(__uint_as_float(0xb94ca1f9u), x2, __uint_as_float(0x3c08839eu));
-        p = __fmaf_rn(p, x2, __uint_as_float(0xbe2aaaa3u));
-        const float cube = __fmul_rn(x, x2);
-        value = __fmaf_rn(cube, p, x);
-    }
-    else
-    {
-        float p = __fmaf_rn(__uint_as_float(0x37ccf5ceu), x2, __uint_as_float(0xbab6061au));
-        p = __fmaf_rn(p, x2, __uint_as_float(0x3d2aaaa5u));
-        p = __fmaf_rn(p, x2, __uint_as_float(0xbf000000u));
-        value = __fmaf_rn(p, x2, 1.0f);
-    }
+    const float value = odd ? cosine_reduced(x2) : sine_reduced(x, x2);
     return __fmul_rn(value, value);
 }
 

@@ -121,14 +121,19 @@ __device__ __forceinline__ float snake_scaled(float v, float alpha, float invers
 {
     // The quadrant is rounded, and its parity read, by adding 1.5 * 2^23: the
     // same quadrant as rintf for |phase * 2/pi| < 2^22, without a float ->
-    // int conversion.  Beyond that the parity may select the other
-    // polynomial, whose square is a value in [0, 1] all the same, so the added
-    // term stays within [0, inverse].
+    // int conversion.  Beyond that the parity may pick the other branch; the
+    // result is still a value in [0, 1], so the added term stays within
+    // [0, inverse].  One polynomial serves both parities: for an odd quadrant
+    // sin^2(phase) = cos^2(x) = 1 - sin^2(x), and |x| <= pi/4 keeps
+    // sin^2(x) <= 1/2, so the subtraction loses nothing.
     const float phase = __fmul_rn(alpha, v);
     const float shifted = __fadd_rn(__fmul_rn(phase, __uint_as_float(0x3f22f983u)), 12582912.0f);
     const float quadrant = __fsub_rn(shifted, 12582912.0f);
     const bool odd = (__float_as_uint(shifted) & 1u) != 0;
-    return __fadd_rn(v, __fmul_rn(sine_squared_reduced(phase, quadrant, odd), inverse));
+    const float x = reduce_quadrant(phase, quadrant);
+    const float s = sine_reduced(x, __fmul_rn(x, x));
+    const float s2 = __fmul_rn(s, s);
+    return __fadd_rn(v, __fmul_rn(odd ? __fsub_rn(1.0f, s2) : s2, inverse));
 }
 
 struct TileCoord
