@@ -49,6 +49,14 @@ std::size_t host_workers(const Context& ctx)
     return ctx.host_threads() ? ctx.host_threads() : hw;
 }
 
+// Host threads for the pinned PCM copies: memory bandwidth saturates with a
+// few, and a piece waits for its slowest thread, so more would only add
+// exposure to a busy host.
+std::size_t copy_workers(const Context& ctx)
+{
+    return std::min<std::size_t>(host_workers(ctx), 8);
+}
+
 template <class F> void parallel_for(std::size_t n, std::size_t max_workers, F&& f)
 {
     const std::size_t workers = std::max<std::size_t>(1, std::min(n, max_workers));
@@ -155,7 +163,7 @@ void upload_pcm(Context& ctx, const std::vector<const float*>& src, const std::v
     cudaEvent_t done[2] = {nullptr, nullptr};
     for (auto& e : done)
         cuda_ok(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
-    const std::size_t workers = host_workers(ctx);
+    const std::size_t workers = copy_workers(ctx);
     try
     {
         for (std::size_t p = 0; p < pieces.size(); ++p)
@@ -678,7 +686,7 @@ void download_pcm(Context& ctx, const std::vector<Header>& headers, const std::v
                 "D2H");
         cuda_ok(cudaEventRecord(done[p & 1], s), "cudaEventRecord");
     };
-    const std::size_t workers = host_workers(ctx);
+    const std::size_t workers = copy_workers(ctx);
     try
     {
         issue(0);
